@@ -1,0 +1,310 @@
+"""bench.py -- G1 MSM points/s at 2^24 points per GPU (BASELINE.json metric,
+configs[1]) on B200, one process per GPU.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--log-n L] [--impl b200|reference]
+
+A step is one full G1 Pippenger MSM of the rank's 2^L-point shard (uniform
+254-bit Fr scalars, points k_i * G1 for seeded uniform k_i, generated on the
+device) plus, for N > 1, the all-gather of the per-rank partial points and
+their fold on every rank (the sharded MSM of N * 2^L points; weak scaling).
+
+value : points/s over all ranks with inputs resident in HBM (1.5 GiB per rank,
+        larger than the 126 MB L2, so no flush is needed between steps).
+e2e   : the same MSM through the host-buffer entry point zk_msm_g1_host, with
+        the points and scalars copied from pinned host memory every step and
+        the result read back to the host.
+roofline: the bucket-accumulation kernel (the dominant one) against the
+        measured INT32 multiply-add (IMAD) rate of this GPU.
+cpu_baseline: the oracle's multi-threaded Pippenger (a CPU restatement of the
+        reference's algorithm) on a 2^18-point sample of the same inputs.
+--impl reference: the reference's own CPU MSM path (its host arithmetic,
+        compiled from its sources into oracle/_ref) on all host cores.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cuda-zkml_b200"))
+
+R_MOD = 21888242871839275222246405745257275088548364400416034343698204186575808495617
+METRIC = "G1 MSM points/s @2^24"
+
+
+def msm_ref_ops(n):
+    """Algorithmic Fp multiplications of the reference's Pippenger at n points:
+    11 n W + 32 W (2^c - 1) with (c, W) = MSMConfig::for_size(n)."""
+    c = 10 if n <= 1 << 10 else 12 if n <= 1 << 14 else 14 if n <= 1 << 18 else 15 if n <= 1 << 22 else 16
+    W = (253 + c) // c
+    return 11 * n * W + 32 * W * ((1 << c) - 1)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def emit(obj):
+    print(json.dumps(obj), flush=True)
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ctypes
+
+    import pyoracle as O
+
+    cores = os.cpu_count() or 1
+    n = args.ref_sample
+    rng = O.Rng(0x5EED0000 + args.log_n)
+    k = rng.fr_vector(n)
+    pts = O.g1_fixed_base(k)
+    sc = rng.fr_vector(n)
+    out = np.zeros(8, np.uint64)
+    inf = ctypes.c_int()
+    if O.ref_available():
+        ref = O.ref()
+        kind = "reference"
+
+        def step():
+            ref.ref_msm_g1_naive_mt(O._p(out), ctypes.byref(inf), O._p(pts), O._p(sc), n, cores)
+        what = "reference host arithmetic (src/field, src/curve) and CPU MSM path (src/msm/msm.cu:330-339)"
+    else:
+        kind = "port"
+
+        def step():
+            out[:] = O.msm_g1(pts, sc, nthreads=cores)
+        what = "oracle restatement of the reference Pippenger (oracle/bn254_oracle.c)"
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = n / dt
+    sample = f"{n} of the 2^{args.log_n} points per step, {what}, {cores} threads"
+    emit({"impl": "reference", "metric": METRIC, "value": value, "unit": "points/s", "n_gpus": args.gpus,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+          "config": {"workload": f"G1 MSM, 2^{args.log_n} points per GPU (configs[1])", "log_n": args.log_n,
+                     "sample_points": n},
+          "cpu_baseline": {"value": value, "unit": "points/s", "cores": cores, "kind": kind, "sample": sample},
+          "e2e": {"value": value, "unit": "points/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+# ---------------------------------------------------------------- B200 arm
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    import zkml_b200 as Z
+    import zkml_dist as D
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    n = 1 << args.log_n
+    # inputs: this rank's shard of the global N * 2^L-point MSM
+    k = Z.random_fr(n, 0x5EED0000 + args.log_n + 1000 * rank)
+    sc = Z.random_fr(n, 0x5EED8000 + args.log_n + 1000 * rank)
+    pts_d = Z.g1_fixed_base(Z.to_device(k, dev))
+    sc_d = Z.to_device(sc, dev)
+    del k
+    torch.cuda.synchronize()
+
+    def reduce_max(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def step_device():
+        part = Z.msm_g1(pts_d, sc_d)
+        if world > 1:
+            part = D.combine(D.gather_partials(part, device=dev), Z.g1_add_affine)
+        return part
+
+    imad = max(Z.probe_imad_rate(local) for _ in range(3))
+
+    for _ in range(args.warmup):
+        step_device()
+    stats = []
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step_device()
+            stats.append(Z.msm_last_stats())
+        e1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = reduce_max(e0.elapsed_time(e1) / args.steps)
+    value = world * n / (ms / 1e3)
+
+    acc_ms = reduce_max(statistics.mean(s["accumulate_ms"] for s in stats))
+    adds = stats[-1]["bucket_adds"]
+    launches = stats[-1]["kernel_launches"] * args.steps
+    # algorithmic IMAD of the accumulate kernel: bucket_adds mixed XYZZ additions
+    # (8M + 2S = 10 Fp multiplications each) x 256 IMAD per 8x32-bit Montgomery mul
+    achieved = adds * 10 * 256 / (acc_ms / 1e3)
+    roofline = {"bound": "int32", "kernel": "msm_accumulate_kernel<G1>", "achieved": achieved / 1e12,
+                "peak": imad / 1e12, "unit": "TIMAD/s", "frac": achieved / imad, "traffic": None,
+                "algorithmic": f"{adds} mixed additions x 10 Fp mul x 256 IMAD per launch",
+                "peak_source": "zk_probe_imad_rate, measured in this run (dependency-free IMAD stream)",
+                "msm_whole_frac_ref_ops": 256 * msm_ref_ops(n) / (stats[-1]["total_device_ms"] / 1e3) / imad}
+    prof = os.path.join(ROOT, "profiles", "msm_accumulate_g1_traffic.json")
+    if os.path.exists(prof):
+        try:
+            tr = json.load(open(prof))
+            if tr.get("log_n") == args.log_n:
+                roofline["traffic"] = tr["dram_bytes_per_launch"]
+        except (OSError, ValueError, KeyError):
+            pass
+
+    # e2e: host buffers (pinned), copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        pts_h = torch.empty((n, 8), dtype=torch.int64, pin_memory=True)
+        sc_h = torch.empty((n, 4), dtype=torch.int64, pin_memory=True)
+        pts_h.copy_(pts_d)
+        sc_h.copy_(sc_d)
+        pts_np = pts_h.numpy().view(np.uint64)
+        sc_np = sc_h.numpy().view(np.uint64)
+
+        def step_host():
+            part = Z.msm_g1(pts_np, sc_np, device=local)
+            if world > 1:
+                part = D.combine(D.gather_partials(part, device=dev), Z.g1_add_affine)
+            return part
+
+        for _ in range(max(1, args.warmup // 2)):
+            step_host()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step_host()
+        torch.cuda.synchronize()
+        dt = reduce_max((time.perf_counter() - t0) / args.steps)
+        e2e = {"value": world * n / dt, "unit": "points/s", "h2d_bytes_per_step": n * (64 + 32),
+               "d2h_bytes_per_step": 64 + 4 + stats[-1]["num_windows"] * 128, "ms_per_step": dt * 1e3,
+               "api": "zk_msm_g1_host (pinned host points + scalars)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import pyoracle as O
+        m = 1 << args.cpu_log_n
+        ph = Z.to_host(pts_d[:m])
+        sh = sc[:m]
+        cores = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        O.msm_g1(ph, sh, nthreads=cores)
+        dt = time.perf_counter() - t0
+        cpu = {"value": m / dt, "unit": "points/s", "cores": cores, "kind": "port",
+               "sample": f"first 2^{args.cpu_log_n} of the rank-0 points/scalars, oracle Pippenger "
+                         f"(reference windows c={'/'.join(map(str, (14 if m <= 1 << 18 else 15,)))}), {cores} threads"}
+
+    if rank == 0:
+        emit({"metric": METRIC, "value": value, "unit": "points/s", "n_gpus": world, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+              "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+              "config": {"workload": f"G1 MSM, 2^{args.log_n} points per GPU (configs[1]); sharded MSM of "
+                                     f"{world} x 2^{args.log_n} points", "log_n": args.log_n,
+                         "window_bits": stats[-1]["window_bits"], "num_windows": stats[-1]["num_windows"],
+                         "parallelism": f"points sharded over {world} GPU(s), partial sums all-gathered",
+                         "l2": "inputs 1.5 GiB per GPU > 126 MB L2 (no flush needed)"},
+              "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+              "clocks": sampler.summary(), "accumulate_ms": acc_ms})
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--log-n", type=int, default=24)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-log-n", type=int, default=18)
+    ap.add_argument("--ref-sample", type=int, default=1 << 13)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

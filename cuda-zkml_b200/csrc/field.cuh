@@ -1,0 +1,278 @@
+// field.cuh -- BN254 Fp / Fr / Fp2 arithmetic for sm_100a.
+//
+// Elements are 8 x 32-bit little-endian limbs in Montgomery form (R = 2^256),
+// bit-identical to the reference's 4 x 64-bit host layout
+// (src/field/fp.cuh:30-34, :322-323), so a buffer of reference Fr/Fp values is a
+// buffer of these.  Every operation returns the canonical residue in [0, m), as
+// the reference does (single conditional subtraction, fp.cuh:417-426), which is
+// what makes every downstream result bit-exact regardless of evaluation order.
+//
+// Multiplication is CIOS Montgomery (Koc, Acar & Kaliski, "Analyzing and
+// comparing Montgomery multiplication algorithms", IEEE Micro 1996) on 32-bit
+// limbs.  Each row "T += a_i * B" is issued as two PTX carry chains: the low
+// halves (mad.lo.cc) into T[0..7] and the high halves (mad.hi.cc) into T[1..8].
+// Both chains are complete multi-word additions, so no carry crosses an asm
+// statement.  With m < 2^254 the accumulator stays below 2^288 (9 words) and
+// below 2m after each shift, so one final conditional subtraction suffices.
+#pragma once
+#include <cstdint>
+
+namespace zk {
+
+// Moduli as constexpr accessors (usable in host and device code, folded to
+// immediates once the limb loops are unrolled).
+#define ZK_LIMBS8(name, a0, a1, a2, a3, a4, a5, a6, a7)                                   \
+    __host__ __device__ static constexpr uint32_t name(int i) {                           \
+        return i == 0 ? a0 : i == 1 ? a1 : i == 2 ? a2 : i == 3 ? a3 : i == 4 ? a4 : i == 5 ? a5 : i == 6 ? a6 : a7; \
+    }
+
+struct ModP {  // BN254 base field p
+    ZK_LIMBS8(m, 0xD87CFD47u, 0x3C208C16u, 0x6871CA8Du, 0x97816A91u, 0x8181585Du, 0xB85045B6u, 0xE131A029u, 0x30644E72u)
+    ZK_LIMBS8(one, 0xC58F0D9Du, 0xD35D438Du, 0xF5C70B3Du, 0x0A78EB28u, 0x7879462Cu, 0x666EA36Fu, 0x9A07DF2Fu, 0x0E0A77C1u)
+    ZK_LIMBS8(r2, 0x538AFA89u, 0xF32CFC5Bu, 0xD44501FBu, 0xB5E71911u, 0x0A417FF6u, 0x47AB1EFFu, 0xCAB8351Fu, 0x06D89F71u)
+    static constexpr uint32_t inv = 0xE4866389u;  // -p^-1 mod 2^32
+};
+
+struct ModR {  // BN254 scalar field r
+    ZK_LIMBS8(m, 0xF0000001u, 0x43E1F593u, 0x79B97091u, 0x2833E848u, 0x8181585Du, 0xB85045B6u, 0xE131A029u, 0x30644E72u)
+    ZK_LIMBS8(one, 0x4FFFFFFBu, 0xAC96341Cu, 0x9F60CD29u, 0x36FC7695u, 0x7879462Eu, 0x666EA36Fu, 0x9A07DF2Fu, 0x0E0A77C1u)
+    ZK_LIMBS8(r2, 0xAE216DA7u, 0x1BB8E645u, 0xE35C59E3u, 0x53FE3AB1u, 0x53BB8085u, 0x8C49833Du, 0x7F4E44A5u, 0x0216D0B1u)
+    static constexpr uint32_t inv = 0xEFFFFFFFu;  // -r^-1 mod 2^32
+};
+
+template <class M>
+struct Fe {
+    uint32_t v[8];
+};
+using Fp = Fe<ModP>;
+using Fr = Fe<ModR>;
+
+// --------------------------------------------------------------- limb rows
+// t[0..8] += a * b[0..7]   (caller guarantees no carry out of t[8])
+__device__ __forceinline__ void mac_row(uint32_t& t0, uint32_t& t1, uint32_t& t2, uint32_t& t3,
+                                        uint32_t& t4, uint32_t& t5, uint32_t& t6, uint32_t& t7,
+                                        uint32_t& t8, uint32_t a, const uint32_t* b) {
+    asm("mad.lo.cc.u32  %0, %9, %10, %0;\n\t"
+        "madc.lo.cc.u32 %1, %9, %11, %1;\n\t"
+        "madc.lo.cc.u32 %2, %9, %12, %2;\n\t"
+        "madc.lo.cc.u32 %3, %9, %13, %3;\n\t"
+        "madc.lo.cc.u32 %4, %9, %14, %4;\n\t"
+        "madc.lo.cc.u32 %5, %9, %15, %5;\n\t"
+        "madc.lo.cc.u32 %6, %9, %16, %6;\n\t"
+        "madc.lo.cc.u32 %7, %9, %17, %7;\n\t"
+        "addc.u32       %8, %8, 0;\n\t"
+        "mad.hi.cc.u32  %1, %9, %10, %1;\n\t"
+        "madc.hi.cc.u32 %2, %9, %11, %2;\n\t"
+        "madc.hi.cc.u32 %3, %9, %12, %3;\n\t"
+        "madc.hi.cc.u32 %4, %9, %13, %4;\n\t"
+        "madc.hi.cc.u32 %5, %9, %14, %5;\n\t"
+        "madc.hi.cc.u32 %6, %9, %15, %6;\n\t"
+        "madc.hi.cc.u32 %7, %9, %16, %7;\n\t"
+        "madc.hi.u32    %8, %9, %17, %8;"
+        : "+r"(t0), "+r"(t1), "+r"(t2), "+r"(t3), "+r"(t4), "+r"(t5), "+r"(t6), "+r"(t7), "+r"(t8)
+        : "r"(a), "r"(b[0]), "r"(b[1]), "r"(b[2]), "r"(b[3]), "r"(b[4]), "r"(b[5]), "r"(b[6]),
+          "r"(b[7]));
+}
+
+// r = t - m if t >= m else t   (t < 2m)
+template <class M>
+__device__ __forceinline__ void cond_sub(uint32_t* r, const uint32_t* t) {
+    uint32_t u[8], bw;
+    asm("sub.cc.u32  %0, %9, %17;\n\t"
+        "subc.cc.u32 %1, %10, %18;\n\t"
+        "subc.cc.u32 %2, %11, %19;\n\t"
+        "subc.cc.u32 %3, %12, %20;\n\t"
+        "subc.cc.u32 %4, %13, %21;\n\t"
+        "subc.cc.u32 %5, %14, %22;\n\t"
+        "subc.cc.u32 %6, %15, %23;\n\t"
+        "subc.cc.u32 %7, %16, %24;\n\t"
+        "subc.u32    %8, 0, 0;"
+        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
+          "=r"(u[7]), "=r"(bw)
+        : "r"(t[0]), "r"(t[1]), "r"(t[2]), "r"(t[3]), "r"(t[4]), "r"(t[5]), "r"(t[6]), "r"(t[7]),
+          "r"(M::m(0)), "r"(M::m(1)), "r"(M::m(2)), "r"(M::m(3)), "r"(M::m(4)), "r"(M::m(5)),
+          "r"(M::m(6)), "r"(M::m(7)));
+#pragma unroll
+    for (int i = 0; i < 8; i++) r[i] = bw ? t[i] : u[i];
+}
+
+// --------------------------------------------------------------- Fe ops
+template <class M>
+__device__ __forceinline__ void fmul(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
+    uint32_t t0 = 0, t1 = 0, t2 = 0, t3 = 0, t4 = 0, t5 = 0, t6 = 0, t7 = 0, t8 = 0;
+    constexpr uint32_t mm[8] = {M::m(0), M::m(1), M::m(2), M::m(3), M::m(4), M::m(5), M::m(6), M::m(7)};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        mac_row(t0, t1, t2, t3, t4, t5, t6, t7, t8, a.v[i], b.v);
+        uint32_t q = t0 * M::inv;
+        mac_row(t0, t1, t2, t3, t4, t5, t6, t7, t8, q, mm);
+        // t0 == 0 now: shift down one word
+        t0 = t1; t1 = t2; t2 = t3; t3 = t4; t4 = t5; t5 = t6; t6 = t7; t7 = t8; t8 = 0;
+    }
+    uint32_t t[8] = {t0, t1, t2, t3, t4, t5, t6, t7};
+    cond_sub<M>(r.v, t);
+}
+
+template <class M>
+__device__ __forceinline__ void fsqr(Fe<M>& r, const Fe<M>& a) { fmul(r, a, a); }
+
+template <class M>
+__device__ __forceinline__ void fadd(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
+    uint32_t t[8];
+    asm("add.cc.u32  %0, %8, %16;\n\t"
+        "addc.cc.u32 %1, %9, %17;\n\t"
+        "addc.cc.u32 %2, %10, %18;\n\t"
+        "addc.cc.u32 %3, %11, %19;\n\t"
+        "addc.cc.u32 %4, %12, %20;\n\t"
+        "addc.cc.u32 %5, %13, %21;\n\t"
+        "addc.cc.u32 %6, %14, %22;\n\t"
+        "addc.u32    %7, %15, %23;"
+        : "=r"(t[0]), "=r"(t[1]), "=r"(t[2]), "=r"(t[3]), "=r"(t[4]), "=r"(t[5]), "=r"(t[6]), "=r"(t[7])
+        : "r"(a.v[0]), "r"(a.v[1]), "r"(a.v[2]), "r"(a.v[3]), "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]),
+          "r"(a.v[7]), "r"(b.v[0]), "r"(b.v[1]), "r"(b.v[2]), "r"(b.v[3]), "r"(b.v[4]), "r"(b.v[5]),
+          "r"(b.v[6]), "r"(b.v[7]));
+    cond_sub<M>(r.v, t);
+}
+
+template <class M>
+__device__ __forceinline__ void fdbl(Fe<M>& r, const Fe<M>& a) { fadd(r, a, a); }
+
+template <class M>
+__device__ __forceinline__ void fsub(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
+    uint32_t t[8], bw;
+    asm("sub.cc.u32  %0, %9, %17;\n\t"
+        "subc.cc.u32 %1, %10, %18;\n\t"
+        "subc.cc.u32 %2, %11, %19;\n\t"
+        "subc.cc.u32 %3, %12, %20;\n\t"
+        "subc.cc.u32 %4, %13, %21;\n\t"
+        "subc.cc.u32 %5, %14, %22;\n\t"
+        "subc.cc.u32 %6, %15, %23;\n\t"
+        "subc.cc.u32 %7, %16, %24;\n\t"
+        "subc.u32    %8, 0, 0;"
+        : "=r"(t[0]), "=r"(t[1]), "=r"(t[2]), "=r"(t[3]), "=r"(t[4]), "=r"(t[5]), "=r"(t[6]),
+          "=r"(t[7]), "=r"(bw)
+        : "r"(a.v[0]), "r"(a.v[1]), "r"(a.v[2]), "r"(a.v[3]), "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]),
+          "r"(a.v[7]), "r"(b.v[0]), "r"(b.v[1]), "r"(b.v[2]), "r"(b.v[3]), "r"(b.v[4]), "r"(b.v[5]),
+          "r"(b.v[6]), "r"(b.v[7]));
+    // add back m masked by the borrow word (0 or 0xffffffff)
+    asm("add.cc.u32  %0, %0, %8;\n\t"
+        "addc.cc.u32 %1, %1, %9;\n\t"
+        "addc.cc.u32 %2, %2, %10;\n\t"
+        "addc.cc.u32 %3, %3, %11;\n\t"
+        "addc.cc.u32 %4, %4, %12;\n\t"
+        "addc.cc.u32 %5, %5, %13;\n\t"
+        "addc.cc.u32 %6, %6, %14;\n\t"
+        "addc.u32    %7, %7, %15;"
+        : "+r"(t[0]), "+r"(t[1]), "+r"(t[2]), "+r"(t[3]), "+r"(t[4]), "+r"(t[5]), "+r"(t[6]), "+r"(t[7])
+        : "r"(M::m(0) & bw), "r"(M::m(1) & bw), "r"(M::m(2) & bw), "r"(M::m(3) & bw),
+          "r"(M::m(4) & bw), "r"(M::m(5) & bw), "r"(M::m(6) & bw), "r"(M::m(7) & bw));
+#pragma unroll
+    for (int i = 0; i < 8; i++) r.v[i] = t[i];
+}
+
+template <class M>
+__device__ __forceinline__ bool fis_zero(const Fe<M>& a) {
+    return (a.v[0] | a.v[1] | a.v[2] | a.v[3] | a.v[4] | a.v[5] | a.v[6] | a.v[7]) == 0;
+}
+template <class M>
+__device__ __forceinline__ void fneg(Fe<M>& r, const Fe<M>& a) {
+    Fe<M> z;
+#pragma unroll
+    for (int i = 0; i < 8; i++) z.v[i] = 0;
+    fsub(r, z, a);
+}
+template <class M>
+__device__ __forceinline__ void fset_zero(Fe<M>& r) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) r.v[i] = 0;
+}
+template <class M>
+__device__ __forceinline__ void fset_one(Fe<M>& r) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) r.v[i] = M::one(i);
+}
+template <class M>
+__device__ __forceinline__ bool feq(const Fe<M>& a, const Fe<M>& b) {
+    uint32_t d = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) d |= a.v[i] ^ b.v[i];
+    return d == 0;
+}
+// standard form: a * 1 * R^-1
+template <class M>
+__device__ __forceinline__ void ffrom_mont(Fe<M>& r, const Fe<M>& a) {
+    Fe<M> one;
+    one.v[0] = 1;
+#pragma unroll
+    for (int i = 1; i < 8; i++) one.v[i] = 0;
+    fmul(r, a, one);
+}
+
+// --------------------------------------------------------------- Fp2
+// Fp2 = Fp[u]/(u^2 + 1), as src/field/fp2.cuh:22-134
+struct Fp2 {
+    Fp c0, c1;
+};
+
+__device__ __forceinline__ void fmul(Fp2& r, const Fp2& a, const Fp2& b) {
+    Fp t0, t1, s0, s1;
+    fmul(t0, a.c0, b.c0);
+    fmul(t1, a.c1, b.c1);
+    fadd(s0, a.c0, a.c1);
+    fadd(s1, b.c0, b.c1);
+    fmul(s0, s0, s1);          // (a0+a1)(b0+b1)
+    fsub(r.c0, t0, t1);        // a0b0 - a1b1
+    fsub(s0, s0, t0);
+    fsub(r.c1, s0, t1);        // a0b1 + a1b0
+}
+__device__ __forceinline__ void fsqr(Fp2& r, const Fp2& a) {
+    Fp s, d, m;
+    fadd(s, a.c0, a.c1);
+    fsub(d, a.c0, a.c1);
+    fmul(m, a.c0, a.c1);
+    fmul(r.c0, s, d);          // a0^2 - a1^2
+    fadd(r.c1, m, m);          // 2 a0 a1
+}
+__device__ __forceinline__ void fadd(Fp2& r, const Fp2& a, const Fp2& b) { fadd(r.c0, a.c0, b.c0); fadd(r.c1, a.c1, b.c1); }
+__device__ __forceinline__ void fsub(Fp2& r, const Fp2& a, const Fp2& b) { fsub(r.c0, a.c0, b.c0); fsub(r.c1, a.c1, b.c1); }
+__device__ __forceinline__ void fdbl(Fp2& r, const Fp2& a) { fadd(r.c0, a.c0, a.c0); fadd(r.c1, a.c1, a.c1); }
+__device__ __forceinline__ void fneg(Fp2& r, const Fp2& a) { fneg(r.c0, a.c0); fneg(r.c1, a.c1); }
+__device__ __forceinline__ bool fis_zero(const Fp2& a) { return fis_zero(a.c0) && fis_zero(a.c1); }
+__device__ __forceinline__ void fset_zero(Fp2& r) { fset_zero(r.c0); fset_zero(r.c1); }
+__device__ __forceinline__ void fset_one(Fp2& r) { fset_one(r.c0); fset_zero(r.c1); }
+
+// --------------------------------------------------------------- loads/stores
+template <class M>
+__device__ __forceinline__ void fload(Fe<M>& r, const void* p) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+    uint4 a = q[0], b = q[1];
+    r.v[0] = a.x; r.v[1] = a.y; r.v[2] = a.z; r.v[3] = a.w;
+    r.v[4] = b.x; r.v[5] = b.y; r.v[6] = b.z; r.v[7] = b.w;
+}
+template <class M>
+__device__ __forceinline__ void fload_nc(Fe<M>& r, const void* p) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+    uint4 a = __ldg(q), b = __ldg(q + 1);
+    r.v[0] = a.x; r.v[1] = a.y; r.v[2] = a.z; r.v[3] = a.w;
+    r.v[4] = b.x; r.v[5] = b.y; r.v[6] = b.z; r.v[7] = b.w;
+}
+template <class M>
+__device__ __forceinline__ void fstore(void* p, const Fe<M>& a) {
+    uint4* q = reinterpret_cast<uint4*>(p);
+    q[0] = make_uint4(a.v[0], a.v[1], a.v[2], a.v[3]);
+    q[1] = make_uint4(a.v[4], a.v[5], a.v[6], a.v[7]);
+}
+__device__ __forceinline__ void fload(Fp2& r, const void* p) {
+    fload(r.c0, p);
+    fload(r.c1, reinterpret_cast<const char*>(p) + 32);
+}
+__device__ __forceinline__ void fload_nc(Fp2& r, const void* p) {
+    fload_nc(r.c0, p);
+    fload_nc(r.c1, reinterpret_cast<const char*>(p) + 32);
+}
+__device__ __forceinline__ void fstore(void* p, const Fp2& a) {
+    fstore(p, a.c0);
+    fstore(reinterpret_cast<char*>(p) + 32, a.c1);
+}
+
+}  // namespace zk

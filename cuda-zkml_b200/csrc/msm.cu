@@ -1,0 +1,861 @@
+// msm.cu -- Pippenger multi-scalar multiplication over BN254 G1 and G2 on
+// sm_100a.
+//
+// Replaces the reference's msm_g1 / msm_g2 (src/msm/msm.cu:320-442, :526-598),
+// which accumulate with one global spin lock per bucket and reduce each window
+// on a single thread.  This pipeline has no locks and no unbounded waits:
+//
+//   1. count    : per scalar, Montgomery -> standard form, signed c-bit digits
+//                 d in [-2^(c-1), 2^(c-1)] (Booth-style recoding, so a window
+//                 has 2^(c-1) buckets instead of the reference's 2^c - 1), and
+//                 a histogram of (window, |d|) over all nonzero digits.
+//   2. scan     : exclusive prefix sum of the histogram -> bucket offsets.
+//   3. scatter  : counting sort; key = sign << 31 | point index, grouped by
+//                 (window, bucket).  All windows share one flat key array.
+//   4. accumulate: the flat key array is cut into equal segments, one thread
+//                 each, so the work per thread is fixed however skewed the
+//                 scalars are.  A thread sums its keys' points run by run into
+//                 XYZZ accumulators (mixed additions, points gathered with
+//                 128-bit loads); a run that covers a whole bucket is written
+//                 straight to the bucket, a run cut by a segment boundary goes
+//                 to one of two per-thread partial slots.
+//   5. fixup    : buckets that straddle segments sum their partial slots.
+//   6. reduce   : per window, chunks of buckets are reduced in parallel with
+//                 the running-sum identity sum_b (b+1) S_b (msm.cu:298-304),
+//                 each chunk corrected by lo * (chunk sum) with a short
+//                 double-and-add.
+//   7. windows  : one block per window tree-sums the chunk results.
+//   8. combine  : the W window sums go to the host, which does the Horner
+//                 combine sum_w 2^(c w) S_w (msm.cu:423-430) and the affine
+//                 normalisation.
+#include "curve.cuh"
+#include "host_field.hpp"
+#include "runtime.cuh"
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+namespace zk {
+
+// ------------------------------------------------------------------ plan
+struct MsmPlan {
+    int c = 0;           // window bits
+    int W = 0;           // windows, W * c >= 255 so the top carry is absorbed
+    uint32_t B = 0;      // buckets per window = 2^(c-1)
+    uint32_t nb = 0;     // W * B
+    uint32_t seg = 0;    // keys per accumulate thread
+    size_t max_keys = 0; // n * W
+    size_t max_segs = 0;
+    uint32_t chunk = 0;  // buckets per reduce thread
+    uint32_t tw = 0;     // reduce threads per window
+    uint32_t tiles = 0;  // scan tiles
+};
+
+static constexpr int kScanTile = 4096;  // 1024 threads x 4
+
+static int default_window_bits(size_t n, bool g2) {
+    const char* env = getenv(g2 ? "ZK_MSM_G2_WINDOW_BITS" : "ZK_MSM_WINDOW_BITS");
+    if (env && atoi(env) >= 2 && atoi(env) <= 22) return atoi(env);
+    int lg = 0;
+    while (((size_t)1 << lg) < n) lg++;
+    int c = lg - 3;
+    if (g2) c = lg - 4;
+    return std::max(3, std::min(c, g2 ? 16 : 18));
+}
+
+static MsmPlan make_plan(size_t n, bool g2) {
+    MsmPlan p;
+    p.c = default_window_bits(n, g2);
+    p.W = (255 + p.c - 1) / p.c;
+    p.B = 1u << (p.c - 1);
+    p.nb = (uint32_t)p.W * p.B;
+    p.seg = g2 ? 64 : 128;
+    p.max_keys = n * (size_t)p.W;
+    p.max_segs = (p.max_keys + p.seg - 1) / p.seg;
+    p.chunk = std::min<uint32_t>(p.B, 32);
+    p.tw = p.B / p.chunk;
+    p.tiles = (p.nb + 1 + kScanTile - 1) / kScanTile;
+    return p;
+}
+
+// ------------------------------------------------------------------ digits
+// Signed-digit recoding of a standard-form scalar held in v[0..7], consumed
+// c bits at a time from the bottom (the 256-bit value is shifted in place).
+__device__ __forceinline__ int next_digit(uint32_t v[8], int c, uint32_t& carry) {
+    uint32_t raw = (v[0] & ((1u << c) - 1)) + carry;
+#pragma unroll
+    for (int i = 0; i < 7; i++) v[i] = __funnelshift_r(v[i], v[i + 1], c);
+    v[7] >>= c;
+    uint32_t half = 1u << (c - 1);
+    if (raw > half) {
+        carry = 1;
+        return (int)raw - (int)(1u << c);
+    }
+    carry = 0;
+    return (int)raw;
+}
+
+__global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
+                                 uint32_t* __restrict__ counts) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        Fr s;
+        fload_nc(s, scalars + i);
+        ffrom_mont(s, s);
+        uint32_t carry = 0;
+        for (int w = 0; w < W; w++) {
+            int d = next_digit(s.v, c, carry);
+            if (d) atomicAdd(&counts[(uint32_t)w * B + (uint32_t)(d < 0 ? -d : d) - 1], 1u);
+        }
+    }
+}
+
+__global__ void msm_scatter_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
+                                   uint32_t* __restrict__ cursors, uint32_t* __restrict__ keys) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        Fr s;
+        fload_nc(s, scalars + i);
+        ffrom_mont(s, s);
+        uint32_t carry = 0;
+        for (int w = 0; w < W; w++) {
+            int d = next_digit(s.v, c, carry);
+            if (d) {
+                uint32_t b = (uint32_t)w * B + (uint32_t)(d < 0 ? -d : d) - 1;
+                uint32_t pos = atomicAdd(&cursors[b], 1u);
+                keys[pos] = (d < 0 ? 0x80000000u : 0u) | (uint32_t)i;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ scan
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t x, uint32_t* warp_sums, uint32_t& total) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint32_t incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        uint32_t ws = lane < nw ? warp_sums[lane] : 0;
+        uint32_t wi = ws;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t y = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += y;
+        }
+        if (lane < nw) warp_sums[lane] = wi - ws;
+        if (lane == 31) warp_sums[32] = wi;
+    }
+    __syncthreads();
+    uint32_t r = incl - x + warp_sums[wid];
+    total = warp_sums[32];
+    __syncthreads();
+    return r;
+}
+
+// tile sums of counts[0..len)
+__global__ void scan_tile_sums_kernel(const uint32_t* __restrict__ in, uint32_t len, uint32_t* __restrict__ tile_sums) {
+    __shared__ uint32_t ws[33];
+    uint32_t base = blockIdx.x * kScanTile + threadIdx.x * 4;
+    uint32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) s += (base + k < len) ? in[base + k] : 0u;
+    uint32_t total;
+    block_exclusive_scan(s, ws, total);
+    if (threadIdx.x == 0) tile_sums[blockIdx.x] = total;
+}
+
+// exclusive scan of the tile sums in place (single block)
+__global__ void scan_tiles_kernel(uint32_t* __restrict__ tile_sums, uint32_t tiles) {
+    __shared__ uint32_t ws[33];
+    uint32_t carry = 0;
+    for (uint32_t base = 0; base < tiles; base += blockDim.x) {
+        uint32_t i = base + threadIdx.x;
+        uint32_t x = i < tiles ? tile_sums[i] : 0u;
+        uint32_t total;
+        uint32_t ex = block_exclusive_scan(x, ws, total);
+        if (i < tiles) tile_sums[i] = ex + carry;
+        carry += total;
+    }
+}
+
+// offsets[i] = exclusive prefix of counts, for i in [0, len]; cursors = copy
+__global__ void scan_finish_kernel(const uint32_t* __restrict__ in, uint32_t len, const uint32_t* __restrict__ tile_offs,
+                                   uint32_t* __restrict__ offsets, uint32_t* __restrict__ cursors) {
+    __shared__ uint32_t ws[33];
+    uint32_t base = blockIdx.x * kScanTile + threadIdx.x * 4;
+    uint32_t v[4], s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        v[k] = (base + k < len) ? in[base + k] : 0u;
+        s += v[k];
+    }
+    uint32_t total;
+    uint32_t ex = block_exclusive_scan(s, ws, total) + tile_offs[blockIdx.x];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        if (base + k <= len) {
+            offsets[base + k] = ex;
+            if (base + k < len) cursors[base + k] = ex;
+        }
+        ex += v[k];
+    }
+}
+
+// ------------------------------------------------------------------ accumulate
+template <class Cv>
+__device__ __forceinline__ void load_signed_point(Affine<typename Cv::F>& a, bool& is_inf, const uint8_t* points, uint32_t key) {
+    using F = typename Cv::F;
+    uint32_t idx = key & 0x7fffffffu;
+    load_affine(a, points + (size_t)idx * Cv::kAffineBytes);
+    is_inf = fis_zero(a.x) && fis_zero(a.y);
+    if (key >> 31) { F t; fneg(t, a.y); a.y = t; }
+}
+
+template <class Cv>
+__global__ void __launch_bounds__(128) msm_accumulate_kernel(
+    const uint32_t* __restrict__ keys, const uint32_t* __restrict__ offsets, uint32_t nb, const uint8_t* __restrict__ points,
+    uint32_t seg, uint8_t* __restrict__ bucket_sums, uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last) {
+    using F = typename Cv::F;
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t K = offsets[nb];
+    const size_t start = t * seg;
+    if (start >= K) return;
+    const uint32_t s0 = (uint32_t)start;
+    const uint32_t s1 = (uint32_t)std::min<size_t>(start + seg, K);
+    // bucket g with offsets[g] <= s0 < offsets[g+1]
+    uint32_t lo = 0, hi = nb;
+    while (hi - lo > 1) {
+        uint32_t mid = (lo + hi) >> 1;
+        if (offsets[mid] <= s0) lo = mid; else hi = mid;
+    }
+    uint32_t g = lo, g_begin = offsets[g], g_end = offsets[g + 1];
+    uint32_t run_start = s0;
+    Xyzz<F> acc;
+    set_identity(acc);
+    auto flush = [&](uint32_t run_end) {
+        uint8_t* dst;
+        if (g_begin >= s0 && g_end <= s1) dst = bucket_sums + (size_t)g * Cv::kXyzzBytes;
+        else if (run_start == s0) dst = part_first + t * Cv::kXyzzBytes;
+        else dst = part_last + t * Cv::kXyzzBytes;
+        (void)run_end;
+        store_xyzz(dst, acc);
+    };
+    for (uint32_t p = s0; p < s1; p++) {
+        if (p >= g_end) {
+            flush(p);
+            do { g++; g_end = offsets[g + 1]; } while (p >= g_end);
+            g_begin = offsets[g];
+            run_start = p;
+            set_identity(acc);
+        }
+        Affine<F> a;
+        bool inf;
+        load_signed_point<Cv>(a, inf, points, keys[p]);
+        if (!inf) madd(acc, a);
+    }
+    flush(s1);
+}
+
+// buckets cut by segment boundaries: sum the partial slots
+template <class Cv>
+__global__ void msm_fixup_kernel(const uint32_t* __restrict__ offsets, uint32_t nb, uint32_t seg, const uint8_t* __restrict__ part_first,
+                                 const uint8_t* __restrict__ part_last, uint8_t* __restrict__ bucket_sums) {
+    using F = typename Cv::F;
+    uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= nb) return;
+    uint32_t b0 = offsets[g], b1 = offsets[g + 1];
+    if (b0 == b1) return;
+    uint32_t sa = b0 / seg, sb = (b1 - 1) / seg;
+    if (sa == sb) return;  // whole bucket inside one segment: already written
+    Xyzz<F> acc, q;
+    load_xyzz(acc, (b0 == sa * seg ? part_first : part_last) + (size_t)sa * Cv::kXyzzBytes);
+    for (uint32_t s = sa + 1; s <= sb; s++) {
+        load_xyzz(q, part_first + (size_t)s * Cv::kXyzzBytes);
+        add(acc, q);
+    }
+    store_xyzz(bucket_sums + (size_t)g * Cv::kXyzzBytes, acc);
+}
+
+// ------------------------------------------------------------------ reduce
+// thread (w, j): buckets [lo, lo + chunk) of window w, weight b + 1.
+template <class Cv>
+__global__ void msm_reduce_kernel(const uint32_t* __restrict__ offsets, const uint8_t* __restrict__ bucket_sums, int W, uint32_t B,
+                                  uint32_t chunk, uint32_t tw, uint8_t* __restrict__ chunk_sums) {
+    using F = typename Cv::F;
+    uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tid >= (uint32_t)W * tw) return;
+    uint32_t w = tid / tw, j = tid % tw;
+    uint32_t lo = j * chunk;
+    Xyzz<F> run, acc, q;
+    set_identity(run);
+    set_identity(acc);
+    for (uint32_t b = lo + chunk; b-- > lo;) {
+        uint32_t g = w * B + b;
+        if (offsets[g] != offsets[g + 1]) {
+            load_xyzz(q, bucket_sums + (size_t)g * Cv::kXyzzBytes);
+            add(run, q);
+        }
+        add(acc, run);
+    }
+    // acc = sum (b - lo + 1) S_b; add lo * run
+    if (lo && !is_identity(run)) {
+        Xyzz<F> m;
+        set_identity(m);
+        int top = 31 - __clz(lo);
+        for (int bit = top; bit >= 0; bit--) {
+            Xyzz<F> d;
+            dbl(d, m);
+            m = d;
+            if ((lo >> bit) & 1) add(m, run);
+        }
+        add(acc, m);
+    }
+    store_xyzz(chunk_sums + (size_t)tid * Cv::kXyzzBytes, acc);
+}
+
+// one block per window: tree-sum of the tw chunk results
+template <class Cv>
+__global__ void msm_window_kernel(const uint8_t* __restrict__ chunk_sums, uint32_t tw, uint8_t* __restrict__ scratch,
+                                  uint8_t* __restrict__ window_sums) {
+    using F = typename Cv::F;
+    const uint32_t w = blockIdx.x;
+    const uint8_t* src = chunk_sums + (size_t)w * tw * Cv::kXyzzBytes;
+    uint8_t* tmp = scratch + (size_t)w * blockDim.x * Cv::kXyzzBytes;
+    Xyzz<F> acc, q;
+    set_identity(acc);
+    for (uint32_t j = threadIdx.x; j < tw; j += blockDim.x) {
+        load_xyzz(q, src + (size_t)j * Cv::kXyzzBytes);
+        add(acc, q);
+    }
+    store_xyzz(tmp + (size_t)threadIdx.x * Cv::kXyzzBytes, acc);
+    __syncthreads();
+    for (uint32_t s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) {
+            load_xyzz(acc, tmp + (size_t)threadIdx.x * Cv::kXyzzBytes);
+            load_xyzz(q, tmp + (size_t)(threadIdx.x + s) * Cv::kXyzzBytes);
+            add(acc, q);
+            store_xyzz(tmp + (size_t)threadIdx.x * Cv::kXyzzBytes, acc);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        load_xyzz(acc, tmp);
+        store_xyzz(window_sums + (size_t)w * Cv::kXyzzBytes, acc);
+    }
+}
+
+// ------------------------------------------------------------------ layout conversion
+// reference host records (x, y, bool infinity + pad) -> packed (all-zero = infinity)
+template <int kCoordWords>
+__global__ void pack_ref_points_kernel(const uint64_t* __restrict__ in, size_t n, uint64_t* __restrict__ out) {
+    constexpr int kIn = kCoordWords + 1;  // + flag word
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t* r = in + i * kIn;
+        bool inf = (r[kCoordWords] & 0xff) != 0;
+#pragma unroll
+        for (int k = 0; k < kCoordWords; k++) out[i * kCoordWords + k] = inf ? 0ull : r[k];
+    }
+}
+
+// ------------------------------------------------------------------ fixed base
+// out_i = k_i * G with a byte comb: table[j][d] = d * 2^(8j) * G (affine).
+template <class Cv>
+__device__ void affine_from_xyzz_dev(Affine<typename Cv::F>& a, const Xyzz<typename Cv::F>& p);
+
+template <class M>
+__device__ void finv_dev(Fe<M>& r, const Fe<M>& a) {
+    // a^(m-2), left-to-right square and multiply over the fixed exponent
+    Fe<M> acc;
+    fset_one(acc);
+#pragma unroll
+    for (int limb = 7; limb >= 0; limb--) {
+        const uint32_t word = limb == 0 ? M::m(0) - 2u : M::m(limb);
+        for (int bit = 31; bit >= 0; bit--) {
+            fsqr(acc, acc);
+            if ((word >> bit) & 1u) fmul(acc, acc, a);
+        }
+    }
+    r = acc;
+}
+__device__ __forceinline__ void finv_dev(Fp2& r, const Fp2& a) {
+    Fp n, t, ni;
+    fsqr(n, a.c0);
+    fsqr(t, a.c1);
+    fadd(n, n, t);
+    finv_dev(ni, n);
+    fmul(r.c0, a.c0, ni);
+    fmul(t, a.c1, ni);
+    fneg(r.c1, t);
+}
+
+template <class Cv>
+__global__ void fixed_base_kernel(const uint8_t* __restrict__ table, const Fr* __restrict__ scalars, size_t n, uint8_t* __restrict__ out) {
+    using F = typename Cv::F;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        Fr s;
+        fload_nc(s, scalars + i);
+        ffrom_mont(s, s);
+        Xyzz<F> acc;
+        set_identity(acc);
+        for (int j = 0; j < 32; j++) {
+            uint32_t d = (s.v[0] & 0xffu);
+#pragma unroll
+            for (int k = 0; k < 7; k++) s.v[k] = __funnelshift_r(s.v[k], s.v[k + 1], 8);
+            s.v[7] >>= 8;
+            if (d) {
+                Affine<F> a;
+                load_affine(a, table + ((size_t)j * 256 + d) * Cv::kAffineBytes);
+                madd(acc, a);
+            }
+        }
+        uint8_t* o = out + i * Cv::kAffineBytes;
+        Affine<F> r;
+        if (is_identity(acc)) {
+            fset_zero(r.x);
+            fset_zero(r.y);
+        } else {
+            F zi, zzi;
+            finv_dev(zi, acc.zz);
+            fmul(r.x, acc.x, zi);
+            finv_dev(zzi, acc.zzz);
+            fmul(r.y, acc.y, zzi);
+        }
+        fstore(o, r.x);
+        fstore(o + sizeof(F), r.y);
+    }
+}
+
+// ================================================================== host side
+template <class Cv>
+struct HostCurve;
+template <>
+struct HostCurve<G1> {
+    using F = zkh::Fe;
+    static constexpr int kWords = 4;  // u64 words per coordinate
+};
+template <>
+struct HostCurve<G2> {
+    using F = zkh::Fp2;
+    static constexpr int kWords = 8;
+};
+
+template <class HF>
+static void host_load(HF& f, const uint64_t* w);
+template <>
+void host_load<zkh::Fe>(zkh::Fe& f, const uint64_t* w) { std::memcpy(f.v, w, 32); }
+template <>
+void host_load<zkh::Fp2>(zkh::Fp2& f, const uint64_t* w) { std::memcpy(f.c0.v, w, 32); std::memcpy(f.c1.v, w + 4, 32); }
+template <class HF>
+static void host_store(uint64_t* w, const HF& f);
+template <>
+void host_store<zkh::Fe>(uint64_t* w, const zkh::Fe& f) { std::memcpy(w, f.v, 32); }
+template <>
+void host_store<zkh::Fp2>(uint64_t* w, const zkh::Fp2& f) { std::memcpy(w, f.c0.v, 32); std::memcpy(w + 4, f.c1.v, 32); }
+
+// Horner combine of W window sums (XYZZ records), then affine; out = x || y
+template <class Cv>
+static void host_combine(const uint64_t* windows, int W, int c, uint64_t* out_affine) {
+    using HF = typename HostCurve<Cv>::F;
+    constexpr int kw = HostCurve<Cv>::kWords;
+    zkh::Xyzz<HF> res, s, d;
+    zkh::set_identity(res);
+    for (int w = W - 1; w >= 0; w--) {
+        for (int i = 0; i < c; i++) {
+            zkh::dbl(d, res);
+            res = d;
+        }
+        const uint64_t* r = windows + (size_t)w * 4 * kw;
+        host_load(s.x, r);
+        host_load(s.y, r + kw);
+        host_load(s.zz, r + 2 * kw);
+        host_load(s.zzz, r + 3 * kw);
+        zkh::add(res, s);
+    }
+    HF x, y;
+    zkh::to_affine(x, y, res);
+    host_store(out_affine, x);
+    host_store(out_affine + kw, y);
+}
+
+static inline unsigned grid_for(size_t work, int threads, int cap) {
+    size_t b = (work + threads - 1) / threads;
+    if (b < 1) b = 1;
+    return (unsigned)std::min<size_t>(b, (size_t)cap);
+}
+
+struct LaunchCounter {
+    int n = 0;
+    void operator++(int) { n++; }
+};
+
+// Bucket sort + accumulate + reduce; writes W XYZZ window sums to `windows_dev`.
+// d_points must already hold the packed points when `points_ready` is recorded.
+template <class Cv>
+static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
+                        const MsmPlan& P, Arena& ar, uint8_t* windows_dev, cudaEvent_t points_ready, LaunchCounter& lc,
+                        cudaEvent_t acc_begin, cudaEvent_t acc_end, uint32_t** total_keys_dev) {
+    uint32_t* counts = ar.take<uint32_t>(P.nb + 1);
+    uint32_t* offsets = ar.take<uint32_t>(P.nb + 1);
+    *total_keys_dev = offsets + P.nb;
+    uint32_t* cursors = ar.take<uint32_t>(P.nb);
+    uint32_t* tile_sums = ar.take<uint32_t>(P.tiles);
+    uint32_t* keys = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
+    uint8_t* part_first = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
+    uint8_t* part_last = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
+    uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
+    uint8_t* chunk_sums = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    constexpr int kWinThreads = 128;
+    uint8_t* win_tmp = ar.take<uint8_t>((size_t)P.W * kWinThreads * Cv::kXyzzBytes);
+
+    const int sms = ctx->num_sms;
+    ZK_TRY_CUDA(cudaMemsetAsync(counts, 0, (P.nb + 1) * sizeof(uint32_t), st));
+    msm_count_kernel<<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts);
+    lc++;
+    scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums);
+    lc++;
+    scan_tiles_kernel<<<1, 1024, 0, st>>>(tile_sums, P.tiles);
+    lc++;
+    scan_finish_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums, offsets, cursors);
+    lc++;
+    msm_scatter_kernel<<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, cursors, keys);
+    lc++;
+    if (points_ready) ZK_TRY_CUDA(cudaStreamWaitEvent(st, points_ready, 0));
+    if (acc_begin) ZK_TRY_CUDA(cudaEventRecord(acc_begin, st));
+    {
+        const int threads = 128;
+        unsigned blocks = (unsigned)((P.max_segs + threads - 1) / threads);
+        if (blocks < 1) blocks = 1;
+        msm_accumulate_kernel<Cv><<<blocks, threads, 0, st>>>(keys, offsets, P.nb, (const uint8_t*)d_points, P.seg, buckets,
+                                                               part_first, part_last);
+        lc++;
+    }
+    if (acc_end) ZK_TRY_CUDA(cudaEventRecord(acc_end, st));
+    msm_fixup_kernel<Cv><<<(P.nb + 127) / 128, 128, 0, st>>>(offsets, P.nb, P.seg, part_first, part_last, buckets);
+    lc++;
+    {
+        uint32_t total = (uint32_t)P.W * P.tw;
+        msm_reduce_kernel<Cv><<<(total + 127) / 128, 128, 0, st>>>(offsets, buckets, P.W, P.B, P.chunk, P.tw, chunk_sums);
+        lc++;
+    }
+    msm_window_kernel<Cv><<<P.W, kWinThreads, 0, st>>>(chunk_sums, P.tw, win_tmp, windows_dev);
+    lc++;
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+template <class Cv>
+static size_t pipeline_bytes(const MsmPlan& P) {
+    constexpr int kWinThreads = 128;
+    size_t b = 0;
+    b += Arena::round((P.nb + 1) * 4) * 2 + Arena::round(P.nb * 4) + Arena::round(P.tiles * 4);
+    b += Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
+    b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes);
+    b += Arena::round((size_t)P.nb * Cv::kXyzzBytes);
+    b += Arena::round((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    b += Arena::round((size_t)P.W * kWinThreads * Cv::kXyzzBytes);
+    return b;
+}
+
+// Full MSM.  src_points / src_scalars are device pointers (host_inputs == 0)
+// or host pointers (host_inputs == 1, copied in chunks on the copy stream).
+// ref_layout: points are reference records (72 / 136 B) rather than packed.
+template <class Cv>
+static int msm_run(int device, cudaStream_t user_stream, const void* src_points, const void* src_scalars, size_t n,
+                   bool host_inputs, bool ref_layout, uint64_t* out_affine) {
+    constexpr int kw = HostCurve<Cv>::kWords;
+    MsmStats& stats = msm_stats();
+    stats = MsmStats();
+    if (n == 0) {
+        std::memset(out_affine, 0, 2 * kw * 8);
+        return ZK_OK;
+    }
+    if (n > 0x7fffffffull) {
+        set_error("msm: n = %zu exceeds 2^31 - 1 points", n);
+        return ZK_ERR_RANGE;
+    }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value);
+    stats.window_bits = P.c;
+    stats.num_windows = P.W;
+
+    const size_t pt_bytes = n * Cv::kAffineBytes;
+    const size_t ref_bytes = ref_layout ? n * (Cv::kAffineBytes + 8) : 0;
+    size_t need = pipeline_bytes<Cv>(P) + Arena::round((size_t)P.W * Cv::kXyzzBytes);
+    const bool own_points = host_inputs || ref_layout;
+    if (own_points) need += Arena::round(pt_bytes);
+    if (ref_layout) need += Arena::round(ref_bytes);
+    if (host_inputs) need += Arena::round(n * 32);
+    ZK_TRY(ensure_scratch(ctx, need));
+    ZK_TRY(ensure_pinned(ctx, (size_t)P.W * Cv::kXyzzBytes + 64));
+    Arena ar;
+    ar.base = (char*)ctx->scratch;
+    uint8_t* windows_dev = ar.take<uint8_t>((size_t)P.W * Cv::kXyzzBytes);
+    const void* d_points = src_points;
+    const void* d_scalars = src_scalars;
+    uint8_t* packed = own_points ? ar.take<uint8_t>(pt_bytes) : nullptr;
+    uint8_t* raw = ref_layout ? ar.take<uint8_t>(ref_bytes) : nullptr;
+    uint8_t* sc = host_inputs ? ar.take<uint8_t>(n * 32) : nullptr;
+    LaunchCounter lc;
+
+    cudaEvent_t t0, t1, a0, a1;
+    ZK_TRY_CUDA(cudaEventCreate(&t0));
+    ZK_TRY_CUDA(cudaEventCreate(&t1));
+    ZK_TRY_CUDA(cudaEventCreate(&a0));
+    ZK_TRY_CUDA(cudaEventCreate(&a1));
+    ZK_TRY(scratch_begin(ctx, st));
+    ZK_TRY_CUDA(cudaEventRecord(t0, st));
+
+    cudaEvent_t points_ready = nullptr;
+    if (host_inputs) {
+        // scalars first on the work stream (the sort needs them); points on the
+        // copy stream, overlapped with the decomposition and sort.
+        ZK_TRY_CUDA(cudaMemcpyAsync(sc, src_scalars, n * 32, cudaMemcpyHostToDevice, st));
+        d_scalars = sc;
+        ZK_TRY_CUDA(cudaEventRecord(ctx->ev_a, st));
+        ZK_TRY_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->ev_a, 0));
+        if (ref_layout) {
+            ZK_TRY_CUDA(cudaMemcpyAsync(raw, src_points, ref_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
+            pack_ref_points_kernel<Cv::kAffineBytes / 8><<<grid_for(n, 256, ctx->num_sms * 8), 256, 0, ctx->copy_stream>>>(
+                (const uint64_t*)raw, n, (uint64_t*)packed);
+            lc++;
+        } else {
+            ZK_TRY_CUDA(cudaMemcpyAsync(packed, src_points, pt_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
+        }
+        ZK_TRY_CUDA(cudaEventRecord(ctx->ev_b, ctx->copy_stream));
+        points_ready = ctx->ev_b;
+        d_points = packed;
+    } else if (ref_layout) {
+        pack_ref_points_kernel<Cv::kAffineBytes / 8><<<grid_for(n, 256, ctx->num_sms * 8), 256, 0, st>>>(
+            (const uint64_t*)src_points, n, (uint64_t*)packed);
+        lc++;
+        d_points = packed;
+    }
+
+    uint32_t* total_keys_dev = nullptr;
+    ZK_TRY(msm_pipeline<Cv>(ctx, st, d_points, d_scalars, n, P, ar, windows_dev, points_ready, lc, a0, a1, &total_keys_dev));
+    ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows_dev, (size_t)P.W * Cv::kXyzzBytes, cudaMemcpyDeviceToHost, st));
+    uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
+    ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, total_keys_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaEventRecord(t1, st));
+    ZK_TRY(scratch_end(ctx, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    float ms_all = 0, ms_acc = 0;
+    cudaEventElapsedTime(&ms_all, t0, t1);
+    cudaEventElapsedTime(&ms_acc, a0, a1);
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    cudaEventDestroy(a0);
+    cudaEventDestroy(a1);
+    stats.kernel_launches = lc.n;
+    stats.accumulate_ms = ms_acc;
+    stats.total_device_ms = ms_all;
+    stats.bucket_adds = *keys_host;
+    host_combine<Cv>((const uint64_t*)ctx->pinned, P.W, P.c, out_affine);
+    return ZK_OK;
+}
+
+// ------------------------------------------------------------------ fixed-base tables
+template <class Cv>
+static int fixed_base_table(DeviceContext* ctx, void** table_dev);
+
+template <class Cv>
+static void host_generator(typename HostCurve<Cv>::F& x, typename HostCurve<Cv>::F& y);
+template <>
+void host_generator<G1>(zkh::Fe& x, zkh::Fe& y) {
+    uint64_t one[4] = {1, 0, 0, 0}, two[4] = {2, 0, 0, 0};
+    zkh::from_std(zkh::kP, x, one);
+    zkh::from_std(zkh::kP, y, two);
+}
+template <>
+void host_generator<G2>(zkh::Fp2& x, zkh::Fp2& y) {
+    // EIP-197 G2 generator, standard form (quoted in src/curve/g2.cuh:8-13)
+    static const uint64_t X0[4] = {0x46DEBD5CD992F6EDULL, 0x674322D4F75EDADDULL, 0x426A00665E5C4479ULL, 0x1800DEEF121F1E76ULL};
+    static const uint64_t X1[4] = {0x97E485B7AEF312C2ULL, 0xF1AA493335A9E712ULL, 0x7260BFB731FB5D25ULL, 0x198E9393920D483AULL};
+    static const uint64_t Y0[4] = {0x4CE6CC0166FA7DAAULL, 0xE3D1E7690C43D37BULL, 0x4AAB71808DCB408FULL, 0x12C85EA5DB8C6DEBULL};
+    static const uint64_t Y1[4] = {0x55ACDADCD122975BULL, 0xBC4B313370B38EF3ULL, 0xEC9E99AD690C3395ULL, 0x090689D0585FF075ULL};
+    zkh::from_std(zkh::kP, x.c0, X0);
+    zkh::from_std(zkh::kP, x.c1, X1);
+    zkh::from_std(zkh::kP, y.c0, Y0);
+    zkh::from_std(zkh::kP, y.c1, Y1);
+}
+
+static std::mutex g_table_mu;
+static void* g_tables[64][2];
+
+template <class Cv>
+static int fixed_base_table(DeviceContext* ctx, void** table_dev) {
+    const int which = std::is_same<Cv, G2>::value ? 1 : 0;
+    std::lock_guard<std::mutex> lock(g_table_mu);
+    if (ctx->device < 0 || ctx->device >= 64) return ZK_ERR_INVALID;
+    if (g_tables[ctx->device][which]) {
+        *table_dev = g_tables[ctx->device][which];
+        return ZK_OK;
+    }
+    using HF = typename HostCurve<Cv>::F;
+    constexpr int kw = HostCurve<Cv>::kWords;
+    std::vector<uint64_t> tab((size_t)32 * 256 * 2 * kw, 0);
+    HF gx, gy;
+    host_generator<Cv>(gx, gy);
+    zkh::Xyzz<HF> base, acc, d;
+    zkh::from_affine(base, gx, gy);
+    for (int j = 0; j < 32; j++) {
+        zkh::set_identity(acc);
+        for (int k = 1; k < 256; k++) {
+            zkh::add(acc, base);
+            HF x, y;
+            zkh::to_affine(x, y, acc);
+            uint64_t* r = &tab[((size_t)j * 256 + k) * 2 * kw];
+            host_store(r, x);
+            host_store(r + kw, y);
+        }
+        for (int i = 0; i < 8; i++) {
+            zkh::dbl(d, base);
+            base = d;
+        }
+    }
+    void* p = nullptr;
+    ZK_TRY_CUDA(cudaMalloc(&p, tab.size() * 8));
+    ZK_TRY_CUDA(cudaMemcpy(p, tab.data(), tab.size() * 8, cudaMemcpyHostToDevice));
+    g_tables[ctx->device][which] = p;
+    *table_dev = p;
+    return ZK_OK;
+}
+
+template <class Cv>
+static int fixed_base_run(int device, cudaStream_t user_stream, void* d_out, const void* d_scalars, size_t n) {
+    if (n == 0) return ZK_OK;
+    if (!d_out || !d_scalars) { set_error("fixed_base: null pointer"); return ZK_ERR_INVALID; }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    void* table;
+    ZK_TRY(fixed_base_table<Cv>(ctx, &table));
+    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    fixed_base_kernel<Cv><<<grid_for(n, 128, ctx->num_sms * 8), 128, 0, st>>>((const uint8_t*)table, (const Fr*)d_scalars, n,
+                                                                              (uint8_t*)d_out);
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+// ------------------------------------------------------------------ host point adds
+template <class Cv>
+static void host_add_affine(const uint64_t* a, const uint64_t* b, uint64_t* out) {
+    using HF = typename HostCurve<Cv>::F;
+    constexpr int kw = HostCurve<Cv>::kWords;
+    auto is_zero_rec = [](const uint64_t* r) {
+        for (int i = 0; i < 2 * kw; i++) if (r[i]) return false;
+        return true;
+    };
+    zkh::Xyzz<HF> pa, pb;
+    zkh::set_identity(pa);
+    zkh::set_identity(pb);
+    HF x, y;
+    if (!is_zero_rec(a)) { host_load(x, a); host_load(y, a + kw); zkh::from_affine(pa, x, y); }
+    if (!is_zero_rec(b)) { host_load(x, b); host_load(y, b + kw); zkh::from_affine(pb, x, y); }
+    zkh::add(pa, pb);
+    zkh::to_affine(x, y, pa);
+    host_store(out, x);
+    host_store(out + kw, y);
+}
+
+}  // namespace zk
+
+// ================================================================== C ABI (MSM part)
+using namespace zk;
+
+extern "C" int zk_msm_g1_device(int device, void* stream, const void* d_points, const void* d_scalars, size_t n, void* out_affine) {
+    clear_error();
+    if ((n && (!d_points || !d_scalars)) || !out_affine) { set_error("zk_msm_g1_device: null pointer"); return ZK_ERR_INVALID; }
+    return msm_run<G1>(device, (cudaStream_t)stream, d_points, d_scalars, n, false, false, (uint64_t*)out_affine);
+}
+extern "C" int zk_msm_g1_host(int device, void* stream, const void* h_points, const void* h_scalars, size_t n, void* out_affine) {
+    clear_error();
+    if ((n && (!h_points || !h_scalars)) || !out_affine) { set_error("zk_msm_g1_host: null pointer"); return ZK_ERR_INVALID; }
+    return msm_run<G1>(device, (cudaStream_t)stream, h_points, h_scalars, n, true, false, (uint64_t*)out_affine);
+}
+extern "C" int zk_msm_g2_device(int device, void* stream, const void* d_points, const void* d_scalars, size_t n, void* out_affine) {
+    clear_error();
+    if ((n && (!d_points || !d_scalars)) || !out_affine) { set_error("zk_msm_g2_device: null pointer"); return ZK_ERR_INVALID; }
+    return msm_run<G2>(device, (cudaStream_t)stream, d_points, d_scalars, n, false, false, (uint64_t*)out_affine);
+}
+extern "C" int zk_msm_g2_host(int device, void* stream, const void* h_points, const void* h_scalars, size_t n, void* out_affine) {
+    clear_error();
+    if ((n && (!h_points || !h_scalars)) || !out_affine) { set_error("zk_msm_g2_host: null pointer"); return ZK_ERR_INVALID; }
+    return msm_run<G2>(device, (cudaStream_t)stream, h_points, h_scalars, n, true, false, (uint64_t*)out_affine);
+}
+
+// Reference-shaped: host ref records, result as a ref Jacobian (x, y, one)
+template <class Cv>
+static int ref_msm(const void* h_points, const void* h_scalars, int n, void* out_jacobian) {
+    clear_error();
+    constexpr int kw = HostCurve<Cv>::kWords;
+    if (n < 0 || !out_jacobian || (n > 0 && (!h_points || !h_scalars))) {
+        set_error("msm: invalid arguments (n = %d)", n);
+        return ZK_ERR_INVALID;
+    }
+    uint64_t aff[16];
+    ZK_TRY(msm_run<Cv>(-1, nullptr, h_points, h_scalars, (size_t)n, true, true, aff));
+    uint64_t* o = (uint64_t*)out_jacobian;
+    bool inf = true;
+    for (int i = 0; i < 2 * kw; i++) if (aff[i]) inf = false;
+    std::memset(o, 0, 3 * kw * 8);
+    if (inf) {
+        std::memcpy(o + kw, zkh::kP.one, 32);  // identity (0, one, 0)
+    } else {
+        std::memcpy(o, aff, 2 * kw * 8);
+        std::memcpy(o + 2 * kw, zkh::kP.one, 32);  // Z = one (c1 = 0 for G2)
+    }
+    return ZK_OK;
+}
+
+extern "C" int zk_msm_g1(const void* h_points, const void* h_scalars, int n, void* out_jacobian) {
+    return ref_msm<G1>(h_points, h_scalars, n, out_jacobian);
+}
+extern "C" int zk_msm_g2(const void* h_points, const void* h_scalars, int n, void* out_jacobian) {
+    return ref_msm<G2>(h_points, h_scalars, n, out_jacobian);
+}
+
+extern "C" int zk_g1_fixed_base_device(int device, void* stream, void* d_out, const void* d_scalars, size_t n) {
+    clear_error();
+    return fixed_base_run<G1>(device, (cudaStream_t)stream, d_out, d_scalars, n);
+}
+extern "C" int zk_g2_fixed_base_device(int device, void* stream, void* d_out, const void* d_scalars, size_t n) {
+    clear_error();
+    return fixed_base_run<G2>(device, (cudaStream_t)stream, d_out, d_scalars, n);
+}
+
+extern "C" int zk_g1_add_affine(const void* a, const void* b, void* out) {
+    clear_error();
+    if (!a || !b || !out) { set_error("zk_g1_add_affine: null pointer"); return ZK_ERR_INVALID; }
+    uint64_t r[8];
+    host_add_affine<G1>((const uint64_t*)a, (const uint64_t*)b, r);
+    std::memcpy(out, r, 64);
+    return ZK_OK;
+}
+extern "C" int zk_g2_add_affine(const void* a, const void* b, void* out) {
+    clear_error();
+    if (!a || !b || !out) { set_error("zk_g2_add_affine: null pointer"); return ZK_ERR_INVALID; }
+    uint64_t r[16];
+    host_add_affine<G2>((const uint64_t*)a, (const uint64_t*)b, r);
+    std::memcpy(out, r, 128);
+    return ZK_OK;
+}
+
+extern "C" int zk_msm_last_stats(zk_msm_stats* out) {
+    if (!out) return ZK_ERR_INVALID;
+    const MsmStats& s = msm_stats();
+    out->kernel_launches = s.kernel_launches;
+    out->accumulate_ms = s.accumulate_ms;
+    out->total_device_ms = s.total_device_ms;
+    out->window_bits = s.window_bits;
+    out->num_windows = s.num_windows;
+    out->bucket_adds = s.bucket_adds;
+    return ZK_OK;
+}

@@ -1,0 +1,513 @@
+// ntt.cu -- BN254 Fr NTT / INTT / coset NTT on sm_100a.
+//
+// Replaces the reference's ntt_gpu (src/ntt/ntt.cu:354-465), which runs a
+// bit-reversal scatter, 10 shared-memory stages with per-butterfly
+// square-and-multiply twiddles, then one global radix-2 launch per remaining
+// stage, each preceded by a host twiddle build and a host-to-device copy.
+//
+// Here the transform is the in-place four-step (Bailey) decomposition
+// n = R_0 R_1 ... R_{P-1}, R_p = 2^r_p <= 256:
+//   pass p views each level block of size N_p = R_p R_{p+1} ... as R_p x M_p
+//   (M_p = N_p / R_p) and, for every column j2, computes the R_p-point DFT
+//   over the rows in shared memory (radix-2 DIF stages, roots of order R_p
+//   from a small table), multiplies output k1 by w_{N_p}^(j2 k1), and stores
+//   it back to row k1 of the same column.
+// After the last pass, element X[f] sits at the mixed-radix digit reversal of
+// f; one permutation kernel moves it to natural order and applies any final
+// scale (n^-1) and coset factor (g^-f), so the whole transform is P + 1
+// launches with 2 (P + 1) streaming passes over HBM.  Inter-pass twiddles
+// w_n^e come from two 2^(L/2)-entry tables (w^lo * w^(hi 2^h)), held in L2;
+// nothing of size n is ever read besides the data.
+//
+// A CTA owns C adjacent columns (C = 8: 256-byte contiguous runs per row) or,
+// in the last pass (M = 1), C adjacent contiguous sub-transforms, so every
+// global access is a full 32-byte sector of a coalesced run.
+#include "field.cuh"
+#include "host_field.hpp"
+#include "runtime.cuh"
+
+#include <cstring>
+#include <map>
+#include <memory>
+#include <vector>
+
+namespace zk {
+
+static constexpr int kMaxLogR = 8;
+static constexpr int kNttThreads = 256;
+static constexpr int kTileElems = 2048;  // R * C per CTA (64 KiB of shared memory)
+
+// ------------------------------------------------------------------ tables
+struct NttDirTables {
+    Fr* roots = nullptr;   // w_{2^r}^t for r = 1..8, t < 2^(r-1), concatenated at offset 2^(r-1) - 1
+    Fr* tw_lo = nullptr;   // w_n^i, i < 2^h
+    Fr* tw_hi = nullptr;   // w_n^(i 2^h), i < 2^(L-h)
+    int h = 0;
+};
+struct CosetTables {       // factor(i) = lo[i & (2^h - 1)] * hi[i >> h]
+    Fr* lo = nullptr;
+    Fr* hi = nullptr;
+    int h = 0;
+};
+struct NttTables {
+    std::map<int, NttDirTables> dir;            // key: L * 2 + inverse
+    std::map<std::vector<uint64_t>, CosetTables> coset;  // key: L, kind, g limbs
+};
+
+static void host_fr_pow_u64(zkh::Fe& r, const zkh::Fe& a, uint64_t e) {
+    uint64_t ee[4] = {e, 0, 0, 0};
+    zkh::pow(zkh::kR, r, a, ee);
+}
+
+// primitive 2^L-th root of unity: 5^((r-1)/2^L); w_{2^28} = 5^((r-1)/2^28)
+// (src/ntt/ntt.cu:43-62), then squared 28 - L times (ntt.cu:64-106)
+static zkh::Fe host_root(int L, bool inverse) {
+    uint64_t e[4];
+    std::memcpy(e, zkh::kR.m, 32);
+    e[0] -= 1;
+    for (int s = 0; s < 28; s++)
+        for (int i = 0; i < 4; i++) e[i] = (e[i] >> 1) | (i < 3 ? e[i + 1] << 63 : 0);
+    uint64_t five[4] = {5, 0, 0, 0};
+    zkh::Fe g, w;
+    zkh::from_std(zkh::kR, g, five);
+    zkh::pow(zkh::kR, w, g, e);
+    if (inverse) {
+        zkh::Fe wi;
+        zkh::inv(zkh::kR, wi, w);
+        w = wi;
+    }
+    for (int i = 0; i < 28 - L; i++) zkh::mul(zkh::kR, w, w, w);
+    return w;
+}
+
+static int upload(Fr** dst, const std::vector<zkh::Fe>& v) {
+    ZK_TRY_CUDA(cudaMalloc((void**)dst, v.size() * 32));
+    ZK_TRY_CUDA(cudaMemcpy(*dst, v.data(), v.size() * 32, cudaMemcpyHostToDevice));
+    return ZK_OK;
+}
+
+static void powers(std::vector<zkh::Fe>& out, const zkh::Fe& start, const zkh::Fe& step, size_t count) {
+    out.resize(count);
+    zkh::Fe cur = start;
+    for (size_t i = 0; i < count; i++) {
+        out[i] = cur;
+        zkh::mul(zkh::kR, cur, cur, step);
+    }
+}
+
+static int get_dir_tables(DeviceContext* ctx, int L, bool inverse, const NttDirTables** out) {
+    if (!ctx->ntt) ctx->ntt = new NttTables();
+    int key = L * 2 + (inverse ? 1 : 0);
+    auto it = ctx->ntt->dir.find(key);
+    if (it != ctx->ntt->dir.end()) {
+        *out = &it->second;
+        return ZK_OK;
+    }
+    NttDirTables t;
+    t.h = (L + 1) / 2;
+    zkh::Fe one = zkh::one(zkh::kR);
+    zkh::Fe w = host_root(L, inverse);
+    std::vector<zkh::Fe> v;
+    powers(v, one, w, (size_t)1 << t.h);
+    ZK_TRY(upload(&t.tw_lo, v));
+    zkh::Fe wh = w;
+    for (int i = 0; i < t.h; i++) zkh::mul(zkh::kR, wh, wh, wh);
+    powers(v, one, wh, (size_t)1 << (L - t.h));
+    ZK_TRY(upload(&t.tw_hi, v));
+    std::vector<zkh::Fe> roots;
+    for (int r = 1; r <= kMaxLogR; r++) {
+        std::vector<zkh::Fe> p;
+        powers(p, one, host_root(r, inverse), (size_t)1 << (r - 1));
+        roots.insert(roots.end(), p.begin(), p.end());
+    }
+    ZK_TRY(upload(&t.roots, roots));
+    auto res = ctx->ntt->dir.emplace(key, t);
+    *out = &res.first->second;
+    return ZK_OK;
+}
+
+// kind 0: g^i          (forward coset pre-multiplication)
+// kind 1: n^-1 g^-i    (inverse coset post-multiplication)
+// kind 2: n^-1 g^i     (INTT followed by the coset shift, fused)
+static int get_coset_tables(DeviceContext* ctx, int L, int kind, const zkh::Fe& g, const CosetTables** out) {
+    if (!ctx->ntt) ctx->ntt = new NttTables();
+    std::vector<uint64_t> key = {(uint64_t)L, (uint64_t)kind, g.v[0], g.v[1], g.v[2], g.v[3]};
+    auto it = ctx->ntt->coset.find(key);
+    if (it != ctx->ntt->coset.end()) {
+        *out = &it->second;
+        return ZK_OK;
+    }
+    CosetTables t;
+    t.h = (L + 1) / 2;
+    zkh::Fe one = zkh::one(zkh::kR), step = g, start = one;
+    if (kind == 1) zkh::inv(zkh::kR, step, g);
+    if (kind >= 1) {
+        zkh::Fe two, ninv;
+        uint64_t s2[4] = {2, 0, 0, 0};
+        zkh::from_std(zkh::kR, two, s2);
+        zkh::inv(zkh::kR, ninv, two);
+        start = one;
+        for (int i = 0; i < L; i++) zkh::mul(zkh::kR, start, start, ninv);
+    }
+    std::vector<zkh::Fe> v;
+    powers(v, start, step, (size_t)1 << t.h);
+    ZK_TRY(upload(&t.lo, v));
+    zkh::Fe sh = step;
+    for (int i = 0; i < t.h; i++) zkh::mul(zkh::kR, sh, sh, sh);
+    powers(v, one, sh, (size_t)1 << (L - t.h));
+    ZK_TRY(upload(&t.hi, v));
+    auto res = ctx->ntt->coset.emplace(key, t);
+    *out = &res.first->second;
+    return ZK_OK;
+}
+
+// ------------------------------------------------------------------ kernels
+__device__ __forceinline__ void table_factor(Fr& f, const Fr* lo, const Fr* hi, int h, uint64_t i) {
+    Fr a, b;
+    fload_nc(a, lo + (i & ((1ull << h) - 1)));
+    fload_nc(b, hi + (i >> h));
+    fmul(f, a, b);
+}
+
+template <int LOGR>
+__global__ void __launch_bounds__(kNttThreads) ntt_pass_kernel(const Fr* __restrict__ src, Fr* __restrict__ dst, int L, int Lp, int C,
+                                                               const Fr* __restrict__ roots, const Fr* __restrict__ tw_lo,
+                                                               const Fr* __restrict__ tw_hi, int h, const Fr* __restrict__ cs_lo,
+                                                               const Fr* __restrict__ cs_hi, int cs_h) {
+    constexpr int R = 1 << LOGR;
+    extern __shared__ uint4 smem_raw[];
+    Fr* sm = reinterpret_cast<Fr*>(smem_raw);
+    Fr* sroot = sm + R * C;
+    const uint64_t M = 1ull << (Lp - LOGR);
+    const uint64_t Np = 1ull << Lp;
+    const uint64_t l0 = (uint64_t)blockIdx.x * C;
+    const int E = R * C;
+    const bool col_major = M >= (uint64_t)C;  // C adjacent columns of one level block
+
+    for (int t = threadIdx.x; t < R / 2; t += blockDim.x) {
+        Fr x;
+        fload_nc(x, roots + (R / 2 - 1) + t);
+        fstore(sroot + t, x);
+    }
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int c, j1;
+        if (col_major) { c = e % C; j1 = e / C; } else { j1 = e % R; c = e / R; }
+        const uint64_t line = l0 + c;
+        const uint64_t gi = (line / M) * Np + (line % M) + (uint64_t)j1 * M;
+        Fr x;
+        fload_nc(x, src + gi);
+        if (cs_lo) {  // first pass of a forward coset transform: gi is the natural index
+            Fr f;
+            table_factor(f, cs_lo, cs_hi, cs_h, gi);
+            fmul(x, x, f);
+        }
+        fstore(sm + j1 * C + c, x);
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int hh = R / 2; hh >= 1; hh >>= 1) {
+        for (int u = threadIdx.x; u < (R / 2) * C; u += blockDim.x) {
+            const int c = u % C, q = u / C;
+            const int qh = q % hh;
+            const int j = (q / hh) * 2 * hh + qh;
+            Fr a, b, s, d;
+            fload(a, sm + j * C + c);
+            fload(b, sm + (j + hh) * C + c);
+            fadd(s, a, b);
+            fsub(d, a, b);
+            const int tix = qh * (R / (2 * hh));
+            if (tix) {
+                Fr w;
+                fload(w, sroot + tix);
+                fmul(d, d, w);
+            }
+            fstore(sm + j * C + c, s);
+            fstore(sm + (j + hh) * C + c, d);
+        }
+        __syncthreads();
+    }
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int c, k1;
+        if (col_major) { c = e % C; k1 = e / C; } else { k1 = e % R; c = e / R; }
+        const uint64_t line = l0 + c;
+        const uint64_t j2 = line % M;
+        const int kr = LOGR ? (int)(__brev((unsigned)k1) >> (32 - LOGR)) : 0;
+        Fr y;
+        fload(y, sm + kr * C + c);
+        const uint64_t en = (j2 * (uint64_t)k1) << (L - Lp);
+        if (en) {
+            Fr w;
+            table_factor(w, tw_lo, tw_hi, h, en);
+            fmul(y, y, w);
+        }
+        fstore(dst + (line / M) * Np + j2 + (uint64_t)k1 * M, y);
+    }
+}
+
+// out[f] = src[pos(f)] * factor(f); pos = mixed-radix digit reversal of f.
+// mode 0: no factor; 1: constant; 2: table factor.  When `pa`/`pb` are given
+// the epilogue is the compute_h pointwise step out = (pa*pb - y) * scale.
+struct PermPlan {
+    int P;
+    int r[4];
+};
+__global__ void ntt_permute_kernel(const Fr* __restrict__ src, Fr* __restrict__ dst, int L, PermPlan pp, int mode, Fr scale,
+                                   const Fr* __restrict__ f_lo, const Fr* __restrict__ f_hi, int fh, const Fr* __restrict__ pa,
+                                   const Fr* __restrict__ pb) {
+    const uint64_t n = 1ull << L;
+    for (uint64_t f = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; f < n; f += (uint64_t)gridDim.x * blockDim.x) {
+        uint64_t rem = f, pos = 0;
+        int suffix = L;
+        for (int p = 0; p < pp.P; p++) {
+            const uint64_t k = rem & ((1ull << pp.r[p]) - 1);
+            rem >>= pp.r[p];
+            suffix -= pp.r[p];
+            pos += k << suffix;
+        }
+        Fr y;
+        fload_nc(y, src + pos);
+        if (pa) {
+            Fr a, b;
+            fload_nc(a, pa + f);
+            fload_nc(b, pb + f);
+            fmul(a, a, b);
+            fsub(y, a, y);
+        }
+        if (mode == 1) {
+            fmul(y, y, scale);
+        } else if (mode == 2) {
+            Fr t;
+            table_factor(t, f_lo, f_hi, fh, f);
+            fmul(y, y, t);
+        }
+        fstore(dst + f, y);
+    }
+}
+
+// ------------------------------------------------------------------ host driver
+static PermPlan make_pass_plan(int L) {
+    PermPlan pp;
+    pp.P = (L + kMaxLogR - 1) / kMaxLogR;
+    if (pp.P < 1) pp.P = 1;
+    int rem = L;
+    for (int p = 0; p < pp.P; p++) {
+        int left = pp.P - p;
+        pp.r[p] = (rem + left - 1) / left;  // balanced, larger passes first
+        rem -= pp.r[p];
+    }
+    return pp;
+}
+
+typedef void (*PassFn)(const Fr*, Fr*, int, int, int, const Fr*, const Fr*, const Fr*, int, const Fr*, const Fr*, int);
+
+static PassFn pass_fn(int logr) {
+    switch (logr) {
+        case 1: return ntt_pass_kernel<1>;
+        case 2: return ntt_pass_kernel<2>;
+        case 3: return ntt_pass_kernel<3>;
+        case 4: return ntt_pass_kernel<4>;
+        case 5: return ntt_pass_kernel<5>;
+        case 6: return ntt_pass_kernel<6>;
+        case 7: return ntt_pass_kernel<7>;
+        case 8: return ntt_pass_kernel<8>;
+        default: return nullptr;
+    }
+}
+
+struct FinalOp {
+    int mode = 0;          // 0 none, 1 constant, 2 table
+    Fr scale{};
+    const CosetTables* tab = nullptr;
+    const Fr* pa = nullptr;  // pointwise epilogue operands
+    const Fr* pb = nullptr;
+};
+
+// Forward/inverse passes from `src` into `buf`, then the permute into `dst`.
+// `pre`: optional coset tables applied on the first pass's loads.
+static int ntt_core(DeviceContext* ctx, cudaStream_t st, Fr* dst, const Fr* src, Fr* buf, int L, bool inverse, const CosetTables* pre,
+                    const FinalOp& fin, int* launches) {
+    const uint64_t n = 1ull << L;
+    if (L == 0) {  // a one-point transform is the identity (times the final factor)
+        PermPlan none;
+        none.P = 0;
+        ntt_permute_kernel<<<1, 32, 0, st>>>(src, dst, 0, none, fin.mode, fin.scale, fin.tab ? fin.tab->lo : nullptr,
+                                             fin.tab ? fin.tab->hi : nullptr, fin.tab ? fin.tab->h : 0, fin.pa, fin.pb);
+        (*launches)++;
+        ZK_TRY_CUDA(cudaGetLastError());
+        return ZK_OK;
+    }
+    const NttDirTables* T;
+    ZK_TRY(get_dir_tables(ctx, L, inverse, &T));
+    PermPlan pp = make_pass_plan(L);
+    int Lp = L;
+    const Fr* in = src;
+    for (int p = 0; p < pp.P; p++) {
+        const int r = pp.r[p];
+        const uint64_t M = 1ull << (Lp - r);
+        const uint64_t lines = n >> r;
+        int C;
+        if (M >= 8) C = 8;
+        else C = (int)std::min<uint64_t>(lines, (uint64_t)std::max(1, kTileElems >> r));
+        const size_t smem = ((size_t)(1 << r) * C + (1 << r) / 2 + 1) * sizeof(Fr);
+        PassFn fn = pass_fn(r);
+        static bool attr_set[kMaxLogR + 1][64];
+        if (!attr_set[r][ctx->device]) {
+            ZK_TRY_CUDA(cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+            attr_set[r][ctx->device] = true;
+        }
+        const unsigned grid = (unsigned)(lines / C);
+        fn<<<grid, kNttThreads, smem, st>>>(in, buf, L, Lp, C, T->roots, T->tw_lo, T->tw_hi, T->h, (p == 0 && pre) ? pre->lo : nullptr,
+                                            (p == 0 && pre) ? pre->hi : nullptr, pre ? pre->h : 0);
+        (*launches)++;
+        in = buf;
+        Lp -= r;
+    }
+    const unsigned pgrid = (unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)ctx->num_sms * 16);
+    ntt_permute_kernel<<<pgrid, 256, 0, st>>>(buf, dst, L, pp, fin.mode, fin.scale, fin.tab ? fin.tab->lo : nullptr,
+                                              fin.tab ? fin.tab->hi : nullptr, fin.tab ? fin.tab->h : 0, fin.pa, fin.pb);
+    (*launches)++;
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+static Fr n_inverse_dev(int L) {
+    zkh::Fe two, half, s = zkh::one(zkh::kR);
+    uint64_t s2[4] = {2, 0, 0, 0};
+    zkh::from_std(zkh::kR, two, s2);
+    zkh::inv(zkh::kR, half, two);
+    for (int i = 0; i < L; i++) zkh::mul(zkh::kR, s, s, half);
+    Fr f;
+    std::memcpy(f.v, s.v, 32);
+    return f;
+}
+
+static thread_local int g_ntt_launches = 0;
+
+int ntt_run(int device, cudaStream_t user_stream, void* d_out, const void* d_in, int L, bool inverse, const void* coset_g) {
+    if (!d_out || !d_in) { set_error("ntt: null pointer"); return ZK_ERR_INVALID; }
+    if (L < 0 || L > ZK_NTT_MAX_LOG) { set_error("ntt: log_n = %d outside [0, %d]", L, ZK_NTT_MAX_LOG); return ZK_ERR_RANGE; }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    const uint64_t n = 1ull << L;
+    ZK_TRY(ensure_scratch(ctx, n * 32));
+    Fr* buf = (Fr*)ctx->scratch;
+    const CosetTables* pre = nullptr;
+    FinalOp fin;
+    zkh::Fe g;
+    if (coset_g) std::memcpy(g.v, coset_g, 32);
+    if (!inverse) {
+        if (coset_g) ZK_TRY(get_coset_tables(ctx, L, 0, g, &pre));
+    } else if (coset_g) {
+        fin.mode = 2;
+        ZK_TRY(get_coset_tables(ctx, L, 1, g, &fin.tab));
+    } else {
+        fin.mode = 1;
+        fin.scale = n_inverse_dev(L);
+    }
+    g_ntt_launches = 0;
+    ZK_TRY(scratch_begin(ctx, st));
+    ZK_TRY(ntt_core(ctx, st, (Fr*)d_out, (const Fr*)d_in, buf, L, inverse, pre, fin, &g_ntt_launches));
+    return scratch_end(ctx, st);
+}
+
+// compute_h after the matvec (src/prover/groth16.cu:322-383)
+int compute_h_run(int device, cudaStream_t user_stream, void* d_h, const void* d_a, const void* d_b, const void* d_c, int L) {
+    if (!d_h || !d_a || !d_b || !d_c) { set_error("compute_h: null pointer"); return ZK_ERR_INVALID; }
+    if (L < 0 || L > ZK_NTT_MAX_LOG - 1) { set_error("compute_h: log_n = %d out of range", L); return ZK_ERR_RANGE; }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    const uint64_t n = 1ull << L;
+    ZK_TRY(ensure_scratch(ctx, 4 * n * 32));
+    Fr* buf = (Fr*)ctx->scratch;
+    Fr* A = buf + n;
+    Fr* B = buf + 2 * n;
+    Fr* Cc = buf + 3 * n;
+    // coset generator g = 5, or 7 when 5^n == 1 (groth16.cu:329-342)
+    zkh::Fe g, z, one = zkh::one(zkh::kR);
+    uint64_t s5[4] = {5, 0, 0, 0}, s7[4] = {7, 0, 0, 0};
+    zkh::from_std(zkh::kR, g, s5);
+    auto vanish = [&](const zkh::Fe& gg) {
+        zkh::Fe t = gg;
+        for (int i = 0; i < L; i++) zkh::mul(zkh::kR, t, t, t);
+        zkh::sub(zkh::kR, t, t, one);
+        return t;
+    };
+    z = vanish(g);
+    if (zkh::is_zero(z)) {
+        zkh::from_std(zkh::kR, g, s7);
+        z = vanish(g);
+    }
+    if (zkh::is_zero(z)) { set_error("compute_h: no valid coset shift"); return ZK_ERR_INVALID; }
+    zkh::Fe zinv;
+    zkh::inv(zkh::kR, zinv, z);
+    const CosetTables *to_coset, *from_coset;
+    ZK_TRY(get_coset_tables(ctx, L, 2, g, &to_coset));    // n^-1 g^i
+    ZK_TRY(get_coset_tables(ctx, L, 1, g, &from_coset));  // n^-1 g^-i
+    int launches = 0;
+    ZK_TRY(scratch_begin(ctx, st));
+    const Fr* ev[3] = {(const Fr*)d_a, (const Fr*)d_b, (const Fr*)d_c};
+    Fr* co[3] = {A, B, Cc};
+    for (int k = 0; k < 3; k++) {
+        FinalOp f1;
+        f1.mode = 2;
+        f1.tab = to_coset;  // coefficients times n^-1 g^i: the coset shift is fused into the INTT
+        ZK_TRY(ntt_core(ctx, st, co[k], ev[k], buf, L, true, nullptr, f1, &launches));
+        FinalOp f2;
+        if (k == 2) {  // pointwise (A B - C) / (g^n - 1) fused into the last forward permute
+            f2.mode = 1;
+            std::memcpy(f2.scale.v, zinv.v, 32);
+            f2.pa = A;
+            f2.pb = B;
+        }
+        ZK_TRY(ntt_core(ctx, st, co[k], co[k], buf, L, false, nullptr, f2, &launches));
+    }
+    FinalOp f3;
+    f3.mode = 2;
+    f3.tab = from_coset;
+    ZK_TRY(ntt_core(ctx, st, (Fr*)d_h, Cc, buf, L, true, nullptr, f3, &launches));
+    g_ntt_launches = launches;
+    return scratch_end(ctx, st);
+}
+
+}  // namespace zk
+
+using namespace zk;
+
+extern "C" int zk_ntt_device(int device, void* stream, void* d_out, const void* d_in, int log_n, int inverse, const void* coset_shift) {
+    clear_error();
+    return ntt_run(device, (cudaStream_t)stream, d_out, d_in, log_n, inverse != 0, coset_shift);
+}
+
+extern "C" int zk_compute_h_device(int device, void* stream, void* d_h, const void* d_a, const void* d_b, const void* d_c, int log_n) {
+    clear_error();
+    return compute_h_run(device, (cudaStream_t)stream, d_h, d_a, d_b, d_c, log_n);
+}
+
+// reference-shaped: synchronous on the current device
+extern "C" int zk_ntt(void* d_out, const void* d_in, int log_n, int inverse) {
+    clear_error();
+    if (log_n < 0 || log_n > ZK_REF_NTT_MAX_LOG) {
+        set_error("[NTT] Error: log_n=%d exceeds max %d", log_n, ZK_REF_NTT_MAX_LOG);
+        return ZK_ERR_RANGE;
+    }
+    ZK_TRY(ntt_run(-1, nullptr, d_out, d_in, log_n, inverse != 0, nullptr));
+    DeviceContext* ctx;
+    ZK_TRY(get_context(-1, &ctx));
+    ZK_TRY_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ZK_OK;
+}
+
+extern "C" int zk_ntt_inplace(void* d_data, int log_n, int inverse) { return zk_ntt(d_data, d_data, log_n, inverse); }
+
+extern "C" int zk_compute_omega(int log_n, int inverse, void* out_fr) {
+    clear_error();
+    if (!out_fr) return ZK_ERR_INVALID;
+    if (log_n < 0 || log_n > ZK_NTT_MAX_LOG) { set_error("compute_omega: log_n = %d out of range", log_n); return ZK_ERR_RANGE; }
+    zkh::Fe w = host_root(log_n, inverse != 0);
+    std::memcpy(out_fr, w.v, 32);
+    return ZK_OK;
+}

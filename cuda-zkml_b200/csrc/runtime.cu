@@ -1,0 +1,182 @@
+// runtime.cu -- device contexts, scratch arenas, error channel, and the small
+// C-ABI utilities (version, device count, last error, IMAD-rate probe).
+#include "runtime.cuh"
+
+#include <cstring>
+#include <string>
+
+namespace zk {
+
+static thread_local char g_err[512];
+static thread_local MsmStats g_msm_stats;
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+}
+void clear_error() { g_err[0] = 0; }
+MsmStats& msm_stats() { return g_msm_stats; }
+
+static std::mutex g_ctx_mu;
+static DeviceContext* g_ctx[64];
+
+int get_context(int device, DeviceContext** out) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        set_error("no usable CUDA device (%s)", e == cudaSuccess ? "device count is 0" : cudaGetErrorString(e));
+        return ZK_ERR_NODEV;
+    }
+    if (device < 0) ZK_TRY_CUDA(cudaGetDevice(&device));
+    if (device >= count || device >= 64) {
+        set_error("device %d out of range (%d visible)", device, count);
+        return ZK_ERR_INVALID;
+    }
+    ZK_TRY_CUDA(cudaSetDevice(device));
+    std::lock_guard<std::mutex> lock(g_ctx_mu);
+    if (!g_ctx[device]) {
+        DeviceContext* c = new DeviceContext();
+        c->device = device;
+        cudaDeviceProp prop;
+        ZK_TRY_CUDA(cudaGetDeviceProperties(&prop, device));
+        if (prop.major < 10) {
+            set_error("device %d is sm_%d%d; this library is built for sm_100a only", device, prop.major, prop.minor);
+            delete c;
+            return ZK_ERR_NODEV;
+        }
+        c->num_sms = prop.multiProcessorCount;
+        ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+        ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_a, cudaEventDisableTiming));
+        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_b, cudaEventDisableTiming));
+        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_c, cudaEventDisableTiming));
+        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->scratch_done, cudaEventDisableTiming));
+        ZK_TRY_CUDA(cudaEventRecord(c->scratch_done, c->stream));
+        g_ctx[device] = c;
+    }
+    *out = g_ctx[device];
+    return ZK_OK;
+}
+
+int ensure_scratch(DeviceContext* ctx, size_t bytes) {
+    if (ctx->scratch_bytes >= bytes) return ZK_OK;
+    ZK_TRY_CUDA(cudaDeviceSynchronize());
+    if (ctx->scratch) ZK_TRY_CUDA(cudaFree(ctx->scratch));
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+    size_t want = bytes + bytes / 8;  // headroom against small growth
+    cudaError_t e = cudaMalloc(&ctx->scratch, want);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        e = cudaMalloc(&ctx->scratch, bytes);
+        want = bytes;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        ctx->scratch = nullptr;
+        set_error("scratch allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+        return ZK_ERR_NOMEM;
+    }
+    ctx->scratch_bytes = want;
+    return ZK_OK;
+}
+
+int scratch_begin(DeviceContext* ctx, cudaStream_t st) {
+    ZK_TRY_CUDA(cudaStreamWaitEvent(st, ctx->scratch_done, 0));
+    return ZK_OK;
+}
+int scratch_end(DeviceContext* ctx, cudaStream_t st) {
+    ZK_TRY_CUDA(cudaEventRecord(ctx->scratch_done, st));
+    return ZK_OK;
+}
+
+int ensure_pinned(DeviceContext* ctx, size_t bytes) {
+    if (ctx->pinned_bytes >= bytes) return ZK_OK;
+    if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    ctx->pinned = nullptr;
+    ctx->pinned_bytes = 0;
+    cudaError_t e = cudaMallocHost(&ctx->pinned, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("pinned staging allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+        return ZK_ERR_NOMEM;
+    }
+    ctx->pinned_bytes = bytes;
+    return ZK_OK;
+}
+
+// ------------------------------------------------------------------ IMAD probe
+// Each thread runs 16 independent multiply-add chains (8 mad.lo, 8 mad.hi);
+// every iteration issues 16 IMAD-class instructions and nothing else.  The
+// result feeds a store so the work cannot be removed.
+__global__ void imad_probe_kernel(uint32_t* out, uint32_t seed, int iters) {
+    uint32_t lo[8], hi[8];
+    const uint32_t b = seed | 1u, c = seed ^ 0x9e3779b9u;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        lo[k] = seed + threadIdx.x * 8 + k;
+        hi[k] = k;
+    }
+    for (int i = 0; i < iters; i++) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            asm volatile("mad.hi.u32 %1, %0, %2, %1;\n\tmad.lo.u32 %0, %0, %2, %3;"
+                         : "+r"(lo[k]), "+r"(hi[k])
+                         : "r"(b), "r"(c));
+        }
+    }
+    uint32_t x = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) x ^= lo[k] ^ hi[k];
+    out[blockIdx.x * blockDim.x + threadIdx.x] = x;
+}
+
+}  // namespace zk
+
+using namespace zk;
+
+extern "C" const char* zk_last_error(void) { return g_err; }
+
+extern "C" int zk_version(void) { return 100; }
+
+extern "C" int zk_device_count(int* count) {
+    clear_error();
+    if (!count) return ZK_ERR_INVALID;
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        c = 0;
+    }
+    *count = c;
+    return ZK_OK;
+}
+
+extern "C" int zk_probe_imad_rate(int device, double* rate) {
+    clear_error();
+    if (!rate) return ZK_ERR_INVALID;
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const int threads = 512, blocks = ctx->num_sms * 4, iters = 4096;
+    uint32_t* buf;
+    ZK_TRY_CUDA(cudaMalloc(&buf, (size_t)threads * blocks * 4));
+    cudaEvent_t a, b;
+    ZK_TRY_CUDA(cudaEventCreate(&a));
+    ZK_TRY_CUDA(cudaEventCreate(&b));
+    imad_probe_kernel<<<blocks, threads, 0, ctx->stream>>>(buf, 12345u, 64);  // warm-up
+    ZK_TRY_CUDA(cudaEventRecord(a, ctx->stream));
+    imad_probe_kernel<<<blocks, threads, 0, ctx->stream>>>(buf, 777u, iters);
+    ZK_TRY_CUDA(cudaEventRecord(b, ctx->stream));
+    ZK_TRY_CUDA(cudaEventSynchronize(b));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaFree(buf);
+    double instr = (double)threads * blocks * iters * 16.0;
+    *rate = instr / (ms * 1e-3);
+    return ZK_OK;
+}

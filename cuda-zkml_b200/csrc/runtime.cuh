@@ -1,0 +1,88 @@
+// runtime.cuh -- per-device context of the B200 prover runtime: streams, a
+// growable device scratch arena, pinned host staging, cached NTT tables and
+// the thread-local error channel behind the C ABI's status codes.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/zkml_b200.h"
+
+namespace zk {
+
+void set_error(const char* fmt, ...);
+void clear_error();
+
+#define ZK_TRY_CUDA(call)                                                                \
+    do {                                                                                 \
+        cudaError_t e_ = (call);                                                         \
+        if (e_ != cudaSuccess) {                                                         \
+            ::zk::set_error("%s:%d %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+            return e_ == cudaErrorMemoryAllocation ? ZK_ERR_NOMEM : ZK_ERR_CUDA;         \
+        }                                                                                \
+    } while (0)
+
+#define ZK_TRY(call)                 \
+    do {                             \
+        int s_ = (call);             \
+        if (s_ != ZK_OK) return s_;  \
+    } while (0)
+
+// bump allocator over one device buffer; all offsets 256-byte aligned
+struct Arena {
+    char* base = nullptr;
+    size_t used = 0;
+    template <class T>
+    T* take(size_t count) {
+        size_t bytes = (count * sizeof(T) + 255) & ~size_t(255);
+        T* p = reinterpret_cast<T*>(base + used);
+        used += bytes;
+        return p;
+    }
+    static size_t round(size_t bytes) { return (bytes + 255) & ~size_t(255); }
+};
+
+struct NttTables;  // ntt.cu
+
+struct DeviceContext {
+    int device = -1;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;   // default work stream
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_c = nullptr;
+    cudaEvent_t scratch_done = nullptr;  // last work that used `scratch`
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    void* pinned = nullptr;          // small pinned host staging (results)
+    size_t pinned_bytes = 0;
+    NttTables* ntt = nullptr;
+    std::mutex mu;                   // one call at a time per device context
+};
+
+// Lazily created context of `device` (-1 = the calling thread's current device).
+// Makes `device` current on the calling thread.
+int get_context(int device, DeviceContext** out);
+// Ensure the scratch arena holds at least `bytes` (synchronises on growth).
+int ensure_scratch(DeviceContext* ctx, size_t bytes);
+int ensure_pinned(DeviceContext* ctx, size_t bytes);
+// Order a call's work on `st` after the previous user of the scratch arena
+// (which may have run on another stream), and mark the end of its use.
+int scratch_begin(DeviceContext* ctx, cudaStream_t st);
+int scratch_end(DeviceContext* ctx, cudaStream_t st);
+
+// per-thread statistics of the last MSM
+struct MsmStats {
+    int kernel_launches = 0;
+    float accumulate_ms = 0.f;
+    float total_device_ms = 0.f;
+    int window_bits = 0;
+    int num_windows = 0;
+    long long bucket_adds = 0;
+};
+MsmStats& msm_stats();
+
+}  // namespace zk

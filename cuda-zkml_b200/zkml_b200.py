@@ -1,0 +1,304 @@
+"""Python binding of libzkml_b200.so (ctypes over the C ABI in include/zkml_b200.h).
+
+Device buffers are torch CUDA tensors (any dtype; the raw bytes are used) and
+calls are ordered on torch's current CUDA stream.  Host buffers are numpy
+arrays.  Field elements are 32-byte Montgomery-form little-endian values:
+numpy uint64 arrays of shape (n, 4); packed G1 points are (n, 8), packed G2
+points (n, 16); the all-zero record is the point at infinity.
+
+There is no CPU fallback: if the shared library is missing this module raises
+at import, and every compute call raises ZkError when no CUDA device is usable.
+"""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzkml_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "zkml_b200.h")
+
+ZK_OK, ZK_ERR_INVALID, ZK_ERR_CUDA, ZK_ERR_NOMEM, ZK_ERR_NODEV, ZK_ERR_RANGE = 0, 1, 2, 3, 4, 5
+
+R_MOD = 21888242871839275222246405745257275088548364400416034343698204186575808495617
+P_MOD = 21888242871839275222246405745257275088696311157297823662689037894645226208583
+
+
+class ZkError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"zkml_b200 status {status}: {message}")
+        self.status = status
+
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is not built (run `make -C {HERE}` or __graft_entry__.build())")
+
+lib = ctypes.CDLL(LIB_PATH)
+lib.zk_last_error.restype = ctypes.c_char_p
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_i = ctypes.c_int
+
+
+class MsmStats(ctypes.Structure):
+    _fields_ = [("kernel_launches", ctypes.c_int), ("accumulate_ms", ctypes.c_float),
+                ("total_device_ms", ctypes.c_float), ("window_bits", ctypes.c_int),
+                ("num_windows", ctypes.c_int), ("bucket_adds", ctypes.c_longlong)]
+
+
+_SIGS = {
+    "zk_device_count": [ctypes.POINTER(ctypes.c_int)],
+    "zk_version": [],
+    "zk_msm_g1": [_vp, _vp, _i, _vp],
+    "zk_msm_g2": [_vp, _vp, _i, _vp],
+    "zk_ntt": [_vp, _vp, _i, _i],
+    "zk_ntt_inplace": [_vp, _i, _i],
+    "zk_compute_omega": [_i, _i, _vp],
+    "zk_msm_g1_device": [_i, _vp, _vp, _vp, _sz, _vp],
+    "zk_msm_g1_host": [_i, _vp, _vp, _vp, _sz, _vp],
+    "zk_msm_g2_device": [_i, _vp, _vp, _vp, _sz, _vp],
+    "zk_msm_g2_host": [_i, _vp, _vp, _vp, _sz, _vp],
+    "zk_ntt_device": [_i, _vp, _vp, _vp, _i, _i, _vp],
+    "zk_compute_h_device": [_i, _vp, _vp, _vp, _vp, _vp, _i],
+    "zk_g1_fixed_base_device": [_i, _vp, _vp, _vp, _sz],
+    "zk_g2_fixed_base_device": [_i, _vp, _vp, _vp, _sz],
+    "zk_g1_add_affine": [_vp, _vp, _vp],
+    "zk_g2_add_affine": [_vp, _vp, _vp],
+    "zk_probe_imad_rate": [_i, ctypes.POINTER(ctypes.c_double)],
+    "zk_msm_last_stats": [ctypes.POINTER(MsmStats)],
+}
+for _name, _args in _SIGS.items():
+    getattr(lib, _name).argtypes = _args
+    getattr(lib, _name).restype = ctypes.c_int
+
+
+def declared_symbols():
+    """Function names declared in include/zkml_b200.h."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*|void)\s+(zk_\w+)\s*\(", text, re.M)))
+
+
+def check(status):
+    if status != ZK_OK:
+        raise ZkError(status, lib.zk_last_error().decode(errors="replace"))
+
+
+def last_error():
+    return lib.zk_last_error().decode(errors="replace")
+
+
+def device_count():
+    c = ctypes.c_int(0)
+    check(lib.zk_device_count(ctypes.byref(c)))
+    return c.value
+
+
+# ------------------------------------------------------------------ helpers
+def _np_ptr(a):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_vp)
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dev_ptr(t):
+    torch = _torch()
+    assert isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous(), "expected a contiguous CUDA tensor"
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t):
+    torch = _torch()
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def to_device(arr, device="cuda"):
+    """numpy uint64 array -> int64 CUDA tensor with the same bytes."""
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(arr).view(np.int64)).to(device)
+
+
+def to_host(t):
+    """CUDA tensor -> numpy uint64 array with the same bytes."""
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+def random_fr(n, seed):
+    """n uniform Fr values (Montgomery form is a bijection of [0, r), so uniform
+    canonical values are uniform Montgomery representations): (n, 4) uint64."""
+    rng = np.random.default_rng(seed)
+    out = np.empty((n, 4), dtype=np.uint64)
+    need = np.arange(n)
+    r_top = R_MOD >> 192
+    while need.size:
+        cand = rng.integers(0, 2**64, size=(need.size, 4), dtype=np.uint64)
+        cand[:, 3] &= np.uint64((1 << 62) - 1)
+        top = cand[:, 3]
+        ok = top < np.uint64(r_top)  # strictly below r's top limb => below r
+        out[need[ok]] = cand[ok]
+        need = need[~ok]
+    return out
+
+
+def fr_from_int(x):
+    """Montgomery form of the integer x mod r as (4,) uint64."""
+    v = (x % R_MOD) * (1 << 256) % R_MOD
+    return np.array([(v >> (64 * i)) & (2**64 - 1) for i in range(4)], dtype=np.uint64)
+
+
+def fr_to_int(limbs):
+    v = sum(int(w) << (64 * i) for i, w in enumerate(np.asarray(limbs, dtype=np.uint64).ravel()))
+    return v * pow(1 << 256, -1, R_MOD) % R_MOD
+
+
+# ------------------------------------------------------------------ MSM
+def msm_g1(points, scalars, device=None):
+    """Sum s_i P_i over G1.  torch CUDA tensors -> device path on the current
+    stream; numpy arrays -> host path (copies pipelined inside).  Returns the
+    affine result as (8,) uint64 (all zero for the identity)."""
+    return _msm(points, scalars, device, g2=False)
+
+
+def msm_g2(points, scalars, device=None):
+    return _msm(points, scalars, device, g2=True)
+
+
+def _msm(points, scalars, device, g2):
+    words = 16 if g2 else 8
+    out = np.zeros(words, dtype=np.uint64)
+    if isinstance(points, np.ndarray):
+        points = np.ascontiguousarray(points, dtype=np.uint64)
+        scalars = np.ascontiguousarray(scalars, dtype=np.uint64)
+        n = scalars.shape[0]
+        fn = lib.zk_msm_g2_host if g2 else lib.zk_msm_g1_host
+        check(fn(-1 if device is None else device, None, _np_ptr(points), _np_ptr(scalars), n, _np_ptr(out)))
+    else:
+        n = scalars.numel() * scalars.element_size() // 32
+        dev = points.device.index if device is None else device
+        fn = lib.zk_msm_g2_device if g2 else lib.zk_msm_g1_device
+        check(fn(dev, _stream(points), _dev_ptr(points), _dev_ptr(scalars), n, _np_ptr(out)))
+    return out
+
+
+def msm_g1_ref(points72, scalars, n=None):
+    """Reference-shaped msm_g1: 72-byte host records (uint8 array), host Fr;
+    returns the 96-byte G1Jacobian as (12,) uint64."""
+    points72 = np.ascontiguousarray(points72, dtype=np.uint8)
+    scalars = np.ascontiguousarray(scalars, dtype=np.uint64)
+    n = scalars.shape[0] if n is None else n
+    out = np.zeros(12, dtype=np.uint64)
+    check(lib.zk_msm_g1(_np_ptr(points72), _np_ptr(scalars), n, _np_ptr(out)))
+    return out
+
+
+def msm_g2_ref(points136, scalars, n=None):
+    points136 = np.ascontiguousarray(points136, dtype=np.uint8)
+    scalars = np.ascontiguousarray(scalars, dtype=np.uint64)
+    n = scalars.shape[0] if n is None else n
+    out = np.zeros(24, dtype=np.uint64)
+    check(lib.zk_msm_g2(_np_ptr(points136), _np_ptr(scalars), n, _np_ptr(out)))
+    return out
+
+
+def packed_to_ref_g1(points):
+    """(n, 8) packed -> (n, 72) uint8 reference G1Affine records."""
+    points = np.ascontiguousarray(points, dtype=np.uint64)
+    n = points.shape[0]
+    rec = np.zeros((n, 9), dtype=np.uint64)
+    rec[:, :8] = points
+    rec[:, 8] = (~points.any(axis=1)).astype(np.uint64)
+    return rec.view(np.uint8).reshape(n, 72)
+
+
+def packed_to_ref_g2(points):
+    points = np.ascontiguousarray(points, dtype=np.uint64)
+    n = points.shape[0]
+    rec = np.zeros((n, 17), dtype=np.uint64)
+    rec[:, :16] = points
+    rec[:, 16] = (~points.any(axis=1)).astype(np.uint64)
+    return rec.view(np.uint8).reshape(n, 136)
+
+
+def msm_last_stats():
+    s = MsmStats()
+    check(lib.zk_msm_last_stats(ctypes.byref(s)))
+    return {k: getattr(s, k) for k, _ in MsmStats._fields_}
+
+
+def g1_fixed_base(scalars_dev, out=None):
+    """k_i * G1 for Montgomery scalars on the device -> (n, 8) int64 CUDA tensor."""
+    torch = _torch()
+    n = scalars_dev.numel() * scalars_dev.element_size() // 32
+    if out is None:
+        out = torch.empty((n, 8), dtype=torch.int64, device=scalars_dev.device)
+    check(lib.zk_g1_fixed_base_device(scalars_dev.device.index, _stream(scalars_dev), _dev_ptr(out), _dev_ptr(scalars_dev), n))
+    return out
+
+
+def g2_fixed_base(scalars_dev, out=None):
+    torch = _torch()
+    n = scalars_dev.numel() * scalars_dev.element_size() // 32
+    if out is None:
+        out = torch.empty((n, 16), dtype=torch.int64, device=scalars_dev.device)
+    check(lib.zk_g2_fixed_base_device(scalars_dev.device.index, _stream(scalars_dev), _dev_ptr(out), _dev_ptr(scalars_dev), n))
+    return out
+
+
+def g1_add_affine(a, b):
+    a = np.ascontiguousarray(a, dtype=np.uint64)
+    b = np.ascontiguousarray(b, dtype=np.uint64)
+    out = np.zeros(8, dtype=np.uint64)
+    check(lib.zk_g1_add_affine(_np_ptr(a), _np_ptr(b), _np_ptr(out)))
+    return out
+
+
+def g2_add_affine(a, b):
+    a = np.ascontiguousarray(a, dtype=np.uint64)
+    b = np.ascontiguousarray(b, dtype=np.uint64)
+    out = np.zeros(16, dtype=np.uint64)
+    check(lib.zk_g2_add_affine(_np_ptr(a), _np_ptr(b), _np_ptr(out)))
+    return out
+
+
+# ------------------------------------------------------------------ NTT
+def ntt(x, log_n, inverse=False, coset=None, out=None):
+    """NTT of a CUDA tensor holding 2^log_n Fr values (natural order in/out).
+    coset: None or a (4,) uint64 Montgomery Fr shift g."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(x)
+    g = None
+    if coset is not None:
+        gc = np.ascontiguousarray(coset, dtype=np.uint64)
+        g = _np_ptr(gc)
+    check(lib.zk_ntt_device(x.device.index, _stream(x), _dev_ptr(out), _dev_ptr(x), log_n, int(inverse), g))
+    return out
+
+
+def ntt_ref(d_out, d_in, log_n, inverse):
+    """Reference-shaped ntt_gpu (synchronous, current device)."""
+    return lib.zk_ntt(_dev_ptr(d_out), _dev_ptr(d_in), log_n, int(inverse))
+
+
+def compute_h(a, b, c, log_n, out=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(a)
+    check(lib.zk_compute_h_device(a.device.index, _stream(a), _dev_ptr(out), _dev_ptr(a), _dev_ptr(b), _dev_ptr(c), log_n))
+    return out
+
+
+def compute_omega(log_n, inverse=False):
+    out = np.zeros(4, dtype=np.uint64)
+    check(lib.zk_compute_omega(log_n, int(inverse), _np_ptr(out)))
+    return out
+
+
+def probe_imad_rate(device=0):
+    r = ctypes.c_double(0)
+    check(lib.zk_probe_imad_rate(device, ctypes.byref(r)))
+    return r.value

@@ -1,0 +1,157 @@
+/*
+ * zkml_b200.h -- C ABI of the B200 (sm_100a) Groth16 proving hot path:
+ * BN254 Pippenger MSM over G1 and G2, and the Fr NTT / INTT / coset NTT.
+ *
+ * Drop-in boundary for gdtsitlauri/cuda-zkml.  The first group of entry
+ * points mirrors the reference's C++ functions one for one (same argument
+ * meaning, host/device placement and struct layouts); the reference links to
+ * them through the thin C++ layer in cuda-zkml_b200/csrc/compat.cpp, which
+ * exports the exact bn254:: signatures.  The second group is the B200-native
+ * interface: packed device-resident data, an explicit device and CUDA stream,
+ * and status codes instead of exit().
+ *
+ * Data layouts (all little-endian, Montgomery form, R = 2^256):
+ *   Fr, Fp              32 B   4 x uint64 limbs (src/field/fp.cuh:30-34, :322-323)
+ *   ref G1 affine       72 B   x(32) y(32) bool infinity at byte 64 + 7 pad
+ *                              (bn254::G1Affine, src/curve/g1.cuh:29-38)
+ *   ref G2 affine      136 B   x.c0 x.c1 y.c0 y.c1 (4 x 32) bool at byte 128
+ *                              (bn254::G2Affine, src/curve/g2.cuh:25-33)
+ *   ref G1 Jacobian     96 B   X Y Z (src/curve/g1.cuh:59-61)
+ *   ref G2 Jacobian    192 B   X Y Z over Fp2 (src/curve/g2.cuh:89-91)
+ *   packed G1 affine    64 B   x y; the all-zero record is the point at infinity
+ *   packed G2 affine   128 B   x.c0 x.c1 y.c0 y.c1; all-zero is infinity
+ *
+ * Every entry point returns ZK_OK or a ZK_ERR_* code; zk_last_error() gives a
+ * thread-local message.  Nothing in this library falls back to the CPU: on a
+ * machine without a usable CUDA device every compute call fails with
+ * ZK_ERR_NODEV.
+ */
+#ifndef ZKML_B200_H
+#define ZKML_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZK_OK 0
+#define ZK_ERR_INVALID 1  /* bad argument: null pointer, negative size, log_n out of range */
+#define ZK_ERR_CUDA 2     /* CUDA runtime error */
+#define ZK_ERR_NOMEM 3    /* device or pinned-host allocation failed */
+#define ZK_ERR_NODEV 4    /* no usable CUDA device */
+#define ZK_ERR_RANGE 5    /* size beyond what the entry point supports */
+
+#define ZK_NTT_MAX_LOG 28      /* 2-adicity of BN254 r */
+#define ZK_REF_NTT_MAX_LOG 24  /* the reference's limit, gpu_config::NTT_MAX_LOG (src/common.cuh:78) */
+
+/* Thread-local description of the last error (empty string after success). */
+const char* zk_last_error(void);
+/* Number of CUDA devices visible to this process (0 when none). */
+int zk_device_count(int* count);
+/* Library version, major * 10000 + minor * 100 + patch. */
+int zk_version(void);
+
+/* ==================================================================
+ * Reference-shaped entry points.  Synchronous; they run on the calling
+ * thread's current CUDA device and its default context stream.
+ * ================================================================== */
+
+/* Replaces bn254::msm_g1(const G1Affine* h_points, const Fr* h_scalars, int n)
+ * (src/msm/msm.cuh:67, src/msm/msm.cu:320-442).  h_points: n host ref-G1
+ * records (72 B); h_scalars: n host Fr (Montgomery).  Writes the sum as a
+ * ref G1 Jacobian (96 B): (x, y, one) or the identity (0, one, 0). */
+int zk_msm_g1(const void* h_points, const void* h_scalars, int n, void* out_jacobian);
+
+/* Replaces bn254::msm_g2(const G2Affine*, const Fr*, int) (src/msm/msm.cuh:68,
+ * src/msm/msm.cu:526-598).  ref G2 records (136 B) in, ref G2 Jacobian (192 B)
+ * out. */
+int zk_msm_g2(const void* h_points, const void* h_scalars, int n, void* out_jacobian);
+
+/* Replaces bn254::ntt_gpu(Fr* d_out, const Fr* d_in, int log_n, bool inverse)
+ * (src/ntt/ntt.cuh:49, src/ntt/ntt.cu:354-465): natural order in and out,
+ * inverse scaled by n^-1, device pointers, d_out may equal d_in.  log_n above
+ * ZK_REF_NTT_MAX_LOG returns ZK_ERR_RANGE with the output untouched (the
+ * reference prints and returns, ntt.cu:357-361). */
+int zk_ntt(void* d_out, const void* d_in, int log_n, int inverse);
+
+/* Replaces bn254::ntt_gpu_inplace(Fr* d_data, int log_n, bool inverse)
+ * (src/ntt/ntt.cuh:50, src/ntt/ntt.cu:467-478). */
+int zk_ntt_inplace(void* d_data, int log_n, int inverse);
+
+/* Replaces bn254::compute_omega / compute_omega_inv (src/ntt/ntt.cuh:53-54,
+ * src/ntt/ntt.cu:64-106): the primitive 2^log_n-th root of unity (or its
+ * inverse) as a Montgomery Fr, 0 <= log_n <= 28. */
+int zk_compute_omega(int log_n, int inverse, void* out_fr);
+
+/* ==================================================================
+ * B200-native entry points.  `stream` is a cudaStream_t (NULL = the
+ * library's per-device stream).  Calls are stream-ordered; those that
+ * return a point to the host synchronise the stream before returning.
+ * ================================================================== */
+
+/* G1 MSM over device-resident packed points (64 B) and Fr scalars.
+ * out_affine: 64 host bytes (x, y Montgomery; all-zero for the identity). */
+int zk_msm_g1_device(int device, void* stream, const void* d_points, const void* d_scalars,
+                     size_t n, void* out_affine);
+/* G1 MSM from HOST packed points and scalars: the copies to the device are
+ * pipelined with the scalar decomposition and bucket sort. */
+int zk_msm_g1_host(int device, void* stream, const void* h_points, const void* h_scalars,
+                   size_t n, void* out_affine);
+/* G2 MSM over device-resident packed points (128 B); out_affine: 128 host bytes. */
+int zk_msm_g2_device(int device, void* stream, const void* d_points, const void* d_scalars,
+                     size_t n, void* out_affine);
+int zk_msm_g2_host(int device, void* stream, const void* h_points, const void* h_scalars,
+                   size_t n, void* out_affine);
+
+/* NTT over device memory.  inverse: 0 forward (omega), 1 inverse (omega^-1,
+ * scaled by n^-1).  coset_shift: NULL for the plain transform, else a host
+ * Montgomery Fr g giving
+ *   forward : out = NTT(a_i * g^i)
+ *   inverse : out_i = INTT(a)_i * g^-i
+ * which are the coset evaluations and interpolations of compute_h
+ * (src/prover/groth16.cu:350-383).  0 <= log_n <= ZK_NTT_MAX_LOG. */
+int zk_ntt_device(int device, void* stream, void* d_out, const void* d_in, int log_n,
+                  int inverse, const void* coset_shift);
+
+/* Quotient polynomial of compute_h after the sparse matvec
+ * (src/prover/groth16.cu:322-383): from the evaluation vectors A*w, B*w, C*w
+ * on the size-2^log_n domain, writes the n coefficients of
+ * h = (A B - C) / (x^n - 1) to d_h, using the coset g = 5 (7 when 5^n = 1).
+ * All buffers are device memory; d_h may alias d_a. */
+int zk_compute_h_device(int device, void* stream, void* d_h, const void* d_a, const void* d_b,
+                        const void* d_c, int log_n);
+
+/* out_i = k_i * G for the curve generator G (G1: 64-B packed records; G2:
+ * 128-B), k_i Montgomery Fr, all in device memory.  Used to generate proving
+ * keys and synthetic inputs on the device. */
+int zk_g1_fixed_base_device(int device, void* stream, void* d_out, const void* d_scalars, size_t n);
+int zk_g2_fixed_base_device(int device, void* stream, void* d_out, const void* d_scalars, size_t n);
+
+/* Host-side point helpers on packed affine records (used to combine the
+ * per-GPU partial results of a sharded MSM). */
+int zk_g1_add_affine(const void* a, const void* b, void* out);
+int zk_g2_add_affine(const void* a, const void* b, void* out);
+
+/* Measured throughput of the INT32 multiply-add pipe on `device` in
+ * instructions per second (a dependency-free IMAD stream at full occupancy):
+ * the denominator of the MSM and NTT rooflines. */
+int zk_probe_imad_rate(int device, double* imad_per_second);
+
+/* Statistics of the most recent MSM on the calling thread: launches of this
+ * library's kernels and the device time of the bucket-accumulation kernel. */
+typedef struct {
+    int kernel_launches;   /* kernels of this library launched by the call */
+    float accumulate_ms;   /* device time of the bucket-accumulation kernel */
+    float total_device_ms; /* device time from the first copy/launch to the last */
+    int window_bits;       /* c */
+    int num_windows;       /* W */
+    long long bucket_adds; /* nonzero signed digits = mixed additions performed */
+} zk_msm_stats;
+int zk_msm_last_stats(zk_msm_stats* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,180 @@
+// ref_driver.cpp -- exposes the reference's own host arithmetic through a C ABI
+// so that the oracle restatement (bn254_oracle.c) and the golden fixtures can be
+// pinned to it.
+//
+// TEST INFRASTRUCTURE ONLY.  Built by oracle/Makefile into oracle/_ref/ against
+// the reference's headers where they lie (src/field/fp.cuh, src/field/fp2.cuh,
+// src/curve/g1.cuh, src/curve/g2.cuh), with the reference's own host shim
+// (tests/host/shim/cuda_runtime.h) standing in for the CUDA runtime, and linked
+// with the reference's src/ntt/ntt.cu (compiled by nvcc) for compute_omega.
+// Nothing from the reference is copied into this repository.
+//
+// All values cross this ABI in the reference's host layout: Montgomery-form
+// 4 x u64 limbs; a G1 point is (x[4], y[4]) + an int infinity flag.
+#include "field/fp.cuh"
+#include "field/fp2.cuh"
+#include "curve/g1.cuh"
+#include "curve/g2.cuh"
+#include "ntt/ntt.cuh"
+
+#include <cstring>
+#include <vector>
+
+using namespace bn254;
+
+static Fp ld_fp(const uint64_t* p) { return Fp(p[0], p[1], p[2], p[3]); }
+static Fr ld_fr(const uint64_t* p) { return Fr(p[0], p[1], p[2], p[3]); }
+static void st(uint64_t* o, const uint64_t* v) { std::memcpy(o, v, 32); }
+
+static G1Affine ld_g1(const uint64_t* p, int inf) {
+    if (inf) return G1Affine();
+    return G1Affine(ld_fp(p), ld_fp(p + 4));
+}
+static void st_g1(uint64_t* o, int* inf, const G1Affine& a) {
+    st(o, a.x.val); st(o + 4, a.y.val); *inf = a.infinity ? 1 : 0;
+}
+static G2Affine ld_g2(const uint64_t* p, int inf) {
+    if (inf) return G2Affine();
+    return G2Affine(Fp2(ld_fp(p), ld_fp(p + 4)), Fp2(ld_fp(p + 8), ld_fp(p + 12)));
+}
+static void st_g2(uint64_t* o, int* inf, const G2Affine& a) {
+    st(o, a.x.c0.val); st(o + 4, a.x.c1.val); st(o + 8, a.y.c0.val); st(o + 12, a.y.c1.val);
+    *inf = a.infinity ? 1 : 0;
+}
+
+extern "C" {
+
+void ref_fp_mul(uint64_t* o, const uint64_t* a, const uint64_t* b) { st(o, (ld_fp(a) * ld_fp(b)).val); }
+void ref_fp_add(uint64_t* o, const uint64_t* a, const uint64_t* b) { st(o, (ld_fp(a) + ld_fp(b)).val); }
+void ref_fp_sub(uint64_t* o, const uint64_t* a, const uint64_t* b) { st(o, (ld_fp(a) - ld_fp(b)).val); }
+void ref_fp_inv(uint64_t* o, const uint64_t* a) { st(o, ld_fp(a).inv().val); }
+void ref_fr_mul(uint64_t* o, const uint64_t* a, const uint64_t* b) { st(o, (ld_fr(a) * ld_fr(b)).val); }
+void ref_fr_add(uint64_t* o, const uint64_t* a, const uint64_t* b) { st(o, (ld_fr(a) + ld_fr(b)).val); }
+void ref_fr_sub(uint64_t* o, const uint64_t* a, const uint64_t* b) { st(o, (ld_fr(a) - ld_fr(b)).val); }
+void ref_fr_from_u64(uint64_t* o, uint64_t v) { st(o, Fr::from_uint(v).val); }
+void ref_fr_to_std(uint64_t* o, const uint64_t* a) { ld_fr(a).to_standard(o); }
+void ref_fp_to_std(uint64_t* o, const uint64_t* a) { ld_fp(a).to_standard(o); }
+void ref_fp_from_std(uint64_t* o, const uint64_t* s) { st(o, Fp::from_standard(s[0], s[1], s[2], s[3]).val); }
+void ref_fp_one(uint64_t* o) { st(o, Fp::one().val); }
+void ref_fr_one(uint64_t* o) { st(o, Fr::one().val); }
+
+void ref_compute_omega(uint64_t* o, int log_n, int inverse) {
+    Fr w = inverse ? compute_omega_inv(log_n) : compute_omega(log_n);
+    st(o, w.val);
+}
+
+void ref_g1_generator(uint64_t* o, int* inf) { st_g1(o, inf, G1Affine::generator()); }
+void ref_g2_generator(uint64_t* o, int* inf) { st_g2(o, inf, G2Affine::generator()); }
+
+// k * P (g1.cuh:204-246), returned affine
+void ref_g1_scalar_mul(uint64_t* o, int* oinf, const uint64_t* p, int pinf, const uint64_t* k) {
+    G1Jacobian j = G1Jacobian::from_affine(ld_g1(p, pinf)).scalar_mul(ld_fr(k));
+    st_g1(o, oinf, j.to_affine());
+}
+// P + Q via Jacobian addition, P + Q via mixed addition, 2P via dbl
+void ref_g1_add(uint64_t* o, int* oinf, const uint64_t* p, int pinf, const uint64_t* q, int qinf) {
+    G1Jacobian j = G1Jacobian::from_affine(ld_g1(p, pinf)) + G1Jacobian::from_affine(ld_g1(q, qinf));
+    st_g1(o, oinf, j.to_affine());
+}
+void ref_g1_madd(uint64_t* o, int* oinf, const uint64_t* p, int pinf, const uint64_t* q, int qinf) {
+    G1Jacobian j = G1Jacobian::from_affine(ld_g1(p, pinf)).add_affine(ld_g1(q, qinf));
+    st_g1(o, oinf, j.to_affine());
+}
+void ref_g1_dbl(uint64_t* o, int* oinf, const uint64_t* p, int pinf) {
+    st_g1(o, oinf, G1Jacobian::from_affine(ld_g1(p, pinf)).dbl().to_affine());
+}
+
+void ref_g2_scalar_mul(uint64_t* o, int* oinf, const uint64_t* p, int pinf, const uint64_t* k) {
+    G2Jacobian j = G2Jacobian::from_affine(ld_g2(p, pinf)).scalar_mul(ld_fr(k));
+    st_g2(o, oinf, j.to_affine());
+}
+void ref_g2_add(uint64_t* o, int* oinf, const uint64_t* p, int pinf, const uint64_t* q, int qinf) {
+    G2Jacobian j = G2Jacobian::from_affine(ld_g2(p, pinf)) + G2Jacobian::from_affine(ld_g2(q, qinf));
+    st_g2(o, oinf, j.to_affine());
+}
+int ref_g2_on_curve(const uint64_t* p) { return ld_g2(p, 0).is_on_curve() ? 1 : 0; }
+int ref_g1_on_curve(const uint64_t* p) { return ld_g1(p, 0).is_on_curve() ? 1 : 0; }
+
+// The reference's small-n MSM path (src/msm/msm.cu:330-339), which is also its
+// test oracle cpu_msm (tests/test_msm.cu:20-28).  points: n x (x[4], y[4]),
+// an all-zero record is the identity.
+void ref_msm_g1_naive(uint64_t* o, int* oinf, const uint64_t* pts, const uint64_t* sc, int n) {
+    G1Jacobian acc = G1Jacobian::identity();
+    for (int i = 0; i < n; i++) {
+        const uint64_t* p = pts + 8 * i;
+        int inf = 1;
+        for (int k = 0; k < 8; k++) if (p[k]) inf = 0;
+        acc = acc + G1Jacobian::from_affine(ld_g1(p, inf)).scalar_mul(ld_fr(sc + 4 * i));
+    }
+    st_g1(o, oinf, acc.to_affine());
+}
+void ref_msm_g2_naive(uint64_t* o, int* oinf, const uint64_t* pts, const uint64_t* sc, int n) {
+    G2Jacobian acc = G2Jacobian::identity();
+    for (int i = 0; i < n; i++) {
+        const uint64_t* p = pts + 16 * i;
+        int inf = 1;
+        for (int k = 0; k < 16; k++) if (p[k]) inf = 0;
+        acc = acc + G2Jacobian::from_affine(ld_g2(p, inf)).scalar_mul(ld_fr(sc + 4 * i));
+    }
+    st_g2(o, oinf, acc.to_affine());
+}
+
+// The reference's NTT test oracle: O(n^2) DFT with compute_omega
+// (tests/test_ntt.cu:19-37), INTT scaled by (2^-1)^log_n as ntt.cu:437-459.
+void ref_ntt_naive(uint64_t* out, const uint64_t* in, int log_n, int inverse) {
+    int n = 1 << log_n;
+    Fr omega = inverse ? compute_omega_inv(log_n) : compute_omega(log_n);
+    std::vector<Fr> res(n);
+    Fr omega_i = Fr::from_uint(1);
+    for (int i = 0; i < n; i++) {
+        Fr sum = Fr::zero();
+        Fr wij = Fr::from_uint(1);
+        for (int j = 0; j < n; j++) {
+            sum = sum + ld_fr(in + 4 * j) * wij;
+            wij = wij * omega_i;
+        }
+        res[i] = sum;
+        omega_i = omega_i * omega;
+    }
+    if (inverse) {
+        Fr two = Fr::from_uint(2);
+        Fr half = two.inv();
+        Fr scale = Fr::from_uint(1);
+        for (int i = 0; i < log_n; i++) scale = scale * half;
+        for (int i = 0; i < n; i++) res[i] = res[i] * scale;
+    }
+    for (int i = 0; i < n; i++) st(out + 4 * i, res[i].val);
+}
+
+}  // extern "C"
+
+#include <thread>
+
+// The reference's CPU MSM path run on `nthreads` host threads: each thread sums
+// s_i * P_i over a contiguous slice with the reference's own scalar_mul and
+// Jacobian addition (src/msm/msm.cu:330-339, src/curve/g1.cuh), and the slices
+// are added at the end.  Used as the timed reference arm of bench.py.
+extern "C" void ref_msm_g1_naive_mt(uint64_t* o, int* oinf, const uint64_t* pts, const uint64_t* sc, int n, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    std::vector<G1Jacobian> part(nthreads, G1Jacobian::identity());
+    std::vector<std::thread> th;
+    for (int t = 0; t < nthreads; t++) {
+        th.emplace_back([&, t]() {
+            int i0 = (int)((long long)n * t / nthreads), i1 = (int)((long long)n * (t + 1) / nthreads);
+            G1Jacobian acc = G1Jacobian::identity();
+            for (int i = i0; i < i1; i++) {
+                const uint64_t* p = pts + 8 * i;
+                int inf = 1;
+                for (int k = 0; k < 8; k++) if (p[k]) inf = 0;
+                acc = acc + G1Jacobian::from_affine(ld_g1(p, inf)).scalar_mul(ld_fr(sc + 4 * i));
+            }
+            part[t] = acc;
+        });
+    }
+    G1Jacobian acc = G1Jacobian::identity();
+    for (int t = 0; t < nthreads; t++) {
+        th[t].join();
+        acc = acc + part[t];
+    }
+    st_g1(o, oinf, acc.to_affine());
+}

@@ -1,0 +1,188 @@
+"""GPU parity of the G1/G2 MSM against the reference-pinned oracle.
+
+Bit-exact: every result is the canonical affine point.  Small cases use the
+golden vectors made by the reference's own arithmetic; medium sizes compare
+with the oracle's Pippenger restatement; full sizes (2^20, 2^24) use the
+size-independent identity sum_i s_i (k_i G) = (sum_i s_i k_i) G."""
+import os
+
+import numpy as np
+import pytest
+
+import pyoracle as O
+import zkml_b200 as Z
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def g(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def cases(gz):
+    return sorted(k[: -len("_result")] for k in gz.files if k.endswith("_result"))
+
+
+def dev(a):
+    return Z.to_device(a)
+
+
+def test_device_is_b200():
+    assert Z.device_count() >= 1
+    assert torch.cuda.get_device_capability(0)[0] >= 10
+
+
+@pytest.mark.parametrize("path", ["device", "host", "ref"])
+def test_g1_golden(path):
+    gz = g("g1_msm.npz")
+    for name in cases(gz):
+        pts, sc, res = gz[name + "_points"], gz[name + "_scalars"], gz[name + "_result"]
+        if path == "device":
+            out = Z.msm_g1(dev(pts), dev(sc))
+        elif path == "host":
+            out = Z.msm_g1(pts, sc)
+        else:
+            jac = Z.msm_g1_ref(Z.packed_to_ref_g1(pts), sc)
+            if res.any():
+                assert O.fp_to_int(jac[8:12]) == 1, name   # Z = one
+                out = jac[:8]
+            else:
+                assert not jac[:4].any() and not jac[8:].any() and O.fp_to_int(jac[4:8]) == 1, name
+                out = np.zeros(8, np.uint64)
+        assert np.array_equal(out, res), (path, name)
+
+
+@pytest.mark.parametrize("path", ["device", "host", "ref"])
+def test_g2_golden(path):
+    gz = g("g2_msm.npz")
+    for name in cases(gz):
+        pts, sc, res = gz[name + "_points"], gz[name + "_scalars"], gz[name + "_result"]
+        if path == "device":
+            out = Z.msm_g2(dev(pts), dev(sc))
+        elif path == "host":
+            out = Z.msm_g2(pts, sc)
+        else:
+            jac = Z.msm_g2_ref(Z.packed_to_ref_g2(pts), sc)
+            out = jac[:16] if res.any() else np.zeros(16, np.uint64)
+        assert np.array_equal(out, res), (path, name)
+
+
+def test_zero_points_is_identity():
+    assert not Z.msm_g1(np.zeros((0, 8), np.uint64), np.zeros((0, 4), np.uint64)).any()
+    jac = Z.msm_g1_ref(np.zeros((0, 72), np.uint8), np.zeros((0, 4), np.uint64), n=0)
+    assert O.fp_to_int(jac[4:8]) == 1 and not jac[8:].any()
+
+
+def test_fixed_base_matches_oracle():
+    rng = O.Rng(11)
+    k = rng.fr_vector(1000)
+    k[3] = 0
+    got = Z.to_host(Z.g1_fixed_base(dev(k)))
+    assert np.array_equal(got, O.g1_fixed_base(k))
+    k2 = k[:64]
+    got2 = Z.to_host(Z.g2_fixed_base(dev(k2)))
+    assert np.array_equal(got2, O.g2_fixed_base(k2))
+
+
+def _random_instance(n, seed, g2=False):
+    rng = O.Rng(seed)
+    k = rng.fr_vector(n)
+    sc = rng.fr_vector(n)
+    kd = dev(k)
+    pts = Z.g2_fixed_base(kd) if g2 else Z.g1_fixed_base(kd)
+    return k, pts, sc
+
+
+@pytest.mark.parametrize("n", [255, 256, 257, 1000, 4097, 1 << 14, 1 << 16])
+def test_g1_matches_oracle(n):
+    _, pts, sc = _random_instance(n, 100 + n)
+    exp = O.msm_g1(Z.to_host(pts), sc, nthreads=os.cpu_count())
+    assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
+
+
+@pytest.mark.parametrize("c", [3, 7, 11, 13, 16, 18])
+def test_g1_window_sizes_agree(c, monkeypatch):
+    n = 5000
+    _, pts, sc = _random_instance(n, 7)
+    exp = O.msm_g1(Z.to_host(pts), sc, nthreads=os.cpu_count())
+    monkeypatch.setenv("ZK_MSM_WINDOW_BITS", str(c))
+    assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
+
+
+def test_g1_skewed_scalars():
+    """Bucket skew: 40% zeros, 30% one repeated scalar, 20% values < 2^16,
+    plus duplicated points and P, -P pairs (the SURVEY's 10%/10% variant is a
+    milder version of this)."""
+    n = 20000
+    rng = O.Rng(21)
+    k = rng.fr_vector(n)
+    sc = rng.fr_vector(n)
+    u = np.random.default_rng(5).random(n)
+    sc[u < 0.4] = 0
+    sc[(u >= 0.4) & (u < 0.7)] = sc[0]
+    small = (u >= 0.7) & (u < 0.9)
+    for i in np.nonzero(small)[0]:
+        sc[i] = O.fr_from_int(int(rng.next() & 0xFFFF))
+    pts = Z.to_host(Z.g1_fixed_base(dev(k)))
+    pts[100:200] = pts[300:400]          # duplicates
+    pts[500:600] = 0                      # infinity
+    exp = O.msm_g1(pts, sc, nthreads=os.cpu_count())
+    assert np.array_equal(Z.msm_g1(dev(pts), dev(sc)), exp)
+    assert np.array_equal(Z.msm_g1(pts, sc), exp)
+
+
+def test_g1_survey_variant_10pct_zero_10pct_small():
+    n = 1 << 16
+    k, pts, sc = _random_instance(n, 0x5EED0010)
+    perm = np.random.default_rng(0x5EED0010).permutation(n)
+    sc[perm[: n // 10]] = 0
+    for i in perm[n // 10: n // 5]:
+        sc[i] = Z.fr_from_int(int(i) & 0xFFFF)
+    exp = O.msm_g1(Z.to_host(pts), sc, nthreads=os.cpu_count())
+    assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
+
+
+@pytest.mark.parametrize("log_n", [20, 24])
+def test_g1_full_size_identity(log_n):
+    """sum_i s_i (k_i G) == (sum_i s_i k_i) G at the benchmark sizes."""
+    n = 1 << log_n
+    k = Z.random_fr(n, 0x5EED0000 + log_n)
+    sc = Z.random_fr(n, 0x5EED1000 + log_n)
+    kd = dev(k)
+    pts = Z.g1_fixed_base(kd)
+    got = Z.msm_g1(pts, dev(sc))
+    dot = O.fr_dot(k, sc)
+    exp = O.g1_fixed_base(dot[None, :])[0]
+    assert np.array_equal(got, exp)
+    # spot-check the generated points themselves
+    idx = np.random.default_rng(1).integers(0, n, 64)
+    ph = Z.to_host(pts[torch.as_tensor(idx, device=pts.device)])
+    assert np.array_equal(ph, O.g1_fixed_base(k[idx]))
+
+
+@pytest.mark.parametrize("n", [129, 1000, 1 << 12])
+def test_g2_matches_oracle(n):
+    _, pts, sc = _random_instance(n, 300 + n, g2=True)
+    exp = O.msm_g2(Z.to_host(pts), sc, nthreads=os.cpu_count())
+    assert np.array_equal(Z.msm_g2(pts, dev(sc)), exp)
+
+
+def test_g2_full_size_identity():
+    n = 1 << 18
+    k = Z.random_fr(n, 41)
+    sc = Z.random_fr(n, 42)
+    pts = Z.g2_fixed_base(dev(k))
+    got = Z.msm_g2(pts, dev(sc))
+    exp = O.g2_fixed_base(O.fr_dot(k, sc)[None, :])[0]
+    assert np.array_equal(got, exp)
+
+
+def test_stats_and_probe():
+    _, pts, sc = _random_instance(4096, 3)
+    Z.msm_g1(pts, dev(sc))
+    st = Z.msm_last_stats()
+    assert st["kernel_launches"] >= 8 and st["accumulate_ms"] > 0
+    assert Z.probe_imad_rate(0) > 1e12
