@@ -257,6 +257,33 @@ def run_b200(args):
                "d2h_bytes_per_step": 64 + 4 + stats[-1]["num_windows"] * 128, "ms_per_step": dt * 1e3,
                "api": "zk_msm_g1_host (pinned host points + scalars)"}
 
+    ntt = None
+    if rank == 0 and not args.no_ntt:
+        ln = args.ntt_log_n
+        nn = 1 << ln
+        x = Z.to_device(Z.random_fr(nn, 0xA0A0 + ln), dev)
+        y = torch.empty_like(x)
+        for _ in range(2):
+            Z.ntt(x, ln, False, out=y)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            Z.ntt(x, ln, False, out=y)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / reps / 1e3
+        alg_bytes = 128 * nn            # two read+write passes of 32-B elements (four-step minimum)
+        alg_imad = (nn // 2) * ln * 256  # radix-2 butterflies x 256 IMAD per Montgomery multiply
+        ntt = {"log_n": ln, "ms": t * 1e3, "elements_per_s": nn / t,
+               "hbm": {"achieved_gbs": alg_bytes / t / 1e9, "peak_gbs": args.hbm_peak,
+                       "frac": alg_bytes / t / 1e9 / args.hbm_peak, "algorithmic": "128 B per element"},
+               "int32": {"achieved_timad": alg_imad / t / 1e12, "peak_timad": imad / 1e12, "frac": alg_imad / t / imad,
+                         "algorithmic": "(n/2) log2 n Montgomery multiplications x 256 IMAD"}}
+        del x, y
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -281,8 +308,9 @@ def run_b200(args):
                          "window_bits": stats[-1]["window_bits"], "num_windows": stats[-1]["num_windows"],
                          "parallelism": f"points sharded over {world} GPU(s), partial sums all-gathered",
                          "l2": "inputs 1.5 GiB per GPU > 126 MB L2 (no flush needed)"},
-              "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-              "clocks": sampler.summary(), "accumulate_ms": acc_ms})
+              "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "ntt": ntt,
+              "clocks": sampler.summary(), "accumulate_ms": acc_ms,
+              "phase_ms": {k: round(v, 3) for k, v in stats[-1]["phase_ms"].items()}})
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -299,7 +327,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-log-n", type=int, default=18)
     ap.add_argument("--ref-sample", type=int, default=1 << 13)
+    ap.add_argument("--no-ntt", action="store_true")
+    ap.add_argument("--ntt-log-n", type=int, default=24)
+    ap.add_argument("--hbm-peak", type=float, default=None, help="HBM GB/s (default: MEASURED_PEAKS.json)")
     args = ap.parse_args()
+    if args.hbm_peak is None:
+        try:
+            args.hbm_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"])
+        except (OSError, ValueError, KeyError):
+            args.hbm_peak = 6650.0  # fallback measurement of this pool
     if args.impl == "reference":
         run_reference(args)
     else:

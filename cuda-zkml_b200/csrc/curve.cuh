@@ -17,6 +17,18 @@
 
 namespace zk {
 
+// Rarely taken paths (doubling when a bucket meets the same point again) are
+// kept out of line unless ZK_RARE_INLINE=1, so the common mixed-addition path
+// stays compact in the instruction cache.
+#ifndef ZK_RARE_INLINE
+#define ZK_RARE_INLINE 0
+#endif
+#if ZK_RARE_INLINE
+#define ZK_RARE __forceinline__
+#else
+#define ZK_RARE __noinline__
+#endif
+
 template <class F>
 struct Affine {
     F x, y;
@@ -41,7 +53,7 @@ __device__ __forceinline__ void from_affine(Xyzz<F>& r, const Affine<F>& a) {
 
 // r = 2 * (x, y) for an affine point (mdbl-2008-s)
 template <class F>
-__device__ __forceinline__ void mdbl(Xyzz<F>& r, const Affine<F>& a) {
+__device__ ZK_RARE void mdbl(Xyzz<F>& r, const Affine<F>& a) {
     F u, v, w, s, m, t;
     fdbl(u, a.y);            // U = 2Y
     fsqr(v, u);              // V = U^2
@@ -63,7 +75,7 @@ __device__ __forceinline__ void mdbl(Xyzz<F>& r, const Affine<F>& a) {
 
 // r = 2 p (dbl-2008-s-1, a = 0); identity maps to identity
 template <class F>
-__device__ __forceinline__ void dbl(Xyzz<F>& r, const Xyzz<F>& p) {
+__device__ ZK_RARE void dbl(Xyzz<F>& r, const Xyzz<F>& p) {
     if (is_identity(p)) { r = p; return; }
     F u, v, w, s, m, t;
     fdbl(u, p.y);            // U = 2 Y1

@@ -49,9 +49,41 @@ using Fr = Fe<ModR>;
 
 // --------------------------------------------------------------- limb rows
 // t[0..8] += a * b[0..7]   (caller guarantees no carry out of t[8])
+//
+// ZK_ROW_PAIRED=1 (default): the low and high halves of each product a*b_j
+// are adjacent in one carry chain.  Products with even j land on words
+// (j, j+1) = 0..7, so they form one contiguous chain; products with odd j
+// land on words 1..8 and form a second one.  ZK_ROW_PAIRED=0: one chain of
+// all low halves (words 0..7) then one of all high halves (words 1..8).
+#ifndef ZK_ROW_PAIRED
+#define ZK_ROW_PAIRED 1
+#endif
+
 __device__ __forceinline__ void mac_row(uint32_t& t0, uint32_t& t1, uint32_t& t2, uint32_t& t3,
                                         uint32_t& t4, uint32_t& t5, uint32_t& t6, uint32_t& t7,
                                         uint32_t& t8, uint32_t a, const uint32_t* b) {
+#if ZK_ROW_PAIRED
+    asm("mad.lo.cc.u32  %0, %9, %10, %0;\n\t"
+        "madc.hi.cc.u32 %1, %9, %10, %1;\n\t"
+        "madc.lo.cc.u32 %2, %9, %12, %2;\n\t"
+        "madc.hi.cc.u32 %3, %9, %12, %3;\n\t"
+        "madc.lo.cc.u32 %4, %9, %14, %4;\n\t"
+        "madc.hi.cc.u32 %5, %9, %14, %5;\n\t"
+        "madc.lo.cc.u32 %6, %9, %16, %6;\n\t"
+        "madc.hi.cc.u32 %7, %9, %16, %7;\n\t"
+        "addc.u32       %8, %8, 0;\n\t"
+        "mad.lo.cc.u32  %1, %9, %11, %1;\n\t"
+        "madc.hi.cc.u32 %2, %9, %11, %2;\n\t"
+        "madc.lo.cc.u32 %3, %9, %13, %3;\n\t"
+        "madc.hi.cc.u32 %4, %9, %13, %4;\n\t"
+        "madc.lo.cc.u32 %5, %9, %15, %5;\n\t"
+        "madc.hi.cc.u32 %6, %9, %15, %6;\n\t"
+        "madc.lo.cc.u32 %7, %9, %17, %7;\n\t"
+        "madc.hi.u32    %8, %9, %17, %8;"
+        : "+r"(t0), "+r"(t1), "+r"(t2), "+r"(t3), "+r"(t4), "+r"(t5), "+r"(t6), "+r"(t7), "+r"(t8)
+        : "r"(a), "r"(b[0]), "r"(b[1]), "r"(b[2]), "r"(b[3]), "r"(b[4]), "r"(b[5]), "r"(b[6]),
+          "r"(b[7]));
+#else
     asm("mad.lo.cc.u32  %0, %9, %10, %0;\n\t"
         "madc.lo.cc.u32 %1, %9, %11, %1;\n\t"
         "madc.lo.cc.u32 %2, %9, %12, %2;\n\t"
@@ -72,6 +104,7 @@ __device__ __forceinline__ void mac_row(uint32_t& t0, uint32_t& t1, uint32_t& t2
         : "+r"(t0), "+r"(t1), "+r"(t2), "+r"(t3), "+r"(t4), "+r"(t5), "+r"(t6), "+r"(t7), "+r"(t8)
         : "r"(a), "r"(b[0]), "r"(b[1]), "r"(b[2]), "r"(b[3]), "r"(b[4]), "r"(b[5]), "r"(b[6]),
           "r"(b[7]));
+#endif
 }
 
 // r = t - m if t >= m else t   (t < 2m)
@@ -97,8 +130,16 @@ __device__ __forceinline__ void cond_sub(uint32_t* r, const uint32_t* t) {
 }
 
 // --------------------------------------------------------------- Fe ops
+// ZK_FMUL_OUTLINE=1 (default) compiles every multiplication as a call to one
+// shared out-of-line body instead of inlining ~300 instructions at each use.
+// The point-addition loops then fit the instruction cache; fully inlined, the
+// MSM kernels stalled mostly on instruction fetch (measured with ncu).
+#ifndef ZK_FMUL_OUTLINE
+#define ZK_FMUL_OUTLINE 1
+#endif
+
 template <class M>
-__device__ __forceinline__ void fmul(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
+__device__ __forceinline__ void fmul_inline(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
     uint32_t t0 = 0, t1 = 0, t2 = 0, t3 = 0, t4 = 0, t5 = 0, t6 = 0, t7 = 0, t8 = 0;
     constexpr uint32_t mm[8] = {M::m(0), M::m(1), M::m(2), M::m(3), M::m(4), M::m(5), M::m(6), M::m(7)};
 #pragma unroll
@@ -111,6 +152,22 @@ __device__ __forceinline__ void fmul(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
     }
     uint32_t t[8] = {t0, t1, t2, t3, t4, t5, t6, t7};
     cond_sub<M>(r.v, t);
+}
+
+template <class M>
+__device__ __noinline__ Fe<M> fmul_outline(Fe<M> a, Fe<M> b) {
+    Fe<M> r;
+    fmul_inline(r, a, b);
+    return r;
+}
+
+template <class M>
+__device__ __forceinline__ void fmul(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
+#if ZK_FMUL_OUTLINE
+    r = fmul_outline<M>(a, b);
+#else
+    fmul_inline(r, a, b);
+#endif
 }
 
 template <class M>

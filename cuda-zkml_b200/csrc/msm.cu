@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 namespace zk {
@@ -54,14 +55,21 @@ struct MsmPlan {
 
 static constexpr int kScanTile = 4096;  // 1024 threads x 4
 
+// Window width c minimising the Fp multiplications of the whole MSM:
+// n W(c) mixed additions (10 mul each) + W(c) 2^(c-1) running-sum steps
+// (2 full additions, 14 mul each, plus the chunk correction), W(c) = ceil(255/c).
+// ZK_MSM_WINDOW_BITS / ZK_MSM_G2_WINDOW_BITS override it.
 static int default_window_bits(size_t n, bool g2) {
     const char* env = getenv(g2 ? "ZK_MSM_G2_WINDOW_BITS" : "ZK_MSM_WINDOW_BITS");
     if (env && atoi(env) >= 2 && atoi(env) <= 22) return atoi(env);
-    int lg = 0;
-    while (((size_t)1 << lg) < n) lg++;
-    int c = lg - 3;
-    if (g2) c = lg - 4;
-    return std::max(3, std::min(c, g2 ? 16 : 18));
+    int best = 3;
+    double best_cost = 1e300;
+    for (int c = 3; c <= (g2 ? 18 : 21); c++) {
+        const double W = (255 + c - 1) / c;
+        const double cost = (double)n * W * 10.0 + W * (double)(1u << (c - 1)) * 30.0;
+        if (cost < best_cost) { best_cost = cost; best = c; }
+    }
+    return best;
 }
 
 static MsmPlan make_plan(size_t n, bool g2) {
@@ -110,21 +118,34 @@ __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c
     }
 }
 
-__global__ void msm_scatter_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
-                                   uint32_t* __restrict__ cursors, uint32_t* __restrict__ keys) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        Fr s;
-        fload_nc(s, scalars + i);
-        ffrom_mont(s, s);
-        uint32_t carry = 0;
-        for (int w = 0; w < W; w++) {
-            int d = next_digit(s.v, c, carry);
-            if (d) {
-                uint32_t b = (uint32_t)w * B + (uint32_t)(d < 0 ? -d : d) - 1;
-                uint32_t pos = atomicAdd(&cursors[b], 1u);
-                keys[pos] = (d < 0 ? 0x80000000u : 0u) | (uint32_t)i;
+// One point per thread; the bucket cursors are claimed for up to 16 windows
+// before any key is stored, so the returning atomics of a thread overlap
+// instead of each waiting for the previous one.
+__global__ void __launch_bounds__(256) msm_scatter_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
+                                                          uint32_t* __restrict__ cursors, uint32_t* __restrict__ keys) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    Fr s;
+    fload_nc(s, scalars + i);
+    ffrom_mont(s, s);
+    uint32_t carry = 0;
+    for (int w0 = 0; w0 < W; w0 += 16) {
+        uint32_t pos[16], key[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            pos[k] = 0xffffffffu;
+            if (w0 + k < W) {
+                const int d = next_digit(s.v, c, carry);
+                if (d) {
+                    const uint32_t b = (uint32_t)(w0 + k) * B + (uint32_t)(d < 0 ? -d : d) - 1;
+                    pos[k] = atomicAdd(&cursors[b], 1u);
+                    key[k] = (d < 0 ? 0x80000000u : 0u) | (uint32_t)i;
+                }
             }
         }
+#pragma unroll
+        for (int k = 0; k < 16; k++)
+            if (pos[k] != 0xffffffffu) keys[pos[k]] = key[k];
     }
 }
 
@@ -219,7 +240,8 @@ __device__ __forceinline__ void load_signed_point(Affine<typename Cv::F>& a, boo
 template <class Cv>
 __global__ void __launch_bounds__(128) msm_accumulate_kernel(
     const uint32_t* __restrict__ keys, const uint32_t* __restrict__ offsets, uint32_t nb, const uint8_t* __restrict__ points,
-    uint32_t seg, uint8_t* __restrict__ bucket_sums, uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last) {
+    uint32_t seg, uint8_t* __restrict__ bucket_sums, uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last,
+    uint32_t* __restrict__ first_bucket, uint32_t* __restrict__ last_bucket) {
     using F = typename Cv::F;
     const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t K = offsets[nb];
@@ -237,17 +259,25 @@ __global__ void __launch_bounds__(128) msm_accumulate_kernel(
     uint32_t run_start = s0;
     Xyzz<F> acc;
     set_identity(acc);
-    auto flush = [&](uint32_t run_end) {
+    // A run covering its whole bucket goes straight to the bucket; a run cut by
+    // the segment boundary goes to the "first" slot when it starts the segment,
+    // else to the "last" slot (it then runs to the segment's end).
+    auto flush = [&]() {
         uint8_t* dst;
-        if (g_begin >= s0 && g_end <= s1) dst = bucket_sums + (size_t)g * Cv::kXyzzBytes;
-        else if (run_start == s0) dst = part_first + t * Cv::kXyzzBytes;
-        else dst = part_last + t * Cv::kXyzzBytes;
-        (void)run_end;
+        if (g_begin >= s0 && g_end <= s1) {
+            dst = bucket_sums + (size_t)g * Cv::kXyzzBytes;
+        } else if (run_start == s0) {
+            dst = part_first + t * Cv::kXyzzBytes;
+            first_bucket[t] = g;
+        } else {
+            dst = part_last + t * Cv::kXyzzBytes;
+            last_bucket[t] = g;
+        }
         store_xyzz(dst, acc);
     };
     for (uint32_t p = s0; p < s1; p++) {
         if (p >= g_end) {
-            flush(p);
+            flush();
             do { g++; g_end = offsets[g + 1]; } while (p >= g_end);
             g_begin = offsets[g];
             run_start = p;
@@ -258,27 +288,62 @@ __global__ void __launch_bounds__(128) msm_accumulate_kernel(
         load_signed_point<Cv>(a, inf, points, keys[p]);
         if (!inf) madd(acc, a);
     }
-    flush(s1);
+    flush();
 }
 
-// buckets cut by segment boundaries: sum the partial slots
+// Buckets cut by segment boundaries.  Bucket g with keys [b0, b1) spans the
+// segments sa = b0 / seg .. sb = (b1 - 1) / seg; its m = sb - sa + 1 partial
+// sums are V_0 (slot "first" of sa when b0 starts that segment, else its
+// "last" slot) and V_j = "first" slot of sa + j.  Round r of a binary tree adds
+// V_{j + 2^r} into V_j for every j divisible by 2^(r + 1), so even a bucket
+// holding millions of keys (the top window, or the many 0/1 scalars of a real
+// witness) is summed in log2(m) parallel steps instead of m serial adds.
 template <class Cv>
-__global__ void msm_fixup_kernel(const uint32_t* __restrict__ offsets, uint32_t nb, uint32_t seg, const uint8_t* __restrict__ part_first,
-                                 const uint8_t* __restrict__ part_last, uint8_t* __restrict__ bucket_sums) {
+__global__ void msm_fixup_round_kernel(const uint32_t* __restrict__ offsets, const uint32_t* __restrict__ first_bucket,
+                                       const uint32_t* __restrict__ last_bucket, size_t nseg, uint32_t seg, uint32_t stride,
+                                       uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last) {
     using F = typename Cv::F;
-    uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= nb) return;
-    uint32_t b0 = offsets[g], b1 = offsets[g + 1];
-    if (b0 == b1) return;
-    uint32_t sa = b0 / seg, sb = (b1 - 1) / seg;
-    if (sa == sb) return;  // whole bucket inside one segment: already written
-    Xyzz<F> acc, q;
-    load_xyzz(acc, (b0 == sa * seg ? part_first : part_last) + (size_t)sa * Cv::kXyzzBytes);
-    for (uint32_t s = sa + 1; s <= sb; s++) {
-        load_xyzz(q, part_first + (size_t)s * Cv::kXyzzBytes);
-        add(acc, q);
+    const size_t s = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= nseg) return;
+    const uint32_t gf = first_bucket[s], gl = last_bucket[s];
+    if (gf != 0xffffffffu) {
+        const uint32_t sa = offsets[gf] / seg, sb = (offsets[gf + 1] - 1) / seg;
+        const uint32_t j = (uint32_t)s - sa, m = sb - sa + 1;
+        if ((j & (2 * stride - 1)) == 0 && j + stride < m) {
+            Xyzz<F> a, b;
+            load_xyzz(a, part_first + s * Cv::kXyzzBytes);
+            load_xyzz(b, part_first + (s + stride) * Cv::kXyzzBytes);
+            add(a, b);
+            store_xyzz(part_first + s * Cv::kXyzzBytes, a);
+        }
     }
-    store_xyzz(bucket_sums + (size_t)g * Cv::kXyzzBytes, acc);
+    if (gl != 0xffffffffu) {  // a "last" slot always holds V_0 of its bucket (sa = s)
+        const uint32_t m = (offsets[gl + 1] - 1) / seg - (uint32_t)s + 1;
+        if (stride < m) {
+            Xyzz<F> a, b;
+            load_xyzz(a, part_last + s * Cv::kXyzzBytes);
+            load_xyzz(b, part_first + (s + stride) * Cv::kXyzzBytes);
+            add(a, b);
+            store_xyzz(part_last + s * Cv::kXyzzBytes, a);
+        }
+    }
+}
+
+// after the rounds: V_0 of every cut bucket is its sum
+template <class Cv>
+__global__ void msm_fixup_final_kernel(const uint32_t* __restrict__ offsets, uint32_t nb, uint32_t seg, const uint8_t* __restrict__ part_first,
+                                       const uint8_t* __restrict__ part_last, uint8_t* __restrict__ bucket_sums) {
+    const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= nb) return;
+    const uint32_t b0 = offsets[g], b1 = offsets[g + 1];
+    if (b0 == b1) return;
+    const uint32_t sa = b0 / seg, sb = (b1 - 1) / seg;
+    if (sa == sb) return;  // whole bucket inside one segment: already written
+    const uint8_t* src = (b0 == sa * seg ? part_first : part_last) + (size_t)sa * Cv::kXyzzBytes;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(bucket_sums + (size_t)g * Cv::kXyzzBytes);
+#pragma unroll
+    for (int i = 0; i < Cv::kXyzzBytes / 16; i++) d4[i] = s4[i];
 }
 
 // ------------------------------------------------------------------ reduce
@@ -320,7 +385,10 @@ __global__ void msm_reduce_kernel(const uint32_t* __restrict__ offsets, const ui
 
 // one block per window: tree-sum of the tw chunk results
 template <class Cv>
-__global__ void msm_window_kernel(const uint8_t* __restrict__ chunk_sums, uint32_t tw, uint8_t* __restrict__ scratch,
+constexpr int win_threads() { return std::is_same<Cv, G2>::value ? 256 : 512; }
+
+template <class Cv>
+__global__ void __launch_bounds__(win_threads<Cv>()) msm_window_kernel(const uint8_t* __restrict__ chunk_sums, uint32_t tw, uint8_t* __restrict__ scratch,
                                   uint8_t* __restrict__ window_sums) {
     using F = typename Cv::F;
     const uint32_t w = blockIdx.x;
@@ -498,7 +566,8 @@ struct LaunchCounter {
 template <class Cv>
 static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
                         const MsmPlan& P, Arena& ar, uint8_t* windows_dev, cudaEvent_t points_ready, LaunchCounter& lc,
-                        cudaEvent_t acc_begin, cudaEvent_t acc_end, uint32_t** total_keys_dev) {
+                        uint32_t** total_keys_dev) {
+    cudaEvent_t* ph = ctx->phase;
     uint32_t* counts = ar.take<uint32_t>(P.nb + 1);
     uint32_t* offsets = ar.take<uint32_t>(P.nb + 1);
     *total_keys_dev = offsets + P.nb;
@@ -507,54 +576,72 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     uint32_t* keys = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
     uint8_t* part_first = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
     uint8_t* part_last = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
+    uint32_t* first_bucket = ar.take<uint32_t>(P.max_segs);
+    uint32_t* last_bucket = ar.take<uint32_t>(P.max_segs);
     uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
     uint8_t* chunk_sums = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
-    constexpr int kWinThreads = 128;
+    constexpr int kWinThreads = win_threads<Cv>();
     uint8_t* win_tmp = ar.take<uint8_t>((size_t)P.W * kWinThreads * Cv::kXyzzBytes);
 
     const int sms = ctx->num_sms;
+    ZK_TRY_CUDA(cudaEventRecord(ph[0], st));
     ZK_TRY_CUDA(cudaMemsetAsync(counts, 0, (P.nb + 1) * sizeof(uint32_t), st));
     msm_count_kernel<<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts);
     lc++;
+    ZK_TRY_CUDA(cudaEventRecord(ph[1], st));
     scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums);
     lc++;
     scan_tiles_kernel<<<1, 1024, 0, st>>>(tile_sums, P.tiles);
     lc++;
     scan_finish_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums, offsets, cursors);
     lc++;
-    msm_scatter_kernel<<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, cursors, keys);
+    ZK_TRY_CUDA(cudaEventRecord(ph[2], st));
+    msm_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, cursors, keys);
     lc++;
+    ZK_TRY_CUDA(cudaMemsetAsync(first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     if (points_ready) ZK_TRY_CUDA(cudaStreamWaitEvent(st, points_ready, 0));
-    if (acc_begin) ZK_TRY_CUDA(cudaEventRecord(acc_begin, st));
+    ZK_TRY_CUDA(cudaEventRecord(ph[3], st));
     {
         const int threads = 128;
         unsigned blocks = (unsigned)((P.max_segs + threads - 1) / threads);
         if (blocks < 1) blocks = 1;
         msm_accumulate_kernel<Cv><<<blocks, threads, 0, st>>>(keys, offsets, P.nb, (const uint8_t*)d_points, P.seg, buckets,
-                                                               part_first, part_last);
+                                                               part_first, part_last, first_bucket, last_bucket);
         lc++;
     }
-    if (acc_end) ZK_TRY_CUDA(cudaEventRecord(acc_end, st));
-    msm_fixup_kernel<Cv><<<(P.nb + 127) / 128, 128, 0, st>>>(offsets, P.nb, P.seg, part_first, part_last, buckets);
-    lc++;
+    ZK_TRY_CUDA(cudaEventRecord(ph[4], st));
+    {
+        const unsigned blocks = (unsigned)((P.max_segs + 127) / 128);
+        for (uint32_t stride = 1; stride < P.max_segs; stride <<= 1) {
+            msm_fixup_round_kernel<Cv><<<blocks, 128, 0, st>>>(offsets, first_bucket, last_bucket, P.max_segs, P.seg, stride,
+                                                                part_first, part_last);
+            lc++;
+        }
+        msm_fixup_final_kernel<Cv><<<(P.nb + 255) / 256, 256, 0, st>>>(offsets, P.nb, P.seg, part_first, part_last, buckets);
+        lc++;
+    }
+    ZK_TRY_CUDA(cudaEventRecord(ph[5], st));
     {
         uint32_t total = (uint32_t)P.W * P.tw;
         msm_reduce_kernel<Cv><<<(total + 127) / 128, 128, 0, st>>>(offsets, buckets, P.W, P.B, P.chunk, P.tw, chunk_sums);
         lc++;
     }
+    ZK_TRY_CUDA(cudaEventRecord(ph[6], st));
     msm_window_kernel<Cv><<<P.W, kWinThreads, 0, st>>>(chunk_sums, P.tw, win_tmp, windows_dev);
     lc++;
+    ZK_TRY_CUDA(cudaEventRecord(ph[7], st));
     ZK_TRY_CUDA(cudaGetLastError());
     return ZK_OK;
 }
 
 template <class Cv>
 static size_t pipeline_bytes(const MsmPlan& P) {
-    constexpr int kWinThreads = 128;
+    constexpr int kWinThreads = win_threads<Cv>();
     size_t b = 0;
     b += Arena::round((P.nb + 1) * 4) * 2 + Arena::round(P.nb * 4) + Arena::round(P.tiles * 4);
     b += Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
-    b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes);
+    b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes) + 2 * Arena::round(P.max_segs * 4);
     b += Arena::round((size_t)P.nb * Cv::kXyzzBytes);
     b += Arena::round((size_t)P.W * P.tw * Cv::kXyzzBytes);
     b += Arena::round((size_t)P.W * kWinThreads * Cv::kXyzzBytes);
@@ -581,7 +668,7 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
-    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    cudaStream_t st = user_stream;  // NULL: the legacy default stream
     MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value);
     stats.window_bits = P.c;
     stats.num_windows = P.W;
@@ -605,11 +692,9 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     uint8_t* sc = host_inputs ? ar.take<uint8_t>(n * 32) : nullptr;
     LaunchCounter lc;
 
-    cudaEvent_t t0, t1, a0, a1;
+    cudaEvent_t t0, t1;
     ZK_TRY_CUDA(cudaEventCreate(&t0));
     ZK_TRY_CUDA(cudaEventCreate(&t1));
-    ZK_TRY_CUDA(cudaEventCreate(&a0));
-    ZK_TRY_CUDA(cudaEventCreate(&a1));
     ZK_TRY(scratch_begin(ctx, st));
     ZK_TRY_CUDA(cudaEventRecord(t0, st));
 
@@ -640,22 +725,21 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     }
 
     uint32_t* total_keys_dev = nullptr;
-    ZK_TRY(msm_pipeline<Cv>(ctx, st, d_points, d_scalars, n, P, ar, windows_dev, points_ready, lc, a0, a1, &total_keys_dev));
+    ZK_TRY(msm_pipeline<Cv>(ctx, st, d_points, d_scalars, n, P, ar, windows_dev, points_ready, lc, &total_keys_dev));
     ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows_dev, (size_t)P.W * Cv::kXyzzBytes, cudaMemcpyDeviceToHost, st));
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
     ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, total_keys_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
     ZK_TRY_CUDA(cudaEventRecord(t1, st));
     ZK_TRY(scratch_end(ctx, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
-    float ms_all = 0, ms_acc = 0;
+    float ms_all = 0;
     cudaEventElapsedTime(&ms_all, t0, t1);
-    cudaEventElapsedTime(&ms_acc, a0, a1);
     cudaEventDestroy(t0);
     cudaEventDestroy(t1);
-    cudaEventDestroy(a0);
-    cudaEventDestroy(a1);
+    for (int i = 0; i < 8; i++) cudaEventElapsedTime(&stats.phase_ms[i], ctx->phase[i], ctx->phase[i + 1]);
     stats.kernel_launches = lc.n;
-    stats.accumulate_ms = ms_acc;
+    stats.accumulate_ms = stats.phase_ms[3];
     stats.total_device_ms = ms_all;
     stats.bucket_adds = *keys_host;
     host_combine<Cv>((const uint64_t*)ctx->pinned, P.W, P.c, out_affine);
@@ -737,7 +821,7 @@ static int fixed_base_run(int device, cudaStream_t user_stream, void* d_out, con
     ZK_TRY(get_context(device, &ctx));
     void* table;
     ZK_TRY(fixed_base_table<Cv>(ctx, &table));
-    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    cudaStream_t st = user_stream;  // NULL: the legacy default stream
     fixed_base_kernel<Cv><<<grid_for(n, 128, ctx->num_sms * 8), 128, 0, st>>>((const uint8_t*)table, (const Fr*)d_scalars, n,
                                                                               (uint8_t*)d_out);
     ZK_TRY_CUDA(cudaGetLastError());
@@ -857,5 +941,6 @@ extern "C" int zk_msm_last_stats(zk_msm_stats* out) {
     out->window_bits = s.window_bits;
     out->num_windows = s.num_windows;
     out->bucket_adds = s.bucket_adds;
+    for (int i = 0; i < 8; i++) out->phase_ms[i] = s.phase_ms[i];
     return ZK_OK;
 }

@@ -389,7 +389,7 @@ int ntt_run(int device, cudaStream_t user_stream, void* d_out, const void* d_in,
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
-    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    cudaStream_t st = user_stream;  // NULL: the legacy default stream
     const uint64_t n = 1ull << L;
     ZK_TRY(ensure_scratch(ctx, n * 32));
     Fr* buf = (Fr*)ctx->scratch;
@@ -419,7 +419,7 @@ int compute_h_run(int device, cudaStream_t user_stream, void* d_h, const void* d
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
-    cudaStream_t st = user_stream ? user_stream : ctx->stream;
+    cudaStream_t st = user_stream;  // NULL: the legacy default stream
     const uint64_t n = 1ull << L;
     ZK_TRY(ensure_scratch(ctx, 4 * n * 32));
     Fr* buf = (Fr*)ctx->scratch;
@@ -497,7 +497,7 @@ extern "C" int zk_ntt(void* d_out, const void* d_in, int log_n, int inverse) {
     ZK_TRY(ntt_run(-1, nullptr, d_out, d_in, log_n, inverse != 0, nullptr));
     DeviceContext* ctx;
     ZK_TRY(get_context(-1, &ctx));
-    ZK_TRY_CUDA(cudaStreamSynchronize(ctx->stream));
+    ZK_TRY_CUDA(cudaStreamSynchronize(0));
     return ZK_OK;
 }
 

@@ -1,5 +1,6 @@
 // runtime.cu -- device contexts, scratch arenas, error channel, and the small
 // C-ABI utilities (version, device count, last error, IMAD-rate probe).
+#include "field.cuh"
 #include "runtime.cuh"
 
 #include <cstring>
@@ -54,6 +55,7 @@ int get_context(int device, DeviceContext** out) {
         ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_c, cudaEventDisableTiming));
         ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->scratch_done, cudaEventDisableTiming));
         ZK_TRY_CUDA(cudaEventRecord(c->scratch_done, c->stream));
+        for (int i = 0; i < 9; i++) ZK_TRY_CUDA(cudaEventCreate(&c->phase[i]));
         g_ctx[device] = c;
     }
     *out = g_ctx[device];
@@ -108,28 +110,34 @@ int ensure_pinned(DeviceContext* ctx, size_t bytes) {
 }
 
 // ------------------------------------------------------------------ IMAD probe
-// Each thread runs 16 independent multiply-add chains (8 mad.lo, 8 mad.hi);
-// every iteration issues 16 IMAD-class instructions and nothing else.  The
-// result feeds a store so the work cannot be removed.
-__global__ void imad_probe_kernel(uint32_t* out, uint32_t seed, int iters) {
-    uint32_t lo[8], hi[8];
-    const uint32_t b = seed | 1u, c = seed ^ 0x9e3779b9u;
+// The probe issues exactly the Montgomery row of field.cuh (mac_row: two
+// mad.lo.cc / madc.hi.cc carry chains over 8 limbs) on 4 independent
+// accumulators per thread at full occupancy.  Each row is 16 IMAD plus one
+// addc; the rate counts the 16 IMAD.
+__device__ __forceinline__ void probe_row(uint32_t* t, uint32_t a, const uint32_t* b) {
+    mac_row(t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[7], t[8], a, b);
+}
+
+__global__ void __launch_bounds__(256) imad_probe_kernel(uint32_t* out, uint32_t seed, int iters) {
+    uint32_t t[4][9], b[8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        lo[k] = seed + threadIdx.x * 8 + k;
-        hi[k] = k;
-    }
+    for (int k = 0; k < 8; k++) b[k] = seed * (k + 3) + threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int k = 0; k < 9; k++) t[j][k] = seed + j * 9 + k;
     for (int i = 0; i < iters; i++) {
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            asm volatile("mad.hi.u32 %1, %0, %2, %1;\n\tmad.lo.u32 %0, %0, %2, %3;"
-                         : "+r"(lo[k]), "+r"(hi[k])
-                         : "r"(b), "r"(c));
+        for (int j = 0; j < 4; j++) {
+            probe_row(t[j], t[j][0] | 1u, b);
+            t[j][8] &= 0xffffu;  // keep the top word small, as in the real rows
         }
     }
     uint32_t x = 0;
 #pragma unroll
-    for (int k = 0; k < 8; k++) x ^= lo[k] ^ hi[k];
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int k = 0; k < 9; k++) x ^= t[j][k];
     out[blockIdx.x * blockDim.x + threadIdx.x] = x;
 }
 
@@ -160,7 +168,7 @@ extern "C" int zk_probe_imad_rate(int device, double* rate) {
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
-    const int threads = 512, blocks = ctx->num_sms * 4, iters = 4096;
+    const int threads = 256, blocks = ctx->num_sms * 8, iters = 2048;
     uint32_t* buf;
     ZK_TRY_CUDA(cudaMalloc(&buf, (size_t)threads * blocks * 4));
     cudaEvent_t a, b;
@@ -176,7 +184,7 @@ extern "C" int zk_probe_imad_rate(int device, double* rate) {
     cudaEventDestroy(a);
     cudaEventDestroy(b);
     cudaFree(buf);
-    double instr = (double)threads * blocks * iters * 16.0;
+    double instr = (double)threads * blocks * iters * 4 * 16.0;  // 4 rows x 16 IMAD
     *rate = instr / (ms * 1e-3);
     return ZK_OK;
 }

@@ -55,6 +55,7 @@ struct DeviceContext {
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_c = nullptr;
     cudaEvent_t scratch_done = nullptr;  // last work that used `scratch`
+    cudaEvent_t phase[9] = {};            // MSM phase boundaries (timing)
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     void* pinned = nullptr;          // small pinned host staging (results)
@@ -82,6 +83,7 @@ struct MsmStats {
     int window_bits = 0;
     int num_windows = 0;
     long long bucket_adds = 0;
+    float phase_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 };
 MsmStats& msm_stats();
 

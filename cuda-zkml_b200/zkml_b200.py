@@ -16,7 +16,7 @@ import re
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libzkml_b200.so")
+LIB_PATH = os.environ.get("ZKML_B200_LIB", os.path.join(HERE, "libzkml_b200.so"))
 HEADER = os.path.join(os.path.dirname(HERE), "include", "zkml_b200.h")
 
 ZK_OK, ZK_ERR_INVALID, ZK_ERR_CUDA, ZK_ERR_NOMEM, ZK_ERR_NODEV, ZK_ERR_RANGE = 0, 1, 2, 3, 4, 5
@@ -44,7 +44,8 @@ _i = ctypes.c_int
 class MsmStats(ctypes.Structure):
     _fields_ = [("kernel_launches", ctypes.c_int), ("accumulate_ms", ctypes.c_float),
                 ("total_device_ms", ctypes.c_float), ("window_bits", ctypes.c_int),
-                ("num_windows", ctypes.c_int), ("bucket_adds", ctypes.c_longlong)]
+                ("num_windows", ctypes.c_int), ("bucket_adds", ctypes.c_longlong),
+                ("phase_ms", ctypes.c_float * 8)]
 
 
 _SIGS = {
@@ -226,7 +227,12 @@ def packed_to_ref_g2(points):
 def msm_last_stats():
     s = MsmStats()
     check(lib.zk_msm_last_stats(ctypes.byref(s)))
-    return {k: getattr(s, k) for k, _ in MsmStats._fields_}
+    d = {k: getattr(s, k) for k, _ in MsmStats._fields_}
+    d["phase_ms"] = dict(zip(MSM_PHASES, list(s.phase_ms)))
+    return d
+
+
+MSM_PHASES = ("count", "scan", "scatter", "accumulate", "fixup", "reduce", "windows", "result_copy")
 
 
 def g1_fixed_base(scalars_dev, out=None):

@@ -55,7 +55,8 @@ int zk_version(void);
 
 /* ==================================================================
  * Reference-shaped entry points.  Synchronous; they run on the calling
- * thread's current CUDA device and its default context stream.
+ * thread's current CUDA device and its legacy default stream, as the
+ * reference does.
  * ================================================================== */
 
 /* Replaces bn254::msm_g1(const G1Affine* h_points, const Fr* h_scalars, int n)
@@ -86,9 +87,10 @@ int zk_ntt_inplace(void* d_data, int log_n, int inverse);
 int zk_compute_omega(int log_n, int inverse, void* out_fr);
 
 /* ==================================================================
- * B200-native entry points.  `stream` is a cudaStream_t (NULL = the
- * library's per-device stream).  Calls are stream-ordered; those that
- * return a point to the host synchronise the stream before returning.
+ * B200-native entry points.  `stream` is a cudaStream_t (NULL = the CUDA
+ * legacy default stream, as in the CUDA runtime API).  Calls are ordered on
+ * that stream; those that return a point to the host synchronise it before
+ * returning.
  * ================================================================== */
 
 /* G1 MSM over device-resident packed points (64 B) and Fr scalars.
@@ -134,8 +136,9 @@ int zk_g2_fixed_base_device(int device, void* stream, void* d_out, const void* d
 int zk_g1_add_affine(const void* a, const void* b, void* out);
 int zk_g2_add_affine(const void* a, const void* b, void* out);
 
-/* Measured throughput of the INT32 multiply-add pipe on `device` in
- * instructions per second (a dependency-free IMAD stream at full occupancy):
+/* Measured throughput of the INT32 multiply-add pipe on `device` in IMAD per
+ * second, issued in the carry-chain form of the Montgomery rows (mad.lo.cc /
+ * madc.hi.cc chains over 8 limbs, independent accumulators, full occupancy):
  * the denominator of the MSM and NTT rooflines. */
 int zk_probe_imad_rate(int device, double* imad_per_second);
 
@@ -148,6 +151,9 @@ typedef struct {
     int window_bits;       /* c */
     int num_windows;       /* W */
     long long bucket_adds; /* nonzero signed digits = mixed additions performed */
+    /* device time per phase: count, scan, scatter, accumulate, fixup, reduce,
+     * window sums, result copy */
+    float phase_ms[8];
 } zk_msm_stats;
 int zk_msm_last_stats(zk_msm_stats* out);
 
