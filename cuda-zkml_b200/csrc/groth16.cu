@@ -1,0 +1,873 @@
+// groth16.cu -- device-resident Groth16 prover, GPU setup and the proving-key,
+// verification-key and proof formats of gdtsitlauri/cuda-zkml.
+//
+// prove (replaces Groth16Prover::prove, src/prover/groth16.cu:655-920, and the
+// host parts of compute_h, :263-390):
+//   witness H2D -> sparse matvec A*w, B*w, C*w on the device (the reference does
+//   it on the host, :275-294) -> compute_h (7 NTTs, coset shift and pointwise
+//   fused, ntt.cu) -> MSMs A, B (G2), L, H, B1 on the device -> on the host:
+//     A = alpha1 + sum w_i A_i + r delta1
+//     B = beta2  + sum w_i B_i + s delta2
+//     C = sum_priv w_i L_i + sum h_j H_j + s A + r (beta1 + sum w_i B1_i)
+//   (the reference's convention, :774-844), serialised as the 256-byte proof.
+// The proving key and the R1CS stay resident on the device between proofs.
+//
+// setup (replaces the host loop of Groth16Prover::setup, :446-642): the QAP
+// evaluations at tau and the query scalars on the host, then every query point
+// k * G by the device fixed-base kernel; the points are canonical, so the key is
+// byte-identical to the reference's for the same toxic waste.
+#include "field.cuh"
+#include "host_field.hpp"
+#include "runtime.cuh"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+namespace zk {
+
+// ------------------------------------------------------------------ helpers
+static zkh::Fe fr_one() { return zkh::one(zkh::kR); }
+static zkh::Fe fr_mul(const zkh::Fe& a, const zkh::Fe& b) { zkh::Fe r; zkh::mul(zkh::kR, r, a, b); return r; }
+static zkh::Fe fr_add(const zkh::Fe& a, const zkh::Fe& b) { zkh::Fe r; zkh::add(zkh::kR, r, a, b); return r; }
+static zkh::Fe fr_sub(const zkh::Fe& a, const zkh::Fe& b) { zkh::Fe r; zkh::sub(zkh::kR, r, a, b); return r; }
+static zkh::Fe fr_inv(const zkh::Fe& a) { zkh::Fe r; zkh::inv(zkh::kR, r, a); return r; }
+
+// primitive 2^L-th root of unity 5^((r-1)/2^L) (src/ntt/ntt.cu:43-106)
+static zkh::Fe root_of_unity(int L) {
+    uint64_t e[4];
+    std::memcpy(e, zkh::kR.m, 32);
+    e[0] -= 1;
+    for (int s = 0; s < 28; s++)
+        for (int i = 0; i < 4; i++) e[i] = (e[i] >> 1) | (i < 3 ? e[i + 1] << 63 : 0);
+    uint64_t five[4] = {5, 0, 0, 0};
+    zkh::Fe g, w;
+    zkh::from_std(zkh::kR, g, five);
+    zkh::pow(zkh::kR, w, g, e);
+    for (int i = 0; i < 28 - L; i++) w = fr_mul(w, w);
+    return w;
+}
+
+// batch inversion (Montgomery's trick); zero entries stay zero
+static void batch_inverse(std::vector<zkh::Fe>& v) {
+    const size_t n = v.size();
+    std::vector<zkh::Fe> pre(n);
+    zkh::Fe acc = fr_one();
+    for (size_t i = 0; i < n; i++) {
+        pre[i] = acc;
+        if (!zkh::is_zero(v[i])) acc = fr_mul(acc, v[i]);
+    }
+    zkh::Fe inv = fr_inv(acc);
+    for (size_t i = n; i-- > 0;) {
+        if (zkh::is_zero(v[i])) continue;
+        zkh::Fe t = fr_mul(inv, pre[i]);
+        inv = fr_mul(inv, v[i]);
+        v[i] = t;
+    }
+}
+
+template <class F>
+static void load_aff(zkh::Xyzz<F>& p, const uint64_t* rec);
+template <>
+void load_aff<zkh::Fe>(zkh::Xyzz<zkh::Fe>& p, const uint64_t* r) {
+    bool z = true;
+    for (int i = 0; i < 8; i++) if (r[i]) z = false;
+    if (z) { zkh::set_identity(p); return; }
+    zkh::Fe x, y;
+    std::memcpy(x.v, r, 32);
+    std::memcpy(y.v, r + 4, 32);
+    zkh::from_affine(p, x, y);
+}
+template <>
+void load_aff<zkh::Fp2>(zkh::Xyzz<zkh::Fp2>& p, const uint64_t* r) {
+    bool z = true;
+    for (int i = 0; i < 16; i++) if (r[i]) z = false;
+    if (z) { zkh::set_identity(p); return; }
+    zkh::Fp2 x, y;
+    std::memcpy(x.c0.v, r, 32);
+    std::memcpy(x.c1.v, r + 4, 32);
+    std::memcpy(y.c0.v, r + 8, 32);
+    std::memcpy(y.c1.v, r + 12, 32);
+    zkh::from_affine(p, x, y);
+}
+static void store_aff(uint64_t* r, const zkh::Xyzz<zkh::Fe>& p) {
+    zkh::Fe x, y;
+    zkh::to_affine(x, y, p);
+    std::memcpy(r, x.v, 32);
+    std::memcpy(r + 4, y.v, 32);
+}
+static void store_aff(uint64_t* r, const zkh::Xyzz<zkh::Fp2>& p) {
+    zkh::Fp2 x, y;
+    zkh::to_affine(x, y, p);
+    std::memcpy(r, x.c0.v, 32);
+    std::memcpy(r + 4, x.c1.v, 32);
+    std::memcpy(r + 8, y.c0.v, 32);
+    std::memcpy(r + 12, y.c1.v, 32);
+}
+
+// ------------------------------------------------------------------ R1CS
+struct SparseEntry {  // zkml::SparseEntry (src/prover/circuit.cuh:31-35)
+    int32_t row;
+    int32_t col;
+    uint64_t v[4];
+};
+static_assert(sizeof(SparseEntry) == 40, "SparseEntry layout");
+
+struct Csr {
+    std::vector<int32_t> row_ptr, col;
+    std::vector<zkh::Fe> val;
+    std::vector<int32_t> long_rows;  // rows with > kShortRow entries
+};
+static constexpr int kShortRow = 64;
+
+struct R1cs {
+    int device = -1;
+    int num_constraints = 0, m = 0, num_public = 0, log_n = 0;
+    uint64_t n = 0;
+    Csr host[3];
+    int32_t* d_row_ptr[3] = {};
+    int32_t* d_col[3] = {};
+    Fr* d_val[3] = {};
+    int32_t* d_long[3] = {};
+    size_t nnz[3] = {};
+};
+
+}  // namespace zk
+
+struct zk_r1cs {
+    zk::R1cs r;
+};
+
+struct zk_groth16_pk {
+    int device = -1;
+    int num_constraints = 0;  // padded domain size n, as the reference stores it (groth16.cu:621)
+    int m = 0, num_public = 0, l = 0, n_h = 0;
+    uint8_t* g1 = nullptr;  // device: A[m] | B1[m] | L[l] | H[n_h]   (64-B packed)
+    uint8_t* g2 = nullptr;  // device: B2[m]                          (128-B packed)
+    uint64_t alpha1[8], beta1[8], delta1[8];
+    uint64_t beta2[16], gamma2[16], delta2[16], g2gen[16], tau2[16];
+    std::vector<uint64_t> ic;  // (num_public + 1) x 8
+    // prover buffers
+    zk::Fr* w = nullptr;
+    zk::Fr* abc = nullptr;  // 3 n
+    zk::Fr* h = nullptr;    // n
+    uint64_t n_buf = 0;
+};
+
+namespace zk {
+
+static thread_local zk_prove_stats g_prove_stats;
+
+// ------------------------------------------------------------------ kernels
+// rows with at most kShortRow entries: one thread per row; long rows are skipped
+// here and done by r1cs_matvec_long_kernel
+__global__ void r1cs_matvec_short_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col, const Fr* __restrict__ val,
+                                         const Fr* __restrict__ w, int rows, uint64_t n, Fr* __restrict__ out) {
+    for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (uint64_t)gridDim.x * blockDim.x) {
+        Fr acc;
+        fset_zero(acc);
+        if (r < (uint64_t)rows) {
+            const int a = row_ptr[r], b = row_ptr[r + 1];
+            if (b - a <= kShortRow) {
+                for (int j = a; j < b; j++) {
+                    Fr v, x;
+                    fload_nc(v, val + j);
+                    fload_nc(x, w + col[j]);
+                    fmul(v, v, x);
+                    fadd(acc, acc, v);
+                }
+            } else {
+                continue;  // written by the long-row kernel
+            }
+        }
+        fstore(out + r, acc);
+    }
+}
+
+// one block per long row: strided partial sums, then a shared-memory tree
+__global__ void __launch_bounds__(256) r1cs_matvec_long_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
+                                                               const Fr* __restrict__ val, const Fr* __restrict__ w,
+                                                               const int32_t* __restrict__ long_rows, Fr* __restrict__ out) {
+    __shared__ Fr part[256];
+    const int r = long_rows[blockIdx.x];
+    const int a = row_ptr[r], b = row_ptr[r + 1];
+    Fr acc;
+    fset_zero(acc);
+    for (int j = a + threadIdx.x; j < b; j += blockDim.x) {
+        Fr v, x;
+        fload_nc(v, val + j);
+        fload_nc(x, w + col[j]);
+        fmul(v, v, x);
+        fadd(acc, acc, v);
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if ((int)threadIdx.x < s) {
+            Fr t = part[threadIdx.x];
+            fadd(t, t, part[threadIdx.x + s]);
+            part[threadIdx.x] = t;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) fstore(out + r, part[0]);
+}
+
+// x -> x * R^2 * R^-1 = Montgomery form of a standard-form Fp value
+__global__ void fp_to_mont_kernel(uint64_t* __restrict__ v, size_t count) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+        Fp x, r2;
+        fload(x, v + 4 * i);
+#pragma unroll
+        for (int k = 0; k < 8; k++) r2.v[k] = ModP::r2(k);
+        fmul(x, x, r2);
+        fstore(v + 4 * i, x);
+    }
+}
+
+// ------------------------------------------------------------------ R1CS upload
+static int r1cs_create(int device, int num_constraints, int num_variables, int num_public, const SparseEntry* const* ent,
+                       const size_t* nnz, R1cs& R) {
+    if (num_constraints < 0 || num_variables <= 0 || num_public < 0 || num_public >= num_variables) {
+        set_error("r1cs: invalid sizes (constraints %d, variables %d, public %d)", num_constraints, num_variables, num_public);
+        return ZK_ERR_INVALID;
+    }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    R.device = ctx->device;
+    R.num_constraints = num_constraints;
+    R.m = num_variables;
+    R.num_public = num_public;
+    // QAP::from_r1cs (groth16.cu:225-242): next power of two, at least 4
+    R.n = 1;
+    R.log_n = 0;
+    while (R.n < (uint64_t)num_constraints) { R.n <<= 1; R.log_n++; }
+    if (R.n < 4) { R.n = 4; R.log_n = 2; }
+    const int rows = (int)std::min<uint64_t>(R.n, (uint64_t)std::max(num_constraints, 0));
+    for (int k = 0; k < 3; k++) {
+        Csr& c = R.host[k];
+        c.row_ptr.assign((size_t)rows + 1, 0);
+        // entries outside the domain or the witness are ignored, as compute_h does (groth16.cu:278-292)
+        for (size_t i = 0; i < nnz[k]; i++) {
+            const SparseEntry& e = ent[k][i];
+            if (e.row >= 0 && e.row < rows && e.col >= 0 && e.col < num_variables) c.row_ptr[(size_t)e.row + 1]++;
+        }
+        for (int r = 0; r < rows; r++) c.row_ptr[(size_t)r + 1] += c.row_ptr[r];
+        const size_t total = (size_t)c.row_ptr[rows];
+        c.col.resize(total);
+        c.val.resize(total);
+        std::vector<int32_t> cur(c.row_ptr.begin(), c.row_ptr.end() - 1);
+        for (size_t i = 0; i < nnz[k]; i++) {
+            const SparseEntry& e = ent[k][i];
+            if (e.row >= 0 && e.row < rows && e.col >= 0 && e.col < num_variables) {
+                const int32_t p = cur[e.row]++;
+                c.col[p] = e.col;
+                std::memcpy(c.val[p].v, e.v, 32);
+            }
+        }
+        c.long_rows.clear();
+        for (int r = 0; r < rows; r++)
+            if (c.row_ptr[(size_t)r + 1] - c.row_ptr[r] > kShortRow) c.long_rows.push_back(r);
+        R.nnz[k] = total;
+        ZK_TRY_CUDA(cudaMalloc(&R.d_row_ptr[k], c.row_ptr.size() * 4));
+        ZK_TRY_CUDA(cudaMemcpy(R.d_row_ptr[k], c.row_ptr.data(), c.row_ptr.size() * 4, cudaMemcpyHostToDevice));
+        ZK_TRY_CUDA(cudaMalloc(&R.d_col[k], std::max<size_t>(total, 1) * 4));
+        ZK_TRY_CUDA(cudaMemcpy(R.d_col[k], c.col.data(), total * 4, cudaMemcpyHostToDevice));
+        ZK_TRY_CUDA(cudaMalloc(&R.d_val[k], std::max<size_t>(total, 1) * 32));
+        ZK_TRY_CUDA(cudaMemcpy(R.d_val[k], c.val.data(), total * 32, cudaMemcpyHostToDevice));
+        ZK_TRY_CUDA(cudaMalloc(&R.d_long[k], std::max<size_t>(c.long_rows.size(), 1) * 4));
+        ZK_TRY_CUDA(cudaMemcpy(R.d_long[k], c.long_rows.data(), c.long_rows.size() * 4, cudaMemcpyHostToDevice));
+    }
+    return ZK_OK;
+}
+
+static int r1cs_matvec(const R1cs& R, cudaStream_t st, const Fr* w, Fr* out3, int num_sms) {
+    const int rows = (int)std::min<uint64_t>(R.n, (uint64_t)R.num_constraints);
+    for (int k = 0; k < 3; k++) {
+        Fr* out = out3 + (size_t)k * R.n;
+        const unsigned grid = (unsigned)std::min<uint64_t>((R.n + 255) / 256, (uint64_t)num_sms * 16);
+        r1cs_matvec_short_kernel<<<grid, 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w, rows, R.n, out);
+        if (!R.host[k].long_rows.empty())
+            r1cs_matvec_long_kernel<<<(unsigned)R.host[k].long_rows.size(), 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w,
+                                                                                         R.d_long[k], out);
+    }
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+// ------------------------------------------------------------------ setup
+// QAP evaluations at tau (groth16.cu:97-189):
+//   L_j(tau) = (tau^n - 1) w^j / (n (tau - w^j)),  X_at[col] += value * L_row(tau)
+static void qap_at_tau(const R1cs& R, const zkh::Fe& tau, std::vector<zkh::Fe> at[3], zkh::Fe& vanish) {
+    const uint64_t n = R.n;
+    const zkh::Fe w = root_of_unity(R.log_n);
+    zkh::Fe tn = tau;
+    for (int i = 0; i < R.log_n; i++) tn = fr_mul(tn, tn);
+    vanish = fr_sub(tn, fr_one());
+    uint64_t s2[4] = {2, 0, 0, 0};
+    zkh::Fe two;
+    zkh::from_std(zkh::kR, two, s2);
+    zkh::Fe half = fr_inv(two), ninv = fr_one();
+    for (int i = 0; i < R.log_n; i++) ninv = fr_mul(ninv, half);
+    std::vector<zkh::Fe> den(n), lag(n);
+    zkh::Fe wj = fr_one();
+    for (uint64_t j = 0; j < n; j++) {
+        den[j] = fr_sub(tau, wj);
+        lag[j] = fr_mul(fr_mul(vanish, wj), ninv);
+        wj = fr_mul(wj, w);
+    }
+    batch_inverse(den);
+    for (uint64_t j = 0; j < n; j++) lag[j] = fr_mul(lag[j], den[j]);
+    for (int k = 0; k < 3; k++) {
+        at[k].assign((size_t)R.m, zkh::zero());
+        const Csr& c = R.host[k];
+        const int rows = (int)c.row_ptr.size() - 1;
+        for (int r = 0; r < rows; r++)
+            for (int p = c.row_ptr[r]; p < c.row_ptr[(size_t)r + 1]; p++) at[k][c.col[p]] = fr_add(at[k][c.col[p]], fr_mul(c.val[p], lag[r]));
+    }
+}
+
+static int setup(const R1cs& R, const zkh::Fe toxic[5], zk_groth16_pk* pk) {
+    const zkh::Fe tau = toxic[0], alpha = toxic[1], beta = toxic[2], gamma = toxic[3], delta = toxic[4];
+    const int m = R.m, pub = R.num_public;
+    const int l = std::max(0, m - pub - 1);
+    const uint64_t n = R.n;
+    std::vector<zkh::Fe> at[3];
+    zkh::Fe vanish;
+    qap_at_tau(R, tau, at, vanish);
+    const zkh::Fe dinv = fr_inv(delta), ginv = fr_inv(gamma);
+    // G1 scalars: A[m] | B[m] | L[l] | H[n] | IC[pub+1] | alpha, beta, delta
+    const size_t nG1 = 2 * (size_t)m + l + n + (size_t)pub + 1 + 3;
+    std::vector<zkh::Fe> s1(nG1);
+    size_t o = 0;
+    for (int i = 0; i < m; i++) s1[o++] = at[0][i];
+    for (int i = 0; i < m; i++) s1[o++] = at[1][i];
+    auto lc = [&](int i) { return fr_add(fr_add(fr_mul(beta, at[0][i]), fr_mul(alpha, at[1][i])), at[2][i]); };
+    for (int i = 0; i < l; i++) s1[o++] = fr_mul(lc(i + 1 + pub), dinv);
+    zkh::Fe tp = fr_mul(vanish, dinv);
+    for (uint64_t i = 0; i < n; i++) { s1[o++] = tp; tp = fr_mul(tp, tau); }
+    for (int i = 0; i <= pub; i++) s1[o++] = fr_mul(lc(i), ginv);
+    s1[o++] = alpha;
+    s1[o++] = beta;
+    s1[o++] = delta;
+    // G2 scalars: B[m] | beta, gamma, delta, tau, 1
+    std::vector<zkh::Fe> s2(at[1]);
+    s2.push_back(beta);
+    s2.push_back(gamma);
+    s2.push_back(delta);
+    s2.push_back(tau);
+    s2.push_back(fr_one());
+
+    DeviceContext* ctx;
+    ZK_TRY(get_context(R.device, &ctx));
+    Fr* d_sc;
+    ZK_TRY_CUDA(cudaMalloc(&d_sc, std::max(nG1, s2.size()) * 32));
+    uint8_t *g1_all, *g2_all;
+    ZK_TRY_CUDA(cudaMalloc(&g1_all, nG1 * 64));
+    ZK_TRY_CUDA(cudaMalloc(&g2_all, s2.size() * 128));
+    ZK_TRY_CUDA(cudaMemcpy(d_sc, s1.data(), nG1 * 32, cudaMemcpyHostToDevice));
+    ZK_TRY(zk_g1_fixed_base_device(R.device, nullptr, g1_all, d_sc, nG1));
+    ZK_TRY_CUDA(cudaDeviceSynchronize());
+    ZK_TRY_CUDA(cudaMemcpy(d_sc, s2.data(), s2.size() * 32, cudaMemcpyHostToDevice));
+    ZK_TRY(zk_g2_fixed_base_device(R.device, nullptr, g2_all, d_sc, s2.size()));
+    ZK_TRY_CUDA(cudaDeviceSynchronize());
+    cudaFree(d_sc);
+
+    pk->device = R.device;
+    pk->num_constraints = (int)n;
+    pk->m = m;
+    pk->num_public = pub;
+    pk->l = l;
+    pk->n_h = (int)n;
+    pk->g1 = g1_all;  // A | B1 | L | H | IC | alpha beta delta (the tail is copied out below)
+    pk->g2 = g2_all;  // B2 | beta gamma delta tau G2
+    const size_t tail1 = 2 * (size_t)m + l + n;
+    std::vector<uint64_t> t1((size_t)(pub + 1 + 3) * 8);
+    ZK_TRY_CUDA(cudaMemcpy(t1.data(), g1_all + tail1 * 64, t1.size() * 8, cudaMemcpyDeviceToHost));
+    pk->ic.assign(t1.begin(), t1.begin() + (size_t)(pub + 1) * 8);
+    std::memcpy(pk->alpha1, &t1[(size_t)(pub + 1) * 8], 64);
+    std::memcpy(pk->beta1, &t1[(size_t)(pub + 2) * 8], 64);
+    std::memcpy(pk->delta1, &t1[(size_t)(pub + 3) * 8], 64);
+    std::vector<uint64_t> t2(5 * 16);
+    ZK_TRY_CUDA(cudaMemcpy(t2.data(), g2_all + (size_t)m * 128, t2.size() * 8, cudaMemcpyDeviceToHost));
+    std::memcpy(pk->beta2, &t2[0], 128);
+    std::memcpy(pk->gamma2, &t2[16], 128);
+    std::memcpy(pk->delta2, &t2[32], 128);
+    std::memcpy(pk->tau2, &t2[48], 128);
+    std::memcpy(pk->g2gen, &t2[64], 128);
+    return ZK_OK;
+}
+
+static int ensure_prover_buffers(zk_groth16_pk* pk, uint64_t n, int m) {
+    if (pk->n_buf >= n && pk->w) return ZK_OK;
+    if (pk->w) cudaFree(pk->w);
+    if (pk->abc) cudaFree(pk->abc);
+    if (pk->h) cudaFree(pk->h);
+    ZK_TRY_CUDA(cudaMalloc(&pk->w, (size_t)std::max<uint64_t>(m, 1) * 32));
+    ZK_TRY_CUDA(cudaMalloc(&pk->abc, 3 * n * 32));
+    ZK_TRY_CUDA(cudaMalloc(&pk->h, n * 32));
+    pk->n_buf = n;
+    return ZK_OK;
+}
+
+// ------------------------------------------------------------------ prove
+static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* h_witness, const zkh::Fe& r, const zkh::Fe& s,
+                 uint64_t outA[8], uint64_t outB[16], uint64_t outC[8]) {
+    zk_prove_stats& stats = g_prove_stats;
+    std::memset(&stats, 0, sizeof stats);
+    if (R.m != pk->m || R.num_public != pk->num_public || (uint64_t)pk->num_constraints != R.n) {
+        set_error("prove: proving key (m %d, public %d, n %d) does not match the circuit (m %d, public %d, n %llu)", pk->m,
+                  pk->num_public, pk->num_constraints, R.m, R.num_public, (unsigned long long)R.n);
+        return ZK_ERR_INVALID;
+    }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(pk->device, &ctx));
+    const uint64_t n = R.n;
+    const int m = R.m, pub = R.num_public;
+    ZK_TRY(ensure_prover_buffers(pk, n, m));
+    cudaEvent_t ev[4];
+    for (auto& e : ev) ZK_TRY_CUDA(cudaEventCreate(&e));
+    ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
+    ZK_TRY_CUDA(cudaMemcpyAsync(pk->w, h_witness, (size_t)m * 32, cudaMemcpyHostToDevice, st));
+    ZK_TRY(r1cs_matvec(R, st, pk->w, pk->abc, ctx->num_sms));
+    ZK_TRY_CUDA(cudaEventRecord(ev[1], st));
+    ZK_TRY(zk_compute_h_device(pk->device, st, pk->h, pk->abc, pk->abc + n, pk->abc + 2 * n, R.log_n));
+    ZK_TRY_CUDA(cudaEventRecord(ev[2], st));
+    ZK_TRY_CUDA(cudaEventSynchronize(ev[2]));
+    float ms;
+    cudaEventElapsedTime(&ms, ev[0], ev[1]);
+    stats.matvec_ms = ms;
+    cudaEventElapsedTime(&ms, ev[1], ev[2]);
+    stats.compute_h_ms = ms;
+
+    uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm[8] = {0}, b_msm[16];
+    const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m, g1H = 2 * (size_t)m + pk->l;
+    zk_msm_stats ms_st;
+    ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1A * 64, pk->w, (size_t)m, a_msm));
+    zk_msm_last_stats(&ms_st);
+    stats.msm_ms[0] = ms_st.total_device_ms;
+    ZK_TRY(zk_msm_g2_device(pk->device, st, pk->g2, pk->w, (size_t)m, b_msm));
+    zk_msm_last_stats(&ms_st);
+    stats.msm_ms[1] = ms_st.total_device_ms;
+    const int num_priv = std::min(pk->l, m - 1 - pub);
+    if (num_priv > 0) {
+        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1L * 64, pk->w + 1 + pub, (size_t)num_priv, l_msm));
+        zk_msm_last_stats(&ms_st);
+        stats.msm_ms[2] = ms_st.total_device_ms;
+    }
+    const int n_h = std::min<int>((int)n, pk->n_h);
+    if (n_h > 0) {
+        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1H * 64, pk->h, (size_t)n_h, h_msm));
+        zk_msm_last_stats(&ms_st);
+        stats.msm_ms[3] = ms_st.total_device_ms;
+    }
+    ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1B1 * 64, pk->w, (size_t)m, b1_msm));
+    zk_msm_last_stats(&ms_st);
+    stats.msm_ms[4] = ms_st.total_device_ms;
+
+    // assembly (groth16.cu:774-844)
+    uint64_t rs[4], ss[4];
+    zkh::to_std(zkh::kR, rs, r);
+    zkh::to_std(zkh::kR, ss, s);
+    using P1 = zkh::Xyzz<zkh::Fe>;
+    using P2 = zkh::Xyzz<zkh::Fp2>;
+    P1 A, t1;
+    load_aff(A, pk->alpha1);
+    load_aff(t1, a_msm);
+    zkh::add(A, t1);
+    load_aff(t1, pk->delta1);
+    zkh::smul(t1, P1(t1), rs);
+    zkh::add(A, t1);
+    store_aff(outA, A);
+    P2 Bp, t2;
+    load_aff(Bp, pk->beta2);
+    load_aff(t2, b_msm);
+    zkh::add(Bp, t2);
+    load_aff(t2, pk->delta2);
+    zkh::smul(t2, P2(t2), ss);
+    zkh::add(Bp, t2);
+    store_aff(outB, Bp);
+    P1 Cp, Aaff, b1;
+    load_aff(Cp, l_msm);
+    load_aff(t1, h_msm);
+    zkh::add(Cp, t1);
+    load_aff(Aaff, outA);          // s * A uses the affine proof point A
+    zkh::smul(t1, Aaff, ss);
+    zkh::add(Cp, t1);
+    load_aff(b1, pk->beta1);
+    load_aff(t1, b1_msm);
+    zkh::add(b1, t1);
+    zkh::smul(t1, b1, rs);
+    zkh::add(Cp, t1);
+    store_aff(outC, Cp);
+    ZK_TRY_CUDA(cudaEventRecord(ev[3], st));
+    ZK_TRY_CUDA(cudaEventSynchronize(ev[3]));
+    cudaEventElapsedTime(&ms, ev[0], ev[3]);
+    stats.total_ms = ms;
+    for (auto& e : ev) cudaEventDestroy(e);
+    return ZK_OK;
+}
+
+// 256-byte proof: A.x A.y B.x.c0 B.x.c1 B.y.c0 B.y.c1 C.x C.y, each 32 B
+// standard form little-endian (groth16.cu:1058-1074)
+static void serialize_proof(uint8_t* out, const uint64_t A[8], const uint64_t B[16], const uint64_t C[8]) {
+    const uint64_t* src[8] = {A, A + 4, B, B + 4, B + 8, B + 12, C, C + 4};
+    for (int k = 0; k < 8; k++) {
+        zkh::Fe f;
+        std::memcpy(f.v, src[k], 32);
+        uint64_t s[4];
+        zkh::to_std(zkh::kP, s, f);
+        std::memcpy(out + 32 * k, s, 32);  // host is little-endian
+    }
+}
+
+// ------------------------------------------------------------------ key files
+// ZKMLPK3 (groth16.cu:1104-1180): magic "ZKMLPK3\0", u32 3, i32 n, i32 m,
+// i32 num_public, G1 alpha beta delta, G2 beta gamma delta, vec G1 tau_g1,
+// vec G2 tau_g2, vec G1 A, vec G1 B1, vec G2 B2, vec G1 L, vec G1 H; a G1 record
+// is u8 infinity + x + y (standard form), G2 is u8 + x.c0 x.c1 y.c0 y.c1, a vec is
+// i32 count + records.
+static void put_fp_std(std::vector<uint8_t>& b, const uint64_t* mont) {
+    zkh::Fe f;
+    std::memcpy(f.v, mont, 32);
+    uint64_t s[4];
+    zkh::to_std(zkh::kP, s, f);
+    const uint8_t* p = (const uint8_t*)s;
+    b.insert(b.end(), p, p + 32);
+}
+static void put_g1(std::vector<uint8_t>& b, const uint64_t* rec) {
+    bool inf = true;
+    for (int i = 0; i < 8; i++) if (rec[i]) inf = false;
+    b.push_back(inf ? 1 : 0);
+    put_fp_std(b, rec);
+    put_fp_std(b, rec + 4);
+}
+static void put_g2(std::vector<uint8_t>& b, const uint64_t* rec) {
+    bool inf = true;
+    for (int i = 0; i < 16; i++) if (rec[i]) inf = false;
+    b.push_back(inf ? 1 : 0);
+    for (int k = 0; k < 4; k++) put_fp_std(b, rec + 4 * k);
+}
+static void put_i32(std::vector<uint8_t>& b, int32_t v) {
+    const uint8_t* p = (const uint8_t*)&v;
+    b.insert(b.end(), p, p + 4);
+}
+
+static int pk_save(const zk_groth16_pk* pk, const char* path) {
+    FILE* f = fopen(path, "wb");
+    if (!f) { set_error("pk_save: cannot open %s", path); return ZK_ERR_INVALID; }
+    std::vector<uint8_t> b;
+    const char magic[8] = {'Z', 'K', 'M', 'L', 'P', 'K', '3', '\0'};
+    b.insert(b.end(), magic, magic + 8);
+    uint32_t version = 3;
+    b.insert(b.end(), (uint8_t*)&version, (uint8_t*)&version + 4);
+    put_i32(b, pk->num_constraints);
+    put_i32(b, pk->m);
+    put_i32(b, pk->num_public);
+    put_g1(b, pk->alpha1);
+    put_g1(b, pk->beta1);
+    put_g1(b, pk->delta1);
+    put_g2(b, pk->beta2);
+    put_g2(b, pk->gamma2);
+    put_g2(b, pk->delta2);
+    put_i32(b, 0);  // tau_powers_g1: never kept (groth16.cu:510-513)
+    put_i32(b, 2);  // tau_powers_g2 = [G2, tau G2] (groth16.cu:517-519)
+    put_g2(b, pk->g2gen);
+    put_g2(b, pk->tau2);
+    bool ok = fwrite(b.data(), 1, b.size(), f) == b.size();
+    auto dump_vec = [&](const uint8_t* dev, size_t count, bool g2) {
+        std::vector<uint64_t> h(count * (g2 ? 16 : 8));
+        if (count) cudaMemcpy(h.data(), dev, h.size() * 8, cudaMemcpyDeviceToHost);
+        std::vector<uint8_t> o;
+        o.reserve(4 + count * (g2 ? 129 : 65));
+        put_i32(o, (int32_t)count);
+        for (size_t i = 0; i < count; i++) {
+            if (g2) put_g2(o, &h[i * 16]);
+            else put_g1(o, &h[i * 8]);
+        }
+        ok = ok && fwrite(o.data(), 1, o.size(), f) == o.size();
+    };
+    const size_t m = (size_t)pk->m;
+    dump_vec(pk->g1, m, false);                                   // A
+    dump_vec(pk->g1 + m * 64, m, false);                          // B1
+    dump_vec(pk->g2, m, true);                                    // B2
+    dump_vec(pk->g1 + 2 * m * 64, (size_t)pk->l, false);          // L
+    dump_vec(pk->g1 + (2 * m + pk->l) * 64, (size_t)pk->n_h, false);  // H
+    fclose(f);
+    if (!ok) { set_error("pk_save: write failed for %s", path); return ZK_ERR_INVALID; }
+    return ZK_OK;
+}
+
+struct Reader {
+    const uint8_t* p;
+    size_t left;
+    bool ok = true;
+    void raw(void* dst, size_t n) {
+        if (!ok || left < n) { ok = false; return; }
+        std::memcpy(dst, p, n);
+        p += n;
+        left -= n;
+    }
+    int32_t i32() { int32_t v = 0; raw(&v, 4); return v; }
+};
+
+// parse into standard-form records (infinity -> all zero); Montgomery
+// conversion happens on the device
+static void get_g1(Reader& R, uint64_t* rec) {
+    uint8_t inf = 0;
+    R.raw(&inf, 1);
+    R.raw(rec, 64);
+    if (inf) std::memset(rec, 0, 64);
+}
+static void get_g2(Reader& R, uint64_t* rec) {
+    uint8_t inf = 0;
+    R.raw(&inf, 1);
+    R.raw(rec, 128);
+    if (inf) std::memset(rec, 0, 128);
+}
+static void std_to_mont_host(uint64_t* v, size_t fe_count) {
+    for (size_t i = 0; i < fe_count; i++) {
+        bool z = (v[4 * i] | v[4 * i + 1] | v[4 * i + 2] | v[4 * i + 3]) == 0;
+        if (z) continue;
+        zkh::Fe f;
+        zkh::from_std(zkh::kP, f, v + 4 * i);
+        std::memcpy(v + 4 * i, f.v, 32);
+    }
+}
+
+static int pk_load(int device, const char* path, zk_groth16_pk* pk) {
+    FILE* f = fopen(path, "rb");
+    if (!f) { set_error("pk_load: cannot open %s", path); return ZK_ERR_INVALID; }
+    fseek(f, 0, SEEK_END);
+    const long size = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    std::vector<uint8_t> buf((size_t)std::max(0L, size));
+    const bool rd = fread(buf.data(), 1, buf.size(), f) == buf.size();
+    fclose(f);
+    if (!rd) { set_error("pk_load: read failed for %s", path); return ZK_ERR_INVALID; }
+    Reader R{buf.data(), buf.size()};
+    char magic[8];
+    R.raw(magic, 8);
+    uint32_t version = 0;
+    R.raw(&version, 4);
+    if (!R.ok || std::memcmp(magic, "ZKMLPK3", 7) != 0 || version != 3) {
+        set_error("pk_load: %s is not a ZKMLPK3 v3 proving key", path);
+        return ZK_ERR_INVALID;
+    }
+    pk->num_constraints = R.i32();
+    pk->m = R.i32();
+    pk->num_public = R.i32();
+    if (!R.ok || pk->num_constraints < 0 || pk->m <= 0 || pk->num_public < 0) {
+        set_error("pk_load: invalid metadata in %s", path);
+        return ZK_ERR_INVALID;
+    }
+    uint64_t small1[3][8], small2[3][16];
+    for (int k = 0; k < 3; k++) get_g1(R, small1[k]);
+    for (int k = 0; k < 3; k++) get_g2(R, small2[k]);
+    const int32_t ntg1 = R.i32();
+    if (!R.ok || ntg1 < 0 || ntg1 > (1 << 28)) { set_error("pk_load: bad tau_g1 count"); return ZK_ERR_INVALID; }
+    for (int32_t i = 0; i < ntg1; i++) { uint64_t t[8]; get_g1(R, t); }
+    const int32_t ntg2 = R.i32();
+    if (!R.ok || ntg2 < 0 || ntg2 > (1 << 28)) { set_error("pk_load: bad tau_g2 count"); return ZK_ERR_INVALID; }
+    uint64_t tg2[2][16] = {};
+    for (int32_t i = 0; i < ntg2; i++) {
+        uint64_t t[16];
+        get_g2(R, t);
+        if (i < 2) std::memcpy(tg2[i], t, 128);
+    }
+    std::vector<uint64_t> g1h, g2h;
+    int32_t counts[5];
+    for (int v = 0; v < 5; v++) {
+        const bool g2 = v == 2;
+        counts[v] = R.i32();
+        if (!R.ok || counts[v] < 0 || counts[v] > (1 << 28)) { set_error("pk_load: bad vector count in %s", path); return ZK_ERR_INVALID; }
+        std::vector<uint64_t>& dst = g2 ? g2h : g1h;
+        const size_t base = dst.size();
+        dst.resize(base + (size_t)counts[v] * (g2 ? 16 : 8));
+        for (int32_t i = 0; i < counts[v]; i++) {
+            if (g2) get_g2(R, &dst[base + (size_t)i * 16]);
+            else get_g1(R, &dst[base + (size_t)i * 8]);
+        }
+    }
+    if (!R.ok) { set_error("pk_load: truncated file %s", path); return ZK_ERR_INVALID; }
+    if (counts[0] < pk->m || counts[1] < pk->m || counts[2] < pk->m) {
+        set_error("pk_load: incomplete v3 proving key in %s", path);  // groth16.cu:1300-1305
+        return ZK_ERR_INVALID;
+    }
+    if (counts[0] != pk->m || counts[1] != pk->m || counts[2] != pk->m) {
+        set_error("pk_load: query vectors longer than num_variables are not supported");
+        return ZK_ERR_RANGE;
+    }
+    pk->l = counts[3];
+    pk->n_h = counts[4];
+    std_to_mont_host(&small1[0][0], 6);
+    std_to_mont_host(&small2[0][0], 12);
+    std_to_mont_host(&tg2[0][0], 8);
+    std::memcpy(pk->alpha1, small1[0], 64);
+    std::memcpy(pk->beta1, small1[1], 64);
+    std::memcpy(pk->delta1, small1[2], 64);
+    std::memcpy(pk->beta2, small2[0], 128);
+    std::memcpy(pk->gamma2, small2[1], 128);
+    std::memcpy(pk->delta2, small2[2], 128);
+    std::memcpy(pk->g2gen, tg2[0], 128);
+    std::memcpy(pk->tau2, tg2[1], 128);
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    pk->device = ctx->device;
+    ZK_TRY_CUDA(cudaMalloc(&pk->g1, std::max<size_t>(g1h.size(), 8) * 8));
+    ZK_TRY_CUDA(cudaMalloc(&pk->g2, std::max<size_t>(g2h.size(), 16) * 8));
+    ZK_TRY_CUDA(cudaMemcpy(pk->g1, g1h.data(), g1h.size() * 8, cudaMemcpyHostToDevice));
+    ZK_TRY_CUDA(cudaMemcpy(pk->g2, g2h.data(), g2h.size() * 8, cudaMemcpyHostToDevice));
+    // standard -> Montgomery on the device; all-zero (infinity) stays zero because 0 * R^2 = 0
+    fp_to_mont_kernel<<<ctx->num_sms * 8, 256>>>((uint64_t*)pk->g1, g1h.size() / 4);
+    fp_to_mont_kernel<<<ctx->num_sms * 8, 256>>>((uint64_t*)pk->g2, g2h.size() / 4);
+    ZK_TRY_CUDA(cudaGetLastError());
+    ZK_TRY_CUDA(cudaDeviceSynchronize());
+    return ZK_OK;
+}
+
+// vk.bin (src/verifier/verifier.cu:103-148): i32 num_public, alpha1 (x, y),
+// beta2 gamma2 delta2 (x.c0 x.c1 y.c0 y.c1), i32 num_ic, ic[] (x, y); standard
+// form, no infinity flags
+static int vk_save(const zk_groth16_pk* pk, const char* path) {
+    if (pk->ic.empty()) { set_error("vk_save: this proving key carries no verification key (loaded from a file)"); return ZK_ERR_INVALID; }
+    std::vector<uint8_t> b;
+    put_i32(b, pk->num_public);
+    put_fp_std(b, pk->alpha1);
+    put_fp_std(b, pk->alpha1 + 4);
+    for (const uint64_t* g : {pk->beta2, pk->gamma2, pk->delta2})
+        for (int k = 0; k < 4; k++) put_fp_std(b, g + 4 * k);
+    const int nic = (int)(pk->ic.size() / 8);
+    put_i32(b, nic);
+    for (int i = 0; i < nic; i++) {
+        put_fp_std(b, &pk->ic[(size_t)i * 8]);
+        put_fp_std(b, &pk->ic[(size_t)i * 8 + 4]);
+    }
+    FILE* f = fopen(path, "wb");
+    if (!f) { set_error("vk_save: cannot open %s", path); return ZK_ERR_INVALID; }
+    const bool ok = fwrite(b.data(), 1, b.size(), f) == b.size();
+    fclose(f);
+    return ok ? ZK_OK : ZK_ERR_INVALID;
+}
+
+}  // namespace zk
+
+// ================================================================== C ABI
+using namespace zk;
+
+extern "C" int zk_r1cs_create(int device, int num_constraints, int num_variables, int num_public, const void* a_entries,
+                              size_t a_nnz, const void* b_entries, size_t b_nnz, const void* c_entries, size_t c_nnz,
+                              zk_r1cs** out) {
+    clear_error();
+    if (!out || (a_nnz && !a_entries) || (b_nnz && !b_entries) || (c_nnz && !c_entries)) return ZK_ERR_INVALID;
+    zk_r1cs* r = new zk_r1cs();
+    const SparseEntry* ent[3] = {(const SparseEntry*)a_entries, (const SparseEntry*)b_entries, (const SparseEntry*)c_entries};
+    const size_t nnz[3] = {a_nnz, b_nnz, c_nnz};
+    int st = r1cs_create(device, num_constraints, num_variables, num_public, ent, nnz, r->r);
+    if (st != ZK_OK) { zk_r1cs_destroy(r); return st; }
+    *out = r;
+    return ZK_OK;
+}
+
+extern "C" void zk_r1cs_destroy(zk_r1cs* r) {
+    if (!r) return;
+    for (int k = 0; k < 3; k++) {
+        cudaFree(r->r.d_row_ptr[k]);
+        cudaFree(r->r.d_col[k]);
+        cudaFree(r->r.d_val[k]);
+        cudaFree(r->r.d_long[k]);
+    }
+    delete r;
+}
+
+extern "C" int zk_r1cs_domain(const zk_r1cs* r, int* log_n) {
+    if (!r || !log_n) return ZK_ERR_INVALID;
+    *log_n = r->r.log_n;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_setup(zk_r1cs* r1cs, const void* toxic, zk_groth16_pk** out) {
+    clear_error();
+    if (!r1cs || !toxic || !out) return ZK_ERR_INVALID;
+    zkh::Fe tx[5];
+    std::memcpy(tx, toxic, sizeof tx);
+    zk_groth16_pk* pk = new zk_groth16_pk();
+    int st = setup(r1cs->r, tx, pk);
+    if (st != ZK_OK) { zk_groth16_pk_destroy(pk); return st; }
+    *out = pk;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_pk_load(int device, const char* path, zk_groth16_pk** out) {
+    clear_error();
+    if (!path || !out) return ZK_ERR_INVALID;
+    zk_groth16_pk* pk = new zk_groth16_pk();
+    int st = pk_load(device, path, pk);
+    if (st != ZK_OK) { zk_groth16_pk_destroy(pk); return st; }
+    *out = pk;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_pk_save(const zk_groth16_pk* pk, const char* path) {
+    clear_error();
+    if (!pk || !path) return ZK_ERR_INVALID;
+    DeviceContext* ctx;
+    ZK_TRY(get_context(pk->device, &ctx));
+    return pk_save(pk, path);
+}
+
+extern "C" int zk_groth16_vk_save(const zk_groth16_pk* pk, const char* path) {
+    clear_error();
+    if (!pk || !path) return ZK_ERR_INVALID;
+    return vk_save(pk, path);
+}
+
+extern "C" int zk_groth16_vk_points(const zk_groth16_pk* pk, void* alpha1, void* beta2, void* gamma2, void* delta2, void* ic,
+                                    int ic_capacity) {
+    if (!pk) return ZK_ERR_INVALID;
+    if (alpha1) std::memcpy(alpha1, pk->alpha1, 64);
+    if (beta2) std::memcpy(beta2, pk->beta2, 128);
+    if (gamma2) std::memcpy(gamma2, pk->gamma2, 128);
+    if (delta2) std::memcpy(delta2, pk->delta2, 128);
+    const int nic = (int)(pk->ic.size() / 8);
+    if (ic) std::memcpy(ic, pk->ic.data(), (size_t)std::min(nic, std::max(ic_capacity, 0)) * 64);
+    return nic;
+}
+
+extern "C" void zk_groth16_pk_destroy(zk_groth16_pk* pk) {
+    if (!pk) return;
+    if (pk->device >= 0) cudaSetDevice(pk->device);
+    cudaFree(pk->g1);
+    cudaFree(pk->g2);
+    cudaFree(pk->w);
+    cudaFree(pk->abc);
+    cudaFree(pk->h);
+    delete pk;
+}
+
+extern "C" int zk_groth16_prove(zk_groth16_pk* pk, const zk_r1cs* r1cs, void* stream, const void* h_witness, const void* r,
+                                const void* s, void* proof256, void* points) {
+    clear_error();
+    if (!pk || !r1cs || !h_witness || !r || !s || !proof256) return ZK_ERR_INVALID;
+    zkh::Fe rr, ss;
+    std::memcpy(rr.v, r, 32);
+    std::memcpy(ss.v, s, 32);
+    uint64_t A[8], B[16], C[8];
+    ZK_TRY(prove(pk, r1cs->r, (cudaStream_t)stream, h_witness, rr, ss, A, B, C));
+    serialize_proof((uint8_t*)proof256, A, B, C);
+    if (points) {
+        uint64_t* p = (uint64_t*)points;
+        std::memcpy(p, A, 64);
+        std::memcpy(p + 8, B, 128);
+        std::memcpy(p + 24, C, 64);
+    }
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_last_stats(zk_prove_stats* out) {
+    if (!out) return ZK_ERR_INVALID;
+    *out = g_prove_stats;
+    return ZK_OK;
+}

@@ -253,4 +253,17 @@ inline void from_affine(Xyzz<F>& r, const F& x, const F& y) {
     r.x = x; r.y = y; fset_one(r.zz); fset_one(r.zzz);
 }
 
+// k * P by left-to-right double-and-add over the standard-form bits of k
+template <class F>
+inline void smul(Xyzz<F>& r, const Xyzz<F>& p, const uint64_t k_std[4]) {
+    Xyzz<F> acc, d;
+    set_identity(acc);
+    for (int bit = 255; bit >= 0; bit--) {
+        dbl(d, acc);
+        acc = d;
+        if ((k_std[bit >> 6] >> (bit & 63)) & 1) add(acc, p);
+    }
+    r = acc;
+}
+
 }  // namespace zkh

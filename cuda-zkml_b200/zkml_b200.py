@@ -308,3 +308,129 @@ def probe_imad_rate(device=0):
     r = ctypes.c_double(0)
     check(lib.zk_probe_imad_rate(device, ctypes.byref(r)))
     return r.value
+
+
+# ------------------------------------------------------------------ Groth16
+ENTRY_DTYPE = np.dtype([("row", "<i4"), ("col", "<i4"), ("v", "<u8", (4,))])  # zkml::SparseEntry
+
+
+class _Synth(ctypes.Structure):
+    _fields_ = [("num_constraints", ctypes.c_int), ("num_variables", ctypes.c_int), ("num_public", ctypes.c_int),
+                ("nnz", ctypes.c_size_t * 3), ("entries", ctypes.c_void_p * 3), ("witness", ctypes.c_void_p)]
+
+
+class ProveStats(ctypes.Structure):
+    _fields_ = [("matvec_ms", ctypes.c_float), ("compute_h_ms", ctypes.c_float), ("msm_ms", ctypes.c_float * 5),
+                ("total_ms", ctypes.c_float)]
+
+
+lib.zk_synth_conv_circuit.argtypes = [_i, _i, _i, _i, _i, _i, _i, _i, ctypes.c_uint64, ctypes.POINTER(_Synth)]
+lib.zk_synth_conv_circuit.restype = _i
+lib.zk_synth_free.argtypes = [ctypes.POINTER(_Synth)]
+lib.zk_synth_free.restype = None
+lib.zk_r1cs_create.argtypes = [_i, _i, _i, _i, _vp, _sz, _vp, _sz, _vp, _sz, ctypes.POINTER(_vp)]
+lib.zk_r1cs_create.restype = _i
+lib.zk_r1cs_destroy.argtypes = [_vp]
+lib.zk_r1cs_destroy.restype = None
+lib.zk_r1cs_domain.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
+lib.zk_groth16_setup.argtypes = [_vp, _vp, ctypes.POINTER(_vp)]
+lib.zk_groth16_pk_load.argtypes = [_i, ctypes.c_char_p, ctypes.POINTER(_vp)]
+lib.zk_groth16_pk_save.argtypes = [_vp, ctypes.c_char_p]
+lib.zk_groth16_vk_save.argtypes = [_vp, ctypes.c_char_p]
+lib.zk_groth16_vk_points.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i]
+lib.zk_groth16_pk_destroy.argtypes = [_vp]
+lib.zk_groth16_pk_destroy.restype = None
+lib.zk_groth16_prove.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
+lib.zk_groth16_last_stats.argtypes = [ctypes.POINTER(ProveStats)]
+
+
+def synth_conv_circuit(layers=2, channels=32, height=32, width=32, bits=24, shift=10, out_bits=23, dense=10, seed=5):
+    """Seeded CONV/ReLU R1CS with a satisfying witness (host numpy copies)."""
+    c = _Synth()
+    check(lib.zk_synth_conv_circuit(layers, channels, height, width, bits, shift, out_bits, dense, seed, ctypes.byref(c)))
+    try:
+        mats = []
+        for k in range(3):
+            nbytes = 40 * c.nnz[k]
+            raw = np.ctypeslib.as_array((ctypes.c_uint8 * max(nbytes, 1)).from_address(c.entries[k]))[:nbytes]
+            mats.append(raw.copy().view(ENTRY_DTYPE))
+        m = c.num_variables
+        w = np.ctypeslib.as_array((ctypes.c_uint64 * (4 * m)).from_address(c.witness)).copy().reshape(m, 4)
+        return {"A": mats[0], "B": mats[1], "C": mats[2], "witness": w, "num_constraints": c.num_constraints,
+                "num_variables": m, "num_public": c.num_public}
+    finally:
+        lib.zk_synth_free(ctypes.byref(c))
+
+
+class R1cs:
+    """Constraint system resident on one device (zk_r1cs)."""
+
+    def __init__(self, circuit, device=0):
+        self.h = _vp()
+        mats = [np.ascontiguousarray(circuit[k]) for k in "ABC"]
+        check(lib.zk_r1cs_create(device, circuit["num_constraints"], circuit["num_variables"], circuit["num_public"],
+                                 _np_ptr(mats[0]), len(mats[0]), _np_ptr(mats[1]), len(mats[1]),
+                                 _np_ptr(mats[2]), len(mats[2]), ctypes.byref(self.h)))
+        ln = ctypes.c_int()
+        check(lib.zk_r1cs_domain(self.h, ctypes.byref(ln)))
+        self.log_n = ln.value
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.zk_r1cs_destroy(self.h)
+            self.h = None
+
+
+class ProvingKey:
+    """Proving key resident on one device (zk_groth16_pk)."""
+
+    def __init__(self, handle):
+        self.h = handle
+
+    @classmethod
+    def setup(cls, r1cs, toxic):
+        """toxic: (tau, alpha, beta, gamma, delta) as Python ints."""
+        tx = np.stack([fr_from_int(t) for t in toxic])
+        h = _vp()
+        check(lib.zk_groth16_setup(r1cs.h, _np_ptr(tx), ctypes.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def load(cls, path, device=0):
+        h = _vp()
+        check(lib.zk_groth16_pk_load(device, path.encode(), ctypes.byref(h)))
+        return cls(h)
+
+    def save(self, path):
+        check(lib.zk_groth16_pk_save(self.h, path.encode()))
+
+    def save_vk(self, path):
+        check(lib.zk_groth16_vk_save(self.h, path.encode()))
+
+    def vk_points(self):
+        a1 = np.zeros(8, np.uint64)
+        b2, g2, d2 = (np.zeros(16, np.uint64) for _ in range(3))
+        nic = lib.zk_groth16_vk_points(self.h, None, None, None, None, None, 0)
+        ic = np.zeros((max(nic, 1), 8), np.uint64)
+        lib.zk_groth16_vk_points(self.h, _np_ptr(a1), _np_ptr(b2), _np_ptr(g2), _np_ptr(d2), _np_ptr(ic), nic)
+        return {"alpha1": a1, "beta2": b2, "gamma2": g2, "delta2": d2, "ic": ic[:nic]}
+
+    def prove(self, r1cs, witness, r, s, stream=None):
+        """witness (m, 4) Montgomery; r, s ints.  Returns (proof bytes, A, B, C)."""
+        witness = np.ascontiguousarray(witness, dtype=np.uint64)
+        rr, ss = fr_from_int(r), fr_from_int(s)
+        proof = np.zeros(256, np.uint8)
+        pts = np.zeros(32, np.uint64)
+        check(lib.zk_groth16_prove(self.h, r1cs.h, stream, _np_ptr(witness), _np_ptr(rr), _np_ptr(ss), _np_ptr(proof), _np_ptr(pts)))
+        return proof.tobytes(), pts[:8], pts[8:24], pts[24:32]
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.zk_groth16_pk_destroy(self.h)
+            self.h = None
+
+
+def prove_last_stats():
+    s = ProveStats()
+    check(lib.zk_groth16_last_stats(ctypes.byref(s)))
+    return {"matvec_ms": s.matvec_ms, "compute_h_ms": s.compute_h_ms, "msm_ms": list(s.msm_ms), "total_ms": s.total_ms}

@@ -157,6 +157,85 @@ typedef struct {
 } zk_msm_stats;
 int zk_msm_last_stats(zk_msm_stats* out);
 
+/* ==================================================================
+ * Groth16 prover (device-resident proving key and constraint system)
+ * ================================================================== */
+typedef struct zk_r1cs zk_r1cs;              /* constraint system in device CSR form */
+typedef struct zk_groth16_pk zk_groth16_pk;  /* proving key resident on one device */
+
+/* Upload an R1CS given as the reference's zkml::R1CS triplet vectors
+ * (SparseEntry {int32 row; int32 col; Fr value}, 40 B; src/prover/circuit.cuh:
+ * 31-49).  The evaluation domain is QAP::from_r1cs's: the next power of two
+ * >= num_constraints, at least 4 (src/prover/groth16.cu:225-242); entries
+ * outside the domain or the witness are ignored, as compute_h does
+ * (groth16.cu:278-292). */
+int zk_r1cs_create(int device, int num_constraints, int num_variables, int num_public,
+                   const void* a_entries, size_t a_nnz, const void* b_entries, size_t b_nnz,
+                   const void* c_entries, size_t c_nnz, zk_r1cs** out);
+void zk_r1cs_destroy(zk_r1cs* r1cs);
+int zk_r1cs_domain(const zk_r1cs* r1cs, int* log_n);
+
+/* Trusted setup on the device for the given toxic waste (5 Montgomery Fr:
+ * tau, alpha, beta, gamma, delta; the reference draws them in this order,
+ * groth16.cu:468-472): QAP evaluations at tau on the host, every query point
+ * k * G by the fixed-base kernel.  Replaces Groth16Prover::setup's point loop
+ * (groth16.cu:446-642); the key is byte-identical for the same toxic waste. */
+int zk_groth16_setup(zk_r1cs* r1cs, const void* toxic, zk_groth16_pk** out);
+/* ZKMLPK3 proving-key files (ProvingKey::save / load_streaming,
+ * groth16.cu:1104-1314), loaded straight into device memory. */
+int zk_groth16_pk_load(int device, const char* path, zk_groth16_pk** out);
+int zk_groth16_pk_save(const zk_groth16_pk* pk, const char* path);
+/* vk.bin (save_vk, src/verifier/verifier.cu:103-148); keys from setup only. */
+int zk_groth16_vk_save(const zk_groth16_pk* pk, const char* path);
+/* Copy the verification-key points (packed affine, Montgomery); returns the
+ * number of IC points and copies at most ic_capacity of them. */
+int zk_groth16_vk_points(const zk_groth16_pk* pk, void* alpha1, void* beta2, void* gamma2,
+                         void* delta2, void* ic, int ic_capacity);
+void zk_groth16_pk_destroy(zk_groth16_pk* pk);
+
+/* Groth16Prover::prove (groth16.cu:655-920) with the key and circuit resident:
+ * h_witness = Fr[num_variables] on the host, r and s the blinding scalars
+ * (Montgomery Fr; the reference draws them with mt19937_64, seed 0xCAFEBABE
+ * under ZKML_DETERMINISTIC_PROVE=1, groth16.cu:709-715).  Writes the 256-byte
+ * proof (Groth16Proof::serialize, groth16.cu:1058-1074) and, if `points` is
+ * not NULL, A (64 B) | B (128 B) | C (64 B) packed affine. */
+int zk_groth16_prove(zk_groth16_pk* pk, const zk_r1cs* r1cs, void* stream, const void* h_witness,
+                     const void* r, const void* s, void* proof256, void* points);
+
+typedef struct {
+    float matvec_ms;     /* witness copy + sparse A*w, B*w, C*w */
+    float compute_h_ms;  /* 7 NTTs with the fused coset steps */
+    float msm_ms[5];     /* A, B (G2), L, H, B1 */
+    float total_ms;      /* whole prove, device time incl. host assembly */
+} zk_prove_stats;
+int zk_groth16_last_stats(zk_prove_stats* out);
+
+/* ==================================================================
+ * Synthetic workloads (seeded, for benchmarks and tests)
+ * ================================================================== */
+
+/* An R1CS with a satisfying witness, in the reference's layout: constraint
+ * matrices as zkml::SparseEntry records {int32 row; int32 col; Fr value}
+ * (40 B, src/prover/circuit.cuh:31-35), witness as Fr[num_variables] ordered
+ * [1, public..., private...]. */
+typedef struct {
+    int num_constraints;
+    int num_variables;
+    int num_public;
+    size_t nnz[3];     /* A, B, C */
+    void* entries[3];  /* malloc'd SparseEntry arrays */
+    void* witness;     /* malloc'd Fr array */
+} zk_synth_circuit;
+
+/* `layers` CONV2D 3x3 (pad 1) layers of channels x height x width with int8
+ * weights, each output through an exact ReLU (bit decomposition of
+ * acc + 2^(b-1), b >= `bits` wide enough for the layer), a right shift by
+ * `shift` and an `out_bits` range check, then `dense_outputs` dense outputs.
+ * Public inputs: the input feature map (values 0..16) and the dense outputs. */
+int zk_synth_conv_circuit(int layers, int channels, int height, int width, int bits, int shift,
+                          int out_bits, int dense_outputs, uint64_t seed, zk_synth_circuit* out);
+void zk_synth_free(zk_synth_circuit* c);
+
 #ifdef __cplusplus
 }
 #endif

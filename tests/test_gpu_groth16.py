@@ -1,0 +1,124 @@
+"""Device setup + prove against the oracle's restatement of the reference's
+Groth16 (oracle/groth16_oracle.py): every proving-key point and the 256-byte
+proof bit-exact under the reference's deterministic seeds, the proof valid by
+the trapdoor check, and the ZKMLPK3 / vk.bin writers read back by an
+independent parser that is pinned to the reference's own files."""
+import os
+
+import numpy as np
+import pytest
+
+import groth16_oracle as G
+import pyoracle as O
+import zkml_b200 as Z
+import zkmlpk3
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def small():
+    c = Z.synth_conv_circuit(2, 2, 4, 4, 24, 10, 23, 3, 7)
+    mats = [c["A"], c["B"], c["C"]]
+    tox = G.toxic_deterministic()
+    pk_o = G.setup(mats, c["num_constraints"], c["num_variables"], c["num_public"], tox)
+    r1 = Z.R1cs(c)
+    pk = Z.ProvingKey.setup(r1, tox)
+    return c, mats, tox, pk_o, r1, pk
+
+
+def test_setup_matches_oracle(small, tmp_path):
+    c, mats, tox, pk_o, r1, pk = small
+    path = str(tmp_path / "pk.bin")
+    pk.save(path)
+    buf = open(path, "rb").read()
+    key = zkmlpk3.parse_pk(buf)
+    assert key["n"] == pk_o["n"] and key["m"] == c["num_variables"] and key["num_public"] == c["num_public"]
+    assert len(buf) == zkmlpk3.pk_size(pk_o["n"], c["num_variables"], pk_o["l"])
+    for name, g2 in (("A", False), ("B1", False), ("B2", True), ("L", False), ("H", False)):
+        exp = pk_o[name]
+        assert len(key[name]) == len(exp), name
+        conv = zkmlpk3.std_g2 if g2 else zkmlpk3.std_g1
+        for i in range(len(exp)):
+            assert key[name][i] == conv(exp[i]), (name, i)
+    for name in ("alpha1", "beta1", "delta1"):
+        assert key[name] == zkmlpk3.std_g1(pk_o[name]), name
+    for name in ("beta2", "gamma2", "delta2"):
+        assert key[name] == zkmlpk3.std_g2(pk_o[name]), name
+    assert key["tau_g2"][1] == zkmlpk3.std_g2(pk_o["tau2"])
+    vk_path = str(tmp_path / "vk.bin")
+    pk.save_vk(vk_path)
+    vk = zkmlpk3.parse_vk(open(vk_path, "rb").read())
+    assert vk["num_public"] == c["num_public"]
+    assert [tuple(v) for v in vk["ic"]] == [zkmlpk3.std_g1(p) for p in pk_o["IC"]]
+    assert vk["alpha1"] == zkmlpk3.std_g1(pk_o["alpha1"])
+
+
+def test_prove_matches_oracle_and_verifies(small):
+    c, mats, tox, pk_o, r1, pk = small
+    r, s = G.blinding_deterministic()
+    proof, A, B, C = pk.prove(r1, c["witness"], r, s)
+    proof_o, Ao, Bo, Co, h = G.prove(pk_o, mats, c["witness"], r, s)
+    assert proof == proof_o
+    assert np.array_equal(A, Ao) and np.array_equal(B, Bo) and np.array_equal(C, Co)
+    assert G.trapdoor_verify(pk_o, c["witness"], r, s, h, A, B, C)
+    st = Z.prove_last_stats()
+    assert st["total_ms"] > 0 and st["compute_h_ms"] > 0
+    # proving twice with the resident key gives the same bytes
+    assert pk.prove(r1, c["witness"], r, s)[0] == proof
+
+
+def test_pk_file_round_trip(small, tmp_path):
+    c, mats, tox, pk_o, r1, pk = small
+    path = str(tmp_path / "pk.bin")
+    pk.save(path)
+    pk2 = Z.ProvingKey.load(path)
+    r, s = G.blinding_deterministic()
+    assert pk2.prove(r1, c["witness"], r, s)[0] == pk.prove(r1, c["witness"], r, s)[0]
+    # fail closed on a corrupt key
+    bad = str(tmp_path / "bad.bin")
+    open(bad, "wb").write(b"ZKMLPK2\0" + open(path, "rb").read()[8:])
+    with pytest.raises(Z.ZkError):
+        Z.ProvingKey.load(bad)
+    open(bad, "wb").write(open(path, "rb").read()[:1000])
+    with pytest.raises(Z.ZkError):
+        Z.ProvingKey.load(bad)
+
+
+def test_wrong_witness_does_not_verify(small):
+    c, mats, tox, pk_o, r1, pk = small
+    bad = c["witness"].copy()
+    bad[c["num_public"] + 5] = Z.fr_from_int(7)
+    r, s = 11, 13
+    proof, A, B, C = pk.prove(r1, bad, r, s)
+    proof_o, Ao, Bo, Co, h = G.prove(pk_o, mats, bad, r, s)
+    assert proof == proof_o
+    assert not G.trapdoor_verify(pk_o, bad, r, s, h, A, B, C)
+
+
+def test_mismatched_key_is_refused(small):
+    c, mats, tox, pk_o, r1, pk = small
+    c2 = Z.synth_conv_circuit(1, 2, 4, 4, 24, 10, 0, 2, 9)
+    r2 = Z.R1cs(c2)
+    with pytest.raises(Z.ZkError):
+        pk.prove(r2, c2["witness"], 3, 5)
+
+
+def test_prove_2_16_config4_shape():
+    """A ~60k-constraint circuit (domain 2^16, the size of SURVEY config 4):
+    the proof passes the trapdoor check (the oracle prove would be slow here,
+    so validity rather than byte equality is checked)."""
+    c = Z.synth_conv_circuit(2, 4, 12, 12, 24, 10, 23, 10, 4)
+    assert 1 << 15 < c["num_constraints"] <= 1 << 16
+    r1 = Z.R1cs(c)
+    assert r1.log_n == 16
+    tox = G.toxic_deterministic()
+    pk = Z.ProvingKey.setup(r1, tox)
+    r, s = G.blinding_deterministic()
+    proof, A, B, C = pk.prove(r1, c["witness"], r, s)
+    mats = [c["A"], c["B"], c["C"]]
+    n, log_n = G.domain(c["num_constraints"])
+    at, vanish = G.qap_at_tau(mats, n, log_n, c["num_variables"], tox[0])
+    pk_o = {"m": c["num_variables"], "num_public": c["num_public"], "_at": at, "_vanish": vanish, "_toxic": tox}
+    h = G.compute_h(mats, G._ints(c["witness"]), n, log_n, c["num_variables"])
+    assert G.trapdoor_verify(pk_o, c["witness"], r, s, h, A, B, C)
