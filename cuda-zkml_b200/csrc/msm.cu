@@ -55,26 +55,41 @@ struct MsmPlan {
 
 static constexpr int kScanTile = 4096;  // 1024 threads x 4
 
-// Window width c minimising the Fp multiplications of the whole MSM:
-// n W(c) mixed additions (10 mul each) + W(c) 2^(c-1) running-sum steps
-// (2 full additions, 14 mul each, plus the chunk correction), W(c) = ceil(255/c).
-// ZK_MSM_WINDOW_BITS / ZK_MSM_G2_WINDOW_BITS override it.
-static int default_window_bits(size_t n, bool g2) {
+// Window width c minimising the Fp multiplications of the whole MSM: one mixed
+// addition (10 mul) per nonzero signed digit, plus 2^(c-1) running-sum steps
+// (2 full additions, 14 mul each, plus the chunk correction) for every window
+// that holds digits.  `hist[b]` counts scalars of bit length b; a b-bit scalar
+// has at most ceil((b + 1) / c) nonzero digits.  Without a histogram every
+// scalar counts as 254 bits.  ZK_MSM_WINDOW_BITS / ZK_MSM_G2_WINDOW_BITS
+// override the choice.
+static int choose_window_bits(size_t n, bool g2, const uint32_t* hist) {
     const char* env = getenv(g2 ? "ZK_MSM_G2_WINDOW_BITS" : "ZK_MSM_WINDOW_BITS");
     if (env && atoi(env) >= 2 && atoi(env) <= 22) return atoi(env);
+    int maxbits = 254;
+    if (hist) {
+        maxbits = 0;
+        for (int b = 0; b < 256; b++)
+            if (hist[b]) maxbits = b;
+    }
     int best = 3;
     double best_cost = 1e300;
     for (int c = 3; c <= (g2 ? 18 : 21); c++) {
-        const double W = (255 + c - 1) / c;
-        const double cost = (double)n * W * 10.0 + W * (double)(1u << (c - 1)) * 30.0;
+        double digits = 0;
+        if (hist) {
+            for (int b = 1; b < 256; b++) digits += (double)hist[b] * (double)((b + 1 + c - 1) / c);
+        } else {
+            digits = (double)n * ((255 + c - 1) / c);
+        }
+        const double windows = (maxbits + 1 + c - 1) / c;
+        const double cost = digits * 10.0 + windows * (double)(1u << (c - 1)) * 30.0;
         if (cost < best_cost) { best_cost = cost; best = c; }
     }
     return best;
 }
 
-static MsmPlan make_plan(size_t n, bool g2) {
+static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist) {
     MsmPlan p;
-    p.c = default_window_bits(n, g2);
+    p.c = choose_window_bits(n, g2, hist);
     p.W = (255 + p.c - 1) / p.c;
     p.B = 1u << (p.c - 1);
     p.nb = (uint32_t)p.W * p.B;
@@ -102,6 +117,26 @@ __device__ __forceinline__ int next_digit(uint32_t v[8], int c, uint32_t& carry)
     }
     carry = 0;
     return (int)raw;
+}
+
+// Bit lengths of the standard-form scalars (0..254), for the window choice.
+__global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restrict__ scalars, size_t n, uint32_t* __restrict__ hist) {
+    __shared__ uint32_t h[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        Fr s;
+        fload_nc(s, scalars + i);
+        ffrom_mont(s, s);
+        int len = 0;
+#pragma unroll
+        for (int k = 7; k >= 0; k--)
+            if (len == 0 && s.v[k]) len = 32 * k + 32 - __clz(s.v[k]);
+        atomicAdd(&h[len], 1u);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+        if (h[i]) atomicAdd(&hist[i], h[i]);
 }
 
 __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
@@ -669,7 +704,27 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
     cudaStream_t st = user_stream;  // NULL: the legacy default stream
-    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value);
+    // Window choice from the scalars' bit lengths (a small device pre-pass; the
+    // host path copies the scalars first for it).
+    uint32_t* hist_dev = nullptr;
+    ZK_TRY(ensure_pinned(ctx, 4096));
+    uint32_t* hist_host = (uint32_t*)ctx->pinned;
+    const void* sc_for_hist = src_scalars;
+    void* sc_copy = nullptr;
+    ZK_TRY(scratch_begin(ctx, st));
+    ZK_TRY_CUDA(cudaMallocAsync((void**)&hist_dev, 256 * sizeof(uint32_t), st));
+    if (host_inputs) {
+        ZK_TRY_CUDA(cudaMallocAsync(&sc_copy, n * 32, st));
+        ZK_TRY_CUDA(cudaMemcpyAsync(sc_copy, src_scalars, n * 32, cudaMemcpyHostToDevice, st));
+        sc_for_hist = sc_copy;
+    }
+    ZK_TRY_CUDA(cudaMemsetAsync(hist_dev, 0, 256 * sizeof(uint32_t), st));
+    msm_bitlen_hist_kernel<<<grid_for(n, 256, ctx->num_sms * 4), 256, 0, st>>>((const Fr*)sc_for_hist, n, hist_dev);
+    ZK_TRY_CUDA(cudaMemcpyAsync(hist_host, hist_dev, 256 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    uint32_t hist[256];
+    std::memcpy(hist, hist_host, sizeof hist);
+    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist);
     stats.window_bits = P.c;
     stats.num_windows = P.W;
 
@@ -679,7 +734,6 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     const bool own_points = host_inputs || ref_layout;
     if (own_points) need += Arena::round(pt_bytes);
     if (ref_layout) need += Arena::round(ref_bytes);
-    if (host_inputs) need += Arena::round(n * 32);
     ZK_TRY(ensure_scratch(ctx, need));
     ZK_TRY(ensure_pinned(ctx, (size_t)P.W * Cv::kXyzzBytes + 64));
     Arena ar;
@@ -689,21 +743,18 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     const void* d_scalars = src_scalars;
     uint8_t* packed = own_points ? ar.take<uint8_t>(pt_bytes) : nullptr;
     uint8_t* raw = ref_layout ? ar.take<uint8_t>(ref_bytes) : nullptr;
-    uint8_t* sc = host_inputs ? ar.take<uint8_t>(n * 32) : nullptr;
     LaunchCounter lc;
 
     cudaEvent_t t0, t1;
     ZK_TRY_CUDA(cudaEventCreate(&t0));
     ZK_TRY_CUDA(cudaEventCreate(&t1));
-    ZK_TRY(scratch_begin(ctx, st));
     ZK_TRY_CUDA(cudaEventRecord(t0, st));
 
     cudaEvent_t points_ready = nullptr;
     if (host_inputs) {
         // scalars first on the work stream (the sort needs them); points on the
         // copy stream, overlapped with the decomposition and sort.
-        ZK_TRY_CUDA(cudaMemcpyAsync(sc, src_scalars, n * 32, cudaMemcpyHostToDevice, st));
-        d_scalars = sc;
+        d_scalars = sc_copy;  // copied for the histogram above
         ZK_TRY_CUDA(cudaEventRecord(ctx->ev_a, st));
         ZK_TRY_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->ev_a, 0));
         if (ref_layout) {
@@ -730,6 +781,8 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
     ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, total_keys_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
+    ZK_TRY_CUDA(cudaFreeAsync(hist_dev, st));
+    if (sc_copy) ZK_TRY_CUDA(cudaFreeAsync(sc_copy, st));
     ZK_TRY_CUDA(cudaEventRecord(t1, st));
     ZK_TRY(scratch_end(ctx, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));

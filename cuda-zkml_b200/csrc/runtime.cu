@@ -48,6 +48,12 @@ int get_context(int device, DeviceContext** out) {
             return ZK_ERR_NODEV;
         }
         c->num_sms = prop.multiProcessorCount;
+        // keep stream-ordered allocations cached in the device's default pool
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+            uint64_t keep = UINT64_MAX;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        }
         ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
         ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
         ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_a, cudaEventDisableTiming));
