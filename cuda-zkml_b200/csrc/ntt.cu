@@ -22,6 +22,11 @@
 // A CTA owns C adjacent columns (C = 8: 256-byte contiguous runs per row) or,
 // in the last pass (M = 1), C adjacent contiguous sub-transforms, so every
 // global access is a full 32-byte sector of a coalesced run.
+// The NTT butterfly loop is small enough for the instruction cache with the
+// Montgomery multiplication inlined; ZK_NTT_FMUL_INLINE selects that.
+#if defined(ZK_NTT_FMUL_INLINE) && ZK_NTT_FMUL_INLINE
+#define ZK_FMUL_OUTLINE 0
+#endif
 #include "field.cuh"
 #include "host_field.hpp"
 #include "runtime.cuh"

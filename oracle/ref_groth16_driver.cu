@@ -11,7 +11,11 @@
 // that the library's own prover produces the reference's proof and proving-key
 // bytes and that the reference's verifier accepts its proofs.
 #include "prover/groth16.cuh"
+#include "verifier/verifier.cuh"
 
+#include <unistd.h>
+
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -61,7 +65,11 @@ int ref_g16_setup_prove(int nc, int m, int pub, const void* a, size_t na, const 
 }
 
 // The reference's verifier on externally produced proof bytes, with the
-// verification key of the deterministic setup of the same circuit.
+// verification key of the deterministic setup of the same circuit.  The proof
+// goes through the CLI's reader, load_proof (src/verifier/verifier.cu:47-101):
+// Groth16Proof::deserialize (src/prover/groth16.cu:1076-1094) builds each point
+// as G1Affine(read_fp(ptr), read_fp(ptr)), whose argument order is unspecified
+// in C++ (GCC reads y first), so it does not round-trip serialize().
 int ref_g16_verify(int nc, int m, int pub, const void* a, size_t na, const void* b, size_t nb, const void* c, size_t ncc,
                    const void* public_inputs, const uint8_t* proof_bytes, int* verified) {
     setenv("ZKML_DETERMINISTIC_SETUP", "1", 1);
@@ -69,7 +77,14 @@ int ref_g16_verify(int nc, int m, int pub, const void* a, size_t na, const void*
     ProvingKey pk;
     VerificationKey vk;
     Groth16Prover::setup(r, pk, vk);
-    Groth16Proof proof = Groth16Proof::deserialize(proof_bytes, 256);
+    char path[] = "/tmp/zkref_proof_XXXXXX";
+    int fd = mkstemp(path);
+    if (fd < 0) return 4;
+    bool wrote = write(fd, proof_bytes, 256) == 256;
+    close(fd);
+    if (!wrote) { unlink(path); return 4; }
+    Groth16Proof proof = load_proof(path);
+    unlink(path);
     std::vector<bn254::Fr> pubs((size_t)pub);
     std::memcpy(pubs.data(), public_inputs, (size_t)pub * sizeof(bn254::Fr));
     *verified = Groth16Verifier::verify(vk, proof, pubs) ? 1 : 0;
