@@ -139,49 +139,42 @@ __global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restri
         if (h[i]) atomicAdd(&hist[i], h[i]);
 }
 
+// Digits are stored window-major (digits[w * n + i] = sign << 31 | bucket + 1,
+// 0 for a zero digit) so that the scatter can run one window after another.
 __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
-                                 uint32_t* __restrict__ counts) {
+                                 uint32_t* __restrict__ counts, uint32_t* __restrict__ digits) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         Fr s;
         fload_nc(s, scalars + i);
         ffrom_mont(s, s);
         uint32_t carry = 0;
         for (int w = 0; w < W; w++) {
-            int d = next_digit(s.v, c, carry);
-            if (d) atomicAdd(&counts[(uint32_t)w * B + (uint32_t)(d < 0 ? -d : d) - 1], 1u);
+            const int d = next_digit(s.v, c, carry);
+            uint32_t code = 0;
+            if (d) {
+                const uint32_t b = (uint32_t)(d < 0 ? -d : d) - 1;
+                atomicAdd(&counts[(uint32_t)w * B + b], 1u);
+                code = (d < 0 ? 0x80000000u : 0u) | (b + 1);
+            }
+            digits[(size_t)w * n + i] = code;
         }
     }
 }
 
-// One point per thread; the bucket cursors are claimed for up to 16 windows
-// before any key is stored, so the returning atomics of a thread overlap
-// instead of each waiting for the previous one.
-__global__ void __launch_bounds__(256) msm_scatter_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
-                                                          uint32_t* __restrict__ cursors, uint32_t* __restrict__ keys) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Counting-sort scatter, window-major: block b covers window b / blocks_per_window,
+// so the blocks resident at any time touch one window's cursors (2^(c-1) words)
+// and key range (about n words), which stay in L2; scattering all windows at once
+// wrote partial sectors all over the whole key array.
+__global__ void __launch_bounds__(256) msm_scatter_kernel(const uint32_t* __restrict__ digits, size_t n, uint32_t B,
+                                                          uint32_t blocks_per_window, uint32_t* __restrict__ cursors,
+                                                          uint32_t* __restrict__ keys) {
+    const uint32_t w = blockIdx.x / blocks_per_window;
+    const size_t i = (size_t)(blockIdx.x % blocks_per_window) * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    Fr s;
-    fload_nc(s, scalars + i);
-    ffrom_mont(s, s);
-    uint32_t carry = 0;
-    for (int w0 = 0; w0 < W; w0 += 16) {
-        uint32_t pos[16], key[16];
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            pos[k] = 0xffffffffu;
-            if (w0 + k < W) {
-                const int d = next_digit(s.v, c, carry);
-                if (d) {
-                    const uint32_t b = (uint32_t)(w0 + k) * B + (uint32_t)(d < 0 ? -d : d) - 1;
-                    pos[k] = atomicAdd(&cursors[b], 1u);
-                    key[k] = (d < 0 ? 0x80000000u : 0u) | (uint32_t)i;
-                }
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < 16; k++)
-            if (pos[k] != 0xffffffffu) keys[pos[k]] = key[k];
-    }
+    const uint32_t code = digits[(size_t)w * n + i];
+    if (!code) return;
+    const uint32_t pos = atomicAdd(&cursors[w * B + (code & 0x7fffffffu) - 1], 1u);
+    keys[pos] = (code & 0x80000000u) | (uint32_t)i;
 }
 
 // ------------------------------------------------------------------ scan
@@ -609,6 +602,7 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     uint32_t* cursors = ar.take<uint32_t>(P.nb);
     uint32_t* tile_sums = ar.take<uint32_t>(P.tiles);
     uint32_t* keys = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
+    uint32_t* digits = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
     uint8_t* part_first = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
     uint8_t* part_last = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
     uint32_t* first_bucket = ar.take<uint32_t>(P.max_segs);
@@ -621,7 +615,7 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     const int sms = ctx->num_sms;
     ZK_TRY_CUDA(cudaEventRecord(ph[0], st));
     ZK_TRY_CUDA(cudaMemsetAsync(counts, 0, (P.nb + 1) * sizeof(uint32_t), st));
-    msm_count_kernel<<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts);
+    msm_count_kernel<<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts, digits);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[1], st));
     scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums);
@@ -631,7 +625,10 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     scan_finish_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums, offsets, cursors);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[2], st));
-    msm_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, cursors, keys);
+    {
+        const uint32_t bpw = (uint32_t)((n + 255) / 256);
+        msm_scatter_kernel<<<bpw * (uint32_t)P.W, 256, 0, st>>>(digits, n, P.B, bpw, cursors, keys);
+    }
     lc++;
     ZK_TRY_CUDA(cudaMemsetAsync(first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     ZK_TRY_CUDA(cudaMemsetAsync(last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
@@ -675,7 +672,7 @@ static size_t pipeline_bytes(const MsmPlan& P) {
     constexpr int kWinThreads = win_threads<Cv>();
     size_t b = 0;
     b += Arena::round((P.nb + 1) * 4) * 2 + Arena::round(P.nb * 4) + Arena::round(P.tiles * 4);
-    b += Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
+    b += 2 * Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
     b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes) + 2 * Arena::round(P.max_segs * 4);
     b += Arena::round((size_t)P.nb * Cv::kXyzzBytes);
     b += Arena::round((size_t)P.W * P.tw * Cv::kXyzzBytes);

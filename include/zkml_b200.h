@@ -137,9 +137,9 @@ int zk_g1_add_affine(const void* a, const void* b, void* out);
 int zk_g2_add_affine(const void* a, const void* b, void* out);
 
 /* Measured throughput of the INT32 multiply-add pipe on `device` in IMAD per
- * second, issued in the carry-chain form of the Montgomery rows (mad.lo.cc /
- * madc.hi.cc chains over 8 limbs, independent accumulators, full occupancy):
- * the denominator of the MSM and NTT rooflines. */
+ * second: the library's own Montgomery multiplication timed on independent
+ * chains at full occupancy, 256 IMAD per multiplication.  The denominator of
+ * the MSM and NTT rooflines. */
 int zk_probe_imad_rate(int device, double* imad_per_second);
 
 /* Statistics of the most recent MSM on the calling thread: launches of this
