@@ -32,8 +32,10 @@
 #include "host_field.hpp"
 #include "runtime.cuh"
 
+#include <atomic>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <memory>
 #include <vector>
 
@@ -479,6 +481,209 @@ int compute_h_run(int device, cudaStream_t user_stream, void* d_h, const void* d
     return scratch_end(ctx, st);
 }
 
+// ------------------------------------------------------------------ allocation-free variant
+// zk_ntt_device_noalloc: the same transform with no device allocation at any
+// call.  Its working buffer and its tables live in g_ntt_noalloc_scratch, one
+// fixed array per device compiled into this library; the tables are
+// regenerated on the device at every call, so nothing is cached between
+// calls, and every word of the array is written by a call before that call
+// reads it (nothing must start at zero).  All calls on one device share the
+// array: calls whose work overlaps in time race.
+static constexpr int kNoallocMaxLog = ZK_NTT_NOALLOC_MAX_LOG;
+static constexpr size_t kNoallocBufElems = (size_t)1 << kNoallocMaxLog;
+static constexpr size_t kNoallocTableElems = 4096;  // >= 255 roots + 4 * 2^((L+1)/2) for L <= 18
+static_assert(255 + 4 * ((size_t)1 << ((kNoallocMaxLog + 1) / 2)) <= kNoallocTableElems, "noalloc table region too small");
+
+static __device__ __align__(256) Fr g_ntt_noalloc_scratch[kNoallocBufElems + kNoallocTableElems];
+
+struct PowSeg {  // out[offset + k] = start * base^k, k < count
+    Fr start, base;
+    uint32_t offset, count;
+};
+struct PowPlan {
+    PowSeg seg[12];
+    int nseg;
+    uint32_t total;  // segments are contiguous: seg[s + 1].offset == seg[s].offset + seg[s].count
+};
+
+__global__ void ntt_powers_kernel(Fr* __restrict__ out, PowPlan plan) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < plan.total; i += gridDim.x * blockDim.x) {
+        int s = 0;
+        while (s + 1 < plan.nseg && i >= plan.seg[s + 1].offset) s++;
+        uint32_t k = i - plan.seg[s].offset;
+        Fr acc = plan.seg[s].start, b = plan.seg[s].base;
+        while (k) {  // square-and-multiply: the canonical Montgomery value equals the host's running product
+            if (k & 1) fmul(acc, acc, b);
+            k >>= 1;
+            if (k) fmul(b, b, b);
+        }
+        fstore(out + i, acc);
+    }
+}
+
+struct NoallocDevice {
+    std::atomic<bool> ready{false};
+    Fr* base = nullptr;  // device address of g_ntt_noalloc_scratch
+    int num_sms = 0;
+};
+static NoallocDevice g_noalloc[64];
+static std::mutex g_noalloc_mu;
+
+// One-time set-up per device, with that device current: the array's device
+// address, the SM count, and the kernels' attributes (which loads their code).
+static int noalloc_setup(int device, NoallocDevice** out) {
+    NoallocDevice& d = g_noalloc[device];
+    if (d.ready.load(std::memory_order_acquire)) {
+        *out = &d;
+        return ZK_OK;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!d.ready.load(std::memory_order_relaxed)) {
+        int major = 0;
+        ZK_TRY_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+        if (major < 10) {
+            set_error("device %d has compute capability %d.x; this library is built for sm_100a only", device, major);
+            return ZK_ERR_NODEV;
+        }
+        ZK_TRY_CUDA(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device));
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_ntt_noalloc_scratch);
+        if (e != cudaSuccess || !ptr) {
+            set_error("ntt_noalloc: cudaGetSymbolAddress failed on device %d (%s)", device, cudaGetErrorString(e));
+            return ZK_ERR_CUDA;
+        }
+        d.base = (Fr*)ptr;
+        for (int r = 1; r <= kMaxLogR; r++)
+            ZK_TRY_CUDA(cudaFuncSetAttribute((const void*)pass_fn(r), cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+        cudaFuncAttributes fa;
+        ZK_TRY_CUDA(cudaFuncGetAttributes(&fa, (const void*)ntt_permute_kernel));
+        ZK_TRY_CUDA(cudaFuncGetAttributes(&fa, (const void*)ntt_powers_kernel));
+        d.ready.store(true, std::memory_order_release);
+    }
+    *out = &d;
+    return ZK_OK;
+}
+
+static void add_seg(PowPlan& plan, const zkh::Fe& start, const zkh::Fe& base, uint32_t count) {
+    PowSeg& s = plan.seg[plan.nseg++];
+    std::memcpy(s.start.v, start.v, 32);
+    std::memcpy(s.base.v, base.v, 32);
+    s.offset = plan.total;
+    s.count = count;
+    plan.total += count;
+}
+
+static int ntt_noalloc_run(int device, cudaStream_t st, void* d_out, const void* d_in, int L, bool inverse, const void* coset_g) {
+    if (!d_out || !d_in) { set_error("ntt_noalloc: null pointer"); return ZK_ERR_INVALID; }
+    if (L < 0 || L > kNoallocMaxLog) {
+        set_error("ntt_noalloc: log_n = %d outside [0, %d] (its fixed buffer holds 2^%d elements)", L, kNoallocMaxLog, kNoallocMaxLog);
+        return ZK_ERR_RANGE;
+    }
+    int count = 0;
+    cudaError_t ce = cudaGetDeviceCount(&count);
+    if (ce != cudaSuccess || count == 0) {
+        set_error("no usable CUDA device (%s)", ce == cudaSuccess ? "device count is 0" : cudaGetErrorString(ce));
+        return ZK_ERR_NODEV;
+    }
+    if (device < 0) ZK_TRY_CUDA(cudaGetDevice(&device));
+    if (device >= count || device >= 64) {
+        set_error("device %d out of range (%d visible)", device, count);
+        return ZK_ERR_INVALID;
+    }
+    ZK_TRY_CUDA(cudaSetDevice(device));
+    NoallocDevice* nd;
+    ZK_TRY(noalloc_setup(device, &nd));
+
+    // table region layout: roots (255) | tw_lo | tw_hi | coset lo | coset hi
+    Fr* buf = nd->base;
+    Fr* tab = nd->base + kNoallocBufElems;
+    const zkh::Fe one = zkh::one(zkh::kR);
+    const int h = (L + 1) / 2;
+    PowPlan plan;
+    plan.nseg = 0;
+    plan.total = 0;
+    NttDirTables T;
+    if (L > 0) {
+        for (int r = 1; r <= kMaxLogR; r++) add_seg(plan, one, host_root(r, inverse), 1u << (r - 1));
+        T.roots = tab;
+        T.h = h;
+        zkh::Fe w = host_root(L, inverse), wh = w;
+        T.tw_lo = tab + plan.total;
+        add_seg(plan, one, w, 1u << h);
+        for (int i = 0; i < h; i++) zkh::mul(zkh::kR, wh, wh, wh);
+        T.tw_hi = tab + plan.total;
+        add_seg(plan, one, wh, 1u << (L - h));
+    }
+    CosetTables cs;
+    const CosetTables* pre = nullptr;
+    FinalOp fin;
+    if (coset_g) {  // the factors of get_coset_tables, kind 0 (forward) or kind 1 (inverse)
+        zkh::Fe g, step, start = one;
+        std::memcpy(g.v, coset_g, 32);
+        step = g;
+        if (inverse) {
+            zkh::inv(zkh::kR, step, g);
+            Fr ninv = n_inverse_dev(L);
+            std::memcpy(start.v, ninv.v, 32);
+        }
+        cs.h = h;
+        cs.lo = tab + plan.total;
+        add_seg(plan, start, step, 1u << h);
+        zkh::Fe sh = step;
+        for (int i = 0; i < h; i++) zkh::mul(zkh::kR, sh, sh, sh);
+        cs.hi = tab + plan.total;
+        add_seg(plan, one, sh, 1u << (L - h));
+        if (inverse) {
+            fin.mode = 2;
+            fin.tab = &cs;
+        } else {
+            pre = &cs;
+        }
+    } else if (inverse) {
+        fin.mode = 1;
+        fin.scale = n_inverse_dev(L);
+    }
+    int launches = 0;
+    if (plan.total) {
+        ntt_powers_kernel<<<(plan.total + 255) / 256, 256, 0, st>>>(tab, plan);
+        launches++;
+    }
+    const uint64_t n = 1ull << L;
+    Fr* dst = (Fr*)d_out;
+    const Fr* src = (const Fr*)d_in;
+    if (L == 0) {
+        PermPlan none;
+        none.P = 0;
+        ntt_permute_kernel<<<1, 32, 0, st>>>(src, dst, 0, none, fin.mode, fin.scale, fin.tab ? fin.tab->lo : nullptr,
+                                             fin.tab ? fin.tab->hi : nullptr, fin.tab ? fin.tab->h : 0, nullptr, nullptr);
+        launches++;
+    } else {
+        PermPlan pp = make_pass_plan(L);
+        int Lp = L;
+        const Fr* in = src;
+        for (int p = 0; p < pp.P; p++) {
+            const int r = pp.r[p];
+            const uint64_t M = 1ull << (Lp - r);
+            const uint64_t lines = n >> r;
+            const int C = M >= 8 ? 8 : (int)std::min<uint64_t>(lines, (uint64_t)std::max(1, kTileElems >> r));
+            const size_t smem = ((size_t)(1 << r) * C + (1 << r) / 2 + 1) * sizeof(Fr);
+            pass_fn(r)<<<(unsigned)(lines / C), kNttThreads, smem, st>>>(in, buf, L, Lp, C, T.roots, T.tw_lo, T.tw_hi, T.h,
+                                                                          (p == 0 && pre) ? pre->lo : nullptr,
+                                                                          (p == 0 && pre) ? pre->hi : nullptr, pre ? pre->h : 0);
+            launches++;
+            in = buf;
+            Lp -= r;
+        }
+        const unsigned pgrid = (unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)nd->num_sms * 16);
+        ntt_permute_kernel<<<pgrid, 256, 0, st>>>(buf, dst, L, pp, fin.mode, fin.scale, fin.tab ? fin.tab->lo : nullptr,
+                                                  fin.tab ? fin.tab->hi : nullptr, fin.tab ? fin.tab->h : 0, nullptr, nullptr);
+        launches++;
+    }
+    ZK_TRY_CUDA(cudaGetLastError());
+    g_ntt_launches = launches;
+    return ZK_OK;
+}
+
 }  // namespace zk
 
 using namespace zk;
@@ -516,4 +721,10 @@ extern "C" int zk_compute_omega(int log_n, int inverse, void* out_fr) {
     zkh::Fe w = host_root(log_n, inverse != 0);
     std::memcpy(out_fr, w.v, 32);
     return ZK_OK;
+}
+
+extern "C" int zk_ntt_device_noalloc(int device, void* stream, void* d_out, const void* d_in, int log_n, int inverse,
+                                     const void* coset_shift) {
+    clear_error();
+    return ntt_noalloc_run(device, (cudaStream_t)stream, d_out, d_in, log_n, inverse != 0, coset_shift);
 }

@@ -117,6 +117,33 @@ int zk_msm_g2_host(int device, void* stream, const void* h_points, const void* h
 int zk_ntt_device(int device, void* stream, void* d_out, const void* d_in, int log_n,
                   int inverse, const void* coset_shift);
 
+/* Allocation-free NTT.  No counterpart in the reference: it is an addition for
+ * callers that must not allocate device memory when they transform, such as a
+ * latency-critical pipeline that cannot tolerate cudaMalloc / cudaFree (which
+ * may synchronise the whole device and stall every stream), or a process
+ * whose device memory is all reserved by its own pool allocator.
+ *
+ * Same arguments and bit-identical results as zk_ntt_device, for
+ * 0 <= log_n <= ZK_NTT_NOALLOC_MAX_LOG (2^18 elements); a larger log_n returns
+ * ZK_ERR_RANGE and launches nothing.  The call allocates nothing, on the
+ * device or through any library: its working buffer (8 MiB) and its twiddle
+ * and coset tables (128 KiB) live in one fixed array compiled into this
+ * library, one per device.
+ *  - The first call on each device does one-time set-up (it looks up that
+ *    array's device address and loads the kernels it launches).  Make that
+ *    first call before any stream capture begins.
+ *  - Every call on a device uses the same array.  Calls whose work can
+ *    overlap in time (different streams, or different host threads without a
+ *    synchronisation between them) race and corrupt each other's results:
+ *    issue them in order on one stream.
+ *  - Nothing in the array has to start at zero: each call writes its tables
+ *    and its buffer before reading them.
+ *  - Asynchronous on `stream` like zk_ntt_device (NULL: legacy default
+ *    stream); d_out may equal d_in. */
+#define ZK_NTT_NOALLOC_MAX_LOG 18
+int zk_ntt_device_noalloc(int device, void* stream, void* d_out, const void* d_in, int log_n,
+                          int inverse, const void* coset_shift);
+
 /* Quotient polynomial of compute_h after the sparse matvec
  * (src/prover/groth16.cu:322-383): from the evaluation vectors A*w, B*w, C*w
  * on the size-2^log_n domain, writes the n coefficients of
