@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 #include <vector>
@@ -153,6 +154,8 @@ struct zk_groth16_pk {
     zk::Fr* w = nullptr;
     zk::Fr* abc = nullptr;  // 3 n
     zk::Fr* h = nullptr;    // n
+    unsigned long long* d_bad = nullptr;  // first failing constraint of the witness check
+    unsigned long long* h_bad = nullptr;  // pinned host copy
     uint64_t n_buf = 0;
 };
 
@@ -161,11 +164,12 @@ namespace zk {
 static thread_local zk_prove_stats g_prove_stats;
 
 // ------------------------------------------------------------------ kernels
-// rows with at most kShortRow entries: one thread per row; long rows are skipped
-// here and done by r1cs_matvec_long_kernel
+// rows [lo, hi) of M w into out[r - lo]; rows at or beyond `rows` (the
+// constraint count) are zero.  Rows with at most kShortRow entries: one thread
+// per row; long rows are skipped here and done by r1cs_matvec_long_kernel.
 __global__ void r1cs_matvec_short_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col, const Fr* __restrict__ val,
-                                         const Fr* __restrict__ w, int rows, uint64_t n, Fr* __restrict__ out) {
-    for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (uint64_t)gridDim.x * blockDim.x) {
+                                         const Fr* __restrict__ w, int rows, uint64_t lo, uint64_t hi, Fr* __restrict__ out) {
+    for (uint64_t r = lo + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < hi; r += (uint64_t)gridDim.x * blockDim.x) {
         Fr acc;
         fset_zero(acc);
         if (r < (uint64_t)rows) {
@@ -182,14 +186,14 @@ __global__ void r1cs_matvec_short_kernel(const int32_t* __restrict__ row_ptr, co
                 continue;  // written by the long-row kernel
             }
         }
-        fstore(out + r, acc);
+        fstore(out + (r - lo), acc);
     }
 }
 
 // one block per long row: strided partial sums, then a shared-memory tree
 __global__ void __launch_bounds__(256) r1cs_matvec_long_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
                                                                const Fr* __restrict__ val, const Fr* __restrict__ w,
-                                                               const int32_t* __restrict__ long_rows, Fr* __restrict__ out) {
+                                                               const int32_t* __restrict__ long_rows, uint64_t lo, Fr* __restrict__ out) {
     __shared__ Fr part[256];
     const int r = long_rows[blockIdx.x];
     const int a = row_ptr[r], b = row_ptr[r + 1];
@@ -212,7 +216,23 @@ __global__ void __launch_bounds__(256) r1cs_matvec_long_kernel(const int32_t* __
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) fstore(out + r, part[0]);
+    if (threadIdx.x == 0) fstore(out + (r - lo), part[0]);
+}
+
+// first index i < count with a_i * b_i != c_i (row0 + i is stored), by atomicMin
+__global__ void hadamard_check_kernel(const Fr* __restrict__ a, const Fr* __restrict__ b, const Fr* __restrict__ c, uint64_t count,
+                                      uint64_t row0, unsigned long long* __restrict__ first_bad) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {
+        Fr x, y, z;
+        fload_nc(x, a + i);
+        fload_nc(y, b + i);
+        fload_nc(z, c + i);
+        fmul(x, x, y);
+        uint32_t d = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) d |= x.v[k] ^ z.v[k];  // canonical representatives: equal values, equal words
+        if (d) atomicMin(first_bad, (unsigned long long)(row0 + i));
+    }
 }
 
 // x -> x * R^2 * R^-1 = Montgomery form of a standard-form Fp value
@@ -283,18 +303,46 @@ static int r1cs_create(int device, int num_constraints, int num_variables, int n
     return ZK_OK;
 }
 
-static int r1cs_matvec(const R1cs& R, cudaStream_t st, const Fr* w, Fr* out3, int num_sms) {
+// rows [lo, hi) of A w, B w, C w into out3 (three vectors of hi - lo elements)
+static int r1cs_matvec_rows(const R1cs& R, cudaStream_t st, const Fr* w, uint64_t lo, uint64_t hi, Fr* out3, int num_sms) {
     const int rows = (int)std::min<uint64_t>(R.n, (uint64_t)R.num_constraints);
+    const uint64_t len = hi - lo;
+    if (len == 0) return ZK_OK;
     for (int k = 0; k < 3; k++) {
-        Fr* out = out3 + (size_t)k * R.n;
-        const unsigned grid = (unsigned)std::min<uint64_t>((R.n + 255) / 256, (uint64_t)num_sms * 16);
-        r1cs_matvec_short_kernel<<<grid, 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w, rows, R.n, out);
-        if (!R.host[k].long_rows.empty())
-            r1cs_matvec_long_kernel<<<(unsigned)R.host[k].long_rows.size(), 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w,
-                                                                                         R.d_long[k], out);
+        Fr* out = out3 + (size_t)k * len;
+        const unsigned grid = (unsigned)std::min<uint64_t>((len + 255) / 256, (uint64_t)num_sms * 16);
+        r1cs_matvec_short_kernel<<<grid, 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w, rows, lo, hi, out);
+        // long rows inside [lo, hi): a contiguous run of the ascending list
+        const std::vector<int32_t>& lr = R.host[k].long_rows;
+        const size_t a = std::lower_bound(lr.begin(), lr.end(), (int64_t)lo) - lr.begin();
+        const size_t b = std::lower_bound(lr.begin(), lr.end(), (int64_t)hi) - lr.begin();
+        if (b > a)
+            r1cs_matvec_long_kernel<<<(unsigned)(b - a), 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w, R.d_long[k] + a, lo,
+                                                                      out);
     }
     ZK_TRY_CUDA(cudaGetLastError());
     return ZK_OK;
+}
+
+static int r1cs_matvec(const R1cs& R, cudaStream_t st, const Fr* w, Fr* out3, int num_sms) {
+    return r1cs_matvec_rows(R, st, w, 0, R.n, out3, num_sms);
+}
+
+// The reference's verify_witness (src/prover/circuit.cuh:93-124): every
+// constraint row r satisfies (A w)_r (B w)_r = (C w)_r.  Enqueues the check of
+// rows [row0, row0 + count) on `st`; *first_bad (device) must start at
+// 0xff..ff and ends as the first failing row, if any.
+static void enqueue_hadamard_check(cudaStream_t st, const Fr* a, const Fr* b, const Fr* c, uint64_t count, uint64_t row0,
+                                   unsigned long long* first_bad, int num_sms) {
+    if (!count) return;
+    const unsigned grid = (unsigned)std::min<uint64_t>((count + 255) / 256, (uint64_t)num_sms * 16);
+    hadamard_check_kernel<<<grid, 256, 0, st>>>(a, b, c, count, row0, first_bad);
+}
+
+static bool witness_check_enabled() {
+    // ZKML_SKIP_WITNESS_CHECK=1 turns the check off, as in Groth16Prover::prove (groth16.cu:691-697)
+    const char* e = std::getenv("ZKML_SKIP_WITNESS_CHECK");
+    return !(e && std::strcmp(e, "1") == 0);
 }
 
 // ------------------------------------------------------------------ setup
@@ -408,66 +456,20 @@ static int ensure_prover_buffers(zk_groth16_pk* pk, uint64_t n, int m) {
     ZK_TRY_CUDA(cudaMalloc(&pk->w, (size_t)std::max<uint64_t>(m, 1) * 32));
     ZK_TRY_CUDA(cudaMalloc(&pk->abc, 3 * n * 32));
     ZK_TRY_CUDA(cudaMalloc(&pk->h, n * 32));
+    if (!pk->d_bad) ZK_TRY_CUDA(cudaMalloc(&pk->d_bad, sizeof(unsigned long long)));
+    if (!pk->h_bad) ZK_TRY_CUDA(cudaMallocHost(&pk->h_bad, sizeof(unsigned long long)));
     pk->n_buf = n;
     return ZK_OK;
 }
 
-// ------------------------------------------------------------------ prove
-static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* h_witness, const zkh::Fe& r, const zkh::Fe& s,
-                 uint64_t outA[8], uint64_t outB[16], uint64_t outC[8]) {
-    zk_prove_stats& stats = g_prove_stats;
-    std::memset(&stats, 0, sizeof stats);
-    if (R.m != pk->m || R.num_public != pk->num_public || (uint64_t)pk->num_constraints != R.n) {
-        set_error("prove: proving key (m %d, public %d, n %d) does not match the circuit (m %d, public %d, n %llu)", pk->m,
-                  pk->num_public, pk->num_constraints, R.m, R.num_public, (unsigned long long)R.n);
-        return ZK_ERR_INVALID;
-    }
-    DeviceContext* ctx;
-    ZK_TRY(get_context(pk->device, &ctx));
-    const uint64_t n = R.n;
-    const int m = R.m, pub = R.num_public;
-    ZK_TRY(ensure_prover_buffers(pk, n, m));
-    cudaEvent_t ev[4];
-    for (auto& e : ev) ZK_TRY_CUDA(cudaEventCreate(&e));
-    ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
-    ZK_TRY_CUDA(cudaMemcpyAsync(pk->w, h_witness, (size_t)m * 32, cudaMemcpyHostToDevice, st));
-    ZK_TRY(r1cs_matvec(R, st, pk->w, pk->abc, ctx->num_sms));
-    ZK_TRY_CUDA(cudaEventRecord(ev[1], st));
-    ZK_TRY(zk_compute_h_device(pk->device, st, pk->h, pk->abc, pk->abc + n, pk->abc + 2 * n, R.log_n));
-    ZK_TRY_CUDA(cudaEventRecord(ev[2], st));
-    ZK_TRY_CUDA(cudaEventSynchronize(ev[2]));
-    float ms;
-    cudaEventElapsedTime(&ms, ev[0], ev[1]);
-    stats.matvec_ms = ms;
-    cudaEventElapsedTime(&ms, ev[1], ev[2]);
-    stats.compute_h_ms = ms;
-
-    uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm[8] = {0}, b_msm[16];
-    const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m, g1H = 2 * (size_t)m + pk->l;
-    zk_msm_stats ms_st;
-    ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1A * 64, pk->w, (size_t)m, a_msm));
-    zk_msm_last_stats(&ms_st);
-    stats.msm_ms[0] = ms_st.total_device_ms;
-    ZK_TRY(zk_msm_g2_device(pk->device, st, pk->g2, pk->w, (size_t)m, b_msm));
-    zk_msm_last_stats(&ms_st);
-    stats.msm_ms[1] = ms_st.total_device_ms;
-    const int num_priv = std::min(pk->l, m - 1 - pub);
-    if (num_priv > 0) {
-        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1L * 64, pk->w + 1 + pub, (size_t)num_priv, l_msm));
-        zk_msm_last_stats(&ms_st);
-        stats.msm_ms[2] = ms_st.total_device_ms;
-    }
-    const int n_h = std::min<int>((int)n, pk->n_h);
-    if (n_h > 0) {
-        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1H * 64, pk->h, (size_t)n_h, h_msm));
-        zk_msm_last_stats(&ms_st);
-        stats.msm_ms[3] = ms_st.total_device_ms;
-    }
-    ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1B1 * 64, pk->w, (size_t)m, b1_msm));
-    zk_msm_last_stats(&ms_st);
-    stats.msm_ms[4] = ms_st.total_device_ms;
-
-    // assembly (groth16.cu:774-844)
+// Proof points from the five MSM sums (groth16.cu:774-844):
+//   A = alpha1 + sum_A + r delta1
+//   B = beta2 + sum_B2 + s delta2
+//   C = sum_L + sum_H + s A + r (beta1 + sum_B1)
+// (the reference folds r s delta1 into s A, with A the affine proof point)
+static void assemble(const zk_groth16_pk* pk, const zkh::Fe& r, const zkh::Fe& s, const uint64_t a_msm[8], const uint64_t b_msm[16],
+                     const uint64_t l_msm[8], const uint64_t h_msm[8], const uint64_t b1_msm[8], uint64_t outA[8], uint64_t outB[16],
+                     uint64_t outC[8]) {
     uint64_t rs[4], ss[4];
     zkh::to_std(zkh::kR, rs, r);
     zkh::to_std(zkh::kR, ss, s);
@@ -502,6 +504,76 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     zkh::smul(t1, b1, rs);
     zkh::add(Cp, t1);
     store_aff(outC, Cp);
+}
+
+// ------------------------------------------------------------------ prove
+static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* h_witness, const zkh::Fe& r, const zkh::Fe& s,
+                 uint64_t outA[8], uint64_t outB[16], uint64_t outC[8]) {
+    zk_prove_stats& stats = g_prove_stats;
+    std::memset(&stats, 0, sizeof stats);
+    if (R.m != pk->m || R.num_public != pk->num_public || (uint64_t)pk->num_constraints != R.n) {
+        set_error("prove: proving key (m %d, public %d, n %d) does not match the circuit (m %d, public %d, n %llu)", pk->m,
+                  pk->num_public, pk->num_constraints, R.m, R.num_public, (unsigned long long)R.n);
+        return ZK_ERR_INVALID;
+    }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(pk->device, &ctx));
+    const uint64_t n = R.n;
+    const int m = R.m, pub = R.num_public;
+    ZK_TRY(ensure_prover_buffers(pk, n, m));
+    cudaEvent_t ev[4];
+    for (auto& e : ev) ZK_TRY_CUDA(cudaEventCreate(&e));
+    ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
+    ZK_TRY_CUDA(cudaMemcpyAsync(pk->w, h_witness, (size_t)m * 32, cudaMemcpyHostToDevice, st));
+    ZK_TRY(r1cs_matvec(R, st, pk->w, pk->abc, ctx->num_sms));
+    const bool check = witness_check_enabled();
+    if (check) {
+        ZK_TRY_CUDA(cudaMemsetAsync(pk->d_bad, 0xff, sizeof(unsigned long long), st));
+        enqueue_hadamard_check(st, pk->abc, pk->abc + n, pk->abc + 2 * n, std::min<uint64_t>(n, (uint64_t)R.num_constraints), 0,
+                               pk->d_bad, ctx->num_sms);
+        ZK_TRY_CUDA(cudaMemcpyAsync(pk->h_bad, pk->d_bad, sizeof(unsigned long long), cudaMemcpyDeviceToHost, st));
+    }
+    ZK_TRY_CUDA(cudaEventRecord(ev[1], st));
+    ZK_TRY(zk_compute_h_device(pk->device, st, pk->h, pk->abc, pk->abc + n, pk->abc + 2 * n, R.log_n));
+    ZK_TRY_CUDA(cudaEventRecord(ev[2], st));
+    ZK_TRY_CUDA(cudaEventSynchronize(ev[2]));
+    if (check && *pk->h_bad != ~0ull) {
+        for (auto& e : ev) cudaEventDestroy(e);
+        set_error("[Prove] Witness does not satisfy R1CS constraints (constraint %llu failed)", *pk->h_bad);
+        return ZK_ERR_INVALID;
+    }
+    float ms;
+    cudaEventElapsedTime(&ms, ev[0], ev[1]);
+    stats.matvec_ms = ms;
+    cudaEventElapsedTime(&ms, ev[1], ev[2]);
+    stats.compute_h_ms = ms;
+
+    uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm[8] = {0}, b_msm[16];
+    const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m, g1H = 2 * (size_t)m + pk->l;
+    zk_msm_stats ms_st;
+    ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1A * 64, pk->w, (size_t)m, a_msm));
+    zk_msm_last_stats(&ms_st);
+    stats.msm_ms[0] = ms_st.total_device_ms;
+    ZK_TRY(zk_msm_g2_device(pk->device, st, pk->g2, pk->w, (size_t)m, b_msm));
+    zk_msm_last_stats(&ms_st);
+    stats.msm_ms[1] = ms_st.total_device_ms;
+    const int num_priv = std::min(pk->l, m - 1 - pub);
+    if (num_priv > 0) {
+        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1L * 64, pk->w + 1 + pub, (size_t)num_priv, l_msm));
+        zk_msm_last_stats(&ms_st);
+        stats.msm_ms[2] = ms_st.total_device_ms;
+    }
+    const int n_h = std::min<int>((int)n, pk->n_h);
+    if (n_h > 0) {
+        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1H * 64, pk->h, (size_t)n_h, h_msm));
+        zk_msm_last_stats(&ms_st);
+        stats.msm_ms[3] = ms_st.total_device_ms;
+    }
+    ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1B1 * 64, pk->w, (size_t)m, b1_msm));
+    zk_msm_last_stats(&ms_st);
+    stats.msm_ms[4] = ms_st.total_device_ms;
+
+    assemble(pk, r, s, a_msm, b_msm, l_msm, h_msm, b1_msm, outA, outB, outC);
     ZK_TRY_CUDA(cudaEventRecord(ev[3], st));
     ZK_TRY_CUDA(cudaEventSynchronize(ev[3]));
     cudaEventElapsedTime(&ms, ev[0], ev[3]);
@@ -844,6 +916,8 @@ extern "C" void zk_groth16_pk_destroy(zk_groth16_pk* pk) {
     cudaFree(pk->w);
     cudaFree(pk->abc);
     cudaFree(pk->h);
+    cudaFree(pk->d_bad);
+    cudaFreeHost(pk->h_bad);
     delete pk;
 }
 
@@ -869,5 +943,78 @@ extern "C" int zk_groth16_prove(zk_groth16_pk* pk, const zk_r1cs* r1cs, void* st
 extern "C" int zk_groth16_last_stats(zk_prove_stats* out) {
     if (!out) return ZK_ERR_INVALID;
     *out = g_prove_stats;
+    return ZK_OK;
+}
+
+// ------------------------------------------------------------------ pieces of a prove split across devices
+extern "C" int zk_r1cs_matvec_rows_device(const zk_r1cs* r1cs, void* stream, const void* d_witness, uint64_t row_lo, uint64_t row_hi,
+                                          void* d_out3) {
+    clear_error();
+    if (!r1cs || !d_witness || (!d_out3 && row_hi > row_lo)) return ZK_ERR_INVALID;
+    const R1cs& R = r1cs->r;
+    if (row_lo > row_hi || row_hi > R.n) {
+        set_error("matvec: rows [%llu, %llu) outside the domain of %llu", (unsigned long long)row_lo, (unsigned long long)row_hi,
+                  (unsigned long long)R.n);
+        return ZK_ERR_RANGE;
+    }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(R.device, &ctx));
+    return r1cs_matvec_rows(R, (cudaStream_t)stream, (const Fr*)d_witness, row_lo, row_hi, (Fr*)d_out3, ctx->num_sms);
+}
+
+extern "C" int zk_fr_hadamard_check_device(int device, void* stream, const void* d_a, const void* d_b, const void* d_c, size_t count,
+                                           uint64_t row0, long long* first_bad) {
+    clear_error();
+    if (!first_bad || (count && (!d_a || !d_b || !d_c))) return ZK_ERR_INVALID;
+    *first_bad = -1;
+    if (!count) return ZK_OK;
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    cudaStream_t st = (cudaStream_t)stream;
+    unsigned long long* d_bad = nullptr;
+    ZK_TRY_CUDA(cudaMallocAsync((void**)&d_bad, sizeof(unsigned long long), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(d_bad, 0xff, sizeof(unsigned long long), st));
+    enqueue_hadamard_check(st, (const Fr*)d_a, (const Fr*)d_b, (const Fr*)d_c, count, row0, d_bad, ctx->num_sms);
+    unsigned long long bad = 0;
+    ZK_TRY_CUDA(cudaMemcpyAsync(&bad, d_bad, sizeof bad, cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaFreeAsync(d_bad, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    *first_bad = bad == ~0ull ? -1 : (long long)bad;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_pk_arrays(const zk_groth16_pk* pk, zk_groth16_arrays* out) {
+    clear_error();
+    if (!pk || !out) return ZK_ERR_INVALID;
+    out->device = pk->device;
+    out->m = pk->m;
+    out->num_public = pk->num_public;
+    out->l = pk->l;
+    out->n_h = pk->n_h;
+    out->a = pk->g1;
+    out->b1 = pk->g1 + (size_t)pk->m * 64;
+    out->l_query = pk->g1 + 2 * (size_t)pk->m * 64;
+    out->h_query = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
+    out->b2 = pk->g2;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, const void* sums, void* proof256,
+                                   void* points) {
+    clear_error();
+    if (!pk || !r || !s || !sums || !proof256) return ZK_ERR_INVALID;
+    zkh::Fe rr, ss;
+    std::memcpy(rr.v, r, 32);
+    std::memcpy(ss.v, s, 32);
+    const uint64_t* q = (const uint64_t*)sums;  // A (8) | B2 (16) | L (8) | H (8) | B1 (8) words
+    uint64_t A[8], B[16], C[8];
+    assemble(pk, rr, ss, q, q + 8, q + 24, q + 32, q + 40, A, B, C);
+    serialize_proof((uint8_t*)proof256, A, B, C);
+    if (points) {
+        uint64_t* p = (uint64_t*)points;
+        std::memcpy(p, A, 64);
+        std::memcpy(p + 8, B, 128);
+        std::memcpy(p + 24, C, 64);
+    }
     return ZK_OK;
 }

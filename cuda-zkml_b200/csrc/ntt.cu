@@ -420,22 +420,10 @@ int ntt_run(int device, cudaStream_t user_stream, void* d_out, const void* d_in,
     return scratch_end(ctx, st);
 }
 
-// compute_h after the matvec (src/prover/groth16.cu:322-383)
-int compute_h_run(int device, cudaStream_t user_stream, void* d_h, const void* d_a, const void* d_b, const void* d_c, int L) {
-    if (!d_h || !d_a || !d_b || !d_c) { set_error("compute_h: null pointer"); return ZK_ERR_INVALID; }
-    if (L < 0 || L > ZK_NTT_MAX_LOG - 1) { set_error("compute_h: log_n = %d out of range", L); return ZK_ERR_RANGE; }
-    DeviceContext* ctx;
-    ZK_TRY(get_context(device, &ctx));
-    std::lock_guard<std::mutex> lock(ctx->mu);
-    cudaStream_t st = user_stream;  // NULL: the legacy default stream
-    const uint64_t n = 1ull << L;
-    ZK_TRY(ensure_scratch(ctx, 4 * n * 32));
-    Fr* buf = (Fr*)ctx->scratch;
-    Fr* A = buf + n;
-    Fr* B = buf + 2 * n;
-    Fr* Cc = buf + 3 * n;
-    // coset generator g = 5, or 7 when 5^n == 1 (groth16.cu:329-342)
-    zkh::Fe g, z, one = zkh::one(zkh::kR);
+// coset generator g = 5, or 7 when 5^n == 1 (groth16.cu:329-342), and
+// (g^n - 1)^-1, the inverse of the vanishing polynomial on the coset
+static int coset_shift(int L, zkh::Fe& g, zkh::Fe& zinv) {
+    zkh::Fe z, one = zkh::one(zkh::kR);
     uint64_t s5[4] = {5, 0, 0, 0}, s7[4] = {7, 0, 0, 0};
     zkh::from_std(zkh::kR, g, s5);
     auto vanish = [&](const zkh::Fe& gg) {
@@ -450,8 +438,40 @@ int compute_h_run(int device, cudaStream_t user_stream, void* d_h, const void* d
         z = vanish(g);
     }
     if (zkh::is_zero(z)) { set_error("compute_h: no valid coset shift"); return ZK_ERR_INVALID; }
-    zkh::Fe zinv;
     zkh::inv(zkh::kR, zinv, z);
+    return ZK_OK;
+}
+
+// out = (a b - c) * zinv, elementwise (out may alias any input)
+__global__ void h_pointwise_kernel(Fr* out, const Fr* a, const Fr* b, const Fr* c, uint64_t n, Fr zinv) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        Fr x, y, z;
+        fload_nc(x, a + i);
+        fload_nc(y, b + i);
+        fload_nc(z, c + i);
+        fmul(x, x, y);
+        fsub(x, x, z);
+        fmul(x, x, zinv);
+        fstore(out + i, x);
+    }
+}
+
+// compute_h after the matvec (src/prover/groth16.cu:322-383)
+int compute_h_run(int device, cudaStream_t user_stream, void* d_h, const void* d_a, const void* d_b, const void* d_c, int L) {
+    if (!d_h || !d_a || !d_b || !d_c) { set_error("compute_h: null pointer"); return ZK_ERR_INVALID; }
+    if (L < 0 || L > ZK_NTT_MAX_LOG - 1) { set_error("compute_h: log_n = %d out of range", L); return ZK_ERR_RANGE; }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    cudaStream_t st = user_stream;  // NULL: the legacy default stream
+    const uint64_t n = 1ull << L;
+    ZK_TRY(ensure_scratch(ctx, 4 * n * 32));
+    Fr* buf = (Fr*)ctx->scratch;
+    Fr* A = buf + n;
+    Fr* B = buf + 2 * n;
+    Fr* Cc = buf + 3 * n;
+    zkh::Fe g, zinv;
+    ZK_TRY(coset_shift(L, g, zinv));
     const CosetTables *to_coset, *from_coset;
     ZK_TRY(get_coset_tables(ctx, L, 2, g, &to_coset));    // n^-1 g^i
     ZK_TRY(get_coset_tables(ctx, L, 1, g, &from_coset));  // n^-1 g^-i
@@ -727,4 +747,32 @@ extern "C" int zk_ntt_device_noalloc(int device, void* stream, void* d_out, cons
                                      const void* coset_shift) {
     clear_error();
     return ntt_noalloc_run(device, (cudaStream_t)stream, d_out, d_in, log_n, inverse != 0, coset_shift);
+}
+
+extern "C" int zk_compute_h_coset_shift(int log_n, void* out_g) {
+    clear_error();
+    if (!out_g) return ZK_ERR_INVALID;
+    if (log_n < 0 || log_n > ZK_NTT_MAX_LOG) { set_error("compute_h: log_n = %d out of range", log_n); return ZK_ERR_RANGE; }
+    zkh::Fe g, zinv;
+    ZK_TRY(coset_shift(log_n, g, zinv));
+    std::memcpy(out_g, g.v, 32);
+    return ZK_OK;
+}
+
+extern "C" int zk_compute_h_pointwise_device(int device, void* stream, void* d_out, const void* d_a, const void* d_b, const void* d_c,
+                                             int log_n) {
+    clear_error();
+    if (!d_out || !d_a || !d_b || !d_c) return ZK_ERR_INVALID;
+    if (log_n < 0 || log_n > ZK_NTT_MAX_LOG) { set_error("compute_h: log_n = %d out of range", log_n); return ZK_ERR_RANGE; }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    zkh::Fe g, zinv;
+    ZK_TRY(coset_shift(log_n, g, zinv));
+    Fr zi;
+    std::memcpy(zi.v, zinv.v, 32);
+    const uint64_t n = 1ull << log_n;
+    const unsigned grid = (unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)ctx->num_sms * 16);
+    h_pointwise_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((Fr*)d_out, (const Fr*)d_a, (const Fr*)d_b, (const Fr*)d_c, n, zi);
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
 }

@@ -48,6 +48,11 @@ class MsmStats(ctypes.Structure):
                 ("phase_ms", ctypes.c_float * 8)]
 
 
+class Groth16Arrays(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("m", ctypes.c_int), ("num_public", ctypes.c_int), ("l", ctypes.c_int),
+                ("n_h", ctypes.c_int), ("a", _vp), ("b1", _vp), ("b2", _vp), ("l_query", _vp), ("h_query", _vp)]
+
+
 _SIGS = {
     "zk_device_count": [ctypes.POINTER(ctypes.c_int)],
     "zk_version": [],
@@ -68,6 +73,12 @@ _SIGS = {
     "zk_g2_add_affine": [_vp, _vp, _vp],
     "zk_probe_imad_rate": [_i, ctypes.POINTER(ctypes.c_double)],
     "zk_msm_last_stats": [ctypes.POINTER(MsmStats)],
+    "zk_r1cs_matvec_rows_device": [_vp, _vp, _vp, ctypes.c_uint64, ctypes.c_uint64, _vp],
+    "zk_fr_hadamard_check_device": [_i, _vp, _vp, _vp, _vp, _sz, ctypes.c_uint64, ctypes.POINTER(ctypes.c_longlong)],
+    "zk_compute_h_coset_shift": [_i, _vp],
+    "zk_compute_h_pointwise_device": [_i, _vp, _vp, _vp, _vp, _vp, _i],
+    "zk_groth16_pk_arrays": [_vp, ctypes.POINTER(Groth16Arrays)],
+    "zk_groth16_assemble": [_vp, _vp, _vp, _vp, _vp, _vp],
 }
 for _name, _args in _SIGS.items():
     getattr(lib, _name).argtypes = _args
@@ -285,6 +296,32 @@ def ntt(x, log_n, inverse=False, coset=None, out=None):
     return out
 
 
+def compute_h_coset_shift(log_n):
+    """compute_h's coset shift g (Montgomery (4,) uint64): 5, or 7 when 5^n = 1."""
+    g = np.zeros(4, np.uint64)
+    check(lib.zk_compute_h_coset_shift(log_n, _np_ptr(g)))
+    return g
+
+
+def compute_h_pointwise(a, b, c, log_n, out=None):
+    """(a b - c) / (g^n - 1) elementwise over coset evaluations (CUDA tensors)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(a)
+    check(lib.zk_compute_h_pointwise_device(a.device.index, _stream(a), _dev_ptr(out), _dev_ptr(a), _dev_ptr(b), _dev_ptr(c),
+                                            log_n))
+    return out
+
+
+def hadamard_check(a, b, c, row0=0):
+    """First row0 + i with a_i b_i != c_i, or -1 (CUDA tensors of equal length)."""
+    bad = ctypes.c_longlong()
+    count = a.numel() * a.element_size() // 32
+    check(lib.zk_fr_hadamard_check_device(a.device.index, _stream(a), _dev_ptr(a), _dev_ptr(b), _dev_ptr(c), count, row0,
+                                          ctypes.byref(bad)))
+    return bad.value
+
+
 def ntt_ref(d_out, d_in, log_n, inverse):
     """Reference-shaped ntt_gpu (synchronous, current device)."""
     return lib.zk_ntt(_dev_ptr(d_out), _dev_ptr(d_in), log_n, int(inverse))
@@ -374,6 +411,18 @@ class R1cs:
         ln = ctypes.c_int()
         check(lib.zk_r1cs_domain(self.h, ctypes.byref(ln)))
         self.log_n = ln.value
+        self.num_constraints = circuit["num_constraints"]
+        self.num_variables = circuit["num_variables"]
+        self.num_public = circuit["num_public"]
+
+    def matvec_rows(self, d_witness, lo, hi, out=None):
+        """Rows [lo, hi) of A w, B w, C w as a (3, hi - lo, 4) int64 CUDA tensor."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty((3, hi - lo, 4), dtype=torch.int64, device=d_witness.device)
+        check(lib.zk_r1cs_matvec_rows_device(self.h, _stream(d_witness), _dev_ptr(d_witness), lo, hi,
+                                             _dev_ptr(out) if hi > lo else None))
+        return out
 
     def __del__(self):
         if getattr(self, "h", None):
@@ -414,6 +463,22 @@ class ProvingKey:
         ic = np.zeros((max(nic, 1), 8), np.uint64)
         lib.zk_groth16_vk_points(self.h, _np_ptr(a1), _np_ptr(b2), _np_ptr(g2), _np_ptr(d2), _np_ptr(ic), nic)
         return {"alpha1": a1, "beta2": b2, "gamma2": g2, "delta2": d2, "ic": ic[:nic]}
+
+    def arrays(self):
+        """Device pointers and sizes of the query arrays (zk_groth16_pk_arrays)."""
+        a = Groth16Arrays()
+        check(lib.zk_groth16_pk_arrays(self.h, ctypes.byref(a)))
+        return {k: getattr(a, k) for k, _ in Groth16Arrays._fields_}
+
+    def assemble(self, r, s, sums):
+        """Proof from the five MSM sums (A, B2, L, H, B1 packed affine; 48 words)."""
+        rr, ss = fr_from_int(r), fr_from_int(s)
+        sums = np.ascontiguousarray(sums, dtype=np.uint64)
+        assert sums.size == 48
+        proof = np.zeros(256, np.uint8)
+        pts = np.zeros(32, np.uint64)
+        check(lib.zk_groth16_assemble(self.h, _np_ptr(rr), _np_ptr(ss), _np_ptr(sums), _np_ptr(proof), _np_ptr(pts)))
+        return proof.tobytes(), pts[:8], pts[8:24], pts[24:32]
 
     def prove(self, r1cs, witness, r, s, stream=None):
         """witness (m, 4) Montgomery; r, s ints.  Returns (proof bytes, A, B, C)."""

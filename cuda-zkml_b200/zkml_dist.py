@@ -43,3 +43,260 @@ def sharded_msm(points, scalars, local_msm, add, group=None, device=None):
     """sum_i s_i P_i over all ranks' slices: local_msm(points, scalars) on this
     rank's slice, all-gather of the partial points, fold with `add`."""
     return combine(gather_partials(local_msm(points, scalars), group, device), add)
+
+
+# ------------------------------------------------------------------ Groth16 prove across ranks
+#
+# Groth16Prover::prove (src/prover/groth16.cu:655-920) runs on device 0 only.
+# Split over `world` ranks, each holding the whole proving key and circuit:
+#   1. rows: rank j computes rows [j S, (j + 1) S) of A w, B w, C w (S = n /
+#      world, rounded up) and checks them (R1CS::verify_witness,
+#      src/prover/circuit.cuh:93-124); the first failing row is an all-reduce
+#      MIN, so every rank fails the same way.
+#   2. all-gather of the three evaluation vectors; polynomial k (A, B, C)
+#      belongs to rank k mod world, which runs its INTT and coset NTT
+#      (groth16.cu:350-363) while the other ranks start their MSM slices.
+#   3. three broadcasts of the coset evaluations; every rank forms
+#      (a b - c) / (g^n - 1) and the coset INTT (groth16.cu:364-383): h.
+#   4. every MSM (A, B2, L, H, B1) is point-sharded over all ranks; the ranks
+#      all-gather their partial sums (5 points each) and fold them.
+#   5. the proof is assembled from the five sums (groth16.cu:774-844).
+# The result is byte-identical to the one-device proof: every step is exact.
+
+MSM_ORDER = ("a", "b2", "l", "h", "b1")  # layout of the 48-word sums record
+_WORDS = {"a": 8, "b2": 16, "l": 8, "h": 8, "b1": 8}
+_NO_ROW = np.iinfo(np.int64).max
+
+
+def prove_msm_sizes(m, num_public, l, n, n_h):
+    """Number of terms of each MSM of a proof (groth16.cu:776-827)."""
+    num_priv = max(0, min(l, m - 1 - num_public))
+    return {"a": m, "b2": m, "l": num_priv, "h": min(n, n_h), "b1": m}
+
+
+def row_chunk(n, world):
+    return -(-n // world)
+
+
+def witness_check_enabled():
+    import os
+    return os.environ.get("ZKML_SKIP_WITNESS_CHECK") != "1"
+
+
+def pack_sums(sums):
+    return np.concatenate([np.asarray(sums[k], dtype=np.uint64).reshape(-1) for k in MSM_ORDER])
+
+
+def unpack_sums(rec):
+    out, o = {}, 0
+    for k in MSM_ORDER:
+        out[k] = rec[o:o + _WORDS[k]]
+        o += _WORDS[k]
+    return out
+
+
+def sharded_prove(prover, comm, witness, r, s, timer=None):
+    """One Groth16 proof with the work of `prover` (this rank's device) shared
+    over `comm`'s ranks.  witness: (m, 4) uint64 Montgomery (host); r, s ints.
+    Returns (proof bytes, A, B, C) on every rank."""
+    rank, world = comm.rank, comm.world
+    n, m, pub = prover.n, prover.m, prover.num_public
+    sizes = prove_msm_sizes(m, pub, prover.l, n, prover.n_h)
+    S = row_chunk(n, world)
+    lo, hi = min(n, rank * S), min(n, (rank + 1) * S)
+    w = prover.upload_witness(witness)
+    abc = prover.matvec_rows(w, lo, hi)          # (3, hi - lo, 4)
+    bad = prover.check_rows(abc, lo) if witness_check_enabled() else -1
+    bad = comm.all_reduce_min(bad if bad >= 0 else _NO_ROW, like=w)
+    if bad != _NO_ROW:
+        raise prover.error(f"[Prove] Witness does not satisfy R1CS constraints (constraint {bad} failed)")
+    full = [comm.all_gather_rows(prover.pad_rows(abc[k], S), S)[:n] for k in range(3)]
+    owners = [k % world for k in range(3)]
+    cosets = [prover.to_coset(full[k]) if owners[k] == rank else prover.empty_vector() for k in range(3)]
+    del full, abc
+
+    def witness_msms():
+        out = {}
+        for key in ("a", "b2", "l", "b1"):
+            a, b = shard_bounds(sizes[key], rank, world)
+            off = 1 + pub if key == "l" else 0
+            out[key] = prover.msm(key, a, b, w, off)
+        return out
+
+    sums = {}
+    first = rank not in owners  # ranks without a polynomial start their MSM slices at once
+    if first:
+        sums.update(witness_msms())
+    for k in range(3):
+        comm.broadcast(cosets[k], owners[k])
+    h = prover.h_from_cosets(*cosets)
+    del cosets
+    if not first:
+        sums.update(witness_msms())
+    a, b = shard_bounds(sizes["h"], rank, world)
+    sums["h"] = prover.msm("h", a, b, h, 0)
+    parts = [unpack_sums(p) for p in comm.all_gather_points(pack_sums(sums))]
+    total = {k: combine([p[k] for p in parts], prover.add_g2 if k == "b2" else prover.add_g1) for k in MSM_ORDER}
+    return prover.assemble(r, s, pack_sums(total))
+
+
+class TorchComm:
+    """Collectives over torch.distributed (NCCL for CUDA tensors, gloo for CPU)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+
+    def all_reduce_min(self, value, like):
+        import torch
+        t = torch.tensor([value], dtype=torch.int64, device=like.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MIN, group=self.group)
+        return int(t.item())
+
+    def all_gather_rows(self, local, chunk):
+        import torch
+        out = torch.empty((self.world * chunk,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+        self.dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
+        return out
+
+    def broadcast(self, t, src):
+        self.dist.broadcast(t, src, group=self.group)
+        return t
+
+    def all_gather_points(self, rec):
+        import torch
+        dev = None
+        if self.dist.get_backend(self.group) == "nccl":
+            dev = torch.device("cuda", torch.cuda.current_device())
+        return gather_partials(rec, self.group, dev)
+
+
+class ThreadComm:
+    """Ranks as threads of one process (sharing one device): an exact
+    stand-in for the collectives, for testing the split on a single GPU."""
+
+    class Shared:
+        def __init__(self, world, timeout=300.0):
+            import threading
+            self.world = world
+            self.barrier = threading.Barrier(world, timeout=timeout)
+            self.slots = [None] * world
+
+    def __init__(self, shared, rank):
+        self.sh, self.rank, self.world = shared, rank, shared.world
+
+    def _exchange(self, item):
+        self.sh.slots[self.rank] = item
+        self.sh.barrier.wait()
+        items = list(self.sh.slots)
+        self.sh.barrier.wait()
+        return items
+
+    @staticmethod
+    def _sync(t):
+        import torch
+        if t is not None and t.is_cuda:
+            torch.cuda.current_stream(t.device).synchronize()
+
+    def all_reduce_min(self, value, like):
+        return min(self._exchange(int(value)))
+
+    def all_gather_rows(self, local, chunk):
+        import torch
+        self._sync(local)
+        items = self._exchange(local)
+        out = torch.cat([x.to(local.device) for x in items])
+        self._sync(out)  # the other ranks' buffers stay untouched until this copy is done
+        self.sh.barrier.wait()
+        return out
+
+    def broadcast(self, t, src):
+        self._sync(t)
+        items = self._exchange(t if self.rank == src else None)
+        if self.rank != src:
+            t.copy_(items[src])
+            self._sync(t)
+        return t
+
+    def all_gather_points(self, rec):
+        return self._exchange(np.array(rec, copy=True))
+
+
+class CudaProver:
+    """This rank's device work for sharded_prove, through the C ABI
+    (key and circuit resident on one device)."""
+
+    def __init__(self, pk, r1cs):
+        import zkml_b200 as Z
+        self.Z, self.pk, self.r1cs = Z, pk, r1cs
+        self.arr = pk.arrays()
+        self.device = self.arr["device"]
+        self.m, self.num_public, self.l, self.n_h = self.arr["m"], self.arr["num_public"], self.arr["l"], self.arr["n_h"]
+        self.log_n = r1cs.log_n
+        self.n = 1 << r1cs.log_n
+        self.g = Z.compute_h_coset_shift(self.log_n)
+        self._pinned = None
+
+    def error(self, msg):
+        return self.Z.ZkError(self.Z.ZK_ERR_INVALID, msg)
+
+    def upload_witness(self, witness):
+        import torch
+        witness = np.ascontiguousarray(witness, dtype=np.uint64)
+        if self._pinned is None or self._pinned.shape[0] != witness.shape[0]:
+            self._pinned = torch.empty((witness.shape[0], 4), dtype=torch.int64, pin_memory=True)
+        self._pinned.numpy()[:] = witness.view(np.int64)
+        return self._pinned.to(torch.device("cuda", self.device), non_blocking=True)
+
+    def matvec_rows(self, w, lo, hi):
+        return self.r1cs.matvec_rows(w, lo, hi)
+
+    def check_rows(self, abc, row0):
+        if abc.shape[1] == 0:
+            return -1
+        return self.Z.hadamard_check(abc[0], abc[1], abc[2], row0)
+
+    def pad_rows(self, v, rows):
+        import torch
+        if v.shape[0] == rows:
+            return v
+        out = torch.zeros((rows, 4), dtype=v.dtype, device=v.device)
+        out[:v.shape[0]] = v
+        return out
+
+    def empty_vector(self):
+        import torch
+        return torch.empty((self.n, 4), dtype=torch.int64, device=torch.device("cuda", self.device))
+
+    def to_coset(self, v):
+        """Evaluations on the domain -> evaluations on the coset g H."""
+        coeffs = self.Z.ntt(v.contiguous(), self.log_n, inverse=True)
+        return self.Z.ntt(coeffs, self.log_n, inverse=False, coset=self.g, out=coeffs)
+
+    def h_from_cosets(self, a, b, c):
+        q = self.Z.compute_h_pointwise(a, b, c, self.log_n)
+        return self.Z.ntt(q, self.log_n, inverse=True, coset=self.g, out=q)
+
+    def msm(self, key, lo, hi, scalars, scalar_offset):
+        import ctypes
+        words = _WORDS[key]
+        out = np.zeros(words, np.uint64)
+        if hi <= lo:
+            return out
+        base = {"a": "a", "b2": "b2", "l": "l_query", "h": "h_query", "b1": "b1"}[key]
+        rec = 128 if key == "b2" else 64
+        pts = ctypes.c_void_p(self.arr[base] + lo * rec)
+        sc = ctypes.c_void_p(scalars.data_ptr() + (scalar_offset + lo) * 32)
+        fn = self.Z.lib.zk_msm_g2_device if key == "b2" else self.Z.lib.zk_msm_g1_device
+        self.Z.check(fn(self.device, self.Z._stream(scalars), pts, sc, hi - lo, out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    def add_g1(self, a, b):
+        return self.Z.g1_add_affine(a, b)
+
+    def add_g2(self, a, b):
+        return self.Z.g2_add_affine(a, b)
+
+    def assemble(self, r, s, sums):
+        return self.pk.assemble(r, s, sums)

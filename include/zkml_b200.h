@@ -237,6 +237,58 @@ typedef struct {
 } zk_prove_stats;
 int zk_groth16_last_stats(zk_prove_stats* out);
 
+/* ------------------------------------------------------------------
+ * Pieces of zk_groth16_prove for a prove split across devices (one process
+ * per GPU).  The reference proves on device 0 only; these entry points let a
+ * host driver shard every step and get the same proof bytes:
+ *   rows of the matvec and the witness check -> all-gather of A w, B w, C w
+ *   -> per polynomial INTT + coset NTT (zk_ntt_device) -> broadcast
+ *   -> zk_compute_h_pointwise_device + coset INTT (h) -> point-sharded MSMs
+ *   over zk_groth16_pk_arrays -> fold the partial sums -> zk_groth16_assemble.
+ * zk_groth16_prove runs the witness check too: unless ZKML_SKIP_WITNESS_CHECK
+ * is "1" it fails with ZK_ERR_INVALID naming the first constraint whose
+ * (A w)(B w) != (C w), like Groth16Prover::prove (groth16.cu:691-697) with
+ * R1CS::verify_witness (src/prover/circuit.cuh:93-124).
+ * ------------------------------------------------------------------ */
+
+/* Rows [row_lo, row_hi) of A w, B w, C w (d_witness: device Fr[num_variables])
+ * into d_out3 = three consecutive vectors of row_hi - row_lo Fr; rows at or
+ * beyond num_constraints are zero.  row_hi <= the domain size. */
+int zk_r1cs_matvec_rows_device(const zk_r1cs* r1cs, void* stream, const void* d_witness,
+                               uint64_t row_lo, uint64_t row_hi, void* d_out3);
+/* *first_bad = row0 + the first i < count with a_i b_i != c_i, or -1.
+ * Synchronous on `stream`. */
+int zk_fr_hadamard_check_device(int device, void* stream, const void* d_a, const void* d_b,
+                                const void* d_c, size_t count, uint64_t row0, long long* first_bad);
+/* compute_h's coset shift g (5, or 7 when 5^n = 1; groth16.cu:329-342). */
+int zk_compute_h_coset_shift(int log_n, void* out_g);
+/* d_out = (a b - c) / (g^n - 1) elementwise over the 2^log_n coset
+ * evaluations (groth16.cu:364-371); d_out may alias an input. */
+int zk_compute_h_pointwise_device(int device, void* stream, void* d_out, const void* d_a,
+                                  const void* d_b, const void* d_c, int log_n);
+
+/* Device-resident query arrays of a proving key (packed affine, Montgomery). */
+typedef struct {
+    int device;
+    int m;            /* entries of a, b1, b2 */
+    int num_public;
+    int l;            /* entries of l_query */
+    int n_h;          /* entries of h_query */
+    const void* a;    /* G1, 64 B each */
+    const void* b1;   /* G1 */
+    const void* b2;   /* G2, 128 B each */
+    const void* l_query;
+    const void* h_query;
+} zk_groth16_arrays;
+int zk_groth16_pk_arrays(const zk_groth16_pk* pk, zk_groth16_arrays* out);
+
+/* Proof from the five MSM sums (packed affine: A 64 B | B2 128 B | L 64 B |
+ * H 64 B | B1 64 B = 384 B) and the blinding scalars, as the assembly of
+ * Groth16Prover::prove (groth16.cu:774-844); writes the 256-byte proof and,
+ * if `points` is not NULL, A | B | C packed affine. */
+int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, const void* sums,
+                        void* proof256, void* points);
+
 /* ==================================================================
  * Synthetic workloads (seeded, for benchmarks and tests)
  * ================================================================== */

@@ -114,11 +114,33 @@ def prove(pk, mats, witness, r, s):
     l_msm = O.msm_g1(pk["L"][:num_priv], witness[1 + pub: 1 + pub + num_priv]) if num_priv > 0 else np.zeros(8, np.uint64)
     h_msm = O.msm_g1(pk["H"][:n], h)
     b1_msm = O.msm_g1(pk["B1"], witness)
+    proof, A, B, C = assemble(pk, a_msm, b_msm, l_msm, h_msm, b1_msm, r, s)
+    return proof, A, B, C, h
+
+
+def assemble(pk, a_msm, b_msm, l_msm, h_msm, b1_msm, r, s):
+    """Proof points from the five MSM sums (groth16.cu:774-844)."""
     one, rr, ss = O.fr_from_int(1), O.fr_from_int(r), O.fr_from_int(s)
     A = O.msm_g1_naive(np.stack([pk["alpha1"], a_msm, pk["delta1"]]), np.stack([one, one, rr]))
     B = O.msm_g2_naive(np.stack([pk["beta2"], b_msm, pk["delta2"]]), np.stack([one, one, ss]))
     C = O.msm_g1_naive(np.stack([l_msm, h_msm, A, pk["beta1"], b1_msm]), np.stack([one, one, ss, rr, rr]))
-    return serialize(A, B, C), A, B, C, h
+    return serialize(A, B, C), A, B, C
+
+
+def coset_shift(log_n):
+    """compute_h's coset shift (groth16.cu:329-342): 5, or 7 when 5^n = 1; as an int."""
+    n = 1 << log_n
+    return 5 if pow(5, n, R) != 1 else 7
+
+
+def first_failing_constraint(mats, w_int, num_constraints, n, m):
+    """R1CS::verify_witness (src/prover/circuit.cuh:93-124): the first row with
+    (A w)(B w) != (C w), or -1."""
+    a, b, c = (matvec(e, w_int, n, m) for e in mats)
+    for i in range(num_constraints):
+        if a[i] * b[i] % R != c[i]:
+            return i
+    return -1
 
 
 def serialize(A, B, C):

@@ -1,0 +1,89 @@
+"""The per-rank work of zkml_dist.sharded_prove done by the CPU oracle
+(oracle/groth16_oracle.py), so that the split of a proof over ranks can be
+checked on CPU with gloo ranks.  Test infrastructure only."""
+import numpy as np
+import torch
+
+import groth16_oracle as G
+import pyoracle as O
+
+_KEYS = {"a": "A", "b2": "B2", "l": "L", "h": "H", "b1": "B1"}
+
+
+def _t(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint64).view(np.int64).copy())
+
+
+def _np(t):
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+class OracleProver:
+    def __init__(self, pk, mats):
+        self.pk, self.mats = pk, mats
+        self.n, self.log_n, self.m = pk["n"], pk["log_n"], pk["m"]
+        self.num_public, self.l, self.n_h = pk["num_public"], pk["l"], pk["n"]
+        self.g = O.fr_from_int(G.coset_shift(self.log_n))
+        self.zinv = pow((pow(G.coset_shift(self.log_n), self.n, G.R) - 1) % G.R, -1, G.R)
+
+    def error(self, msg):
+        return RuntimeError(msg)
+
+    def upload_witness(self, witness):
+        return _t(witness)
+
+    def matvec_rows(self, w, lo, hi):
+        w_int = [O.fr_to_int(x) for x in _np(w)]
+        out = np.zeros((3, hi - lo, 4), np.uint64)
+        for k, e in enumerate(self.mats):
+            full = G.matvec(e, w_int, self.n, self.m)
+            for i in range(lo, hi):
+                out[k, i - lo] = O.fr_from_int(full[i])
+        return _t(out)
+
+    def check_rows(self, abc, row0):
+        a, b, c = (_np(abc[k]) for k in range(3))
+        for i in range(a.shape[0]):
+            if O.fr_to_int(a[i]) * O.fr_to_int(b[i]) % G.R != O.fr_to_int(c[i]):
+                return row0 + i
+        return -1
+
+    def pad_rows(self, v, rows):
+        if v.shape[0] == rows:
+            return v
+        out = torch.zeros((rows, 4), dtype=v.dtype)
+        out[:v.shape[0]] = v
+        return out
+
+    def empty_vector(self):
+        return torch.zeros((self.n, 4), dtype=torch.int64)
+
+    def to_coset(self, v):
+        coeffs = O.ntt(_np(v), self.log_n, True)
+        return _t(O.coset_ntt(coeffs, self.log_n, False, self.g))
+
+    def h_from_cosets(self, a, b, c):
+        a, b, c = _np(a), _np(b), _np(c)
+        q = np.stack([O.fr_from_int((O.fr_to_int(a[i]) * O.fr_to_int(b[i]) - O.fr_to_int(c[i])) * self.zinv % G.R)
+                      for i in range(self.n)])
+        return _t(O.coset_ntt(q, self.log_n, True, self.g))
+
+    def msm(self, key, lo, hi, scalars, off):
+        pts = self.pk[_KEYS[key]][lo:hi]
+        words = 16 if key == "b2" else 8
+        if hi <= lo:
+            return np.zeros(words, np.uint64)
+        sc = _np(scalars)[off + lo:off + hi]
+        return O.msm_g2(pts, sc) if key == "b2" else O.msm_g1(pts, sc)
+
+    def add_g1(self, a, b):
+        one = O.fr_from_int(1)
+        return O.msm_g1_naive(np.stack([a, b]), np.stack([one, one]))
+
+    def add_g2(self, a, b):
+        one = O.fr_from_int(1)
+        return O.msm_g2_naive(np.stack([a, b]), np.stack([one, one]))
+
+    def assemble(self, r, s, sums):
+        q = np.asarray(sums, dtype=np.uint64)
+        return G.assemble(self.pk, q[0:8], q[8:24], q[24:32], q[32:40], q[40:48], r, s)

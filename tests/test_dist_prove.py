@@ -1,0 +1,99 @@
+"""A Groth16 proof split over gloo ranks on CPU (zkml_dist.sharded_prove): the
+oracle does each rank's device work (tests/oracle_prover.py), the ranks share
+rows, polynomials and MSM slices through real torch.distributed collectives,
+and the proof must be byte-identical to the one-device oracle proof.  A
+witness that breaks a constraint must fail on every rank with the first
+failing row, like R1CS::verify_witness."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CIRCUIT = (1, 1, 3, 3, 24, 10, 23, 2, 11)  # layers, channels, h, w, bits, shift, out_bits, dense, seed
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _circuit():
+    import zkml_b200 as Z
+    return Z.synth_conv_circuit(*CIRCUIT)
+
+
+def _worker(rank, world, port, corrupt, out_dir):
+    import sys
+    for sub in ("oracle", "cuda-zkml_b200", "tests"):
+        sys.path.insert(0, os.path.join(ROOT, sub))
+    import torch.distributed as dist
+
+    import groth16_oracle as G
+    import zkml_dist as D
+    from oracle_prover import OracleProver
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        c = _circuit()
+        mats = [c["A"], c["B"], c["C"]]
+        pk = G.setup(mats, c["num_constraints"], c["num_variables"], c["num_public"], G.toxic_deterministic())
+        w = np.array(c["witness"], copy=True)
+        if corrupt is not None:
+            w[corrupt] = w[corrupt] ^ np.uint64(1)  # still < r: the low limb of a reduced value
+        r, s = G.blinding_deterministic()
+        try:
+            proof = D.sharded_prove(OracleProver(pk, mats), D.TorchComm(), w, r, s)[0]
+            open(os.path.join(out_dir, f"proof{rank}.bin"), "wb").write(proof)
+        except RuntimeError as e:
+            open(os.path.join(out_dir, f"err{rank}.txt"), "w").write(str(e))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_prove_matches_one_device(tmp_path, world):
+    import groth16_oracle as G
+    mp.spawn(_worker, args=(world, _free_port(), None, str(tmp_path)), nprocs=world, join=True)
+    c = _circuit()
+    mats = [c["A"], c["B"], c["C"]]
+    pk = G.setup(mats, c["num_constraints"], c["num_variables"], c["num_public"], G.toxic_deterministic())
+    r, s = G.blinding_deterministic()
+    exp = G.prove(pk, mats, c["witness"], r, s)[0]
+    for rank in range(world):
+        assert open(tmp_path / f"proof{rank}.bin", "rb").read() == exp, rank
+
+
+def test_sharded_prove_rejects_bad_witness(tmp_path):
+    import groth16_oracle as G
+    import pyoracle as O
+    c = _circuit()
+    victim = c["num_variables"] - 1  # a private wire
+    mp.spawn(_worker, args=(2, _free_port(), victim, str(tmp_path)), nprocs=2, join=True)
+    mats = [c["A"], c["B"], c["C"]]
+    w = np.array(c["witness"], copy=True)
+    w[victim] ^= np.uint64(1)
+    n = G.domain(c["num_constraints"])[0]
+    row = G.first_failing_constraint(mats, [O.fr_to_int(x) for x in w], c["num_constraints"], n, c["num_variables"])
+    assert row >= 0
+    for rank in range(2):
+        msg = open(tmp_path / f"err{rank}.txt").read()
+        assert f"constraint {row} failed" in msg, msg
+
+
+def test_prove_plan_sizes():
+    import zkml_dist as D
+    s = D.prove_msm_sizes(m=10, num_public=3, l=6, n=16, n_h=16)
+    assert s == {"a": 10, "b2": 10, "l": 6, "h": 16, "b1": 10}
+    assert D.prove_msm_sizes(m=5, num_public=4, l=0, n=8, n_h=8)["l"] == 0
+    rec = np.arange(48, dtype=np.uint64)
+    assert np.array_equal(D.pack_sums(D.unpack_sums(rec)), rec)
+    assert D.row_chunk(16, 3) == 6 and D.row_chunk(4, 8) == 1

@@ -85,11 +85,17 @@ def test_pk_file_round_trip(small, tmp_path):
         Z.ProvingKey.load(bad)
 
 
-def test_wrong_witness_does_not_verify(small):
+def test_wrong_witness_does_not_verify(small, monkeypatch):
+    """With the witness check off (ZKML_SKIP_WITNESS_CHECK=1, as the reference
+    allows) a wrong witness still proves, to the oracle's bytes, and the proof
+    fails the check; with the check on, the prover refuses it."""
     c, mats, tox, pk_o, r1, pk = small
     bad = c["witness"].copy()
     bad[c["num_public"] + 5] = Z.fr_from_int(7)
     r, s = 11, 13
+    with pytest.raises(Z.ZkError, match="does not satisfy R1CS constraints"):
+        pk.prove(r1, bad, r, s)
+    monkeypatch.setenv("ZKML_SKIP_WITNESS_CHECK", "1")
     proof, A, B, C = pk.prove(r1, bad, r, s)
     proof_o, Ao, Bo, Co, h = G.prove(pk_o, mats, bad, r, s)
     assert proof == proof_o
