@@ -222,7 +222,14 @@ def bench_prove_sharded(Z, args, dev, world, rank):
         t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         times.append(float(t.item()) / 1e3)
+    # one more, untimed, with the device synchronised at each phase boundary
+    marks = []
+    D.sharded_prove(prover, comm, w, 12345, 67890, marks=marks)
+    mine = {marks[i][0]: round(1e3 * (marks[i][1] - marks[i - 1][1]), 3) for i in range(1, len(marks))}
+    per_rank = [None] * world
+    dist.all_gather_object(per_rank, mine)
     return {"config": f"synthetic CONV 2 x {args.prove_channels}ch x {args.prove_hw}x{args.prove_hw} + dense 10 (config 5 shape)",
+            "phase_ms_per_rank": per_rank,
             "constraints": c["num_constraints"], "variables": c["num_variables"], "public": c["num_public"],
             "nnz": [len(c["A"]), len(c["B"]), len(c["C"])], "log_n": r1.log_n,
             "prove_ms": 1e3 * statistics.median(times), "prove_ms_min": 1e3 * min(times), "steps": args.prove_steps,

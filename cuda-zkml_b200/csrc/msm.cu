@@ -50,7 +50,10 @@ struct MsmPlan {
     size_t max_segs = 0;
     uint32_t chunk = 0;  // buckets per reduce thread
     uint32_t tw = 0;     // reduce threads per window
+    uint32_t chunk2 = 0; // chunk results per second-level thread
+    uint32_t tw2 = 0;    // second-level threads per window
     uint32_t tiles = 0;  // scan tiles
+    bool agg = false;    // warp-aggregated bucket atomics (many equal digits)
 };
 
 static constexpr int kScanTile = 4096;  // 1024 threads x 4
@@ -87,18 +90,43 @@ static int choose_window_bits(size_t n, bool g2, const uint32_t* hist) {
     return best;
 }
 
-static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist) {
+static uint32_t pow2_clamp(double x, uint32_t lo, uint32_t hi) {
+    uint32_t p = lo;
+    while (p < hi && (double)p * 2 <= x) p *= 2;
+    return p;
+}
+
+static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist, int num_sms) {
     MsmPlan p;
     p.c = choose_window_bits(n, g2, hist);
     p.W = (255 + p.c - 1) / p.c;
     p.B = 1u << (p.c - 1);
     p.nb = (uint32_t)p.W * p.B;
-    p.seg = g2 ? 64 : 128;
     p.max_keys = n * (size_t)p.W;
-    p.max_segs = (p.max_keys + p.seg - 1) / p.seg;
-    p.chunk = std::min<uint32_t>(p.B, 32);
+    // Upper bound on the keys (nonzero signed digits): a b-bit scalar has at
+    // most ceil((b + 1) / c) of them.
+    size_t key_bound = p.max_keys;
+    if (hist) {
+        size_t d = 0;
+        for (int b = 1; b < 256; b++) d += (size_t)hist[b] * (size_t)((b + 1 + p.c - 1) / p.c);
+        key_bound = std::min(key_bound, d);
+    }
+    // Keys per accumulate thread and buckets per reduce thread: long serial
+    // chains when there is work for every SM many times over, short ones when
+    // there is little (a witness MSM, a shard of one), so that enough threads
+    // run to hide the latency of the dependent multiplications.
+    const double sms = (double)std::max(num_sms, 1);
+    p.seg = pow2_clamp((double)key_bound / (sms * 512.0), g2 ? 8 : 16, g2 ? 64 : 128);
+    p.max_segs = std::max<size_t>(1, (key_bound + p.seg - 1) / p.seg);
+    p.chunk = std::min<uint32_t>(p.B, pow2_clamp((double)p.nb / (sms * 256.0), 2, 32));
     p.tw = p.B / p.chunk;
+    p.chunk2 = std::min<uint32_t>(p.tw, pow2_clamp((double)p.W * p.tw / (sms * 64.0), 2, 16));
+    p.tw2 = p.tw / p.chunk2;
     p.tiles = (p.nb + 1 + kScanTile - 1) / kScanTile;
+    // Scalars 1..3 (0/1 range-check bits of a witness) all fall in window 0's
+    // first buckets: one atomic per warp and bucket instead of one per lane.
+    // For spread-out scalars the grouping costs more than it saves.
+    p.agg = hist && ((size_t)hist[1] + hist[2]) * 256 >= n;
     return p;
 }
 
@@ -141,8 +169,12 @@ __global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restri
 
 // Digits are stored window-major (digits[w * n + i] = sign << 31 | bucket + 1,
 // 0 for a zero digit) so that the scatter can run one window after another.
+// The lanes of a warp that hit the same bucket add their count with one atomic
+// (witness scalars put most digits in one bucket: 0/1 range-check bits).
+template <bool kAgg>
 __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
                                  uint32_t* __restrict__ counts, uint32_t* __restrict__ digits) {
+    const uint32_t lane = threadIdx.x & 31;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         Fr s;
         fload_nc(s, scalars + i);
@@ -150,11 +182,17 @@ __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c
         uint32_t carry = 0;
         for (int w = 0; w < W; w++) {
             const int d = next_digit(s.v, c, carry);
-            uint32_t code = 0;
+            uint32_t code = 0, key = 0xffffffffu;
             if (d) {
                 const uint32_t b = (uint32_t)(d < 0 ? -d : d) - 1;
-                atomicAdd(&counts[(uint32_t)w * B + b], 1u);
+                key = (uint32_t)w * B + b;
                 code = (d < 0 ? 0x80000000u : 0u) | (b + 1);
+            }
+            if (kAgg) {
+                const uint32_t peers = __match_any_sync(__activemask(), key);
+                if (d && lane == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&counts[key], (uint32_t)__popc(peers));
+            } else if (d) {
+                atomicAdd(&counts[key], 1u);
             }
             digits[(size_t)w * n + i] = code;
         }
@@ -165,16 +203,28 @@ __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c
 // so the blocks resident at any time touch one window's cursors (2^(c-1) words)
 // and key range (about n words), which stay in L2; scattering all windows at once
 // wrote partial sectors all over the whole key array.
+template <bool kAgg>
 __global__ void __launch_bounds__(256) msm_scatter_kernel(const uint32_t* __restrict__ digits, size_t n, uint32_t B,
                                                           uint32_t blocks_per_window, uint32_t* __restrict__ cursors,
                                                           uint32_t* __restrict__ keys) {
     const uint32_t w = blockIdx.x / blocks_per_window;
     const size_t i = (size_t)(blockIdx.x % blocks_per_window) * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const uint32_t code = digits[(size_t)w * n + i];
+    const uint32_t code = i < n ? digits[(size_t)w * n + i] : 0u;
+    const uint32_t key = code ? w * B + (code & 0x7fffffffu) - 1 : 0xffffffffu;
+    if (!kAgg) {
+        if (!code) return;
+        keys[atomicAdd(&cursors[key], 1u)] = (code & 0x80000000u) | (uint32_t)i;
+        return;
+    }
+    // lanes with the same bucket take consecutive slots from one atomic
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t peers = __match_any_sync(0xffffffffu, key);
     if (!code) return;
-    const uint32_t pos = atomicAdd(&cursors[w * B + (code & 0x7fffffffu) - 1], 1u);
-    keys[pos] = (code & 0x80000000u) | (uint32_t)i;
+    const uint32_t leader = (uint32_t)(__ffs(peers) - 1);
+    uint32_t base = 0;
+    if (lane == leader) base = atomicAdd(&cursors[key], (uint32_t)__popc(peers));
+    base = __shfl_sync(peers, base, leader);
+    keys[base + (uint32_t)__popc(peers & ((1u << lane) - 1))] = (code & 0x80000000u) | (uint32_t)i;
 }
 
 // ------------------------------------------------------------------ scan
@@ -325,7 +375,9 @@ __global__ void __launch_bounds__(128) msm_accumulate_kernel(
 // "last" slot) and V_j = "first" slot of sa + j.  Round r of a binary tree adds
 // V_{j + 2^r} into V_j for every j divisible by 2^(r + 1), so even a bucket
 // holding millions of keys (the top window, or the many 0/1 scalars of a real
-// witness) is summed in log2(m) parallel steps instead of m serial adds.
+// witness) is summed in log2(m) parallel steps instead of m serial adds.  (A
+// wider tree needs fewer launches but puts radix - 1 dependent additions in
+// each round; on deep trees that measured slower.)
 template <class Cv>
 __global__ void msm_fixup_round_kernel(const uint32_t* __restrict__ offsets, const uint32_t* __restrict__ first_bucket,
                                        const uint32_t* __restrict__ last_bucket, size_t nseg, uint32_t seg, uint32_t stride,
@@ -375,10 +427,17 @@ __global__ void msm_fixup_final_kernel(const uint32_t* __restrict__ offsets, uin
 }
 
 // ------------------------------------------------------------------ reduce
-// thread (w, j): buckets [lo, lo + chunk) of window w, weight b + 1.
+// The window sum is T_w = sum_b (b + 1) S_b over the bucket sums S_b.  Level 1:
+// thread (w, j) takes the buckets [lo, lo + chunk), lo = j chunk, and forms
+//   acc_j = sum (b - lo + 1) S_b   and   run_j = sum S_b
+// by running sums, so that T_w = sum_j acc_j + chunk * U, U = sum_j j run_j.
+// Level 2 forms U the same way over groups of chunk2 chunk results; only its
+// few threads pay a double-and-add for their group's start, and the window
+// kernel adds the pieces (chunk is a power of two: U is doubled log2(chunk)
+// times).  One level with a double-and-add per chunk did ~30% more additions.
 template <class Cv>
 __global__ void msm_reduce_kernel(const uint32_t* __restrict__ offsets, const uint8_t* __restrict__ bucket_sums, int W, uint32_t B,
-                                  uint32_t chunk, uint32_t tw, uint8_t* __restrict__ chunk_sums) {
+                                  uint32_t chunk, uint32_t tw, uint8_t* __restrict__ chunk_acc, uint8_t* __restrict__ chunk_run) {
     using F = typename Cv::F;
     uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
     if (tid >= (uint32_t)W * tw) return;
@@ -395,7 +454,33 @@ __global__ void msm_reduce_kernel(const uint32_t* __restrict__ offsets, const ui
         }
         add(acc, run);
     }
-    // acc = sum (b - lo + 1) S_b; add lo * run
+    store_xyzz(chunk_acc + (size_t)tid * Cv::kXyzzBytes, acc);
+    store_xyzz(chunk_run + (size_t)tid * Cv::kXyzzBytes, run);
+}
+
+// thread (w, k): chunk results [k chunk2, (k + 1) chunk2) of window w ->
+//   x_k = sum acc_j   and   u_k = sum_j j run_j
+template <class Cv>
+__global__ void msm_reduce2_kernel(const uint8_t* __restrict__ chunk_acc, const uint8_t* __restrict__ chunk_run, int W, uint32_t tw,
+                                   uint32_t chunk2, uint32_t tw2, uint8_t* __restrict__ part_x, uint8_t* __restrict__ part_u) {
+    using F = typename Cv::F;
+    uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tid >= (uint32_t)W * tw2) return;
+    uint32_t w = tid / tw2, k = tid % tw2;
+    uint32_t lo = k * chunk2;
+    Xyzz<F> x, run, y, q;
+    set_identity(x);
+    set_identity(run);
+    set_identity(y);
+    for (uint32_t j = lo + chunk2; j-- > lo;) {
+        const size_t r = (size_t)w * tw + j;
+        add(y, run);  // before adding run_j: y = sum (j - lo) run_j
+        load_xyzz(q, chunk_run + r * Cv::kXyzzBytes);
+        add(run, q);
+        load_xyzz(q, chunk_acc + r * Cv::kXyzzBytes);
+        add(x, q);
+    }
+    // u_k = y + lo run
     if (lo && !is_identity(run)) {
         Xyzz<F> m;
         set_identity(m);
@@ -406,42 +491,61 @@ __global__ void msm_reduce_kernel(const uint32_t* __restrict__ offsets, const ui
             m = d;
             if ((lo >> bit) & 1) add(m, run);
         }
-        add(acc, m);
+        add(y, m);
     }
-    store_xyzz(chunk_sums + (size_t)tid * Cv::kXyzzBytes, acc);
+    store_xyzz(part_x + (size_t)tid * Cv::kXyzzBytes, x);
+    store_xyzz(part_u + (size_t)tid * Cv::kXyzzBytes, y);
 }
 
-// one block per window: tree-sum of the tw chunk results
+// one block per window: tree sums of the x_k and of the u_k, then
+// T_w = sum x_k + chunk * sum u_k
 template <class Cv>
-constexpr int win_threads() { return std::is_same<Cv, G2>::value ? 256 : 512; }
+constexpr int win_threads() { return std::is_same<Cv, G2>::value ? 128 : 256; }
 
 template <class Cv>
-__global__ void __launch_bounds__(win_threads<Cv>()) msm_window_kernel(const uint8_t* __restrict__ chunk_sums, uint32_t tw, uint8_t* __restrict__ scratch,
-                                  uint8_t* __restrict__ window_sums) {
+__global__ void __launch_bounds__(win_threads<Cv>()) msm_window_kernel(const uint8_t* __restrict__ part_x, const uint8_t* __restrict__ part_u,
+                                                                       uint32_t tw2, int log_chunk, uint8_t* __restrict__ scratch,
+                                                                       uint8_t* __restrict__ window_sums) {
     using F = typename Cv::F;
     const uint32_t w = blockIdx.x;
-    const uint8_t* src = chunk_sums + (size_t)w * tw * Cv::kXyzzBytes;
-    uint8_t* tmp = scratch + (size_t)w * blockDim.x * Cv::kXyzzBytes;
-    Xyzz<F> acc, q;
-    set_identity(acc);
-    for (uint32_t j = threadIdx.x; j < tw; j += blockDim.x) {
-        load_xyzz(q, src + (size_t)j * Cv::kXyzzBytes);
-        add(acc, q);
+    uint8_t* tx = scratch + (size_t)w * 2 * blockDim.x * Cv::kXyzzBytes;
+    uint8_t* tu = tx + (size_t)blockDim.x * Cv::kXyzzBytes;
+    Xyzz<F> x, u, q;
+    set_identity(x);
+    set_identity(u);
+    for (uint32_t k = threadIdx.x; k < tw2; k += blockDim.x) {
+        const size_t r = (size_t)w * tw2 + k;
+        load_xyzz(q, part_x + r * Cv::kXyzzBytes);
+        add(x, q);
+        load_xyzz(q, part_u + r * Cv::kXyzzBytes);
+        add(u, q);
     }
-    store_xyzz(tmp + (size_t)threadIdx.x * Cv::kXyzzBytes, acc);
+    store_xyzz(tx + (size_t)threadIdx.x * Cv::kXyzzBytes, x);
+    store_xyzz(tu + (size_t)threadIdx.x * Cv::kXyzzBytes, u);
     __syncthreads();
     for (uint32_t s = blockDim.x / 2; s > 0; s >>= 1) {
         if (threadIdx.x < s) {
-            load_xyzz(acc, tmp + (size_t)threadIdx.x * Cv::kXyzzBytes);
-            load_xyzz(q, tmp + (size_t)(threadIdx.x + s) * Cv::kXyzzBytes);
-            add(acc, q);
-            store_xyzz(tmp + (size_t)threadIdx.x * Cv::kXyzzBytes, acc);
+            load_xyzz(x, tx + (size_t)threadIdx.x * Cv::kXyzzBytes);
+            load_xyzz(q, tx + (size_t)(threadIdx.x + s) * Cv::kXyzzBytes);
+            add(x, q);
+            store_xyzz(tx + (size_t)threadIdx.x * Cv::kXyzzBytes, x);
+            load_xyzz(u, tu + (size_t)threadIdx.x * Cv::kXyzzBytes);
+            load_xyzz(q, tu + (size_t)(threadIdx.x + s) * Cv::kXyzzBytes);
+            add(u, q);
+            store_xyzz(tu + (size_t)threadIdx.x * Cv::kXyzzBytes, u);
         }
         __syncthreads();
     }
     if (threadIdx.x == 0) {
-        load_xyzz(acc, tmp);
-        store_xyzz(window_sums + (size_t)w * Cv::kXyzzBytes, acc);
+        load_xyzz(x, tx);
+        load_xyzz(u, tu);
+        for (int i = 0; i < log_chunk; i++) {
+            Xyzz<F> d;
+            dbl(d, u);
+            u = d;
+        }
+        add(x, u);
+        store_xyzz(window_sums + (size_t)w * Cv::kXyzzBytes, x);
     }
 }
 
@@ -608,14 +712,20 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     uint32_t* first_bucket = ar.take<uint32_t>(P.max_segs);
     uint32_t* last_bucket = ar.take<uint32_t>(P.max_segs);
     uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
-    uint8_t* chunk_sums = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    uint8_t* chunk_acc = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    uint8_t* chunk_run = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    uint8_t* part_x = ar.take<uint8_t>((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
+    uint8_t* part_u = ar.take<uint8_t>((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
     constexpr int kWinThreads = win_threads<Cv>();
-    uint8_t* win_tmp = ar.take<uint8_t>((size_t)P.W * kWinThreads * Cv::kXyzzBytes);
+    uint8_t* win_tmp = ar.take<uint8_t>((size_t)P.W * 2 * kWinThreads * Cv::kXyzzBytes);
 
     const int sms = ctx->num_sms;
     ZK_TRY_CUDA(cudaEventRecord(ph[0], st));
     ZK_TRY_CUDA(cudaMemsetAsync(counts, 0, (P.nb + 1) * sizeof(uint32_t), st));
-    msm_count_kernel<<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts, digits);
+    if (P.agg)
+        msm_count_kernel<true><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts, digits);
+    else
+        msm_count_kernel<false><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts, digits);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[1], st));
     scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums);
@@ -627,7 +737,10 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     ZK_TRY_CUDA(cudaEventRecord(ph[2], st));
     {
         const uint32_t bpw = (uint32_t)((n + 255) / 256);
-        msm_scatter_kernel<<<bpw * (uint32_t)P.W, 256, 0, st>>>(digits, n, P.B, bpw, cursors, keys);
+        if (P.agg)
+            msm_scatter_kernel<true><<<bpw * (uint32_t)P.W, 256, 0, st>>>(digits, n, P.B, bpw, cursors, keys);
+        else
+            msm_scatter_kernel<false><<<bpw * (uint32_t)P.W, 256, 0, st>>>(digits, n, P.B, bpw, cursors, keys);
     }
     lc++;
     ZK_TRY_CUDA(cudaMemsetAsync(first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
@@ -645,7 +758,7 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     ZK_TRY_CUDA(cudaEventRecord(ph[4], st));
     {
         const unsigned blocks = (unsigned)((P.max_segs + 127) / 128);
-        for (uint32_t stride = 1; stride < P.max_segs; stride <<= 1) {
+        for (uint64_t stride = 1; stride < P.max_segs; stride <<= 1) {
             msm_fixup_round_kernel<Cv><<<blocks, 128, 0, st>>>(offsets, first_bucket, last_bucket, P.max_segs, P.seg, stride,
                                                                 part_first, part_last);
             lc++;
@@ -656,11 +769,14 @@ static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_point
     ZK_TRY_CUDA(cudaEventRecord(ph[5], st));
     {
         uint32_t total = (uint32_t)P.W * P.tw;
-        msm_reduce_kernel<Cv><<<(total + 127) / 128, 128, 0, st>>>(offsets, buckets, P.W, P.B, P.chunk, P.tw, chunk_sums);
+        msm_reduce_kernel<Cv><<<(total + 127) / 128, 128, 0, st>>>(offsets, buckets, P.W, P.B, P.chunk, P.tw, chunk_acc, chunk_run);
+        lc++;
+        uint32_t total2 = (uint32_t)P.W * P.tw2;
+        msm_reduce2_kernel<Cv><<<(total2 + 127) / 128, 128, 0, st>>>(chunk_acc, chunk_run, P.W, P.tw, P.chunk2, P.tw2, part_x, part_u);
         lc++;
     }
     ZK_TRY_CUDA(cudaEventRecord(ph[6], st));
-    msm_window_kernel<Cv><<<P.W, kWinThreads, 0, st>>>(chunk_sums, P.tw, win_tmp, windows_dev);
+    msm_window_kernel<Cv><<<P.W, kWinThreads, 0, st>>>(part_x, part_u, P.tw2, 31 - __builtin_clz(P.chunk), win_tmp, windows_dev);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[7], st));
     ZK_TRY_CUDA(cudaGetLastError());
@@ -675,8 +791,9 @@ static size_t pipeline_bytes(const MsmPlan& P) {
     b += 2 * Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
     b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes) + 2 * Arena::round(P.max_segs * 4);
     b += Arena::round((size_t)P.nb * Cv::kXyzzBytes);
-    b += Arena::round((size_t)P.W * P.tw * Cv::kXyzzBytes);
-    b += Arena::round((size_t)P.W * kWinThreads * Cv::kXyzzBytes);
+    b += 2 * Arena::round((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    b += 2 * Arena::round((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
+    b += Arena::round((size_t)P.W * 2 * kWinThreads * Cv::kXyzzBytes);
     return b;
 }
 
@@ -721,7 +838,7 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     uint32_t hist[256];
     std::memcpy(hist, hist_host, sizeof hist);
-    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist);
+    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
     stats.window_bits = P.c;
     stats.num_windows = P.W;
 

@@ -95,25 +95,34 @@ def unpack_sums(rec):
     return out
 
 
-def sharded_prove(prover, comm, witness, r, s, timer=None):
+def sharded_prove(prover, comm, witness, r, s, marks=None):
     """One Groth16 proof with the work of `prover` (this rank's device) shared
     over `comm`'s ranks.  witness: (m, 4) uint64 Montgomery (host); r, s ints.
-    Returns (proof bytes, A, B, C) on every rank."""
+    Returns (proof bytes, A, B, C) on every rank.  `marks`: optional list that
+    receives (phase, seconds) pairs, the device synchronised at each mark
+    (for profiling only: it removes the overlap between phases)."""
     rank, world = comm.rank, comm.world
+    mark = (lambda name: marks.append((name, prover.sync_time()))) if marks is not None else (lambda name: None)
+    mark("start")
     n, m, pub = prover.n, prover.m, prover.num_public
     sizes = prove_msm_sizes(m, pub, prover.l, n, prover.n_h)
     S = row_chunk(n, world)
     lo, hi = min(n, rank * S), min(n, (rank + 1) * S)
     w = prover.upload_witness(witness)
+    mark("witness")
     abc = prover.matvec_rows(w, lo, hi)          # (3, hi - lo, 4)
+    mark("matvec")
     bad = prover.check_rows(abc, lo) if witness_check_enabled() else -1
     bad = comm.all_reduce_min(bad if bad >= 0 else _NO_ROW, like=w)
+    mark("check")
     if bad != _NO_ROW:
         raise prover.error(f"[Prove] Witness does not satisfy R1CS constraints (constraint {bad} failed)")
     full = [comm.all_gather_rows(prover.pad_rows(abc[k], S), S)[:n] for k in range(3)]
+    mark("gather")
     owners = [k % world for k in range(3)]
     cosets = [prover.to_coset(full[k]) if owners[k] == rank else prover.empty_vector() for k in range(3)]
     del full, abc
+    mark("cosets")
 
     def witness_msms():
         out = {}
@@ -123,21 +132,22 @@ def sharded_prove(prover, comm, witness, r, s, timer=None):
             out[key] = prover.msm(key, a, b, w, off)
         return out
 
-    sums = {}
-    first = rank not in owners  # ranks without a polynomial start their MSM slices at once
-    if first:
-        sums.update(witness_msms())
+    sums = witness_msms()  # before the broadcasts: they wait for the slowest polynomial owner
+    mark("witness_msms")
     for k in range(3):
         comm.broadcast(cosets[k], owners[k])
+    mark("broadcast")
     h = prover.h_from_cosets(*cosets)
     del cosets
-    if not first:
-        sums.update(witness_msms())
+    mark("h")
     a, b = shard_bounds(sizes["h"], rank, world)
     sums["h"] = prover.msm("h", a, b, h, 0)
+    mark("h_msm")
     parts = [unpack_sums(p) for p in comm.all_gather_points(pack_sums(sums))]
     total = {k: combine([p[k] for p in parts], prover.add_g2 if k == "b2" else prover.add_g1) for k in MSM_ORDER}
-    return prover.assemble(r, s, pack_sums(total))
+    out = prover.assemble(r, s, pack_sums(total))
+    mark("assemble")
+    return out
 
 
 class TorchComm:
@@ -242,12 +252,24 @@ class CudaProver:
         return self.Z.ZkError(self.Z.ZK_ERR_INVALID, msg)
 
     def upload_witness(self, witness):
+        """Host witness -> device.  A witness already in pinned memory is copied
+        straight from it; otherwise it is staged through a pinned buffer."""
         import torch
         witness = np.ascontiguousarray(witness, dtype=np.uint64)
-        if self._pinned is None or self._pinned.shape[0] != witness.shape[0]:
-            self._pinned = torch.empty((witness.shape[0], 4), dtype=torch.int64, pin_memory=True)
-        self._pinned.numpy()[:] = witness.view(np.int64)
-        return self._pinned.to(torch.device("cuda", self.device), non_blocking=True)
+        src = torch.from_numpy(witness.view(np.int64))
+        if not src.is_pinned():
+            if self._pinned is None or self._pinned.shape[0] != witness.shape[0]:
+                self._pinned = torch.empty((witness.shape[0], 4), dtype=torch.int64, pin_memory=True)
+            self._pinned.copy_(src)
+            src = self._pinned
+        return src.to(torch.device("cuda", self.device), non_blocking=True)
+
+    def sync_time(self):
+        import time
+
+        import torch
+        torch.cuda.synchronize(self.device)
+        return time.perf_counter()
 
     def matvec_rows(self, w, lo, hi):
         return self.r1cs.matvec_rows(w, lo, hi)

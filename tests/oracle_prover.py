@@ -29,6 +29,10 @@ class OracleProver:
     def error(self, msg):
         return RuntimeError(msg)
 
+    def sync_time(self):
+        import time
+        return time.perf_counter()
+
     def upload_witness(self, witness):
         return _t(witness)
 
