@@ -83,8 +83,11 @@ def witness_check_enabled():
     return os.environ.get("ZKML_SKIP_WITNESS_CHECK") != "1"
 
 
-def pack_sums(sums):
-    return np.concatenate([np.asarray(sums[k], dtype=np.uint64).reshape(-1) for k in MSM_ORDER])
+def pack_sums(sums, times=()):
+    """48 words of sums (A, B2, L, H, B1), then any float64 timings as their bits."""
+    parts = [np.asarray(sums[k], dtype=np.uint64).reshape(-1) for k in MSM_ORDER]
+    parts.append(np.asarray(times, dtype=np.float64).view(np.uint64))
+    return np.concatenate(parts)
 
 
 def unpack_sums(rec):
@@ -92,7 +95,43 @@ def unpack_sums(rec):
     for k in MSM_ORDER:
         out[k] = rec[o:o + _WORDS[k]]
         o += _WORDS[k]
+    out["times"] = np.asarray(rec[o:], dtype=np.uint64).view(np.float64)
     return out
+
+
+def weighted_bounds(n, shares, rank):
+    """[start, end) of rank's slice of n items when the ranks take the
+    fractions `shares` (summing to 1); contiguous, covering [0, n)."""
+    acc = np.concatenate([[0.0], np.cumsum(np.asarray(shares, dtype=np.float64))])
+    acc /= acc[-1] if acc[-1] > 0 else 1.0
+    cut = [int(round(x * n)) for x in acc]
+    cut[-1] = n
+    return cut[rank], cut[rank + 1]
+
+
+def balance_shares(poly_s, msm_s, shares, damping=0.5):
+    """Fractions of the witness MSMs for the next proof.  Rank r spends poly_s[r]
+    on its polynomials and msm_s[r] on its share shares[r] of the witness MSMs
+    before the coset broadcasts, which wait for the slowest rank; choose new
+    shares s with poly_s[r] + s_r * C equal where possible (C = sum msm_s, the
+    whole witness-MSM time), s_r >= 0, and move halfway there."""
+    poly = np.asarray(poly_s, dtype=np.float64)
+    C = float(np.sum(msm_s))
+    world = len(poly)
+    if C <= 0:
+        return list(shares)
+    active = np.ones(world, dtype=bool)
+    target = np.zeros(world)
+    for _ in range(world):  # water-filling: ranks above the level take nothing
+        T = (poly[active].sum() + C) / active.sum()
+        target = np.where(active, (T - poly) / C, 0.0)
+        if (target >= 0).all():
+            break
+        active &= target > 0
+    target = np.clip(target, 0.0, None)
+    target /= target.sum()
+    new = damping * np.asarray(shares, dtype=np.float64) + (1 - damping) * target
+    return [float(x) for x in new / new.sum()]
 
 
 def sharded_prove(prover, comm, witness, r, s, marks=None):
@@ -106,9 +145,16 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     mark("start")
     n, m, pub = prover.n, prover.m, prover.num_public
     sizes = prove_msm_sizes(m, pub, prover.l, n, prover.n_h)
+    shares = getattr(prover, "witness_shares", None)
+    if shares is None or len(shares) != world:
+        shares = [1.0 / world] * world
     S = row_chunk(n, world)
     lo, hi = min(n, rank * S), min(n, (rank + 1) * S)
-    w = prover.upload_witness(witness)
+    # every rank needs the whole witness (the matvec reads any column): each
+    # uploads one slice and the slices are all-gathered over the interconnect
+    Sw = row_chunk(m, world)
+    wlo, whi = min(m, rank * Sw), min(m, (rank + 1) * Sw)
+    w = comm.all_gather_rows(prover.pad_rows(prover.upload_witness(witness[wlo:whi]), Sw), Sw)[:m]
     mark("witness")
     abc = prover.matvec_rows(w, lo, hi)          # (3, hi - lo, 4)
     mark("matvec")
@@ -120,19 +166,21 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     full = [comm.all_gather_rows(prover.pad_rows(abc[k], S), S)[:n] for k in range(3)]
     mark("gather")
     owners = [k % world for k in range(3)]
+    t_poly = prover.timer()
     cosets = [prover.to_coset(full[k]) if owners[k] == rank else prover.empty_vector() for k in range(3)]
+    t_poly = prover.elapsed(t_poly)
     del full, abc
     mark("cosets")
 
-    def witness_msms():
-        out = {}
-        for key in ("a", "b2", "l", "b1"):
-            a, b = shard_bounds(sizes[key], rank, world)
-            off = 1 + pub if key == "l" else 0
-            out[key] = prover.msm(key, a, b, w, off)
-        return out
-
-    sums = witness_msms()  # before the broadcasts: they wait for the slowest polynomial owner
+    # the witness MSMs come before the broadcasts, which wait for the slowest
+    # polynomial owner: owners take smaller slices (balance_shares)
+    t_msm = prover.timer()
+    sums = {}
+    for key in ("a", "b2", "l", "b1"):
+        a, b = weighted_bounds(sizes[key], shares, rank)
+        off = 1 + pub if key == "l" else 0
+        sums[key] = prover.msm(key, a, b, w, off)
+    t_msm = prover.elapsed(t_msm)
     mark("witness_msms")
     for k in range(3):
         comm.broadcast(cosets[k], owners[k])
@@ -143,8 +191,9 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     a, b = shard_bounds(sizes["h"], rank, world)
     sums["h"] = prover.msm("h", a, b, h, 0)
     mark("h_msm")
-    parts = [unpack_sums(p) for p in comm.all_gather_points(pack_sums(sums))]
+    parts = [unpack_sums(p) for p in comm.all_gather_points(pack_sums(sums, (t_poly(), t_msm())))]
     total = {k: combine([p[k] for p in parts], prover.add_g2 if k == "b2" else prover.add_g1) for k in MSM_ORDER}
+    prover.witness_shares = balance_shares([p["times"][0] for p in parts], [p["times"][1] for p in parts], shares)
     out = prover.assemble(r, s, pack_sums(total))
     mark("assemble")
     return out
@@ -270,6 +319,24 @@ class CudaProver:
         import torch
         torch.cuda.synchronize(self.device)
         return time.perf_counter()
+
+    def timer(self):
+        """Start a device-time measurement on the current stream."""
+        import torch
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def elapsed(self, start):
+        """Stop it; returns a callable giving the seconds, read once the work is done."""
+        import torch
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+
+        def read():
+            end.synchronize()
+            return start.elapsed_time(end) / 1e3
+        return read
 
     def matvec_rows(self, w, lo, hi):
         return self.r1cs.matvec_rows(w, lo, hi)

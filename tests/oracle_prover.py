@@ -33,6 +33,15 @@ class OracleProver:
         import time
         return time.perf_counter()
 
+    def timer(self):
+        import time
+        return time.perf_counter()
+
+    def elapsed(self, start):
+        import time
+        dt = time.perf_counter() - start
+        return lambda: dt
+
     def upload_witness(self, witness):
         return _t(witness)
 

@@ -97,3 +97,28 @@ def test_prove_plan_sizes():
     rec = np.arange(48, dtype=np.uint64)
     assert np.array_equal(D.pack_sums(D.unpack_sums(rec)), rec)
     assert D.row_chunk(16, 3) == 6 and D.row_chunk(4, 8) == 1
+
+
+def test_weighted_bounds_cover():
+    import zkml_dist as D
+    for n in (0, 1, 7, 1000, 3244043):
+        for shares in ([1.0], [0.5, 0.5], [0.2, 0.3, 0.5], [0.0, 1.0, 0.0], [0.01] * 3 + [0.97 / 5] * 5):
+            spans = [D.weighted_bounds(n, shares, r) for r in range(len(shares))]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(len(spans) - 1))
+            assert all(b >= a for a, b in spans)
+
+
+def test_balance_shares_moves_work_off_polynomial_owners():
+    import zkml_dist as D
+    # two ranks: rank 0 owns two polynomials (2 x 2.9 ms), rank 1 one; 7.7 ms of witness MSMs
+    s = [0.5, 0.5]
+    for _ in range(12):
+        s = D.balance_shares([5.8, 2.9], [7.7 * x for x in s], s)
+    assert abs(s[0] - (5.8 + 2.9 + 7.7) / 2 / 7.7 + 5.8 / 7.7) < 0.02  # poly + share * C equal on both ranks
+    # eight ranks: the three owners end up with (almost) nothing
+    s = [1 / 8] * 8
+    for _ in range(12):
+        s = D.balance_shares([2.9] * 3 + [0.0] * 5, [7.7 * x for x in s], s)
+    assert max(s[:3]) < 0.01 and abs(sum(s) - 1) < 1e-9
+    assert D.balance_shares([0.0], [1.0], [1.0]) == [1.0]
