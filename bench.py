@@ -314,10 +314,13 @@ def run_b200(args):
                 "msm_whole_frac_ref_ops": 256 * msm_ref_ops(n) / (stats[-1]["total_device_ms"] / 1e3) / imad}
     prof = os.path.join(ROOT, "profiles", "msm_accumulate_g1_traffic.json")
     if os.path.exists(prof):
+        # DRAM bytes per addition from one ncu capture of the accumulate kernel,
+        # scaled by this launch's additions (the capture's points exceed L2 too)
         try:
             tr = json.load(open(prof))
-            if tr.get("log_n") == args.log_n:
-                roofline["traffic"] = tr["dram_bytes_per_launch"]
+            roofline["traffic"] = tr["bytes_per_addition"] * adds
+            roofline["traffic_source"] = (f"ncu dram__bytes_read+write of one 2^{tr['capture_log_n']} launch "
+                                          f"({tr['bytes_per_addition']:.1f} B per addition) x {adds} additions")
         except (OSError, ValueError, KeyError):
             pass
 

@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -157,6 +158,11 @@ struct zk_groth16_pk {
     unsigned long long* d_bad = nullptr;  // first failing constraint of the witness check
     unsigned long long* h_bad = nullptr;  // pinned host copy
     uint64_t n_buf = 0;
+    // 2^i delta1 and 2^i delta2 (i < 256), built on first use: r delta1 and
+    // s delta2 of every proof as sums of table entries
+    mutable std::mutex tab_mu;
+    mutable std::vector<zkh::Xyzz<zkh::Fe>> d1_pow;
+    mutable std::vector<zkh::Xyzz<zkh::Fp2>> d2_pow;
 };
 
 namespace zk {
@@ -462,48 +468,79 @@ static int ensure_prover_buffers(zk_groth16_pk* pk, uint64_t n, int m) {
     return ZK_OK;
 }
 
+// k * P from the table tab[i] = 2^i P: one addition per set bit of k
+template <class F>
+static void fixed_mul(zkh::Xyzz<F>& out, const std::vector<zkh::Xyzz<F>>& tab, const uint64_t k_std[4]) {
+    zkh::set_identity(out);
+    for (int bit = 0; bit < 256; bit++)
+        if ((k_std[bit >> 6] >> (bit & 63)) & 1) zkh::add(out, tab[bit]);
+}
+
+template <class F>
+static void build_pow2(std::vector<zkh::Xyzz<F>>& tab, const uint64_t* base) {
+    zkh::Xyzz<F> p, d;
+    load_aff(p, base);
+    tab.resize(256);
+    for (int i = 0; i < 256; i++) {
+        tab[i] = p;
+        zkh::dbl(d, p);
+        p = d;
+    }
+}
+
 // Proof points from the five MSM sums (groth16.cu:774-844):
 //   A = alpha1 + sum_A + r delta1
 //   B = beta2 + sum_B2 + s delta2
 //   C = sum_L + sum_H + s A + r (beta1 + sum_B1)
 // (the reference folds r s delta1 into s A, with A the affine proof point)
-static void assemble(const zk_groth16_pk* pk, const zkh::Fe& r, const zkh::Fe& s, const uint64_t a_msm[8], const uint64_t b_msm[16],
-                     const uint64_t l_msm[8], const uint64_t h_msm[8], const uint64_t b1_msm[8], uint64_t outA[8], uint64_t outB[16],
-                     uint64_t outC[8]) {
+static void assemble_xyzz(const zk_groth16_pk* pk, const zkh::Fe& r, const zkh::Fe& s, const zkh::Xyzz<zkh::Fe>& a_msm,
+                          const zkh::Xyzz<zkh::Fp2>& b_msm, const zkh::Xyzz<zkh::Fe>& l_msm, const zkh::Xyzz<zkh::Fe>& h_msm,
+                          const zkh::Xyzz<zkh::Fe>& b1_msm, uint64_t outA[8], uint64_t outB[16], uint64_t outC[8]) {
     uint64_t rs[4], ss[4];
     zkh::to_std(zkh::kR, rs, r);
     zkh::to_std(zkh::kR, ss, s);
     using P1 = zkh::Xyzz<zkh::Fe>;
     using P2 = zkh::Xyzz<zkh::Fp2>;
+    {
+        std::lock_guard<std::mutex> lock(pk->tab_mu);
+        if (pk->d1_pow.empty()) build_pow2(pk->d1_pow, pk->delta1);
+        if (pk->d2_pow.empty()) build_pow2(pk->d2_pow, pk->delta2);
+    }
     P1 A, t1;
     load_aff(A, pk->alpha1);
-    load_aff(t1, a_msm);
-    zkh::add(A, t1);
-    load_aff(t1, pk->delta1);
-    zkh::smul(t1, P1(t1), rs);
+    zkh::add(A, a_msm);
+    fixed_mul(t1, pk->d1_pow, rs);
     zkh::add(A, t1);
     store_aff(outA, A);
     P2 Bp, t2;
     load_aff(Bp, pk->beta2);
-    load_aff(t2, b_msm);
-    zkh::add(Bp, t2);
-    load_aff(t2, pk->delta2);
-    zkh::smul(t2, P2(t2), ss);
+    zkh::add(Bp, b_msm);
+    fixed_mul(t2, pk->d2_pow, ss);
     zkh::add(Bp, t2);
     store_aff(outB, Bp);
-    P1 Cp, Aaff, b1;
-    load_aff(Cp, l_msm);
-    load_aff(t1, h_msm);
-    zkh::add(Cp, t1);
+    P1 Cp = l_msm, Aaff, b1;
+    zkh::add(Cp, h_msm);
     load_aff(Aaff, outA);          // s * A uses the affine proof point A
     zkh::smul(t1, Aaff, ss);
     zkh::add(Cp, t1);
     load_aff(b1, pk->beta1);
-    load_aff(t1, b1_msm);
-    zkh::add(b1, t1);
+    zkh::add(b1, b1_msm);
     zkh::smul(t1, b1, rs);
     zkh::add(Cp, t1);
     store_aff(outC, Cp);
+}
+
+static void assemble(const zk_groth16_pk* pk, const zkh::Fe& r, const zkh::Fe& s, const uint64_t a_msm[8], const uint64_t b_msm[16],
+                     const uint64_t l_msm[8], const uint64_t h_msm[8], const uint64_t b1_msm[8], uint64_t outA[8], uint64_t outB[16],
+                     uint64_t outC[8]) {
+    zkh::Xyzz<zkh::Fe> a, l, h, b1;
+    zkh::Xyzz<zkh::Fp2> b;
+    load_aff(a, a_msm);
+    load_aff(b, b_msm);
+    load_aff(l, l_msm);
+    load_aff(h, h_msm);
+    load_aff(b1, b1_msm);
+    assemble_xyzz(pk, r, s, a, b, l, h, b1, outA, outB, outC);
 }
 
 // ------------------------------------------------------------------ prove
@@ -996,6 +1033,45 @@ extern "C" int zk_groth16_pk_arrays(const zk_groth16_pk* pk, zk_groth16_arrays* 
     out->l_query = pk->g1 + 2 * (size_t)pk->m * 64;
     out->h_query = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
     out->b2 = pk->g2;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_assemble_parts(const zk_groth16_pk* pk, const void* r, const void* s, const void* parts, int nparts,
+                                         void* proof256, void* points) {
+    clear_error();
+    if (!pk || !r || !s || !proof256 || nparts < 0 || (nparts && !parts)) return ZK_ERR_INVALID;
+    zkh::Fe rr, ss;
+    std::memcpy(rr.v, r, 32);
+    std::memcpy(ss.v, s, 32);
+    zkh::Xyzz<zkh::Fe> a, l, h, b1, t;
+    zkh::Xyzz<zkh::Fp2> b, t2;
+    zkh::set_identity(a);
+    zkh::set_identity(l);
+    zkh::set_identity(h);
+    zkh::set_identity(b1);
+    zkh::set_identity(b);
+    for (int i = 0; i < nparts; i++) {  // A (8) | B2 (16) | L (8) | H (8) | B1 (8) words per part
+        const uint64_t* q = (const uint64_t*)parts + (size_t)i * 48;
+        load_aff(t, q);
+        zkh::add(a, t);
+        load_aff(t2, q + 8);
+        zkh::add(b, t2);
+        load_aff(t, q + 24);
+        zkh::add(l, t);
+        load_aff(t, q + 32);
+        zkh::add(h, t);
+        load_aff(t, q + 40);
+        zkh::add(b1, t);
+    }
+    uint64_t A[8], B[16], C[8];
+    assemble_xyzz(pk, rr, ss, a, b, l, h, b1, A, B, C);
+    serialize_proof((uint8_t*)proof256, A, B, C);
+    if (points) {
+        uint64_t* p = (uint64_t*)points;
+        std::memcpy(p, A, 64);
+        std::memcpy(p + 8, B, 128);
+        std::memcpy(p + 24, C, 64);
+    }
     return ZK_OK;
 }
 

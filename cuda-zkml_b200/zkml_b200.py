@@ -79,6 +79,7 @@ _SIGS = {
     "zk_compute_h_pointwise_device": [_i, _vp, _vp, _vp, _vp, _vp, _i],
     "zk_groth16_pk_arrays": [_vp, ctypes.POINTER(Groth16Arrays)],
     "zk_groth16_assemble": [_vp, _vp, _vp, _vp, _vp, _vp],
+    "zk_groth16_assemble_parts": [_vp, _vp, _vp, _vp, _i, _vp, _vp],
 }
 for _name, _args in _SIGS.items():
     getattr(lib, _name).argtypes = _args
@@ -478,6 +479,16 @@ class ProvingKey:
         proof = np.zeros(256, np.uint8)
         pts = np.zeros(32, np.uint64)
         check(lib.zk_groth16_assemble(self.h, _np_ptr(rr), _np_ptr(ss), _np_ptr(sums), _np_ptr(proof), _np_ptr(pts)))
+        return proof.tobytes(), pts[:8], pts[8:24], pts[24:32]
+
+    def assemble_parts(self, r, s, parts):
+        """Proof from per-rank partial sums (a list of 48-word records), summed first."""
+        rr, ss = fr_from_int(r), fr_from_int(s)
+        rec = np.ascontiguousarray(np.stack([np.asarray(p, dtype=np.uint64)[:48] for p in parts]))
+        proof = np.zeros(256, np.uint8)
+        pts = np.zeros(32, np.uint64)
+        check(lib.zk_groth16_assemble_parts(self.h, _np_ptr(rr), _np_ptr(ss), _np_ptr(rec), len(parts), _np_ptr(proof),
+                                            _np_ptr(pts)))
         return proof.tobytes(), pts[:8], pts[8:24], pts[24:32]
 
     def prove(self, r1cs, witness, r, s, stream=None):

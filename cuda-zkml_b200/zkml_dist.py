@@ -65,6 +65,10 @@ def sharded_msm(points, scalars, local_msm, add, group=None, device=None):
 
 MSM_ORDER = ("a", "b2", "l", "h", "b1")  # layout of the 48-word sums record
 _WORDS = {"a": 8, "b2": 16, "l": 8, "h": 8, "b1": 8}
+WITNESS_MSMS = ("a", "b2", "l", "b1")
+# relative cost per point when the witness MSMs are cut into pieces (a G2
+# point costs about 1.5 G1 points at witness-scalar sizes)
+_MSM_WEIGHT = {"a": 1.0, "b2": 1.5, "l": 1.0, "b1": 1.0}
 _NO_ROW = np.iinfo(np.int64).max
 
 
@@ -109,7 +113,29 @@ def weighted_bounds(n, shares, rank):
     return cut[rank], cut[rank + 1]
 
 
-def balance_shares(poly_s, msm_s, shares, damping=0.5):
+def witness_pieces(sizes, shares, rank):
+    """This rank's [(msm, lo, hi)] of the witness MSMs.  The four MSMs are laid
+    end to end (weighted by _MSM_WEIGHT) and cut at the cumulative shares, so a
+    rank gets one contiguous run touching one or two MSMs instead of a small
+    slice of each: every MSM call has a fixed cost."""
+    lens = [sizes[k] * _MSM_WEIGHT[k] for k in WITNESS_MSMS]
+    total = float(sum(lens))
+    cum = np.concatenate([[0.0], np.cumsum(np.asarray(shares, dtype=np.float64))])
+    cum = cum / (cum[-1] if cum[-1] > 0 else 1.0) * total
+    out, off = [], 0.0
+    for k, length in zip(WITNESS_MSMS, lens):
+        w = _MSM_WEIGHT[k]
+
+        def point(x):
+            return int(min(sizes[k], max(0, round((x - off) / w))))
+        lo, hi = point(cum[rank]), point(cum[rank + 1])  # cum runs from 0 to total: the cuts cover [0, size)
+        if hi > lo:
+            out.append((k, lo, hi))
+        off += length
+    return out
+
+
+def balance_shares(poly_s, msm_s, shares, damping=0.5, floor=0.02):
     """Fractions of the witness MSMs for the next proof.  Rank r spends poly_s[r]
     on its polynomials and msm_s[r] on its share shares[r] of the witness MSMs
     before the coset broadcasts, which wait for the slowest rank; choose new
@@ -131,7 +157,11 @@ def balance_shares(poly_s, msm_s, shares, damping=0.5):
     target = np.clip(target, 0.0, None)
     target /= target.sum()
     new = damping * np.asarray(shares, dtype=np.float64) + (1 - damping) * target
-    return [float(x) for x in new / new.sum()]
+    new /= new.sum()
+    if (new >= floor).any():  # a sliver of work costs a whole MSM's fixed overhead
+        new = np.where(new < floor, 0.0, new)
+        new /= new.sum()
+    return [float(x) for x in new]
 
 
 def sharded_prove(prover, comm, witness, r, s, marks=None):
@@ -175,11 +205,9 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     # the witness MSMs come before the broadcasts, which wait for the slowest
     # polynomial owner: owners take smaller slices (balance_shares)
     t_msm = prover.timer()
-    sums = {}
-    for key in ("a", "b2", "l", "b1"):
-        a, b = weighted_bounds(sizes[key], shares, rank)
-        off = 1 + pub if key == "l" else 0
-        sums[key] = prover.msm(key, a, b, w, off)
+    sums = {k: np.zeros(_WORDS[k], np.uint64) for k in WITNESS_MSMS}
+    for key, a, b in witness_pieces(sizes, shares, rank):
+        sums[key] = prover.msm(key, a, b, w, 1 + pub if key == "l" else 0)
     t_msm = prover.elapsed(t_msm)
     mark("witness_msms")
     for k in range(3):
@@ -191,10 +219,10 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     a, b = shard_bounds(sizes["h"], rank, world)
     sums["h"] = prover.msm("h", a, b, h, 0)
     mark("h_msm")
-    parts = [unpack_sums(p) for p in comm.all_gather_points(pack_sums(sums, (t_poly(), t_msm())))]
-    total = {k: combine([p[k] for p in parts], prover.add_g2 if k == "b2" else prover.add_g1) for k in MSM_ORDER}
+    recs = comm.all_gather_points(pack_sums(sums, (t_poly(), t_msm())))
+    parts = [unpack_sums(p) for p in recs]
     prover.witness_shares = balance_shares([p["times"][0] for p in parts], [p["times"][1] for p in parts], shares)
-    out = prover.assemble(r, s, pack_sums(total))
+    out = prover.assemble_parts(r, s, [np.asarray(p, dtype=np.uint64)[:48] for p in recs])
     mark("assemble")
     return out
 
@@ -389,3 +417,6 @@ class CudaProver:
 
     def assemble(self, r, s, sums):
         return self.pk.assemble(r, s, sums)
+
+    def assemble_parts(self, r, s, parts):
+        return self.pk.assemble_parts(r, s, parts)

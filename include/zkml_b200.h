@@ -288,6 +288,9 @@ int zk_groth16_pk_arrays(const zk_groth16_pk* pk, zk_groth16_arrays* out);
  * if `points` is not NULL, A | B | C packed affine. */
 int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, const void* sums,
                         void* proof256, void* points);
+/* The same from nparts partial records of 384 B (one per rank), summed first. */
+int zk_groth16_assemble_parts(const zk_groth16_pk* pk, const void* r, const void* s,
+                              const void* parts, int nparts, void* proof256, void* points);
 
 /* ==================================================================
  * Synthetic workloads (seeded, for benchmarks and tests)

@@ -97,6 +97,14 @@ class OracleProver:
         one = O.fr_from_int(1)
         return O.msm_g2_naive(np.stack([a, b]), np.stack([one, one]))
 
+    def assemble_parts(self, r, s, parts):
+        import zkml_dist as D
+        tot = {}
+        for k in D.MSM_ORDER:
+            add = self.add_g2 if k == "b2" else self.add_g1
+            tot[k] = D.combine([D.unpack_sums(p)[k] for p in parts], add)
+        return self.assemble(r, s, D.pack_sums(tot))
+
     def assemble(self, r, s, sums):
         q = np.asarray(sums, dtype=np.uint64)
         return G.assemble(self.pk, q[0:8], q[8:24], q[24:32], q[32:40], q[40:48], r, s)
