@@ -448,7 +448,7 @@ __global__ void msm_reduce_kernel(const uint32_t* __restrict__ offsets, const ui
     set_identity(acc);
     for (uint32_t b = lo + chunk; b-- > lo;) {
         uint32_t g = w * B + b;
-        if (offsets[g] != offsets[g + 1]) {
+        if (!offsets || offsets[g] != offsets[g + 1]) {  // null: every bucket is written (the identity when empty)
             load_xyzz(q, bucket_sums + (size_t)g * Cv::kXyzzBytes);
             add(run, q);
         }
@@ -546,6 +546,20 @@ __global__ void __launch_bounds__(win_threads<Cv>()) msm_window_kernel(const uin
         }
         add(x, u);
         store_xyzz(window_sums + (size_t)w * Cv::kXyzzBytes, x);
+    }
+}
+
+// dst[g] += src[g] over all buckets (the bucket sums of two batches of points)
+template <class Cv>
+__global__ void msm_merge_buckets_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, uint32_t nb) {
+    using F = typename Cv::F;
+    for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < nb; g += gridDim.x * blockDim.x) {
+        Xyzz<F> a, b;
+        load_xyzz(b, src + (size_t)g * Cv::kXyzzBytes);
+        if (is_identity(b)) continue;
+        load_xyzz(a, dst + (size_t)g * Cv::kXyzzBytes);
+        add(a, b);
+        store_xyzz(dst + (size_t)g * Cv::kXyzzBytes, a);
     }
 }
 
@@ -693,108 +707,260 @@ struct LaunchCounter {
     void operator++(int) { n++; }
 };
 
-// Bucket sort + accumulate + reduce; writes W XYZZ window sums to `windows_dev`.
-// d_points must already hold the packed points when `points_ready` is recorded.
+// Scratch of the bucket phase (sort + accumulate + fixup), reused by every batch.
+struct SortScratch {
+    uint32_t *counts, *offsets, *cursors, *tile_sums, *keys, *digits, *first_bucket, *last_bucket;
+    uint8_t *part_first, *part_last;
+};
 template <class Cv>
-static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
-                        const MsmPlan& P, Arena& ar, uint8_t* windows_dev, cudaEvent_t points_ready, LaunchCounter& lc,
-                        uint32_t** total_keys_dev) {
-    cudaEvent_t* ph = ctx->phase;
-    uint32_t* counts = ar.take<uint32_t>(P.nb + 1);
-    uint32_t* offsets = ar.take<uint32_t>(P.nb + 1);
-    *total_keys_dev = offsets + P.nb;
-    uint32_t* cursors = ar.take<uint32_t>(P.nb);
-    uint32_t* tile_sums = ar.take<uint32_t>(P.tiles);
-    uint32_t* keys = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
-    uint32_t* digits = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
-    uint8_t* part_first = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
-    uint8_t* part_last = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
-    uint32_t* first_bucket = ar.take<uint32_t>(P.max_segs);
-    uint32_t* last_bucket = ar.take<uint32_t>(P.max_segs);
-    uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
-    uint8_t* chunk_acc = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
-    uint8_t* chunk_run = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
-    uint8_t* part_x = ar.take<uint8_t>((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
-    uint8_t* part_u = ar.take<uint8_t>((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
-    constexpr int kWinThreads = win_threads<Cv>();
-    uint8_t* win_tmp = ar.take<uint8_t>((size_t)P.W * 2 * kWinThreads * Cv::kXyzzBytes);
+static SortScratch take_sort_scratch(Arena& ar, const MsmPlan& P) {
+    SortScratch S;
+    S.counts = ar.take<uint32_t>(P.nb + 1);
+    S.offsets = ar.take<uint32_t>(P.nb + 1);
+    S.cursors = ar.take<uint32_t>(P.nb);
+    S.tile_sums = ar.take<uint32_t>(P.tiles);
+    S.keys = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
+    S.digits = ar.take<uint32_t>(std::max<size_t>(P.max_keys, 1));
+    S.part_first = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
+    S.part_last = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
+    S.first_bucket = ar.take<uint32_t>(P.max_segs);
+    S.last_bucket = ar.take<uint32_t>(P.max_segs);
+    return S;
+}
+template <class Cv>
+static size_t sort_scratch_bytes(const MsmPlan& P) {
+    size_t b = Arena::round((P.nb + 1) * 4) * 2 + Arena::round(P.nb * 4) + Arena::round(P.tiles * 4);
+    b += 2 * Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
+    b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes) + 2 * Arena::round(P.max_segs * 4);
+    return b;
+}
 
+struct ReduceScratch {
+    uint8_t *chunk_acc, *chunk_run, *part_x, *part_u, *win_tmp;
+};
+template <class Cv>
+static ReduceScratch take_reduce_scratch(Arena& ar, const MsmPlan& P) {
+    ReduceScratch R;
+    R.chunk_acc = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    R.chunk_run = ar.take<uint8_t>((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    R.part_x = ar.take<uint8_t>((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
+    R.part_u = ar.take<uint8_t>((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
+    R.win_tmp = ar.take<uint8_t>((size_t)P.W * 2 * win_threads<Cv>() * Cv::kXyzzBytes);
+    return R;
+}
+template <class Cv>
+static size_t reduce_scratch_bytes(const MsmPlan& P) {
+    size_t b = 2 * Arena::round((size_t)P.W * P.tw * Cv::kXyzzBytes);
+    b += 2 * Arena::round((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
+    b += Arena::round((size_t)P.W * 2 * win_threads<Cv>() * Cv::kXyzzBytes);
+    return b;
+}
+
+// Bucket sort + accumulate + fixup of n points into `buckets` (the sums of the
+// nonempty buckets; S.offsets tells which).  d_points must hold the packed
+// points when `points_ready` is recorded.  Records phase events 0..5.
+template <class Cv>
+static int msm_bucket_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
+                            const MsmPlan& P, const SortScratch& S, uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
+    cudaEvent_t* ph = ctx->phase;
     const int sms = ctx->num_sms;
     ZK_TRY_CUDA(cudaEventRecord(ph[0], st));
-    ZK_TRY_CUDA(cudaMemsetAsync(counts, 0, (P.nb + 1) * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(S.counts, 0, (P.nb + 1) * sizeof(uint32_t), st));
     if (P.agg)
-        msm_count_kernel<true><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts, digits);
+        msm_count_kernel<true><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, S.counts, S.digits);
     else
-        msm_count_kernel<false><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, counts, digits);
+        msm_count_kernel<false><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, S.counts, S.digits);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[1], st));
-    scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums);
+    scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(S.counts, P.nb, S.tile_sums);
     lc++;
-    scan_tiles_kernel<<<1, 1024, 0, st>>>(tile_sums, P.tiles);
+    scan_tiles_kernel<<<1, 1024, 0, st>>>(S.tile_sums, P.tiles);
     lc++;
-    scan_finish_kernel<<<P.tiles, 1024, 0, st>>>(counts, P.nb, tile_sums, offsets, cursors);
+    scan_finish_kernel<<<P.tiles, 1024, 0, st>>>(S.counts, P.nb, S.tile_sums, S.offsets, S.cursors);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[2], st));
     {
         const uint32_t bpw = (uint32_t)((n + 255) / 256);
         if (P.agg)
-            msm_scatter_kernel<true><<<bpw * (uint32_t)P.W, 256, 0, st>>>(digits, n, P.B, bpw, cursors, keys);
+            msm_scatter_kernel<true><<<bpw * (uint32_t)P.W, 256, 0, st>>>(S.digits, n, P.B, bpw, S.cursors, S.keys);
         else
-            msm_scatter_kernel<false><<<bpw * (uint32_t)P.W, 256, 0, st>>>(digits, n, P.B, bpw, cursors, keys);
+            msm_scatter_kernel<false><<<bpw * (uint32_t)P.W, 256, 0, st>>>(S.digits, n, P.B, bpw, S.cursors, S.keys);
     }
     lc++;
-    ZK_TRY_CUDA(cudaMemsetAsync(first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
-    ZK_TRY_CUDA(cudaMemsetAsync(last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(S.last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     if (points_ready) ZK_TRY_CUDA(cudaStreamWaitEvent(st, points_ready, 0));
     ZK_TRY_CUDA(cudaEventRecord(ph[3], st));
     {
         const int threads = 128;
         unsigned blocks = (unsigned)((P.max_segs + threads - 1) / threads);
         if (blocks < 1) blocks = 1;
-        msm_accumulate_kernel<Cv><<<blocks, threads, 0, st>>>(keys, offsets, P.nb, (const uint8_t*)d_points, P.seg, buckets,
-                                                               part_first, part_last, first_bucket, last_bucket);
+        msm_accumulate_kernel<Cv><<<blocks, threads, 0, st>>>(S.keys, S.offsets, P.nb, (const uint8_t*)d_points, P.seg, buckets,
+                                                               S.part_first, S.part_last, S.first_bucket, S.last_bucket);
         lc++;
     }
     ZK_TRY_CUDA(cudaEventRecord(ph[4], st));
     {
         const unsigned blocks = (unsigned)((P.max_segs + 127) / 128);
         for (uint64_t stride = 1; stride < P.max_segs; stride <<= 1) {
-            msm_fixup_round_kernel<Cv><<<blocks, 128, 0, st>>>(offsets, first_bucket, last_bucket, P.max_segs, P.seg, stride,
-                                                                part_first, part_last);
+            msm_fixup_round_kernel<Cv><<<blocks, 128, 0, st>>>(S.offsets, S.first_bucket, S.last_bucket, P.max_segs, P.seg, stride,
+                                                                S.part_first, S.part_last);
             lc++;
         }
-        msm_fixup_final_kernel<Cv><<<(P.nb + 255) / 256, 256, 0, st>>>(offsets, P.nb, P.seg, part_first, part_last, buckets);
+        msm_fixup_final_kernel<Cv><<<(P.nb + 255) / 256, 256, 0, st>>>(S.offsets, P.nb, P.seg, S.part_first, S.part_last, buckets);
         lc++;
     }
     ZK_TRY_CUDA(cudaEventRecord(ph[5], st));
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+// Running sums over the buckets of every window; writes W XYZZ window sums.
+// offsets == nullptr: every bucket holds its sum (the identity when empty).
+// Records phase events 6..7.
+template <class Cv>
+static int msm_reduce_phase(DeviceContext* ctx, cudaStream_t st, const MsmPlan& P, const uint32_t* offsets, const uint8_t* buckets,
+                            const ReduceScratch& R, uint8_t* windows_dev, LaunchCounter& lc) {
+    cudaEvent_t* ph = ctx->phase;
     {
         uint32_t total = (uint32_t)P.W * P.tw;
-        msm_reduce_kernel<Cv><<<(total + 127) / 128, 128, 0, st>>>(offsets, buckets, P.W, P.B, P.chunk, P.tw, chunk_acc, chunk_run);
+        msm_reduce_kernel<Cv><<<(total + 127) / 128, 128, 0, st>>>(offsets, buckets, P.W, P.B, P.chunk, P.tw, R.chunk_acc, R.chunk_run);
         lc++;
         uint32_t total2 = (uint32_t)P.W * P.tw2;
-        msm_reduce2_kernel<Cv><<<(total2 + 127) / 128, 128, 0, st>>>(chunk_acc, chunk_run, P.W, P.tw, P.chunk2, P.tw2, part_x, part_u);
+        msm_reduce2_kernel<Cv><<<(total2 + 127) / 128, 128, 0, st>>>(R.chunk_acc, R.chunk_run, P.W, P.tw, P.chunk2, P.tw2, R.part_x,
+                                                                      R.part_u);
         lc++;
     }
     ZK_TRY_CUDA(cudaEventRecord(ph[6], st));
-    msm_window_kernel<Cv><<<P.W, kWinThreads, 0, st>>>(part_x, part_u, P.tw2, 31 - __builtin_clz(P.chunk), win_tmp, windows_dev);
+    msm_window_kernel<Cv><<<P.W, win_threads<Cv>(), 0, st>>>(R.part_x, R.part_u, P.tw2, 31 - __builtin_clz(P.chunk), R.win_tmp,
+                                                             windows_dev);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[7], st));
     ZK_TRY_CUDA(cudaGetLastError());
     return ZK_OK;
 }
 
+// Bucket sort + accumulate + reduce; writes W XYZZ window sums to `windows_dev`.
+template <class Cv>
+static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
+                        const MsmPlan& P, Arena& ar, uint8_t* windows_dev, cudaEvent_t points_ready, LaunchCounter& lc,
+                        uint32_t** total_keys_dev) {
+    const SortScratch S = take_sort_scratch<Cv>(ar, P);
+    *total_keys_dev = S.offsets + P.nb;
+    uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
+    const ReduceScratch R = take_reduce_scratch<Cv>(ar, P);
+    ZK_TRY(msm_bucket_phase<Cv>(ctx, st, d_points, d_scalars, n, P, S, buckets, points_ready, lc));
+    return msm_reduce_phase<Cv>(ctx, st, P, S.offsets, buckets, R, windows_dev, lc);
+}
+
 template <class Cv>
 static size_t pipeline_bytes(const MsmPlan& P) {
-    constexpr int kWinThreads = win_threads<Cv>();
-    size_t b = 0;
-    b += Arena::round((P.nb + 1) * 4) * 2 + Arena::round(P.nb * 4) + Arena::round(P.tiles * 4);
-    b += 2 * Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
-    b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes) + 2 * Arena::round(P.max_segs * 4);
-    b += Arena::round((size_t)P.nb * Cv::kXyzzBytes);
-    b += 2 * Arena::round((size_t)P.W * P.tw * Cv::kXyzzBytes);
-    b += 2 * Arena::round((size_t)P.W * P.tw2 * Cv::kXyzzBytes);
-    b += Arena::round((size_t)P.W * 2 * kWinThreads * Cv::kXyzzBytes);
-    return b;
+    return sort_scratch_bytes<Cv>(P) + Arena::round((size_t)P.nb * Cv::kXyzzBytes) + reduce_scratch_bytes<Cv>(P);
+}
+
+// Host inputs from n >= kPipelineMinPoints: two batches of points, each sorted,
+// accumulated and fixed up into its own bucket array while the next batch is
+// still crossing PCIe; the two arrays are merged (one XYZZ addition per bucket)
+// before the one reduce.  Unpipelined, the accumulate waited for all 1.6 GB of a
+// 2^24 MSM to land.
+static constexpr size_t kPipelineMinPoints = (size_t)1 << 20;
+
+template <class Cv>
+static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const void* h_points, const void* h_scalars, size_t n,
+                                  uint64_t* out_affine) {
+    MsmStats& stats = msm_stats();
+    const size_t n0 = std::min(n, ((n / 2) + 255) & ~(size_t)255);
+    const size_t nk[2] = {n0, n - n0}, off[2] = {0, n0};
+    cudaStream_t cs = ctx->copy_stream;
+    cudaEvent_t* ev = ctx->batch_ready;  // scalars 0, points 0, scalars 1, points 1
+    ZK_TRY(ensure_pinned(ctx, 4096));
+    uint32_t* hist_host = (uint32_t*)ctx->pinned;
+    ZK_TRY(scratch_begin(ctx, st));
+    cudaEvent_t t0, t1;
+    ZK_TRY_CUDA(cudaEventCreate(&t0));
+    ZK_TRY_CUDA(cudaEventCreate(&t1));
+    ZK_TRY_CUDA(cudaEventRecord(t0, st));
+    // inputs in the stream-ordered pool (the arena is sized after the plan)
+    uint8_t* d_pts = nullptr;
+    Fr* d_sc = nullptr;
+    uint32_t* hist_dev = nullptr;
+    ZK_TRY_CUDA(cudaMallocAsync((void**)&d_pts, n * Cv::kAffineBytes, st));
+    ZK_TRY_CUDA(cudaMallocAsync((void**)&d_sc, n * 32, st));
+    ZK_TRY_CUDA(cudaMallocAsync((void**)&hist_dev, 256 * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaEventRecord(ctx->ev_a, st));
+    ZK_TRY_CUDA(cudaStreamWaitEvent(cs, ctx->ev_a, 0));
+    for (int k = 0; k < 2; k++) {  // in arrival order on one copy engine
+        ZK_TRY_CUDA(cudaMemcpyAsync(d_sc + off[k], (const uint8_t*)h_scalars + off[k] * 32, nk[k] * 32, cudaMemcpyHostToDevice, cs));
+        ZK_TRY_CUDA(cudaEventRecord(ev[2 * k], cs));
+        ZK_TRY_CUDA(cudaMemcpyAsync(d_pts + off[k] * Cv::kAffineBytes, (const uint8_t*)h_points + off[k] * Cv::kAffineBytes,
+                                    nk[k] * Cv::kAffineBytes, cudaMemcpyHostToDevice, cs));
+        ZK_TRY_CUDA(cudaEventRecord(ev[2 * k + 1], cs));
+    }
+    // the plan from the first batch's scalars
+    ZK_TRY_CUDA(cudaStreamWaitEvent(st, ev[0], 0));
+    ZK_TRY_CUDA(cudaMemsetAsync(hist_dev, 0, 256 * sizeof(uint32_t), st));
+    msm_bitlen_hist_kernel<<<grid_for(n0, 256, ctx->num_sms * 4), 256, 0, st>>>(d_sc, n0, hist_dev);
+    ZK_TRY_CUDA(cudaMemcpyAsync(hist_host, hist_dev, 256 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    uint32_t hist[256];
+    for (int b = 0; b < 256; b++) hist[b] = (uint32_t)std::min<double>(4e9, (double)hist_host[b] * (double)n / (double)n0);
+    const MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
+    // per batch, any scalar may have all W digits nonzero: the second batch's
+    // histogram is not looked at, so its key bound is the trivial one
+    MsmPlan Pb = P;
+    Pb.max_keys = nk[0] * (size_t)P.W;
+    Pb.max_segs = std::max<size_t>(1, (Pb.max_keys + P.seg - 1) / P.seg);
+    stats.window_bits = P.c;
+    stats.num_windows = P.W;
+
+    const size_t bucket_bytes = (size_t)P.nb * Cv::kXyzzBytes;
+    const size_t need = Arena::round((size_t)P.W * Cv::kXyzzBytes) + Arena::round(2 * sizeof(uint32_t)) + sort_scratch_bytes<Cv>(Pb) +
+                        2 * Arena::round(bucket_bytes) + reduce_scratch_bytes<Cv>(P);
+    ZK_TRY(ensure_scratch(ctx, need));
+    ZK_TRY(ensure_pinned(ctx, (size_t)P.W * Cv::kXyzzBytes + 64));
+    Arena ar;
+    ar.base = (char*)ctx->scratch;
+    uint8_t* windows_dev = ar.take<uint8_t>((size_t)P.W * Cv::kXyzzBytes);
+    uint32_t* keys_total = ar.take<uint32_t>(2);
+    const SortScratch S = take_sort_scratch<Cv>(ar, Pb);
+    uint8_t* buckets[2];
+    buckets[0] = ar.take<uint8_t>(bucket_bytes);
+    buckets[1] = ar.take<uint8_t>(bucket_bytes);
+    const ReduceScratch R = take_reduce_scratch<Cv>(ar, P);
+    LaunchCounter lc;
+    for (int k = 0; k < 2; k++) {
+        // empty buckets must read as the identity (all-zero XYZZ) for the merge
+        ZK_TRY_CUDA(cudaMemsetAsync(buckets[k], 0, bucket_bytes, st));
+        ZK_TRY_CUDA(cudaStreamWaitEvent(st, ev[2 * k], 0));
+        ZK_TRY(msm_bucket_phase<Cv>(ctx, st, d_pts + off[k] * Cv::kAffineBytes, d_sc + off[k], nk[k], Pb, S, buckets[k], ev[2 * k + 1],
+                                    lc));
+        ZK_TRY_CUDA(cudaMemcpyAsync(keys_total + k, S.offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+    }
+    msm_merge_buckets_kernel<Cv><<<grid_for(P.nb, 128, ctx->num_sms * 8), 128, 0, st>>>(buckets[0], buckets[1], P.nb);
+    lc++;
+    ZK_TRY(msm_reduce_phase<Cv>(ctx, st, P, nullptr, buckets[0], R, windows_dev, lc));
+    ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows_dev, (size_t)P.W * Cv::kXyzzBytes, cudaMemcpyDeviceToHost, st));
+    uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
+    ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, keys_total, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
+    ZK_TRY_CUDA(cudaFreeAsync(d_pts, st));
+    ZK_TRY_CUDA(cudaFreeAsync(d_sc, st));
+    ZK_TRY_CUDA(cudaFreeAsync(hist_dev, st));
+    ZK_TRY_CUDA(cudaEventRecord(t1, st));
+    ZK_TRY(scratch_end(ctx, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    float ms_all = 0;
+    cudaEventElapsedTime(&ms_all, t0, t1);
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    // phase times of the second batch and the reduce
+    for (int i = 0; i < 8; i++) cudaEventElapsedTime(&stats.phase_ms[i], ctx->phase[i], ctx->phase[i + 1]);
+    stats.kernel_launches = lc.n;
+    stats.accumulate_ms = stats.phase_ms[3];
+    stats.total_device_ms = ms_all;
+    stats.bucket_adds = (long long)keys_host[0] + keys_host[1];
+    host_combine<Cv>((const uint64_t*)ctx->pinned, P.W, P.c, out_affine);
+    return ZK_OK;
 }
 
 // Full MSM.  src_points / src_scalars are device pointers (host_inputs == 0)
@@ -818,6 +984,8 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
     cudaStream_t st = user_stream;  // NULL: the legacy default stream
+    if (host_inputs && !ref_layout && n >= kPipelineMinPoints)
+        return msm_run_host_pipelined<Cv>(ctx, st, src_points, src_scalars, n, out_affine);
     // Window choice from the scalars' bit lengths (a small device pre-pass; the
     // host path copies the scalars first for it).
     uint32_t* hist_dev = nullptr;
