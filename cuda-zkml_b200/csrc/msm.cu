@@ -756,12 +756,11 @@ static size_t reduce_scratch_bytes(const MsmPlan& P) {
     return b;
 }
 
-// Bucket sort + accumulate + fixup of n points into `buckets` (the sums of the
-// nonempty buckets; S.offsets tells which).  d_points must hold the packed
-// points when `points_ready` is recorded.  Records phase events 0..5.
+// Signed digits and the counting sort of n scalars into S (keys grouped by
+// bucket, offsets).  Records phase events 0..2.
 template <class Cv>
-static int msm_bucket_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
-                            const MsmPlan& P, const SortScratch& S, uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
+static int msm_sort_phase(DeviceContext* ctx, cudaStream_t st, const void* d_scalars, size_t n, const MsmPlan& P,
+                          const SortScratch& S, LaunchCounter& lc) {
     cudaEvent_t* ph = ctx->phase;
     const int sms = ctx->num_sms;
     ZK_TRY_CUDA(cudaEventRecord(ph[0], st));
@@ -789,6 +788,17 @@ static int msm_bucket_phase(DeviceContext* ctx, cudaStream_t st, const void* d_p
     lc++;
     ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     ZK_TRY_CUDA(cudaMemsetAsync(S.last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+// Accumulate + fixup of the sorted keys in S into `buckets` (the sums of the
+// nonempty buckets; S.offsets tells which).  d_points must hold the packed
+// points when `points_ready` is recorded.  Records phase events 3..5.
+template <class Cv>
+static int msm_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const MsmPlan& P, const SortScratch& S,
+                                uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
+    cudaEvent_t* ph = ctx->phase;
     if (points_ready) ZK_TRY_CUDA(cudaStreamWaitEvent(st, points_ready, 0));
     ZK_TRY_CUDA(cudaEventRecord(ph[3], st));
     {
@@ -813,6 +823,13 @@ static int msm_bucket_phase(DeviceContext* ctx, cudaStream_t st, const void* d_p
     ZK_TRY_CUDA(cudaEventRecord(ph[5], st));
     ZK_TRY_CUDA(cudaGetLastError());
     return ZK_OK;
+}
+
+template <class Cv>
+static int msm_bucket_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
+                            const MsmPlan& P, const SortScratch& S, uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
+    ZK_TRY(msm_sort_phase<Cv>(ctx, st, d_scalars, n, P, S, lc));
+    return msm_accumulate_phase<Cv>(ctx, st, d_points, P, S, buckets, points_ready, lc);
 }
 
 // Running sums over the buckets of every window; writes W XYZZ window sums.
@@ -858,21 +875,34 @@ static size_t pipeline_bytes(const MsmPlan& P) {
     return sort_scratch_bytes<Cv>(P) + Arena::round((size_t)P.nb * Cv::kXyzzBytes) + reduce_scratch_bytes<Cv>(P);
 }
 
-// Host inputs from n >= kPipelineMinPoints: two batches of points, each sorted,
-// accumulated and fixed up into its own bucket array while the next batch is
-// still crossing PCIe; the two arrays are merged (one XYZZ addition per bucket)
-// before the one reduce.  Unpipelined, the accumulate waited for all 1.6 GB of a
-// 2^24 MSM to land.
+// Host inputs from n >= kPipelineMinPoints: kBatches batches of points (a short
+// first one, so that accumulation starts early).  The copy stream lands each
+// batch's scalars and points in turn; the auxiliary stream sorts a batch as
+// soon as its scalars land; the work stream accumulates and fixes it up into
+// its own bucket array as soon as its points land, while later batches are
+// still crossing PCIe and being sorted.  The arrays are merged (one XYZZ
+// addition per bucket and extra batch) before the one reduce.  Unpipelined, the
+// accumulate waited for all 1.6 GB of a 2^24 MSM to land.
 static constexpr size_t kPipelineMinPoints = (size_t)1 << 20;
+static constexpr int kBatches = 3;
+static constexpr double kBatchFrac[kBatches] = {0.25, 0.375, 0.375};
 
 template <class Cv>
 static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const void* h_points, const void* h_scalars, size_t n,
                                   uint64_t* out_affine) {
     MsmStats& stats = msm_stats();
-    const size_t n0 = std::min(n, ((n / 2) + 255) & ~(size_t)255);
-    const size_t nk[2] = {n0, n - n0}, off[2] = {0, n0};
-    cudaStream_t cs = ctx->copy_stream;
-    cudaEvent_t* ev = ctx->batch_ready;  // scalars 0, points 0, scalars 1, points 1
+    size_t nk[kBatches], off[kBatches];
+    {
+        size_t o = 0;
+        for (int k = 0; k < kBatches; k++) {
+            size_t len = k == kBatches - 1 ? n - o : std::min(n - o, ((size_t)(kBatchFrac[k] * (double)n) + 255) & ~(size_t)255);
+            off[k] = o;
+            nk[k] = len;
+            o += len;
+        }
+    }
+    cudaStream_t cs = ctx->copy_stream, as = ctx->aux_stream;
+    cudaEvent_t* ev = ctx->batch_ev;  // batch k: [3k] scalars landed, [3k + 1] points landed, [3k + 2] keys sorted
     ZK_TRY(ensure_pinned(ctx, 4096));
     uint32_t* hist_host = (uint32_t*)ctx->pinned;
     ZK_TRY(scratch_begin(ctx, st));
@@ -887,61 +917,73 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     ZK_TRY_CUDA(cudaMallocAsync((void**)&d_pts, n * Cv::kAffineBytes, st));
     ZK_TRY_CUDA(cudaMallocAsync((void**)&d_sc, n * 32, st));
     ZK_TRY_CUDA(cudaMallocAsync((void**)&hist_dev, 256 * sizeof(uint32_t), st));
-    ZK_TRY_CUDA(cudaEventRecord(ctx->ev_a, st));
+    ZK_TRY_CUDA(cudaEventRecord(ctx->ev_a, st));  // after the previous users of the scratch, and the allocations
     ZK_TRY_CUDA(cudaStreamWaitEvent(cs, ctx->ev_a, 0));
-    for (int k = 0; k < 2; k++) {  // in arrival order on one copy engine
+    ZK_TRY_CUDA(cudaStreamWaitEvent(as, ctx->ev_a, 0));
+    for (int k = 0; k < kBatches; k++) {  // in arrival order on one copy engine
         ZK_TRY_CUDA(cudaMemcpyAsync(d_sc + off[k], (const uint8_t*)h_scalars + off[k] * 32, nk[k] * 32, cudaMemcpyHostToDevice, cs));
-        ZK_TRY_CUDA(cudaEventRecord(ev[2 * k], cs));
+        ZK_TRY_CUDA(cudaEventRecord(ev[3 * k], cs));
         ZK_TRY_CUDA(cudaMemcpyAsync(d_pts + off[k] * Cv::kAffineBytes, (const uint8_t*)h_points + off[k] * Cv::kAffineBytes,
                                     nk[k] * Cv::kAffineBytes, cudaMemcpyHostToDevice, cs));
-        ZK_TRY_CUDA(cudaEventRecord(ev[2 * k + 1], cs));
+        ZK_TRY_CUDA(cudaEventRecord(ev[3 * k + 1], cs));
     }
     // the plan from the first batch's scalars
     ZK_TRY_CUDA(cudaStreamWaitEvent(st, ev[0], 0));
     ZK_TRY_CUDA(cudaMemsetAsync(hist_dev, 0, 256 * sizeof(uint32_t), st));
-    msm_bitlen_hist_kernel<<<grid_for(n0, 256, ctx->num_sms * 4), 256, 0, st>>>(d_sc, n0, hist_dev);
+    msm_bitlen_hist_kernel<<<grid_for(nk[0], 256, ctx->num_sms * 4), 256, 0, st>>>(d_sc, nk[0], hist_dev);
     ZK_TRY_CUDA(cudaMemcpyAsync(hist_host, hist_dev, 256 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     uint32_t hist[256];
-    for (int b = 0; b < 256; b++) hist[b] = (uint32_t)std::min<double>(4e9, (double)hist_host[b] * (double)n / (double)n0);
+    for (int b = 0; b < 256; b++) hist[b] = (uint32_t)std::min<double>(4e9, (double)hist_host[b] * (double)n / (double)nk[0]);
     const MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
-    // per batch, any scalar may have all W digits nonzero: the second batch's
-    // histogram is not looked at, so its key bound is the trivial one
-    MsmPlan Pb = P;
-    Pb.max_keys = nk[0] * (size_t)P.W;
-    Pb.max_segs = std::max<size_t>(1, (Pb.max_keys + P.seg - 1) / P.seg);
+    // per batch, any scalar may have all W digits nonzero: the later batches'
+    // histograms are not looked at, so their key bound is the trivial one
+    MsmPlan Pb[kBatches];
+    for (int k = 0; k < kBatches; k++) {
+        Pb[k] = P;
+        Pb[k].max_keys = nk[k] * (size_t)P.W;
+        Pb[k].max_segs = std::max<size_t>(1, (Pb[k].max_keys + P.seg - 1) / P.seg);
+    }
     stats.window_bits = P.c;
     stats.num_windows = P.W;
 
     const size_t bucket_bytes = (size_t)P.nb * Cv::kXyzzBytes;
-    const size_t need = Arena::round((size_t)P.W * Cv::kXyzzBytes) + Arena::round(2 * sizeof(uint32_t)) + sort_scratch_bytes<Cv>(Pb) +
-                        2 * Arena::round(bucket_bytes) + reduce_scratch_bytes<Cv>(P);
-    ZK_TRY(ensure_scratch(ctx, need));
+    size_t need = Arena::round((size_t)P.W * Cv::kXyzzBytes) + Arena::round(kBatches * sizeof(uint32_t)) + reduce_scratch_bytes<Cv>(P);
+    for (int k = 0; k < kBatches; k++) need += sort_scratch_bytes<Cv>(Pb[k]) + Arena::round(bucket_bytes);
+    ZK_TRY(ensure_scratch(ctx, need));  // may synchronise the device (growth only)
     ZK_TRY(ensure_pinned(ctx, (size_t)P.W * Cv::kXyzzBytes + 64));
     Arena ar;
     ar.base = (char*)ctx->scratch;
     uint8_t* windows_dev = ar.take<uint8_t>((size_t)P.W * Cv::kXyzzBytes);
-    uint32_t* keys_total = ar.take<uint32_t>(2);
-    const SortScratch S = take_sort_scratch<Cv>(ar, Pb);
-    uint8_t* buckets[2];
-    buckets[0] = ar.take<uint8_t>(bucket_bytes);
-    buckets[1] = ar.take<uint8_t>(bucket_bytes);
+    uint32_t* keys_total = ar.take<uint32_t>(kBatches);
+    SortScratch S[kBatches];
+    uint8_t* buckets[kBatches];
+    for (int k = 0; k < kBatches; k++) {
+        S[k] = take_sort_scratch<Cv>(ar, Pb[k]);
+        buckets[k] = ar.take<uint8_t>(bucket_bytes);
+    }
     const ReduceScratch R = take_reduce_scratch<Cv>(ar, P);
     LaunchCounter lc;
-    for (int k = 0; k < 2; k++) {
+    for (int k = 0; k < kBatches; k++) {  // sorts, on the auxiliary stream
+        ZK_TRY_CUDA(cudaStreamWaitEvent(as, ev[3 * k], 0));
+        ZK_TRY(msm_sort_phase<Cv>(ctx, as, d_sc + off[k], nk[k], Pb[k], S[k], lc));
+        ZK_TRY_CUDA(cudaEventRecord(ev[3 * k + 2], as));
+    }
+    for (int k = 0; k < kBatches; k++) {  // accumulates, on the work stream
         // empty buckets must read as the identity (all-zero XYZZ) for the merge
         ZK_TRY_CUDA(cudaMemsetAsync(buckets[k], 0, bucket_bytes, st));
-        ZK_TRY_CUDA(cudaStreamWaitEvent(st, ev[2 * k], 0));
-        ZK_TRY(msm_bucket_phase<Cv>(ctx, st, d_pts + off[k] * Cv::kAffineBytes, d_sc + off[k], nk[k], Pb, S, buckets[k], ev[2 * k + 1],
-                                    lc));
-        ZK_TRY_CUDA(cudaMemcpyAsync(keys_total + k, S.offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+        ZK_TRY_CUDA(cudaStreamWaitEvent(st, ev[3 * k + 2], 0));
+        ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, d_pts + off[k] * Cv::kAffineBytes, Pb[k], S[k], buckets[k], ev[3 * k + 1], lc));
+        ZK_TRY_CUDA(cudaMemcpyAsync(keys_total + k, S[k].offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
     }
-    msm_merge_buckets_kernel<Cv><<<grid_for(P.nb, 128, ctx->num_sms * 8), 128, 0, st>>>(buckets[0], buckets[1], P.nb);
-    lc++;
+    for (int k = 1; k < kBatches; k++) {
+        msm_merge_buckets_kernel<Cv><<<grid_for(P.nb, 128, ctx->num_sms * 8), 128, 0, st>>>(buckets[0], buckets[k], P.nb);
+        lc++;
+    }
     ZK_TRY(msm_reduce_phase<Cv>(ctx, st, P, nullptr, buckets[0], R, windows_dev, lc));
     ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows_dev, (size_t)P.W * Cv::kXyzzBytes, cudaMemcpyDeviceToHost, st));
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
-    ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, keys_total, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, keys_total, kBatches * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
     ZK_TRY_CUDA(cudaFreeAsync(d_pts, st));
     ZK_TRY_CUDA(cudaFreeAsync(d_sc, st));
@@ -953,12 +995,13 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     cudaEventElapsedTime(&ms_all, t0, t1);
     cudaEventDestroy(t0);
     cudaEventDestroy(t1);
-    // phase times of the second batch and the reduce
+    // phase times of the last batch (its sort ran on the auxiliary stream) and the reduce
     for (int i = 0; i < 8; i++) cudaEventElapsedTime(&stats.phase_ms[i], ctx->phase[i], ctx->phase[i + 1]);
     stats.kernel_launches = lc.n;
     stats.accumulate_ms = stats.phase_ms[3];
     stats.total_device_ms = ms_all;
-    stats.bucket_adds = (long long)keys_host[0] + keys_host[1];
+    stats.bucket_adds = 0;
+    for (int k = 0; k < kBatches; k++) stats.bucket_adds += keys_host[k];
     host_combine<Cv>((const uint64_t*)ctx->pinned, P.W, P.c, out_affine);
     return ZK_OK;
 }

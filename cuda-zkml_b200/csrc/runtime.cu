@@ -62,7 +62,8 @@ int get_context(int device, DeviceContext** out) {
         ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->scratch_done, cudaEventDisableTiming));
         ZK_TRY_CUDA(cudaEventRecord(c->scratch_done, c->stream));
         for (int i = 0; i < 9; i++) ZK_TRY_CUDA(cudaEventCreate(&c->phase[i]));
-        for (int i = 0; i < 4; i++) ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->batch_ready[i], cudaEventDisableTiming));
+        ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->aux_stream, cudaStreamNonBlocking));
+        for (int i = 0; i < 12; i++) ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->batch_ev[i], cudaEventDisableTiming));
         g_ctx[device] = c;
     }
     *out = g_ctx[device];

@@ -56,7 +56,8 @@ struct DeviceContext {
     cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_c = nullptr;
     cudaEvent_t scratch_done = nullptr;  // last work that used `scratch`
     cudaEvent_t phase[9] = {};            // MSM phase boundaries (timing)
-    cudaEvent_t batch_ready[4] = {};      // pipelined host MSM: scalars / points of two batches landed
+    cudaStream_t aux_stream = nullptr;    // pipelined host MSM: sorts beside the accumulates
+    cudaEvent_t batch_ev[12] = {};        // pipelined host MSM: per batch scalars landed, points landed, keys sorted
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     void* pinned = nullptr;          // small pinned host staging (results)
