@@ -46,17 +46,25 @@ static constexpr int kNttThreads = 256;
 static constexpr int kTileElems = 2048;  // R * C per CTA (64 KiB of shared memory)
 
 // ------------------------------------------------------------------ tables
+// Twiddle and coset factors are read through table_factor: factor(i) =
+// lo[i & (2^h - 1)] * hi[i >> h] from two 2^(L/2)-entry tables, or, when h < 0,
+// lo[i] from one table of all n factors.  The full tables (built once per size
+// up to 2^kFullTableMaxLog, by the same products) trade one Montgomery product
+// per factor for a 32-byte load: the transform is IMAD-bound with DRAM ~5% busy.
+static constexpr int kFullTableMaxLog = 24;
+
 struct NttDirTables {
     Fr* roots = nullptr;   // w_{2^r}^t for r = 1..8, t < 2^(r-1), concatenated at offset 2^(r-1) - 1
-    Fr* tw_lo = nullptr;   // w_n^i, i < 2^h
+    Fr* tw_lo = nullptr;   // w_n^i, i < 2^h (all i < n when h < 0)
     Fr* tw_hi = nullptr;   // w_n^(i 2^h), i < 2^(L-h)
     int h = 0;
 };
-struct CosetTables {       // factor(i) = lo[i & (2^h - 1)] * hi[i >> h]
+struct CosetTables {       // factor(i) = lo[i & (2^h - 1)] * hi[i >> h], or lo[i] when h < 0
     Fr* lo = nullptr;
     Fr* hi = nullptr;
     int h = 0;
 };
+static int expand_full_table(DeviceContext* ctx, Fr** lo, Fr** hi, int* h, int L);
 struct NttTables {
     std::map<int, NttDirTables> dir;            // key: L * 2 + inverse
     std::map<std::vector<uint64_t>, CosetTables> coset;  // key: L, kind, g limbs
@@ -129,6 +137,7 @@ static int get_dir_tables(DeviceContext* ctx, int L, bool inverse, const NttDirT
         roots.insert(roots.end(), p.begin(), p.end());
     }
     ZK_TRY(upload(&t.roots, roots));
+    if (L <= kFullTableMaxLog) ZK_TRY(expand_full_table(ctx, &t.tw_lo, &t.tw_hi, &t.h, L));
     auto res = ctx->ntt->dir.emplace(key, t);
     *out = &res.first->second;
     return ZK_OK;
@@ -164,6 +173,7 @@ static int get_coset_tables(DeviceContext* ctx, int L, int kind, const zkh::Fe& 
     for (int i = 0; i < t.h; i++) zkh::mul(zkh::kR, sh, sh, sh);
     powers(v, one, sh, (size_t)1 << (L - t.h));
     ZK_TRY(upload(&t.hi, v));
+    if (L <= kFullTableMaxLog) ZK_TRY(expand_full_table(ctx, &t.lo, &t.hi, &t.h, L));
     auto res = ctx->ntt->coset.emplace(key, t);
     *out = &res.first->second;
     return ZK_OK;
@@ -171,10 +181,40 @@ static int get_coset_tables(DeviceContext* ctx, int L, int kind, const zkh::Fe& 
 
 // ------------------------------------------------------------------ kernels
 __device__ __forceinline__ void table_factor(Fr& f, const Fr* lo, const Fr* hi, int h, uint64_t i) {
+    if (h < 0) {  // one table of all n factors
+        fload_nc(f, lo + i);
+        return;
+    }
     Fr a, b;
     fload_nc(a, lo + (i & ((1ull << h) - 1)));
     fload_nc(b, hi + (i >> h));
     fmul(f, a, b);
+}
+
+// full[i] = lo[i & (2^h - 1)] * hi[i >> h], i < n: the same product table_factor forms
+__global__ void expand_table_kernel(Fr* __restrict__ full, const Fr* __restrict__ lo, const Fr* __restrict__ hi, int h, uint64_t n) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        Fr x;
+        table_factor(x, lo, hi, h, i);
+        fstore(full + i, x);
+    }
+}
+
+// Replace the two split tables by the full table of 2^L factors (once per size).
+static int expand_full_table(DeviceContext* ctx, Fr** lo, Fr** hi, int* h, int L) {
+    const uint64_t n = 1ull << L;
+    Fr* full = nullptr;
+    ZK_TRY_CUDA(cudaMalloc(&full, n * sizeof(Fr)));
+    const unsigned grid = (unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)ctx->num_sms * 16);
+    expand_table_kernel<<<grid, 256, 0, ctx->stream>>>(full, *lo, *hi, *h, n);
+    ZK_TRY_CUDA(cudaGetLastError());
+    ZK_TRY_CUDA(cudaStreamSynchronize(ctx->stream));
+    cudaFree(*lo);
+    cudaFree(*hi);
+    *lo = full;
+    *hi = nullptr;
+    *h = -1;
+    return ZK_OK;
 }
 
 template <int LOGR>
