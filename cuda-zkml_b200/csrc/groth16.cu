@@ -120,9 +120,15 @@ static_assert(sizeof(SparseEntry) == 40, "SparseEntry layout");
 struct Csr {
     std::vector<int32_t> row_ptr, col;
     std::vector<zkh::Fe> val;
-    std::vector<int32_t> long_rows;  // rows with > kShortRow entries
+    std::vector<int32_t> mid_rows;   // rows with kShortRow < entries <= kMidRow (ascending)
+    std::vector<int32_t> long_rows;  // rows with > kMidRow entries (ascending)
 };
-static constexpr int kShortRow = 64;
+// Row lengths: up to kShortRow entries one thread per row, up to kMidRow one
+// warp per row (the 289-entry rows of a 3x3x32 convolution), beyond that one
+// block per row (dense layers).  A block per 289-entry row left most of its
+// threads idle through a synchronised shared-memory tree.
+static constexpr int kShortRow = 16;
+static constexpr int kMidRow = 2048;
 
 struct R1cs {
     int device = -1;
@@ -132,6 +138,7 @@ struct R1cs {
     int32_t* d_row_ptr[3] = {};
     int32_t* d_col[3] = {};
     Fr* d_val[3] = {};
+    int32_t* d_mid[3] = {};
     int32_t* d_long[3] = {};
     size_t nnz[3] = {};
 };
@@ -189,11 +196,40 @@ __global__ void r1cs_matvec_short_kernel(const int32_t* __restrict__ row_ptr, co
                     fadd(acc, acc, v);
                 }
             } else {
-                continue;  // written by the long-row kernel
+                continue;  // written by the warp or block kernel
             }
         }
         fstore(out + (r - lo), acc);
     }
+}
+
+// one warp per medium row: strided partial sums, then a shuffle tree
+__global__ void __launch_bounds__(256) r1cs_matvec_warp_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
+                                                               const Fr* __restrict__ val, const Fr* __restrict__ w,
+                                                               const int32_t* __restrict__ rows, size_t count, uint64_t lo,
+                                                               Fr* __restrict__ out) {
+    const uint32_t lane = threadIdx.x & 31;
+    const size_t wid = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (wid >= count) return;  // uniform across the warp
+    const int r = rows[wid];
+    const int a = row_ptr[r], b = row_ptr[r + 1];
+    Fr acc;
+    fset_zero(acc);
+    for (int j = a + (int)lane; j < b; j += 32) {
+        Fr v, x;
+        fload_nc(v, val + j);
+        fload_nc(x, w + col[j]);
+        fmul(v, v, x);
+        fadd(acc, acc, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Fr t;
+#pragma unroll
+        for (int k = 0; k < 8; k++) t.v[k] = __shfl_down_sync(0xffffffffu, acc.v[k], o);
+        fadd(acc, acc, t);  // lanes >= 32 - o add their own value again; only lane 0 is kept
+    }
+    if (lane == 0) fstore(out + (r - lo), acc);
 }
 
 // one block per long row: strided partial sums, then a shared-memory tree
@@ -293,9 +329,13 @@ static int r1cs_create(int device, int num_constraints, int num_variables, int n
                 std::memcpy(c.val[p].v, e.v, 32);
             }
         }
+        c.mid_rows.clear();
         c.long_rows.clear();
-        for (int r = 0; r < rows; r++)
-            if (c.row_ptr[(size_t)r + 1] - c.row_ptr[r] > kShortRow) c.long_rows.push_back(r);
+        for (int r = 0; r < rows; r++) {
+            const int32_t len = c.row_ptr[(size_t)r + 1] - c.row_ptr[r];
+            if (len > kMidRow) c.long_rows.push_back(r);
+            else if (len > kShortRow) c.mid_rows.push_back(r);
+        }
         R.nnz[k] = total;
         ZK_TRY_CUDA(cudaMalloc(&R.d_row_ptr[k], c.row_ptr.size() * 4));
         ZK_TRY_CUDA(cudaMemcpy(R.d_row_ptr[k], c.row_ptr.data(), c.row_ptr.size() * 4, cudaMemcpyHostToDevice));
@@ -303,6 +343,8 @@ static int r1cs_create(int device, int num_constraints, int num_variables, int n
         ZK_TRY_CUDA(cudaMemcpy(R.d_col[k], c.col.data(), total * 4, cudaMemcpyHostToDevice));
         ZK_TRY_CUDA(cudaMalloc(&R.d_val[k], std::max<size_t>(total, 1) * 32));
         ZK_TRY_CUDA(cudaMemcpy(R.d_val[k], c.val.data(), total * 32, cudaMemcpyHostToDevice));
+        ZK_TRY_CUDA(cudaMalloc(&R.d_mid[k], std::max<size_t>(c.mid_rows.size(), 1) * 4));
+        ZK_TRY_CUDA(cudaMemcpy(R.d_mid[k], c.mid_rows.data(), c.mid_rows.size() * 4, cudaMemcpyHostToDevice));
         ZK_TRY_CUDA(cudaMalloc(&R.d_long[k], std::max<size_t>(c.long_rows.size(), 1) * 4));
         ZK_TRY_CUDA(cudaMemcpy(R.d_long[k], c.long_rows.data(), c.long_rows.size() * 4, cudaMemcpyHostToDevice));
     }
@@ -318,7 +360,13 @@ static int r1cs_matvec_rows(const R1cs& R, cudaStream_t st, const Fr* w, uint64_
         Fr* out = out3 + (size_t)k * len;
         const unsigned grid = (unsigned)std::min<uint64_t>((len + 255) / 256, (uint64_t)num_sms * 16);
         r1cs_matvec_short_kernel<<<grid, 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w, rows, lo, hi, out);
-        // long rows inside [lo, hi): a contiguous run of the ascending list
+        // medium and long rows inside [lo, hi): contiguous runs of the ascending lists
+        const std::vector<int32_t>& mr = R.host[k].mid_rows;
+        const size_t ma = std::lower_bound(mr.begin(), mr.end(), (int64_t)lo) - mr.begin();
+        const size_t mb = std::lower_bound(mr.begin(), mr.end(), (int64_t)hi) - mr.begin();
+        if (mb > ma)
+            r1cs_matvec_warp_kernel<<<(unsigned)((mb - ma + 7) / 8), 256, 0, st>>>(R.d_row_ptr[k], R.d_col[k], R.d_val[k], w,
+                                                                                  R.d_mid[k] + ma, mb - ma, lo, out);
         const std::vector<int32_t>& lr = R.host[k].long_rows;
         const size_t a = std::lower_bound(lr.begin(), lr.end(), (int64_t)lo) - lr.begin();
         const size_t b = std::lower_bound(lr.begin(), lr.end(), (int64_t)hi) - lr.begin();
@@ -886,6 +934,7 @@ extern "C" void zk_r1cs_destroy(zk_r1cs* r) {
         cudaFree(r->r.d_row_ptr[k]);
         cudaFree(r->r.d_col[k]);
         cudaFree(r->r.d_val[k]);
+        cudaFree(r->r.d_mid[k]);
         cudaFree(r->r.d_long[k]);
     }
     delete r;
