@@ -217,6 +217,45 @@ static int expand_full_table(DeviceContext* ctx, Fr** lo, Fr** hi, int* h, int L
     return ZK_OK;
 }
 
+// K consecutive radix-2 DIF stages (half sizes hh, hh/2, ..., hh/2^(K-1)) on
+// groups of 2^K elements held in registers: element t of a group sits at row
+// j0 + t s (s = hh / 2^(K-1)), and stage i pairs t with t + 2^(K-1-i).  The
+// twiddle of a pair is w_{2h}^qh with h the stage's half size and qh the upper
+// element's position mod h, as in one radix-2 stage at a time; K stages cost
+// one shared-memory round trip and one barrier instead of K.
+template <int K>
+__device__ __forceinline__ void dif_stages(Fr* sm, const Fr* sroot, int R, int C, int hh) {
+    constexpr int G = 1 << K;
+    const int s = hh >> (K - 1);
+    for (int g = threadIdx.x; g < (R / G) * C; g += blockDim.x) {
+        const int c = g % C, q = g / C;
+        const int m = q % s, j0 = (q / s) * 2 * hh + m;
+        Fr x[G];
+#pragma unroll
+        for (int t = 0; t < G; t++) fload(x[t], sm + (j0 + t * s) * C + c);
+#pragma unroll
+        for (int i = 0; i < K; i++) {
+            const int half = 1 << (K - 1 - i);
+            const int hi = hh >> i;
+#pragma unroll
+            for (int t = 0; t < G; t++) {
+                if (t & half) continue;
+                Fr a = x[t], b = x[t + half];
+                fadd(x[t], a, b);
+                fsub(x[t + half], a, b);
+                const int tix = (m + (t & (half - 1)) * s) * (R / (2 * hi));
+                if (tix) {
+                    Fr w;
+                    fload(w, sroot + tix);
+                    fmul(x[t + half], x[t + half], w);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < G; t++) fstore(sm + (j0 + t * s) * C + c, x[t]);
+    }
+}
+
 template <int LOGR>
 __global__ void __launch_bounds__(kNttThreads) ntt_pass_kernel(const Fr* __restrict__ src, Fr* __restrict__ dst, int L, int Lp, int C,
                                                                const Fr* __restrict__ roots, const Fr* __restrict__ tw_lo,
@@ -252,26 +291,20 @@ __global__ void __launch_bounds__(kNttThreads) ntt_pass_kernel(const Fr* __restr
         fstore(sm + j1 * C + c, x);
     }
     __syncthreads();
+    // radix-2 DIF stages hh = R/2, R/4, ..., 1, up to three at a time in registers
+    int hh = R / 2;
+    if (LOGR >= 3) {
 #pragma unroll 1
-    for (int hh = R / 2; hh >= 1; hh >>= 1) {
-        for (int u = threadIdx.x; u < (R / 2) * C; u += blockDim.x) {
-            const int c = u % C, q = u / C;
-            const int qh = q % hh;
-            const int j = (q / hh) * 2 * hh + qh;
-            Fr a, b, s, d;
-            fload(a, sm + j * C + c);
-            fload(b, sm + (j + hh) * C + c);
-            fadd(s, a, b);
-            fsub(d, a, b);
-            const int tix = qh * (R / (2 * hh));
-            if (tix) {
-                Fr w;
-                fload(w, sroot + tix);
-                fmul(d, d, w);
-            }
-            fstore(sm + j * C + c, s);
-            fstore(sm + (j + hh) * C + c, d);
+        for (; hh >= 4; hh >>= 3) {
+            dif_stages<3>(sm, sroot, R, C, hh);
+            __syncthreads();
         }
+    }
+    if (hh == 2) {
+        dif_stages<2>(sm, sroot, R, C, hh);
+        __syncthreads();
+    } else if (hh == 1) {
+        dif_stages<1>(sm, sroot, R, C, hh);
         __syncthreads();
     }
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -393,8 +426,8 @@ static int ntt_core(DeviceContext* ctx, cudaStream_t st, Fr* dst, const Fr* src,
         const int r = pp.r[p];
         const uint64_t M = 1ull << (Lp - r);
         const uint64_t lines = n >> r;
-        int C;
-        if (M >= 8) C = 8;
+        int C;  // columns per CTA: R C = kTileElems where the level block allows, at least 8 adjacent
+        if (M >= 8) C = (int)std::min<uint64_t>(M, (uint64_t)std::max(8, kTileElems >> r));
         else C = (int)std::min<uint64_t>(lines, (uint64_t)std::max(1, kTileElems >> r));
         const size_t smem = ((size_t)(1 << r) * C + (1 << r) / 2 + 1) * sizeof(Fr);
         PassFn fn = pass_fn(r);
