@@ -170,6 +170,10 @@ struct zk_groth16_pk {
     mutable std::mutex tab_mu;
     mutable std::vector<zkh::Xyzz<zkh::Fe>> d1_pow;
     mutable std::vector<zkh::Xyzz<zkh::Fp2>> d2_pow;
+    // window tables of the H query (2^(c j) H_i, j < h_W), built on first use
+    uint8_t* h_tab = nullptr;
+    int h_c = 0, h_W = 0;
+    std::mutex h_mu;
 };
 
 namespace zk {
@@ -591,6 +595,40 @@ static void assemble(const zk_groth16_pk* pk, const zkh::Fe& r, const zkh::Fe& s
     assemble_xyzz(pk, r, s, a, b, l, h, b1, outA, outB, outC);
 }
 
+// The H MSM of every proof runs over the same bases (the key's H query) with
+// uniform 254-bit scalars (h's coefficients): precomputed window tables let all
+// its windows share one bucket set and one reduce (msm.cu, msm_tables_run).
+// Below kHTablesMin points the plain MSM is as fast.
+static constexpr int kHTablesMin = 1 << 16;
+
+static int ensure_h_tables(zk_groth16_pk* pk, cudaStream_t st) {
+    std::lock_guard<std::mutex> lock(pk->h_mu);
+    if (pk->h_tab || pk->n_h < kHTablesMin) return ZK_OK;
+    int c, W;
+    g1_window_tables_shape((size_t)pk->n_h, &c, &W);
+    uint8_t* tab = nullptr;
+    ZK_TRY_CUDA(cudaMalloc(&tab, (size_t)W * pk->n_h * 64));
+    const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
+    int rc = g1_window_tables_build(pk->device, st, hq, (size_t)pk->n_h, c, W, tab);
+    if (rc == ZK_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = ZK_ERR_CUDA;
+    if (rc != ZK_OK) {
+        cudaFree(tab);
+        return rc;
+    }
+    pk->h_tab = tab;
+    pk->h_c = c;
+    pk->h_W = W;
+    return ZK_OK;
+}
+
+// sum_{i in [lo, hi)} h_i H_i; d_h holds all n_h coefficients
+static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, size_t hi, uint64_t out[8]) {
+    ZK_TRY(ensure_h_tables(pk, st));
+    if (pk->h_tab) return g1_window_tables_msm(pk->device, st, pk->h_tab, (size_t)pk->n_h, pk->h_c, pk->h_W, lo, hi, d_h + lo, out);
+    const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
+    return zk_msm_g1_device(pk->device, st, hq + lo * 64, d_h + lo, hi - lo, out);
+}
+
 // ------------------------------------------------------------------ prove
 static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* h_witness, const zkh::Fe& r, const zkh::Fe& s,
                  uint64_t outA[8], uint64_t outB[16], uint64_t outC[8]) {
@@ -633,8 +671,8 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     cudaEventElapsedTime(&ms, ev[1], ev[2]);
     stats.compute_h_ms = ms;
 
-    uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm[8] = {0}, b_msm[16];
-    const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m, g1H = 2 * (size_t)m + pk->l;
+    uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm_out[8] = {0}, b_msm[16];
+    const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m;
     zk_msm_stats ms_st;
     ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1A * 64, pk->w, (size_t)m, a_msm));
     zk_msm_last_stats(&ms_st);
@@ -650,7 +688,7 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     }
     const int n_h = std::min<int>((int)n, pk->n_h);
     if (n_h > 0) {
-        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1H * 64, pk->h, (size_t)n_h, h_msm));
+        ZK_TRY(h_msm(pk, st, pk->h, 0, (size_t)n_h, h_msm_out));
         zk_msm_last_stats(&ms_st);
         stats.msm_ms[3] = ms_st.total_device_ms;
     }
@@ -658,7 +696,7 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     zk_msm_last_stats(&ms_st);
     stats.msm_ms[4] = ms_st.total_device_ms;
 
-    assemble(pk, r, s, a_msm, b_msm, l_msm, h_msm, b1_msm, outA, outB, outC);
+    assemble(pk, r, s, a_msm, b_msm, l_msm, h_msm_out, b1_msm, outA, outB, outC);
     ZK_TRY_CUDA(cudaEventRecord(ev[3], st));
     ZK_TRY_CUDA(cudaEventSynchronize(ev[3]));
     cudaEventElapsedTime(&ms, ev[0], ev[3]);
@@ -1004,6 +1042,7 @@ extern "C" void zk_groth16_pk_destroy(zk_groth16_pk* pk) {
     cudaFree(pk->h);
     cudaFree(pk->d_bad);
     cudaFreeHost(pk->h_bad);
+    cudaFree(pk->h_tab);
     delete pk;
 }
 
@@ -1142,4 +1181,24 @@ extern "C" int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const
         std::memcpy(p + 24, C, 64);
     }
     return ZK_OK;
+}
+
+extern "C" int zk_groth16_precompute(zk_groth16_pk* pk, void* stream) {
+    clear_error();
+    if (!pk) return ZK_ERR_INVALID;
+    DeviceContext* ctx;
+    ZK_TRY(get_context(pk->device, &ctx));
+    return ensure_h_tables(pk, (cudaStream_t)stream);
+}
+
+extern "C" int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const void* d_h, uint64_t lo, uint64_t hi, void* out_affine) {
+    clear_error();
+    if (!pk || !out_affine || (hi > lo && !d_h)) return ZK_ERR_INVALID;
+    if (lo > hi || hi > (uint64_t)pk->n_h) {
+        set_error("h_msm: [%llu, %llu) outside the %d-point H query", (unsigned long long)lo, (unsigned long long)hi, pk->n_h);
+        return ZK_ERR_RANGE;
+    }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(pk->device, &ctx));
+    return h_msm(pk, (cudaStream_t)stream, (const Fr*)d_h, lo, hi, (uint64_t*)out_affine);
 }

@@ -54,6 +54,11 @@ struct MsmPlan {
     uint32_t tw2 = 0;    // second-level threads per window
     uint32_t tiles = 0;  // scan tiles
     bool agg = false;    // warp-aggregated bucket atomics (many equal digits)
+    // window w's digits go to buckets w * wstride + b and keys i + w * kstride:
+    // (B, 0) for W separate windows; (0, n) for precomputed window tables,
+    // where the point of (i, w) is 2^(c w) P_i, stored at index i + w n
+    uint32_t wstride = 0;
+    size_t kstride = 0;
 };
 
 static constexpr int kScanTile = 4096;  // 1024 threads x 4
@@ -127,6 +132,8 @@ static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist, int num_sms) {
     // first buckets: one atomic per warp and bucket instead of one per lane.
     // For spread-out scalars the grouping costs more than it saves.
     p.agg = hist && ((size_t)hist[1] + hist[2]) * 256 >= n;
+    p.wstride = p.B;
+    p.kstride = 0;
     return p;
 }
 
@@ -172,7 +179,7 @@ __global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restri
 // The lanes of a warp that hit the same bucket add their count with one atomic
 // (witness scalars put most digits in one bucket: 0/1 range-check bits).
 template <bool kAgg>
-__global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t B,
+__global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t wstride,
                                  uint32_t* __restrict__ counts, uint32_t* __restrict__ digits) {
     const uint32_t lane = threadIdx.x & 31;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
@@ -185,7 +192,7 @@ __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c
             uint32_t code = 0, key = 0xffffffffu;
             if (d) {
                 const uint32_t b = (uint32_t)(d < 0 ? -d : d) - 1;
-                key = (uint32_t)w * B + b;
+                key = (uint32_t)w * wstride + b;
                 code = (d < 0 ? 0x80000000u : 0u) | (b + 1);
             }
             if (kAgg) {
@@ -204,16 +211,17 @@ __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c
 // and key range (about n words), which stay in L2; scattering all windows at once
 // wrote partial sectors all over the whole key array.
 template <bool kAgg>
-__global__ void __launch_bounds__(256) msm_scatter_kernel(const uint32_t* __restrict__ digits, size_t n, uint32_t B,
-                                                          uint32_t blocks_per_window, uint32_t* __restrict__ cursors,
+__global__ void __launch_bounds__(256) msm_scatter_kernel(const uint32_t* __restrict__ digits, size_t n, uint32_t wstride,
+                                                          size_t kstride, uint32_t blocks_per_window, uint32_t* __restrict__ cursors,
                                                           uint32_t* __restrict__ keys) {
     const uint32_t w = blockIdx.x / blocks_per_window;
     const size_t i = (size_t)(blockIdx.x % blocks_per_window) * blockDim.x + threadIdx.x;
     const uint32_t code = i < n ? digits[(size_t)w * n + i] : 0u;
-    const uint32_t key = code ? w * B + (code & 0x7fffffffu) - 1 : 0xffffffffu;
+    const uint32_t key = code ? w * wstride + (code & 0x7fffffffu) - 1 : 0xffffffffu;
+    const uint32_t idx = (uint32_t)(i + w * kstride);  // < 2^31, checked by the caller
     if (!kAgg) {
         if (!code) return;
-        keys[atomicAdd(&cursors[key], 1u)] = (code & 0x80000000u) | (uint32_t)i;
+        keys[atomicAdd(&cursors[key], 1u)] = (code & 0x80000000u) | idx;
         return;
     }
     // lanes with the same bucket take consecutive slots from one atomic
@@ -224,7 +232,7 @@ __global__ void __launch_bounds__(256) msm_scatter_kernel(const uint32_t* __rest
     uint32_t base = 0;
     if (lane == leader) base = atomicAdd(&cursors[key], (uint32_t)__popc(peers));
     base = __shfl_sync(peers, base, leader);
-    keys[base + (uint32_t)__popc(peers & ((1u << lane) - 1))] = (code & 0x80000000u) | (uint32_t)i;
+    keys[base + (uint32_t)__popc(peers & ((1u << lane) - 1))] = (code & 0x80000000u) | idx;
 }
 
 // ------------------------------------------------------------------ scan
@@ -644,6 +652,48 @@ __global__ void fixed_base_kernel(const uint8_t* __restrict__ table, const Fr* _
     }
 }
 
+// out[j n + i] = 2^(c j) P_i (packed affine), j < W: the window tables of a
+// fixed set of bases (all-zero records stay the identity)
+template <class Cv>
+__global__ void window_tables_kernel(const uint8_t* __restrict__ pts, size_t n, int c, int W, uint8_t* __restrict__ out) {
+    using F = typename Cv::F;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        Affine<F> a;
+        load_affine(a, pts + i * Cv::kAffineBytes);
+        fstore(out + i * Cv::kAffineBytes, a.x);
+        fstore(out + i * Cv::kAffineBytes + sizeof(F), a.y);
+        const bool inf = fis_zero(a.x) && fis_zero(a.y);
+        Xyzz<F> cur, d;
+        cur.x = a.x;
+        cur.y = a.y;
+        fset_one(cur.zz);
+        fset_one(cur.zzz);
+        for (int j = 1; j < W; j++) {
+            Affine<F> r;
+            if (inf) {
+                fset_zero(r.x);
+                fset_zero(r.y);
+            } else {
+                for (int t = 0; t < c; t++) {
+                    dbl(d, cur);
+                    cur = d;
+                }
+                // 1 / zz = zzz / (zz zzz), 1 / zzz = zz / (zz zzz): one inversion
+                F q, qi, zi, zzi;
+                fmul(q, cur.zz, cur.zzz);
+                finv_dev(qi, q);
+                fmul(zi, cur.zzz, qi);
+                fmul(zzi, cur.zz, qi);
+                fmul(r.x, cur.x, zi);
+                fmul(r.y, cur.y, zzi);
+            }
+            uint8_t* o = out + ((size_t)j * n + i) * Cv::kAffineBytes;
+            fstore(o, r.x);
+            fstore(o + sizeof(F), r.y);
+        }
+    }
+}
+
 // ================================================================== host side
 template <class Cv>
 struct HostCurve;
@@ -766,9 +816,11 @@ static int msm_sort_phase(DeviceContext* ctx, cudaStream_t st, const void* d_sca
     ZK_TRY_CUDA(cudaEventRecord(ph[0], st));
     ZK_TRY_CUDA(cudaMemsetAsync(S.counts, 0, (P.nb + 1) * sizeof(uint32_t), st));
     if (P.agg)
-        msm_count_kernel<true><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, S.counts, S.digits);
+        msm_count_kernel<true><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.wstride, S.counts,
+                                                                            S.digits);
     else
-        msm_count_kernel<false><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.B, S.counts, S.digits);
+        msm_count_kernel<false><<<grid_for(n, 256, sms * 16), 256, 0, st>>>((const Fr*)d_scalars, n, P.c, P.W, P.wstride, S.counts,
+                                                                             S.digits);
     lc++;
     ZK_TRY_CUDA(cudaEventRecord(ph[1], st));
     scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(S.counts, P.nb, S.tile_sums);
@@ -781,9 +833,9 @@ static int msm_sort_phase(DeviceContext* ctx, cudaStream_t st, const void* d_sca
     {
         const uint32_t bpw = (uint32_t)((n + 255) / 256);
         if (P.agg)
-            msm_scatter_kernel<true><<<bpw * (uint32_t)P.W, 256, 0, st>>>(S.digits, n, P.B, bpw, S.cursors, S.keys);
+            msm_scatter_kernel<true><<<bpw * (uint32_t)P.W, 256, 0, st>>>(S.digits, n, P.wstride, P.kstride, bpw, S.cursors, S.keys);
         else
-            msm_scatter_kernel<false><<<bpw * (uint32_t)P.W, 256, 0, st>>>(S.digits, n, P.B, bpw, S.cursors, S.keys);
+            msm_scatter_kernel<false><<<bpw * (uint32_t)P.W, 256, 0, st>>>(S.digits, n, P.wstride, P.kstride, bpw, S.cursors, S.keys);
     }
     lc++;
     ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
@@ -1004,6 +1056,116 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     for (int k = 0; k < kBatches; k++) stats.bucket_adds += keys_host[k];
     host_combine<Cv>((const uint64_t*)ctx->pinned, P.W, P.c, out_affine);
     return ZK_OK;
+}
+
+// MSM over fixed bases with precomputed window tables (window_tables_kernel):
+// the W digits of scalar i select the multiples 2^(c w) P_i, so every window
+// shares one set of 2^(c-1) buckets and one reduce, and c can be wider than a
+// plain MSM affords (the bucket reduction is paid once, not W times).
+template <class Cv>
+static int msm_tables_run(int device, cudaStream_t st, const uint8_t* tables, size_t n_total, int c, int W, size_t lo, size_t hi,
+                          const void* d_scalars, uint64_t* out_affine) {
+    constexpr int kw = HostCurve<Cv>::kWords;
+    MsmStats& stats = msm_stats();
+    stats = MsmStats();
+    if (hi <= lo) {
+        std::memset(out_affine, 0, 2 * kw * 8);
+        return ZK_OK;
+    }
+    if (hi > n_total || (size_t)W * n_total >= 0x80000000ull || c < 2 || c > 24 || (size_t)W * c < 255) {
+        set_error("msm tables: bad range or shape (n %zu, slice [%zu, %zu), c %d, W %d)", n_total, lo, hi, c, W);
+        return ZK_ERR_RANGE;
+    }
+    const size_t n = hi - lo;
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const double sms = (double)std::max(ctx->num_sms, 1);
+    MsmPlan P;
+    P.c = c;
+    P.W = W;
+    P.B = 1u << (c - 1);
+    P.nb = P.B;
+    P.wstride = 0;
+    P.kstride = n_total;
+    P.max_keys = n * (size_t)W;
+    P.seg = pow2_clamp((double)P.max_keys / (sms * 512.0), 16, 128);
+    P.max_segs = std::max<size_t>(1, (P.max_keys + P.seg - 1) / P.seg);
+    P.tiles = (P.nb + 1 + kScanTile - 1) / kScanTile;
+    P.agg = false;
+    MsmPlan Pr = P;  // the reduce sees one window
+    Pr.W = 1;
+    Pr.chunk = std::min<uint32_t>(P.B, pow2_clamp((double)P.B / (sms * 256.0), 2, 32));
+    Pr.tw = P.B / Pr.chunk;
+    Pr.chunk2 = std::min<uint32_t>(Pr.tw, pow2_clamp((double)Pr.tw / (sms * 64.0), 2, 16));
+    Pr.tw2 = Pr.tw / Pr.chunk2;
+    stats.window_bits = c;
+    stats.num_windows = W;
+    const size_t need = Arena::round(Cv::kXyzzBytes) + sort_scratch_bytes<Cv>(P) + Arena::round((size_t)P.nb * Cv::kXyzzBytes) +
+                        reduce_scratch_bytes<Cv>(Pr);
+    ZK_TRY(ensure_scratch(ctx, need));
+    ZK_TRY(ensure_pinned(ctx, Cv::kXyzzBytes + 64));
+    Arena ar;
+    ar.base = (char*)ctx->scratch;
+    uint8_t* windows_dev = ar.take<uint8_t>(Cv::kXyzzBytes);
+    const SortScratch S = take_sort_scratch<Cv>(ar, P);
+    uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
+    const ReduceScratch R = take_reduce_scratch<Cv>(ar, Pr);
+    LaunchCounter lc;
+    cudaEvent_t t0, t1;
+    ZK_TRY_CUDA(cudaEventCreate(&t0));
+    ZK_TRY_CUDA(cudaEventCreate(&t1));
+    ZK_TRY(scratch_begin(ctx, st));
+    ZK_TRY_CUDA(cudaEventRecord(t0, st));
+    ZK_TRY(msm_sort_phase<Cv>(ctx, st, d_scalars, n, P, S, lc));
+    ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, tables + lo * Cv::kAffineBytes, P, S, buckets, nullptr, lc));
+    ZK_TRY(msm_reduce_phase<Cv>(ctx, st, Pr, S.offsets, buckets, R, windows_dev, lc));
+    ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows_dev, Cv::kXyzzBytes, cudaMemcpyDeviceToHost, st));
+    uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + Cv::kXyzzBytes);
+    ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, S.offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
+    ZK_TRY_CUDA(cudaEventRecord(t1, st));
+    ZK_TRY(scratch_end(ctx, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    float ms_all = 0;
+    cudaEventElapsedTime(&ms_all, t0, t1);
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    for (int i = 0; i < 8; i++) cudaEventElapsedTime(&stats.phase_ms[i], ctx->phase[i], ctx->phase[i + 1]);
+    stats.kernel_launches = lc.n;
+    stats.accumulate_ms = stats.phase_ms[3];
+    stats.total_device_ms = ms_all;
+    stats.bucket_adds = *keys_host;
+    host_combine<Cv>((const uint64_t*)ctx->pinned, 1, c, out_affine);
+    return ZK_OK;
+}
+
+// Window width for precomputed tables of n bases: minimise the mixed additions
+// (n ceil(255 / c), 10 Fp mul each) plus one bucket reduction (2^(c-1) x 30).
+void g1_window_tables_shape(size_t n, int* c_out, int* W_out) {
+    int best = 12;
+    double best_cost = 1e300;
+    for (int c = 8; c <= 22; c++) {
+        const double W = (255 + c - 1) / c;
+        const double cost = (double)n * W * 10.0 + (double)(1u << (c - 1)) * 30.0;
+        if (cost < best_cost) { best_cost = cost; best = c; }
+    }
+    *c_out = best;
+    *W_out = (255 + best - 1) / best;
+}
+
+int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out) {
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    if (!n) return ZK_OK;
+    window_tables_kernel<G1><<<grid_for(n, 128, ctx->num_sms * 8), 128, 0, st>>>((const uint8_t*)d_points, n, c, W, (uint8_t*)d_out);
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t n_total, int c, int W, size_t lo, size_t hi,
+                         const void* d_scalars, uint64_t* out_affine) {
+    return msm_tables_run<G1>(device, st, (const uint8_t*)tables, n_total, c, W, lo, hi, d_scalars, out_affine);
 }
 
 // Full MSM.  src_points / src_scalars are device pointers (host_inputs == 0)

@@ -89,4 +89,11 @@ struct MsmStats {
 };
 MsmStats& msm_stats();
 
+// Precomputed window tables of fixed G1 bases (msm.cu): 2^(c j) P_i for j < W
+// at index j n + i; the MSM of scalars[0, hi - lo) against bases [lo, hi).
+void g1_window_tables_shape(size_t n, int* c, int* W);
+int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out);
+int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t n_total, int c, int W, size_t lo, size_t hi,
+                         const void* d_scalars, uint64_t* out_affine);
+
 }  // namespace zk

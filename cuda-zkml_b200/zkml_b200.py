@@ -80,6 +80,8 @@ _SIGS = {
     "zk_groth16_pk_arrays": [_vp, ctypes.POINTER(Groth16Arrays)],
     "zk_groth16_assemble": [_vp, _vp, _vp, _vp, _vp, _vp],
     "zk_groth16_assemble_parts": [_vp, _vp, _vp, _vp, _i, _vp, _vp],
+    "zk_groth16_h_msm_device": [_vp, _vp, _vp, ctypes.c_uint64, ctypes.c_uint64, _vp],
+    "zk_groth16_precompute": [_vp, _vp],
 }
 for _name, _args in _SIGS.items():
     getattr(lib, _name).argtypes = _args
@@ -480,6 +482,17 @@ class ProvingKey:
         pts = np.zeros(32, np.uint64)
         check(lib.zk_groth16_assemble(self.h, _np_ptr(rr), _np_ptr(ss), _np_ptr(sums), _np_ptr(proof), _np_ptr(pts)))
         return proof.tobytes(), pts[:8], pts[8:24], pts[24:32]
+
+    def precompute(self, stream=None):
+        """Build the H-query window tables now (else the first proof does)."""
+        check(lib.zk_groth16_precompute(self.h, stream))
+
+    def h_msm(self, d_h, lo, hi):
+        """sum_{i in [lo, hi)} h_i H_i over the key's H query (d_h: all n_h
+        coefficients on the device); packed affine (8,) uint64."""
+        out = np.zeros(8, np.uint64)
+        check(lib.zk_groth16_h_msm_device(self.h, _stream(d_h), _dev_ptr(d_h), lo, hi, _np_ptr(out)))
+        return out
 
     def assemble_parts(self, r, s, parts):
         """Proof from per-rank partial sums (a list of 48-word records), summed first."""

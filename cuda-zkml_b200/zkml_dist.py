@@ -401,6 +401,8 @@ class CudaProver:
         out = np.zeros(words, np.uint64)
         if hi <= lo:
             return out
+        if key == "h" and scalar_offset == 0:  # over the key's precomputed H tables
+            return self.pk.h_msm(scalars, lo, hi)
         base = {"a": "a", "b2": "b2", "l": "l_query", "h": "h_query", "b1": "b1"}[key]
         rec = 128 if key == "b2" else 64
         pts = ctypes.c_void_p(self.arr[base] + lo * rec)
