@@ -101,6 +101,18 @@ static uint32_t pow2_clamp(double x, uint32_t lo, uint32_t hi) {
     return p;
 }
 
+// Upper bound on the keys (nonzero signed digits): a b-bit scalar has at most
+// ceil((b + 1) / c) of them.
+static size_t plan_key_bound(const MsmPlan& p, const uint32_t* hist) {
+    size_t key_bound = p.max_keys;
+    if (hist) {
+        size_t d = 0;
+        for (int b = 1; b < 256; b++) d += (size_t)hist[b] * (size_t)((b + 1 + p.c - 1) / p.c);
+        key_bound = std::min(key_bound, d);
+    }
+    return key_bound;
+}
+
 static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist, int num_sms) {
     MsmPlan p;
     p.c = choose_window_bits(n, g2, hist);
@@ -108,14 +120,7 @@ static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist, int num_sms) {
     p.B = 1u << (p.c - 1);
     p.nb = (uint32_t)p.W * p.B;
     p.max_keys = n * (size_t)p.W;
-    // Upper bound on the keys (nonzero signed digits): a b-bit scalar has at
-    // most ceil((b + 1) / c) of them.
-    size_t key_bound = p.max_keys;
-    if (hist) {
-        size_t d = 0;
-        for (int b = 1; b < 256; b++) d += (size_t)hist[b] * (size_t)((b + 1 + p.c - 1) / p.c);
-        key_bound = std::min(key_bound, d);
-    }
+    const size_t key_bound = plan_key_bound(p, hist);
     // Keys per accumulate thread and buckets per reduce thread: long serial
     // chains when there is work for every SM many times over, short ones when
     // there is little (a witness MSM, a shard of one), so that enough threads
@@ -838,8 +843,6 @@ static int msm_sort_phase(DeviceContext* ctx, cudaStream_t st, const void* d_sca
             msm_scatter_kernel<false><<<bpw * (uint32_t)P.W, 256, 0, st>>>(S.digits, n, P.wstride, P.kstride, bpw, S.cursors, S.keys);
     }
     lc++;
-    ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
-    ZK_TRY_CUDA(cudaMemsetAsync(S.last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     ZK_TRY_CUDA(cudaGetLastError());
     return ZK_OK;
 }
@@ -851,6 +854,8 @@ template <class Cv>
 static int msm_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const MsmPlan& P, const SortScratch& S,
                                 uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
     cudaEvent_t* ph = ctx->phase;
+    ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(S.last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     if (points_ready) ZK_TRY_CUDA(cudaStreamWaitEvent(st, points_ready, 0));
     ZK_TRY_CUDA(cudaEventRecord(ph[3], st));
     {
@@ -1166,6 +1171,95 @@ int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, si
 int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t n_total, int c, int W, size_t lo, size_t hi,
                          const void* d_scalars, uint64_t* out_affine) {
     return msm_tables_run<G1>(device, st, (const uint8_t*)tables, n_total, c, W, lo, hi, d_scalars, out_affine);
+}
+
+// Several MSMs over one vector of device scalars (the witness of a proof, for
+// the A, B1 and B2 queries): one bit-length histogram, one plan and one counting
+// sort, then an accumulate + reduce per point set (G1 or G2 packed affine).
+int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
+                           const int* is_g2, uint64_t* const* outs, float* set_ms) {
+    MsmStats& stats = msm_stats();
+    stats = MsmStats();
+    for (int k = 0; k < n_sets; k++) {
+        std::memset(outs[k], 0, is_g2[k] ? 128 : 64);
+        if (set_ms) set_ms[k] = 0.f;
+    }
+    if (n == 0 || n_sets == 0) return ZK_OK;
+    if (n > 0x7fffffffull || n_sets > 8) {
+        set_error("msm: %zu points or %d point sets out of range", n, n_sets);
+        return ZK_ERR_RANGE;
+    }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const double sms = (double)std::max(ctx->num_sms, 1);
+    uint32_t* hist_dev = nullptr;
+    ZK_TRY(ensure_pinned(ctx, 4096));
+    uint32_t* hist_host = (uint32_t*)ctx->pinned;
+    ZK_TRY(scratch_begin(ctx, st));
+    ZK_TRY_CUDA(cudaMallocAsync((void**)&hist_dev, 256 * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(hist_dev, 0, 256 * sizeof(uint32_t), st));
+    msm_bitlen_hist_kernel<<<grid_for(n, 256, ctx->num_sms * 4), 256, 0, st>>>((const Fr*)d_scalars, n, hist_dev);
+    ZK_TRY_CUDA(cudaMemcpyAsync(hist_host, hist_dev, 256 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY_CUDA(cudaFreeAsync(hist_dev, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    uint32_t hist[256];
+    std::memcpy(hist, hist_host, sizeof hist);
+    const MsmPlan P = make_plan(n, false, hist, ctx->num_sms);  // the sort, and the G1 accumulates
+    MsmPlan P2 = P;                                             // G2 accumulates: shorter segments
+    P2.seg = pow2_clamp((double)plan_key_bound(P, hist) / (sms * 512.0), 8, 64);
+    P2.max_segs = std::max<size_t>(1, (plan_key_bound(P, hist) + P2.seg - 1) / P2.seg);
+    stats.window_bits = P.c;
+    stats.num_windows = P.W;
+
+    size_t need = sort_scratch_bytes<G1>(P) + Arena::round(P2.max_segs * G2::kXyzzBytes) * 2 + Arena::round(P2.max_segs * 4) * 2 +
+                  Arena::round((size_t)P.nb * G2::kXyzzBytes) + reduce_scratch_bytes<G2>(P) +
+                  Arena::round((size_t)n_sets * P.W * G2::kXyzzBytes);
+    ZK_TRY(ensure_scratch(ctx, need));
+    ZK_TRY(ensure_pinned(ctx, (size_t)n_sets * P.W * G2::kXyzzBytes + 64));
+    Arena ar;
+    ar.base = (char*)ctx->scratch;
+    const SortScratch S = take_sort_scratch<G1>(ar, P);
+    SortScratch S2 = S;  // same keys, G2-sized partial slots
+    S2.part_first = ar.take<uint8_t>(P2.max_segs * G2::kXyzzBytes);
+    S2.part_last = ar.take<uint8_t>(P2.max_segs * G2::kXyzzBytes);
+    S2.first_bucket = ar.take<uint32_t>(P2.max_segs);
+    S2.last_bucket = ar.take<uint32_t>(P2.max_segs);
+    uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * G2::kXyzzBytes);
+    const ReduceScratch R = take_reduce_scratch<G2>(ar, P);  // the larger record size serves both curves
+    uint8_t* windows = ar.take<uint8_t>((size_t)n_sets * P.W * G2::kXyzzBytes);
+    LaunchCounter lc;
+    cudaEvent_t ev[9];
+    for (int k = 0; k <= n_sets; k++) ZK_TRY_CUDA(cudaEventCreate(&ev[k]));
+    ZK_TRY(msm_sort_phase<G1>(ctx, st, d_scalars, n, P, S, lc));
+    ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
+    for (int k = 0; k < n_sets; k++) {
+        uint8_t* win = windows + (size_t)k * P.W * G2::kXyzzBytes;
+        if (is_g2[k]) {
+            ZK_TRY(msm_accumulate_phase<G2>(ctx, st, d_points[k], P2, S2, buckets, nullptr, lc));
+            ZK_TRY(msm_reduce_phase<G2>(ctx, st, P2, S.offsets, buckets, R, win, lc));
+        } else {
+            ZK_TRY(msm_accumulate_phase<G1>(ctx, st, d_points[k], P, S, buckets, nullptr, lc));
+            ZK_TRY(msm_reduce_phase<G1>(ctx, st, P, S.offsets, buckets, R, win, lc));
+        }
+        ZK_TRY_CUDA(cudaEventRecord(ev[k + 1], st));
+    }
+    ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows, (size_t)n_sets * P.W * G2::kXyzzBytes, cudaMemcpyDeviceToHost, st));
+    uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)n_sets * P.W * G2::kXyzzBytes);
+    ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, S.offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ZK_TRY(scratch_end(ctx, st));
+    ZK_TRY_CUDA(cudaStreamSynchronize(st));
+    if (set_ms)  // the shared sort is not in any set's time
+        for (int k = 0; k < n_sets; k++) cudaEventElapsedTime(&set_ms[k], ev[k], ev[k + 1]);
+    for (int k = 0; k <= n_sets; k++) cudaEventDestroy(ev[k]);
+    stats.kernel_launches = lc.n;
+    stats.bucket_adds = (long long)*keys_host * n_sets;
+    for (int k = 0; k < n_sets; k++) {
+        const uint64_t* win = (const uint64_t*)((const uint8_t*)ctx->pinned + (size_t)k * P.W * G2::kXyzzBytes);
+        if (is_g2[k]) host_combine<G2>(win, P.W, P.c, outs[k]);
+        else host_combine<G1>(win, P.W, P.c, outs[k]);
+    }
+    return ZK_OK;
 }
 
 // Full MSM.  src_points / src_scalars are device pointers (host_inputs == 0)

@@ -93,6 +93,10 @@ MsmStats& msm_stats();
 // at index j n + i; the MSM of scalars[0, hi - lo) against bases [lo, hi).
 void g1_window_tables_shape(size_t n, int* c, int* W);
 int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out);
+// Several MSMs (G1 or G2 point sets) over the same device scalars with one
+// shared counting sort (msm.cu); outs[k]: 64 or 128 host bytes.
+int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
+                           const int* is_g2, uint64_t* const* outs, float* set_ms);
 int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t n_total, int c, int W, size_t lo, size_t hi,
                          const void* d_scalars, uint64_t* out_affine);
 
