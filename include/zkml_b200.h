@@ -290,9 +290,10 @@ int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, c
                         void* proof256, void* points);
 /* The H MSM of a proof, sum_{i in [lo, hi)} h_i H_i over the key's H query
  * (groth16.cu:817), with d_h the n_h device coefficients of h.  From 2^16
- * points it runs over precomputed window tables of the query (2^(c j) H_i:
- * c = 20 and 13 tables, 3.5 GB, at 2^22), built on first use or by
- * zk_groth16_precompute; all windows then share one bucket set and one reduce. */
+ * points, for a slice of at least 3/4 of the query, it runs over precomputed
+ * window tables of the query (2^(c j) H_i: c = 20 and 13 tables, 3.5 GB, at
+ * 2^22), built on first use or by zk_groth16_precompute; all windows then share
+ * one bucket set and one reduce.  Smaller slices run the plain MSM. */
 int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const void* d_h, uint64_t lo, uint64_t hi,
                             void* out_affine);
 /* Build the key's precomputed tables now instead of at the first proof. */
