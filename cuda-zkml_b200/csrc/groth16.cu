@@ -679,16 +679,20 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm_out[8] = {0}, b_msm[16];
     const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m;
     zk_msm_stats ms_st;
-    {  // A, B (G2) and B1 share the witness as scalars: one counting sort for the three
-        const void* pts[3] = {pk->g1 + g1A * 64, pk->g2, pk->g1 + g1B1 * 64};
-        const int g2[3] = {0, 1, 0};
-        uint64_t* outs[3] = {a_msm, b_msm, b1_msm};
-        float set_ms[3] = {0, 0, 0};
+    {  // A, B (G2), B1 and L share the witness as scalars: one counting sort for the
+       // four (L takes the private range of it, groth16.cu:810)
+        const int num_priv = std::max(0, std::min(pk->l, m - 1 - pub));
+        const int sets = num_priv > 0 ? 4 : 3;
+        const void* pts[4] = {pk->g1 + g1A * 64, pk->g2, pk->g1 + g1B1 * 64, pk->g1 + g1L * 64};
+        const int g2[4] = {0, 1, 0, 0};
+        const uint32_t range[8] = {0, 0xffffffffu, 0, 0xffffffffu, 0, 0xffffffffu, (uint32_t)(1 + pub), (uint32_t)(1 + pub + num_priv)};
+        uint64_t* outs[4] = {a_msm, b_msm, b1_msm, l_msm};
+        float set_ms[4] = {0, 0, 0, 0};
         cudaEvent_t s0, s1;
         ZK_TRY_CUDA(cudaEventCreate(&s0));
         ZK_TRY_CUDA(cudaEventCreate(&s1));
         ZK_TRY_CUDA(cudaEventRecord(s0, st));
-        ZK_TRY(msm_shared_scalars_run(pk->device, st, pk->w, (size_t)m, 3, pts, g2, outs, set_ms));
+        ZK_TRY(msm_shared_scalars_run(pk->device, st, pk->w, (size_t)m, sets, pts, g2, range, outs, set_ms));
         ZK_TRY_CUDA(cudaEventRecord(s1, st));
         ZK_TRY_CUDA(cudaEventSynchronize(s1));
         float all = 0;
@@ -696,15 +700,10 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
         cudaEventDestroy(s0);
         cudaEventDestroy(s1);
         // the shared histogram and sort are charged to A
-        stats.msm_ms[0] = all - set_ms[1] - set_ms[2];
+        stats.msm_ms[0] = all - set_ms[1] - set_ms[2] - set_ms[3];
         stats.msm_ms[1] = set_ms[1];
         stats.msm_ms[4] = set_ms[2];
-    }
-    const int num_priv = std::min(pk->l, m - 1 - pub);
-    if (num_priv > 0) {
-        ZK_TRY(zk_msm_g1_device(pk->device, st, pk->g1 + g1L * 64, pk->w + 1 + pub, (size_t)num_priv, l_msm));
-        zk_msm_last_stats(&ms_st);
-        stats.msm_ms[2] = ms_st.total_device_ms;
+        stats.msm_ms[2] = set_ms[3];
     }
     const int n_h = std::min<int>((int)n, pk->n_h);
     if (n_h > 0) {

@@ -319,11 +319,19 @@ __global__ void scan_finish_kernel(const uint32_t* __restrict__ in, uint32_t len
 }
 
 // ------------------------------------------------------------------ accumulate
+// The point of a key: keys whose index lies outside [idx_lo, idx_hi) are skipped
+// (an MSM over a sub-range of scalars that shares another MSM's sort); the
+// others read point idx - idx_lo.
 template <class Cv>
-__device__ __forceinline__ void load_signed_point(Affine<typename Cv::F>& a, bool& is_inf, const uint8_t* points, uint32_t key) {
+__device__ __forceinline__ void load_signed_point(Affine<typename Cv::F>& a, bool& is_inf, const uint8_t* points, uint32_t key,
+                                                  uint32_t idx_lo, uint32_t idx_hi) {
     using F = typename Cv::F;
     uint32_t idx = key & 0x7fffffffu;
-    load_affine(a, points + (size_t)idx * Cv::kAffineBytes);
+    if (idx < idx_lo || idx >= idx_hi) {
+        is_inf = true;
+        return;
+    }
+    load_affine(a, points + (size_t)(idx - idx_lo) * Cv::kAffineBytes);
     is_inf = fis_zero(a.x) && fis_zero(a.y);
     if (key >> 31) { F t; fneg(t, a.y); a.y = t; }
 }
@@ -332,7 +340,7 @@ template <class Cv>
 __global__ void __launch_bounds__(128) msm_accumulate_kernel(
     const uint32_t* __restrict__ keys, const uint32_t* __restrict__ offsets, uint32_t nb, const uint8_t* __restrict__ points,
     uint32_t seg, uint8_t* __restrict__ bucket_sums, uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last,
-    uint32_t* __restrict__ first_bucket, uint32_t* __restrict__ last_bucket) {
+    uint32_t* __restrict__ first_bucket, uint32_t* __restrict__ last_bucket, uint32_t idx_lo, uint32_t idx_hi) {
     using F = typename Cv::F;
     const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t K = offsets[nb];
@@ -376,7 +384,7 @@ __global__ void __launch_bounds__(128) msm_accumulate_kernel(
         }
         Affine<F> a;
         bool inf;
-        load_signed_point<Cv>(a, inf, points, keys[p]);
+        load_signed_point<Cv>(a, inf, points, keys[p], idx_lo, idx_hi);
         if (!inf) madd(acc, a);
     }
     flush();
@@ -852,7 +860,8 @@ static int msm_sort_phase(DeviceContext* ctx, cudaStream_t st, const void* d_sca
 // points when `points_ready` is recorded.  Records phase events 3..5.
 template <class Cv>
 static int msm_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const MsmPlan& P, const SortScratch& S,
-                                uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
+                                uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc, uint32_t idx_lo = 0,
+                                uint32_t idx_hi = 0xffffffffu) {
     cudaEvent_t* ph = ctx->phase;
     ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     ZK_TRY_CUDA(cudaMemsetAsync(S.last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
@@ -863,7 +872,8 @@ static int msm_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void*
         unsigned blocks = (unsigned)((P.max_segs + threads - 1) / threads);
         if (blocks < 1) blocks = 1;
         msm_accumulate_kernel<Cv><<<blocks, threads, 0, st>>>(S.keys, S.offsets, P.nb, (const uint8_t*)d_points, P.seg, buckets,
-                                                               S.part_first, S.part_last, S.first_bucket, S.last_bucket);
+                                                               S.part_first, S.part_last, S.first_bucket, S.last_bucket, idx_lo,
+                                                               idx_hi);
         lc++;
     }
     ZK_TRY_CUDA(cudaEventRecord(ph[4], st));
@@ -1174,10 +1184,12 @@ int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t
 }
 
 // Several MSMs over one vector of device scalars (the witness of a proof, for
-// the A, B1 and B2 queries): one bit-length histogram, one plan and one counting
-// sort, then an accumulate + reduce per point set (G1 or G2 packed affine).
+// the A, B1, B2 and L queries): one bit-length histogram, one plan and one
+// counting sort, then an accumulate + reduce per point set (G1 or G2 packed
+// affine).  idx_range (optional, 2 per set): set k uses the scalars
+// [lo, hi) only, against its points 0 .. hi - lo.
 int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
-                           const int* is_g2, uint64_t* const* outs, float* set_ms) {
+                           const int* is_g2, const uint32_t* idx_range, uint64_t* const* outs, float* set_ms) {
     MsmStats& stats = msm_stats();
     stats = MsmStats();
     for (int k = 0; k < n_sets; k++) {
@@ -1235,11 +1247,12 @@ int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, s
     ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
     for (int k = 0; k < n_sets; k++) {
         uint8_t* win = windows + (size_t)k * P.W * G2::kXyzzBytes;
+        const uint32_t ilo = idx_range ? idx_range[2 * k] : 0u, ihi = idx_range ? idx_range[2 * k + 1] : 0xffffffffu;
         if (is_g2[k]) {
-            ZK_TRY(msm_accumulate_phase<G2>(ctx, st, d_points[k], P2, S2, buckets, nullptr, lc));
+            ZK_TRY(msm_accumulate_phase<G2>(ctx, st, d_points[k], P2, S2, buckets, nullptr, lc, ilo, ihi));
             ZK_TRY(msm_reduce_phase<G2>(ctx, st, P2, S.offsets, buckets, R, win, lc));
         } else {
-            ZK_TRY(msm_accumulate_phase<G1>(ctx, st, d_points[k], P, S, buckets, nullptr, lc));
+            ZK_TRY(msm_accumulate_phase<G1>(ctx, st, d_points[k], P, S, buckets, nullptr, lc, ilo, ihi));
             ZK_TRY(msm_reduce_phase<G1>(ctx, st, P, S.offsets, buckets, R, win, lc));
         }
         ZK_TRY_CUDA(cudaEventRecord(ev[k + 1], st));

@@ -96,7 +96,7 @@ int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, si
 // Several MSMs (G1 or G2 point sets) over the same device scalars with one
 // shared counting sort (msm.cu); outs[k]: 64 or 128 host bytes.
 int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
-                           const int* is_g2, uint64_t* const* outs, float* set_ms);
+                           const int* is_g2, const uint32_t* idx_range, uint64_t* const* outs, float* set_ms);
 int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t n_total, int c, int W, size_t lo, size_t hi,
                          const void* d_scalars, uint64_t* out_affine);
 
