@@ -256,8 +256,20 @@ __device__ __forceinline__ void dif_stages(Fr* sm, const Fr* sroot, int R, int C
     }
 }
 
+// Radix-2 stages held in registers per shared-memory round trip (1..3) and the
+// CTAs per SM the passes are compiled for.  Measured at 2^24 (forward): groups of
+// 4 at 3 CTAs per SM (76 registers, no spills) 4.92 ms; groups of 8 at 2 CTAs
+// (124 registers) 5.07 ms, at 3 CTAs (80 registers, spills) 5.03 ms; groups of
+// 8 left unbounded (144 registers, 1 CTA) 7.10 ms; one stage at a time 5.58 ms.
+#ifndef ZK_NTT_MAXK
+#define ZK_NTT_MAXK 2
+#endif
+#ifndef ZK_NTT_MINB
+#define ZK_NTT_MINB 3
+#endif
+
 template <int LOGR>
-__global__ void __launch_bounds__(kNttThreads) ntt_pass_kernel(const Fr* __restrict__ src, Fr* __restrict__ dst, int L, int Lp, int C,
+__global__ void __launch_bounds__(kNttThreads, ZK_NTT_MINB) ntt_pass_kernel(const Fr* __restrict__ src, Fr* __restrict__ dst, int L, int Lp, int C,
                                                                const Fr* __restrict__ roots, const Fr* __restrict__ tw_lo,
                                                                const Fr* __restrict__ tw_hi, int h, const Fr* __restrict__ cs_lo,
                                                                const Fr* __restrict__ cs_hi, int cs_h) {
@@ -291,19 +303,24 @@ __global__ void __launch_bounds__(kNttThreads) ntt_pass_kernel(const Fr* __restr
         fstore(sm + j1 * C + c, x);
     }
     __syncthreads();
-    // radix-2 DIF stages hh = R/2, R/4, ..., 1, up to three at a time in registers
+    // radix-2 DIF stages hh = R/2, R/4, ..., 1, up to ZK_NTT_MAXK at a time in registers
     int hh = R / 2;
-    if (LOGR >= 3) {
+    if (ZK_NTT_MAXK >= 3 && LOGR >= 3) {
 #pragma unroll 1
         for (; hh >= 4; hh >>= 3) {
             dif_stages<3>(sm, sroot, R, C, hh);
             __syncthreads();
         }
     }
-    if (hh == 2) {
-        dif_stages<2>(sm, sroot, R, C, hh);
-        __syncthreads();
-    } else if (hh == 1) {
+    if (ZK_NTT_MAXK >= 2) {
+#pragma unroll 1
+        for (; hh >= 2; hh >>= 2) {
+            dif_stages<2>(sm, sroot, R, C, hh);
+            __syncthreads();
+        }
+    }
+#pragma unroll 1
+    for (; hh >= 1; hh >>= 1) {
         dif_stages<1>(sm, sroot, R, C, hh);
         __syncthreads();
     }
