@@ -634,6 +634,44 @@ static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, s
     return zk_msm_g1_device(pk->device, st, hq + lo * 64, d_h + lo, hi - lo, out);
 }
 
+// The MSMs of a proof whose scalars are the witness (groth16.cu:776-827), over
+// the witness slice [lo, hi): A, B (G2) and B1 over its points [lo, hi), L over
+// the private part of the slice (L_j pairs with w_{1 + pub + j}).  One
+// histogram and one counting sort serve the four.  *all_ms: device time.
+static int witness_msms(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_w, size_t lo, size_t hi, uint64_t a[8], uint64_t b[16],
+                        uint64_t b1[8], uint64_t l[8], float set_ms[4], float* all_ms) {
+    const size_t m = (size_t)pk->m, pub = (size_t)pk->num_public;
+    const size_t num_priv = (size_t)std::max(0, std::min(pk->l, pk->m - 1 - pk->num_public));
+    if (lo > hi || hi > m) {
+        set_error("witness MSMs: slice [%zu, %zu) outside the %zu-entry witness", lo, hi, m);
+        return ZK_ERR_RANGE;
+    }
+    // L's scalars w[1 + pub, 1 + pub + num_priv) inside the slice, as local indices
+    const size_t l_lo = std::max(lo, 1 + pub), l_hi = std::min(hi, 1 + pub + num_priv);
+    const bool has_l = l_hi > l_lo;
+    const int sets = has_l ? 4 : 3;
+    const void* pts[4] = {pk->g1 + lo * 64, pk->g2 + lo * 128, pk->g1 + (m + lo) * 64,
+                          pk->g1 + (2 * m + (has_l ? l_lo - 1 - pub : 0)) * 64};
+    const int g2[4] = {0, 1, 0, 0};
+    const uint32_t range[8] = {0, 0xffffffffu, 0, 0xffffffffu, 0, 0xffffffffu, (uint32_t)(has_l ? l_lo - lo : 0),
+                               (uint32_t)(has_l ? l_hi - lo : 0)};
+    std::memset(l, 0, 64);
+    uint64_t* outs[4] = {a, b, b1, l};
+    cudaEvent_t s0, s1;
+    ZK_TRY_CUDA(cudaEventCreate(&s0));
+    ZK_TRY_CUDA(cudaEventCreate(&s1));
+    ZK_TRY_CUDA(cudaEventRecord(s0, st));
+    const int rc = msm_shared_scalars_run(pk->device, st, d_w + lo, hi - lo, sets, pts, g2, range, outs, set_ms);
+    if (rc == ZK_OK) {
+        cudaEventRecord(s1, st);
+        cudaEventSynchronize(s1);
+        cudaEventElapsedTime(all_ms, s0, s1);
+    }
+    cudaEventDestroy(s0);
+    cudaEventDestroy(s1);
+    return rc;
+}
+
 // ------------------------------------------------------------------ prove
 static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* h_witness, const zkh::Fe& r, const zkh::Fe& s,
                  uint64_t outA[8], uint64_t outB[16], uint64_t outC[8]) {
@@ -679,26 +717,9 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm_out[8] = {0}, b_msm[16];
     const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m;
     zk_msm_stats ms_st;
-    {  // A, B (G2), B1 and L share the witness as scalars: one counting sort for the
-       // four (L takes the private range of it, groth16.cu:810)
-        const int num_priv = std::max(0, std::min(pk->l, m - 1 - pub));
-        const int sets = num_priv > 0 ? 4 : 3;
-        const void* pts[4] = {pk->g1 + g1A * 64, pk->g2, pk->g1 + g1B1 * 64, pk->g1 + g1L * 64};
-        const int g2[4] = {0, 1, 0, 0};
-        const uint32_t range[8] = {0, 0xffffffffu, 0, 0xffffffffu, 0, 0xffffffffu, (uint32_t)(1 + pub), (uint32_t)(1 + pub + num_priv)};
-        uint64_t* outs[4] = {a_msm, b_msm, b1_msm, l_msm};
-        float set_ms[4] = {0, 0, 0, 0};
-        cudaEvent_t s0, s1;
-        ZK_TRY_CUDA(cudaEventCreate(&s0));
-        ZK_TRY_CUDA(cudaEventCreate(&s1));
-        ZK_TRY_CUDA(cudaEventRecord(s0, st));
-        ZK_TRY(msm_shared_scalars_run(pk->device, st, pk->w, (size_t)m, sets, pts, g2, range, outs, set_ms));
-        ZK_TRY_CUDA(cudaEventRecord(s1, st));
-        ZK_TRY_CUDA(cudaEventSynchronize(s1));
-        float all = 0;
-        cudaEventElapsedTime(&all, s0, s1);
-        cudaEventDestroy(s0);
-        cudaEventDestroy(s1);
+    {  // A, B (G2), B1 and L share the witness as scalars: one counting sort
+        float set_ms[4] = {0, 0, 0, 0}, all = 0;
+        ZK_TRY(witness_msms(pk, st, pk->w, 0, (size_t)m, a_msm, b_msm, b1_msm, l_msm, set_ms, &all));
         // the shared histogram and sort are charged to A
         stats.msm_ms[0] = all - set_ms[1] - set_ms[2] - set_ms[3];
         stats.msm_ms[1] = set_ms[1];
@@ -1217,4 +1238,15 @@ extern "C" int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const vo
     DeviceContext* ctx;
     ZK_TRY(get_context(pk->device, &ctx));
     return h_msm(pk, (cudaStream_t)stream, (const Fr*)d_h, lo, hi, (uint64_t*)out_affine);
+}
+
+extern "C" int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, const void* d_witness, uint64_t lo, uint64_t hi,
+                                              void* sums) {
+    clear_error();
+    if (!pk || !sums || (hi > lo && !d_witness)) return ZK_ERR_INVALID;
+    DeviceContext* ctx;
+    ZK_TRY(get_context(pk->device, &ctx));
+    uint64_t* q = (uint64_t*)sums;  // A (8) | B2 (16) | L (8) | H (8, untouched) | B1 (8) words
+    float set_ms[4], all = 0;
+    return witness_msms(pk, (cudaStream_t)stream, (const Fr*)d_witness, lo, hi, q, q + 8, q + 40, q + 24, set_ms, &all);
 }

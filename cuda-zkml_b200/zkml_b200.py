@@ -82,6 +82,7 @@ _SIGS = {
     "zk_groth16_assemble_parts": [_vp, _vp, _vp, _vp, _i, _vp, _vp],
     "zk_groth16_h_msm_device": [_vp, _vp, _vp, ctypes.c_uint64, ctypes.c_uint64, _vp],
     "zk_groth16_precompute": [_vp, _vp],
+    "zk_groth16_witness_msms_device": [_vp, _vp, _vp, ctypes.c_uint64, ctypes.c_uint64, _vp],
 }
 for _name, _args in _SIGS.items():
     getattr(lib, _name).argtypes = _args
@@ -486,6 +487,13 @@ class ProvingKey:
     def precompute(self, stream=None):
         """Build the H-query window tables now (else the first proof does)."""
         check(lib.zk_groth16_precompute(self.h, stream))
+
+    def witness_msms(self, d_w, lo, hi):
+        """A, B2, B1 and L sums over the witness slice [lo, hi) (d_w: the whole
+        witness on the device), one shared sort: a 48-word sums record with H zero."""
+        rec = np.zeros(48, np.uint64)
+        check(lib.zk_groth16_witness_msms_device(self.h, _stream(d_w), _dev_ptr(d_w), lo, hi, _np_ptr(rec)))
+        return rec
 
     def h_msm(self, d_h, lo, hi):
         """sum_{i in [lo, hi)} h_i H_i over the key's H query (d_h: all n_h

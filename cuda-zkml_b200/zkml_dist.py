@@ -58,17 +58,16 @@ def sharded_msm(points, scalars, local_msm, add, group=None, device=None):
 #      (groth16.cu:350-363) while the other ranks start their MSM slices.
 #   3. three broadcasts of the coset evaluations; every rank forms
 #      (a b - c) / (g^n - 1) and the coset INTT (groth16.cu:364-383): h.
-#   4. every MSM (A, B2, L, H, B1) is point-sharded over all ranks; the ranks
-#      all-gather their partial sums (5 points each) and fold them.
+#   4. every MSM (A, B2, L, H, B1) is point-sharded over all ranks: a rank's
+#      share of the witness MSMs is one slice of the witness, whose four MSMs
+#      share one counting sort; the ranks all-gather their partial sums (5
+#      points each) and fold them.
 #   5. the proof is assembled from the five sums (groth16.cu:774-844).
 # The result is byte-identical to the one-device proof: every step is exact.
 
 MSM_ORDER = ("a", "b2", "l", "h", "b1")  # layout of the 48-word sums record
 _WORDS = {"a": 8, "b2": 16, "l": 8, "h": 8, "b1": 8}
 WITNESS_MSMS = ("a", "b2", "l", "b1")
-# relative cost per point when the witness MSMs are cut into pieces (a G2
-# point costs about 1.5 G1 points at witness-scalar sizes)
-_MSM_WEIGHT = {"a": 1.0, "b2": 1.5, "l": 1.0, "b1": 1.0}
 _NO_ROW = np.iinfo(np.int64).max
 
 
@@ -111,28 +110,6 @@ def weighted_bounds(n, shares, rank):
     cut = [int(round(x * n)) for x in acc]
     cut[-1] = n
     return cut[rank], cut[rank + 1]
-
-
-def witness_pieces(sizes, shares, rank):
-    """This rank's [(msm, lo, hi)] of the witness MSMs.  The four MSMs are laid
-    end to end (weighted by _MSM_WEIGHT) and cut at the cumulative shares, so a
-    rank gets one contiguous run touching one or two MSMs instead of a small
-    slice of each: every MSM call has a fixed cost."""
-    lens = [sizes[k] * _MSM_WEIGHT[k] for k in WITNESS_MSMS]
-    total = float(sum(lens))
-    cum = np.concatenate([[0.0], np.cumsum(np.asarray(shares, dtype=np.float64))])
-    cum = cum / (cum[-1] if cum[-1] > 0 else 1.0) * total
-    out, off = [], 0.0
-    for k, length in zip(WITNESS_MSMS, lens):
-        w = _MSM_WEIGHT[k]
-
-        def point(x):
-            return int(min(sizes[k], max(0, round((x - off) / w))))
-        lo, hi = point(cum[rank]), point(cum[rank + 1])  # cum runs from 0 to total: the cuts cover [0, size)
-        if hi > lo:
-            out.append((k, lo, hi))
-        off += length
-    return out
 
 
 def balance_shares(poly_s, msm_s, shares, damping=0.5, floor=0.02):
@@ -203,11 +180,10 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     mark("cosets")
 
     # the witness MSMs come before the broadcasts, which wait for the slowest
-    # polynomial owner: owners take smaller slices (balance_shares)
+    # polynomial owner: owners take smaller slices of the witness (balance_shares)
     t_msm = prover.timer()
-    sums = {k: np.zeros(_WORDS[k], np.uint64) for k in WITNESS_MSMS}
-    for key, a, b in witness_pieces(sizes, shares, rank):
-        sums[key] = prover.msm(key, a, b, w, 1 + pub if key == "l" else 0)
+    a, b = weighted_bounds(m, shares, rank)
+    sums = unpack_sums(prover.witness_msms(w, a, b))
     t_msm = prover.elapsed(t_msm)
     mark("witness_msms")
     for k in range(3):
@@ -394,6 +370,9 @@ class CudaProver:
     def h_from_cosets(self, a, b, c):
         q = self.Z.compute_h_pointwise(a, b, c, self.log_n)
         return self.Z.ntt(q, self.log_n, inverse=True, coset=self.g, out=q)
+
+    def witness_msms(self, w, lo, hi):
+        return self.pk.witness_msms(w, lo, hi)
 
     def msm(self, key, lo, hi, scalars, scalar_offset):
         import ctypes

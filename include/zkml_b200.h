@@ -296,6 +296,13 @@ int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, c
  * one bucket set and one reduce.  Smaller slices run the plain MSM. */
 int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const void* d_h, uint64_t lo, uint64_t hi,
                             void* out_affine);
+/* The MSMs of a proof whose scalars are the witness, over the witness slice
+ * [lo, hi) (d_witness: all num_variables device Fr): sum w_i A_i, w_i B2_i and
+ * w_i B1_i for i in the slice, and w_i L_{i - 1 - pub} for the private i in it,
+ * with one shared counting sort.  Writes A, B2, L and B1 into a 384-byte sums
+ * record (the layout of zk_groth16_assemble; H is left untouched). */
+int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, const void* d_witness, uint64_t lo,
+                                   uint64_t hi, void* sums);
 /* Build the key's precomputed tables now instead of at the first proof. */
 int zk_groth16_precompute(zk_groth16_pk* pk, void* stream);
 

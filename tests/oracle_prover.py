@@ -89,6 +89,17 @@ class OracleProver:
         sc = _np(scalars)[off + lo:off + hi]
         return O.msm_g2(pts, sc) if key == "b2" else O.msm_g1(pts, sc)
 
+    def witness_msms(self, w, lo, hi):
+        """A, B2, B1 over the witness slice [lo, hi), L over its private part."""
+        import zkml_dist as D
+        pub = self.num_public
+        num_priv = max(0, min(self.l, self.m - 1 - pub))
+        sums = {"a": self.msm("a", lo, hi, w, 0), "b2": self.msm("b2", lo, hi, w, 0), "b1": self.msm("b1", lo, hi, w, 0),
+                "h": np.zeros(8, np.uint64)}
+        l_lo, l_hi = max(lo, 1 + pub), min(hi, 1 + pub + num_priv)
+        sums["l"] = self.msm("l", l_lo - 1 - pub, l_hi - 1 - pub, w, 1 + pub) if l_hi > l_lo else np.zeros(8, np.uint64)
+        return D.pack_sums(sums)
+
     def add_g1(self, a, b):
         one = O.fr_from_int(1)
         return O.msm_g1_naive(np.stack([a, b]), np.stack([one, one]))

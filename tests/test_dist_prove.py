@@ -122,21 +122,3 @@ def test_balance_shares_moves_work_off_polynomial_owners():
         s = D.balance_shares([2.9] * 3 + [0.0] * 5, [7.7 * x for x in s], s)
     assert max(s[:3]) < 0.01 and abs(sum(s) - 1) < 1e-9
     assert D.balance_shares([0.0], [1.0], [1.0]) == [1.0]
-
-
-def test_witness_pieces_cover_each_msm_once():
-    import zkml_dist as D
-    sizes = {"a": 1001, "b2": 1001, "l": 700, "h": 1024, "b1": 1001}
-    for shares in ([1.0], [0.5, 0.5], [0.0, 0.0, 0.0, 0.2, 0.2, 0.2, 0.2, 0.2], [0.1, 0.6, 0.3], [0.31, 0.69]):
-        got = {k: [] for k in D.WITNESS_MSMS}
-        for r in range(len(shares)):
-            pieces = D.witness_pieces(sizes, shares, r)
-            assert len({k for k, _, _ in pieces}) == len(pieces)  # one run per MSM per rank
-            if shares[r] == 0:
-                assert pieces == []
-            for k, lo, hi in pieces:
-                got[k].append((lo, hi))
-        for k in D.WITNESS_MSMS:
-            spans = sorted(got[k])
-            assert spans[0][0] == 0 and spans[-1][1] == sizes[k], (k, shares)
-            assert all(spans[i][1] == spans[i + 1][0] for i in range(len(spans) - 1)), (k, shares)
