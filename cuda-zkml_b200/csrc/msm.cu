@@ -340,7 +340,8 @@ template <class Cv>
 __global__ void __launch_bounds__(128) msm_accumulate_kernel(
     const uint32_t* __restrict__ keys, const uint32_t* __restrict__ offsets, uint32_t nb, const uint8_t* __restrict__ points,
     uint32_t seg, uint8_t* __restrict__ bucket_sums, uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last,
-    uint32_t* __restrict__ first_bucket, uint32_t* __restrict__ last_bucket, uint32_t idx_lo, uint32_t idx_hi) {
+    uint32_t* __restrict__ first_bucket, uint32_t* __restrict__ last_bucket, uint32_t idx_lo, uint32_t idx_hi,
+    uint32_t* __restrict__ max_span) {
     using F = typename Cv::F;
     const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t K = offsets[nb];
@@ -365,12 +366,16 @@ __global__ void __launch_bounds__(128) msm_accumulate_kernel(
         uint8_t* dst;
         if (g_begin >= s0 && g_end <= s1) {
             dst = bucket_sums + (size_t)g * Cv::kXyzzBytes;
-        } else if (run_start == s0) {
-            dst = part_first + t * Cv::kXyzzBytes;
-            first_bucket[t] = g;
         } else {
-            dst = part_last + t * Cv::kXyzzBytes;
-            last_bucket[t] = g;
+            if (run_start == s0) {
+                dst = part_first + t * Cv::kXyzzBytes;
+                first_bucket[t] = g;
+            } else {
+                dst = part_last + t * Cv::kXyzzBytes;
+                last_bucket[t] = g;
+            }
+            // the widest cut bucket bounds the fixup rounds that have work
+            atomicMax(max_span, (g_end - 1) / seg - g_begin / seg + 1);
         }
         store_xyzz(dst, acc);
     };
@@ -402,30 +407,32 @@ __global__ void __launch_bounds__(128) msm_accumulate_kernel(
 template <class Cv>
 __global__ void msm_fixup_round_kernel(const uint32_t* __restrict__ offsets, const uint32_t* __restrict__ first_bucket,
                                        const uint32_t* __restrict__ last_bucket, size_t nseg, uint32_t seg, uint32_t stride,
-                                       uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last) {
+                                       uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last,
+                                       const uint32_t* __restrict__ max_span) {
     using F = typename Cv::F;
-    const size_t s = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= nseg) return;
-    const uint32_t gf = first_bucket[s], gl = last_bucket[s];
-    if (gf != 0xffffffffu) {
-        const uint32_t sa = offsets[gf] / seg, sb = (offsets[gf + 1] - 1) / seg;
-        const uint32_t j = (uint32_t)s - sa, m = sb - sa + 1;
-        if ((j & (2 * stride - 1)) == 0 && j + stride < m) {
-            Xyzz<F> a, b;
-            load_xyzz(a, part_first + s * Cv::kXyzzBytes);
-            load_xyzz(b, part_first + (s + stride) * Cv::kXyzzBytes);
-            add(a, b);
-            store_xyzz(part_first + s * Cv::kXyzzBytes, a);
+    if (stride >= *max_span) return;  // no bucket spans more than `stride` segments
+    for (size_t s = (size_t)blockIdx.x * blockDim.x + threadIdx.x; s < nseg; s += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t gf = first_bucket[s], gl = last_bucket[s];
+        if (gf != 0xffffffffu) {
+            const uint32_t sa = offsets[gf] / seg, sb = (offsets[gf + 1] - 1) / seg;
+            const uint32_t j = (uint32_t)s - sa, m = sb - sa + 1;
+            if ((j & (2 * stride - 1)) == 0 && j + stride < m) {
+                Xyzz<F> a, b;
+                load_xyzz(a, part_first + s * Cv::kXyzzBytes);
+                load_xyzz(b, part_first + (s + stride) * Cv::kXyzzBytes);
+                add(a, b);
+                store_xyzz(part_first + s * Cv::kXyzzBytes, a);
+            }
         }
-    }
-    if (gl != 0xffffffffu) {  // a "last" slot always holds V_0 of its bucket (sa = s)
-        const uint32_t m = (offsets[gl + 1] - 1) / seg - (uint32_t)s + 1;
-        if (stride < m) {
-            Xyzz<F> a, b;
-            load_xyzz(a, part_last + s * Cv::kXyzzBytes);
-            load_xyzz(b, part_first + (s + stride) * Cv::kXyzzBytes);
-            add(a, b);
-            store_xyzz(part_last + s * Cv::kXyzzBytes, a);
+        if (gl != 0xffffffffu) {  // a "last" slot always holds V_0 of its bucket (sa = s)
+            const uint32_t m = (offsets[gl + 1] - 1) / seg - (uint32_t)s + 1;
+            if (stride < m) {
+                Xyzz<F> a, b;
+                load_xyzz(a, part_last + s * Cv::kXyzzBytes);
+                load_xyzz(b, part_first + (s + stride) * Cv::kXyzzBytes);
+                add(a, b);
+                store_xyzz(part_last + s * Cv::kXyzzBytes, a);
+            }
         }
     }
 }
@@ -772,7 +779,7 @@ struct LaunchCounter {
 
 // Scratch of the bucket phase (sort + accumulate + fixup), reused by every batch.
 struct SortScratch {
-    uint32_t *counts, *offsets, *cursors, *tile_sums, *keys, *digits, *first_bucket, *last_bucket;
+    uint32_t *counts, *offsets, *cursors, *tile_sums, *keys, *digits, *first_bucket, *last_bucket, *max_span;
     uint8_t *part_first, *part_last;
 };
 template <class Cv>
@@ -788,13 +795,14 @@ static SortScratch take_sort_scratch(Arena& ar, const MsmPlan& P) {
     S.part_last = ar.take<uint8_t>(P.max_segs * Cv::kXyzzBytes);
     S.first_bucket = ar.take<uint32_t>(P.max_segs);
     S.last_bucket = ar.take<uint32_t>(P.max_segs);
+    S.max_span = ar.take<uint32_t>(1);
     return S;
 }
 template <class Cv>
 static size_t sort_scratch_bytes(const MsmPlan& P) {
     size_t b = Arena::round((P.nb + 1) * 4) * 2 + Arena::round(P.nb * 4) + Arena::round(P.tiles * 4);
     b += 2 * Arena::round(std::max<size_t>(P.max_keys, 1) * 4);
-    b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes) + 2 * Arena::round(P.max_segs * 4);
+    b += 2 * Arena::round(P.max_segs * Cv::kXyzzBytes) + 2 * Arena::round(P.max_segs * 4) + Arena::round(4);
     return b;
 }
 
@@ -865,6 +873,7 @@ static int msm_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void*
     cudaEvent_t* ph = ctx->phase;
     ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
     ZK_TRY_CUDA(cudaMemsetAsync(S.last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(S.max_span, 0, sizeof(uint32_t), st));
     if (points_ready) ZK_TRY_CUDA(cudaStreamWaitEvent(st, points_ready, 0));
     ZK_TRY_CUDA(cudaEventRecord(ph[3], st));
     {
@@ -873,15 +882,16 @@ static int msm_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void*
         if (blocks < 1) blocks = 1;
         msm_accumulate_kernel<Cv><<<blocks, threads, 0, st>>>(S.keys, S.offsets, P.nb, (const uint8_t*)d_points, P.seg, buckets,
                                                                S.part_first, S.part_last, S.first_bucket, S.last_bucket, idx_lo,
-                                                               idx_hi);
+                                                               idx_hi, S.max_span);
         lc++;
     }
     ZK_TRY_CUDA(cudaEventRecord(ph[4], st));
     {
-        const unsigned blocks = (unsigned)((P.max_segs + 127) / 128);
+        // grid-stride: a round with no work (past the widest cut bucket) is a short launch
+        const unsigned blocks = grid_for(P.max_segs, 128, ctx->num_sms * 16);
         for (uint64_t stride = 1; stride < P.max_segs; stride <<= 1) {
             msm_fixup_round_kernel<Cv><<<blocks, 128, 0, st>>>(S.offsets, S.first_bucket, S.last_bucket, P.max_segs, P.seg, stride,
-                                                                S.part_first, S.part_last);
+                                                                S.part_first, S.part_last, S.max_span);
             lc++;
         }
         msm_fixup_final_kernel<Cv><<<(P.nb + 255) / 256, 256, 0, st>>>(S.offsets, P.nb, P.seg, S.part_first, S.part_last, buckets);
