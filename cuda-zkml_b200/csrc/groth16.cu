@@ -657,19 +657,15 @@ static int witness_msms(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_w, size_
                                (uint32_t)(has_l ? l_hi - lo : 0)};
     std::memset(l, 0, 64);
     uint64_t* outs[4] = {a, b, b1, l};
-    cudaEvent_t s0, s1;
-    ZK_TRY_CUDA(cudaEventCreate(&s0));
-    ZK_TRY_CUDA(cudaEventCreate(&s1));
-    ZK_TRY_CUDA(cudaEventRecord(s0, st));
-    const int rc = msm_shared_scalars_run(pk->device, st, d_w + lo, hi - lo, sets, pts, g2, range, outs, set_ms);
-    if (rc == ZK_OK) {
-        cudaEventRecord(s1, st);
-        cudaEventSynchronize(s1);
-        cudaEventElapsedTime(all_ms, s0, s1);
-    }
-    cudaEventDestroy(s0);
-    cudaEventDestroy(s1);
-    return rc;
+    ScopedEvent s0, s1;
+    ZK_TRY_CUDA(cudaEventCreate(&s0.e));
+    ZK_TRY_CUDA(cudaEventCreate(&s1.e));
+    ZK_TRY_CUDA(cudaEventRecord(s0.e, st));
+    ZK_TRY(msm_shared_scalars_run(pk->device, st, d_w + lo, hi - lo, sets, pts, g2, range, outs, set_ms));
+    ZK_TRY_CUDA(cudaEventRecord(s1.e, st));
+    ZK_TRY_CUDA(cudaEventSynchronize(s1.e));
+    cudaEventElapsedTime(all_ms, s0.e, s1.e);
+    return ZK_OK;
 }
 
 // ------------------------------------------------------------------ prove
@@ -687,8 +683,9 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     const uint64_t n = R.n;
     const int m = R.m, pub = R.num_public;
     ZK_TRY(ensure_prover_buffers(pk, n, m));
-    cudaEvent_t ev[4];
-    for (auto& e : ev) ZK_TRY_CUDA(cudaEventCreate(&e));
+    ScopedEvent evs[4];
+    for (auto& e : evs) ZK_TRY_CUDA(cudaEventCreate(&e.e));
+    cudaEvent_t ev[4] = {evs[0].e, evs[1].e, evs[2].e, evs[3].e};
     ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
     ZK_TRY_CUDA(cudaMemcpyAsync(pk->w, h_witness, (size_t)m * 32, cudaMemcpyHostToDevice, st));
     ZK_TRY(r1cs_matvec(R, st, pk->w, pk->abc, ctx->num_sms));
@@ -704,7 +701,6 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     ZK_TRY_CUDA(cudaEventRecord(ev[2], st));
     ZK_TRY_CUDA(cudaEventSynchronize(ev[2]));
     if (check && *pk->h_bad != ~0ull) {
-        for (auto& e : ev) cudaEventDestroy(e);
         set_error("[Prove] Witness does not satisfy R1CS constraints (constraint %llu failed)", *pk->h_bad);
         return ZK_ERR_INVALID;
     }
@@ -738,7 +734,6 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     ZK_TRY_CUDA(cudaEventSynchronize(ev[3]));
     cudaEventElapsedTime(&ms, ev[0], ev[3]);
     stats.total_ms = ms;
-    for (auto& e : ev) cudaEventDestroy(e);
     return ZK_OK;
 }
 
@@ -1133,13 +1128,13 @@ extern "C" int zk_fr_hadamard_check_device(int device, void* stream, const void*
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     cudaStream_t st = (cudaStream_t)stream;
-    unsigned long long* d_bad = nullptr;
-    ZK_TRY_CUDA(cudaMallocAsync((void**)&d_bad, sizeof(unsigned long long), st));
+    PoolBuffer bad_buf;
+    ZK_TRY_CUDA(bad_buf.alloc(sizeof(unsigned long long), st));
+    unsigned long long* d_bad = (unsigned long long*)bad_buf.p;
     ZK_TRY_CUDA(cudaMemsetAsync(d_bad, 0xff, sizeof(unsigned long long), st));
     enqueue_hadamard_check(st, (const Fr*)d_a, (const Fr*)d_b, (const Fr*)d_c, count, row0, d_bad, ctx->num_sms);
     unsigned long long bad = 0;
     ZK_TRY_CUDA(cudaMemcpyAsync(&bad, d_bad, sizeof bad, cudaMemcpyDeviceToHost, st));
-    ZK_TRY_CUDA(cudaFreeAsync(d_bad, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     *first_bad = bad == ~0ull ? -1 : (long long)bad;
     return ZK_OK;

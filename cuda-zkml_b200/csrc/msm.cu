@@ -983,17 +983,18 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     ZK_TRY(ensure_pinned(ctx, 4096));
     uint32_t* hist_host = (uint32_t*)ctx->pinned;
     ZK_TRY(scratch_begin(ctx, st));
-    cudaEvent_t t0, t1;
-    ZK_TRY_CUDA(cudaEventCreate(&t0));
-    ZK_TRY_CUDA(cudaEventCreate(&t1));
-    ZK_TRY_CUDA(cudaEventRecord(t0, st));
+    ScopedEvent t0, t1;
+    ZK_TRY_CUDA(cudaEventCreate(&t0.e));
+    ZK_TRY_CUDA(cudaEventCreate(&t1.e));
+    ZK_TRY_CUDA(cudaEventRecord(t0.e, st));
     // inputs in the stream-ordered pool (the arena is sized after the plan)
-    uint8_t* d_pts = nullptr;
-    Fr* d_sc = nullptr;
-    uint32_t* hist_dev = nullptr;
-    ZK_TRY_CUDA(cudaMallocAsync((void**)&d_pts, n * Cv::kAffineBytes, st));
-    ZK_TRY_CUDA(cudaMallocAsync((void**)&d_sc, n * 32, st));
-    ZK_TRY_CUDA(cudaMallocAsync((void**)&hist_dev, 256 * sizeof(uint32_t), st));
+    PoolBuffer pts_buf, sc_buf, hist_buf;
+    ZK_TRY_CUDA(pts_buf.alloc(n * Cv::kAffineBytes, st));
+    ZK_TRY_CUDA(sc_buf.alloc(n * 32, st));
+    ZK_TRY_CUDA(hist_buf.alloc(256 * sizeof(uint32_t), st));
+    uint8_t* d_pts = (uint8_t*)pts_buf.p;
+    Fr* d_sc = (Fr*)sc_buf.p;
+    uint32_t* hist_dev = (uint32_t*)hist_buf.p;
     ZK_TRY_CUDA(cudaEventRecord(ctx->ev_a, st));  // after the previous users of the scratch, and the allocations
     ZK_TRY_CUDA(cudaStreamWaitEvent(cs, ctx->ev_a, 0));
     ZK_TRY_CUDA(cudaStreamWaitEvent(as, ctx->ev_a, 0));
@@ -1062,16 +1063,11 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
     ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, keys_total, kBatches * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
-    ZK_TRY_CUDA(cudaFreeAsync(d_pts, st));
-    ZK_TRY_CUDA(cudaFreeAsync(d_sc, st));
-    ZK_TRY_CUDA(cudaFreeAsync(hist_dev, st));
-    ZK_TRY_CUDA(cudaEventRecord(t1, st));
+    ZK_TRY_CUDA(cudaEventRecord(t1.e, st));
     ZK_TRY(scratch_end(ctx, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     float ms_all = 0;
-    cudaEventElapsedTime(&ms_all, t0, t1);
-    cudaEventDestroy(t0);
-    cudaEventDestroy(t1);
+    cudaEventElapsedTime(&ms_all, t0.e, t1.e);
     // phase times of the last batch (its sort ran on the auxiliary stream) and the reduce
     for (int i = 0; i < 8; i++) cudaEventElapsedTime(&stats.phase_ms[i], ctx->phase[i], ctx->phase[i + 1]);
     stats.kernel_launches = lc.n;
@@ -1137,11 +1133,11 @@ static int msm_tables_run(int device, cudaStream_t st, const uint8_t* tables, si
     uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
     const ReduceScratch R = take_reduce_scratch<Cv>(ar, Pr);
     LaunchCounter lc;
-    cudaEvent_t t0, t1;
-    ZK_TRY_CUDA(cudaEventCreate(&t0));
-    ZK_TRY_CUDA(cudaEventCreate(&t1));
+    ScopedEvent t0, t1;
+    ZK_TRY_CUDA(cudaEventCreate(&t0.e));
+    ZK_TRY_CUDA(cudaEventCreate(&t1.e));
     ZK_TRY(scratch_begin(ctx, st));
-    ZK_TRY_CUDA(cudaEventRecord(t0, st));
+    ZK_TRY_CUDA(cudaEventRecord(t0.e, st));
     ZK_TRY(msm_sort_phase<Cv>(ctx, st, d_scalars, n, P, S, lc));
     ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, tables + lo * Cv::kAffineBytes, P, S, buckets, nullptr, lc));
     ZK_TRY(msm_reduce_phase<Cv>(ctx, st, Pr, S.offsets, buckets, R, windows_dev, lc));
@@ -1149,13 +1145,11 @@ static int msm_tables_run(int device, cudaStream_t st, const uint8_t* tables, si
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + Cv::kXyzzBytes);
     ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, S.offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
-    ZK_TRY_CUDA(cudaEventRecord(t1, st));
+    ZK_TRY_CUDA(cudaEventRecord(t1.e, st));
     ZK_TRY(scratch_end(ctx, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     float ms_all = 0;
-    cudaEventElapsedTime(&ms_all, t0, t1);
-    cudaEventDestroy(t0);
-    cudaEventDestroy(t1);
+    cudaEventElapsedTime(&ms_all, t0.e, t1.e);
     for (int i = 0; i < 8; i++) cudaEventElapsedTime(&stats.phase_ms[i], ctx->phase[i], ctx->phase[i + 1]);
     stats.kernel_launches = lc.n;
     stats.accumulate_ms = stats.phase_ms[3];
@@ -1215,15 +1209,17 @@ int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, s
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
     const double sms = (double)std::max(ctx->num_sms, 1);
-    uint32_t* hist_dev = nullptr;
     ZK_TRY(ensure_pinned(ctx, 4096));
     uint32_t* hist_host = (uint32_t*)ctx->pinned;
     ZK_TRY(scratch_begin(ctx, st));
-    ZK_TRY_CUDA(cudaMallocAsync((void**)&hist_dev, 256 * sizeof(uint32_t), st));
-    ZK_TRY_CUDA(cudaMemsetAsync(hist_dev, 0, 256 * sizeof(uint32_t), st));
-    msm_bitlen_hist_kernel<<<grid_for(n, 256, ctx->num_sms * 4), 256, 0, st>>>((const Fr*)d_scalars, n, hist_dev);
-    ZK_TRY_CUDA(cudaMemcpyAsync(hist_host, hist_dev, 256 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
-    ZK_TRY_CUDA(cudaFreeAsync(hist_dev, st));
+    {
+        PoolBuffer hist_buf;
+        ZK_TRY_CUDA(hist_buf.alloc(256 * sizeof(uint32_t), st));
+        uint32_t* hist_dev = (uint32_t*)hist_buf.p;
+        ZK_TRY_CUDA(cudaMemsetAsync(hist_dev, 0, 256 * sizeof(uint32_t), st));
+        msm_bitlen_hist_kernel<<<grid_for(n, 256, ctx->num_sms * 4), 256, 0, st>>>((const Fr*)d_scalars, n, hist_dev);
+        ZK_TRY_CUDA(cudaMemcpyAsync(hist_host, hist_dev, 256 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    }
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     uint32_t hist[256];
     std::memcpy(hist, hist_host, sizeof hist);
@@ -1251,10 +1247,10 @@ int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, s
     const ReduceScratch R = take_reduce_scratch<G2>(ar, P);  // the larger record size serves both curves
     uint8_t* windows = ar.take<uint8_t>((size_t)n_sets * P.W * G2::kXyzzBytes);
     LaunchCounter lc;
-    cudaEvent_t ev[9];
-    for (int k = 0; k <= n_sets; k++) ZK_TRY_CUDA(cudaEventCreate(&ev[k]));
+    ScopedEvent ev[9];
+    for (int k = 0; k <= n_sets; k++) ZK_TRY_CUDA(cudaEventCreate(&ev[k].e));
     ZK_TRY(msm_sort_phase<G1>(ctx, st, d_scalars, n, P, S, lc));
-    ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
+    ZK_TRY_CUDA(cudaEventRecord(ev[0].e, st));
     for (int k = 0; k < n_sets; k++) {
         uint8_t* win = windows + (size_t)k * P.W * G2::kXyzzBytes;
         const uint32_t ilo = idx_range ? idx_range[2 * k] : 0u, ihi = idx_range ? idx_range[2 * k + 1] : 0xffffffffu;
@@ -1265,7 +1261,7 @@ int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, s
             ZK_TRY(msm_accumulate_phase<G1>(ctx, st, d_points[k], P, S, buckets, nullptr, lc, ilo, ihi));
             ZK_TRY(msm_reduce_phase<G1>(ctx, st, P, S.offsets, buckets, R, win, lc));
         }
-        ZK_TRY_CUDA(cudaEventRecord(ev[k + 1], st));
+        ZK_TRY_CUDA(cudaEventRecord(ev[k + 1].e, st));
     }
     ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows, (size_t)n_sets * P.W * G2::kXyzzBytes, cudaMemcpyDeviceToHost, st));
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)n_sets * P.W * G2::kXyzzBytes);
@@ -1273,8 +1269,7 @@ int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, s
     ZK_TRY(scratch_end(ctx, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     if (set_ms)  // the shared sort is not in any set's time
-        for (int k = 0; k < n_sets; k++) cudaEventElapsedTime(&set_ms[k], ev[k], ev[k + 1]);
-    for (int k = 0; k <= n_sets; k++) cudaEventDestroy(ev[k]);
+        for (int k = 0; k < n_sets; k++) cudaEventElapsedTime(&set_ms[k], ev[k].e, ev[k + 1].e);
     stats.kernel_launches = lc.n;
     stats.bucket_adds = (long long)*keys_host * n_sets;
     for (int k = 0; k < n_sets; k++) {
@@ -1310,15 +1305,17 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
         return msm_run_host_pipelined<Cv>(ctx, st, src_points, src_scalars, n, out_affine);
     // Window choice from the scalars' bit lengths (a small device pre-pass; the
     // host path copies the scalars first for it).
-    uint32_t* hist_dev = nullptr;
     ZK_TRY(ensure_pinned(ctx, 4096));
     uint32_t* hist_host = (uint32_t*)ctx->pinned;
     const void* sc_for_hist = src_scalars;
-    void* sc_copy = nullptr;
     ZK_TRY(scratch_begin(ctx, st));
-    ZK_TRY_CUDA(cudaMallocAsync((void**)&hist_dev, 256 * sizeof(uint32_t), st));
+    PoolBuffer hist_buf, sc_buf;  // returned to the pool on every exit path, after the queued work
+    ZK_TRY_CUDA(hist_buf.alloc(256 * sizeof(uint32_t), st));
+    uint32_t* hist_dev = (uint32_t*)hist_buf.p;
+    void* sc_copy = nullptr;
     if (host_inputs) {
-        ZK_TRY_CUDA(cudaMallocAsync(&sc_copy, n * 32, st));
+        ZK_TRY_CUDA(sc_buf.alloc(n * 32, st));
+        sc_copy = sc_buf.p;
         ZK_TRY_CUDA(cudaMemcpyAsync(sc_copy, src_scalars, n * 32, cudaMemcpyHostToDevice, st));
         sc_for_hist = sc_copy;
     }
@@ -1349,10 +1346,10 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     uint8_t* raw = ref_layout ? ar.take<uint8_t>(ref_bytes) : nullptr;
     LaunchCounter lc;
 
-    cudaEvent_t t0, t1;
-    ZK_TRY_CUDA(cudaEventCreate(&t0));
-    ZK_TRY_CUDA(cudaEventCreate(&t1));
-    ZK_TRY_CUDA(cudaEventRecord(t0, st));
+    ScopedEvent t0, t1;
+    ZK_TRY_CUDA(cudaEventCreate(&t0.e));
+    ZK_TRY_CUDA(cudaEventCreate(&t1.e));
+    ZK_TRY_CUDA(cudaEventRecord(t0.e, st));
 
     cudaEvent_t points_ready = nullptr;
     if (host_inputs) {
@@ -1385,15 +1382,11 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
     ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, total_keys_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
-    ZK_TRY_CUDA(cudaFreeAsync(hist_dev, st));
-    if (sc_copy) ZK_TRY_CUDA(cudaFreeAsync(sc_copy, st));
-    ZK_TRY_CUDA(cudaEventRecord(t1, st));
+    ZK_TRY_CUDA(cudaEventRecord(t1.e, st));
     ZK_TRY(scratch_end(ctx, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     float ms_all = 0;
-    cudaEventElapsedTime(&ms_all, t0, t1);
-    cudaEventDestroy(t0);
-    cudaEventDestroy(t1);
+    cudaEventElapsedTime(&ms_all, t0.e, t1.e);
     for (int i = 0; i < 8; i++) cudaEventElapsedTime(&stats.phase_ms[i], ctx->phase[i], ctx->phase[i + 1]);
     stats.kernel_launches = lc.n;
     stats.accumulate_ms = stats.phase_ms[3];

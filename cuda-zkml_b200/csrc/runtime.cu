@@ -171,21 +171,19 @@ extern "C" int zk_probe_imad_rate(int device, double* rate) {
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
     const int threads = 256, blocks = ctx->num_sms * 8, iters = 256;
-    uint32_t* buf;
-    ZK_TRY_CUDA(cudaMalloc(&buf, (size_t)threads * blocks * 4));
-    cudaEvent_t a, b;
-    ZK_TRY_CUDA(cudaEventCreate(&a));
-    ZK_TRY_CUDA(cudaEventCreate(&b));
+    PoolBuffer out;
+    ZK_TRY_CUDA(out.alloc((size_t)threads * blocks * 4, ctx->stream));
+    uint32_t* buf = (uint32_t*)out.p;
+    ScopedEvent a, b;
+    ZK_TRY_CUDA(cudaEventCreate(&a.e));
+    ZK_TRY_CUDA(cudaEventCreate(&b.e));
     imad_probe_kernel<<<blocks, threads, 0, ctx->stream>>>(buf, 12345u, 64);  // warm-up
-    ZK_TRY_CUDA(cudaEventRecord(a, ctx->stream));
+    ZK_TRY_CUDA(cudaEventRecord(a.e, ctx->stream));
     imad_probe_kernel<<<blocks, threads, 0, ctx->stream>>>(buf, 777u, iters);
-    ZK_TRY_CUDA(cudaEventRecord(b, ctx->stream));
-    ZK_TRY_CUDA(cudaEventSynchronize(b));
+    ZK_TRY_CUDA(cudaEventRecord(b.e, ctx->stream));
+    ZK_TRY_CUDA(cudaEventSynchronize(b.e));
     float ms = 0;
-    cudaEventElapsedTime(&ms, a, b);
-    cudaEventDestroy(a);
-    cudaEventDestroy(b);
-    cudaFree(buf);
+    cudaEventElapsedTime(&ms, a.e, b.e);
     double instr = (double)threads * blocks * iters * 4 * 256.0;  // 4 chains x 256 IMAD per multiplication
     *rate = instr / (ms * 1e-3);
     return ZK_OK;

@@ -32,6 +32,34 @@ void clear_error();
         if (s_ != ZK_OK) return s_;  \
     } while (0)
 
+// A CUDA event owned by a scope: destroyed on every exit path, errors included.
+struct ScopedEvent {
+    cudaEvent_t e = nullptr;
+    ScopedEvent() = default;
+    ScopedEvent(const ScopedEvent&) = delete;
+    ScopedEvent& operator=(const ScopedEvent&) = delete;
+    ~ScopedEvent() {
+        if (e) cudaEventDestroy(e);
+    }
+};
+
+// A stream-ordered pool allocation owned by a scope: returned with
+// cudaFreeAsync on its stream (after the work queued there) on every exit path.
+struct PoolBuffer {
+    void* p = nullptr;
+    cudaStream_t st = nullptr;
+    PoolBuffer() = default;
+    PoolBuffer(const PoolBuffer&) = delete;
+    PoolBuffer& operator=(const PoolBuffer&) = delete;
+    ~PoolBuffer() {
+        if (p) cudaFreeAsync(p, st);
+    }
+    cudaError_t alloc(size_t bytes, cudaStream_t stream) {
+        st = stream;
+        return cudaMallocAsync(&p, bytes, stream);
+    }
+};
+
 // bump allocator over one device buffer; all offsets 256-byte aligned
 struct Arena {
     char* base = nullptr;
