@@ -310,7 +310,7 @@ def run_b200(args):
     roofline = {"bound": "int32", "kernel": "msm_accumulate_kernel<G1>", "achieved": achieved / 1e12,
                 "peak": imad / 1e12, "unit": "TIMAD/s", "frac": achieved / imad, "traffic": None,
                 "algorithmic": f"{adds} mixed additions x 10 Fp mul x 256 IMAD per launch",
-                "peak_source": "zk_probe_imad_rate, measured in this run (dependency-free IMAD stream)",
+                "peak_source": "zk_probe_imad_rate, measured in this run (the Montgomery multiplication itself on 4 independent chains per thread, counted as 256 IMAD)",
                 "msm_whole_frac_ref_ops": 256 * msm_ref_ops(n) / (stats[-1]["total_device_ms"] / 1e3) / imad}
     prof = os.path.join(ROOT, "profiles", "msm_accumulate_g1_traffic.json")
     if os.path.exists(prof):
