@@ -90,9 +90,7 @@ __device__ ZK_RARE void dbl(Xyzz<F>& r, const Xyzz<F>& p) {
     F x3;
     fsub(x3, t, s);          // X3 = M^2 - 2S
     fsub(t, s, x3);
-    fmul(t, m, t);
-    fmul(s, w, p.y);
-    fsub(r.y, t, s);         // Y3 = M (S - X3) - W Y1
+    fmulsub(r.y, m, t, w, p.y);  // Y3 = M (S - X3) - W Y1, one reduction
     fmul(r.zz, v, p.zz);     // ZZ3 = V ZZ1
     fmul(r.zzz, w, p.zzz);   // ZZZ3 = W ZZZ1
     r.x = x3;
@@ -120,9 +118,7 @@ __device__ __forceinline__ void madd(Xyzz<F>& acc, const Affine<F>& a) {
     fsub(t, t, q);
     fsub(t, t, q);           // X3 = R^2 - PPP - 2Q
     fsub(q, q, t);
-    fmul(q, r, q);           // R (Q - X3)
-    fmul(s2, acc.y, ppp);
-    fsub(acc.y, q, s2);      // Y3 = R (Q - X3) - Y1 PPP
+    fmulsub(acc.y, r, q, acc.y, ppp);  // Y3 = R (Q - X3) - Y1 PPP, one reduction
     acc.x = t;
     fmul(acc.zz, acc.zz, pp);     // ZZ3 = ZZ1 PP
     fmul(acc.zzz, acc.zzz, ppp);  // ZZZ3 = ZZZ1 PPP
@@ -153,9 +149,7 @@ __device__ __forceinline__ void add(Xyzz<F>& acc, const Xyzz<F>& b) {
     fsub(t, t, q);
     fsub(t, t, q);           // X3
     fsub(q, q, t);
-    fmul(q, r, q);
-    fmul(s1, s1, ppp);
-    fsub(acc.y, q, s1);      // Y3 = R (Q - X3) - S1 PPP
+    fmulsub(acc.y, r, q, s1, ppp);  // Y3 = R (Q - X3) - S1 PPP, one reduction
     acc.x = t;
     fmul(acc.zz, acc.zz, b.zz);
     fmul(acc.zz, acc.zz, pp);     // ZZ3 = ZZ1 ZZ2 PP
