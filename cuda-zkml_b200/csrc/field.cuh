@@ -276,6 +276,27 @@ __device__ __forceinline__ void fneg(Fe<M>& r, const Fe<M>& a) {
     fsub(r, z, a);
 }
 
+// r = sum_{k < K} a_k b_k with one Montgomery reduction (K <= 4).  For both
+// BN254 moduli m < 0.76 2^254, so within a step the accumulator stays below
+// (K + 1) 2^32 m < 2^288 (9 words) and the result below m (1 + K m / R) < 1.76 m:
+// one final conditional subtraction, as for a single product.
+template <class M, int K>
+__device__ __forceinline__ void fmulsum_inline(Fe<M>& r, const Fe<M>* a, const Fe<M>* b) {
+    static_assert(K >= 1 && K <= 4, "at most four products share a reduction");
+    uint32_t t0 = 0, t1 = 0, t2 = 0, t3 = 0, t4 = 0, t5 = 0, t6 = 0, t7 = 0, t8 = 0;
+    constexpr uint32_t mm[8] = {M::m(0), M::m(1), M::m(2), M::m(3), M::m(4), M::m(5), M::m(6), M::m(7)};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+#pragma unroll
+        for (int k = 0; k < K; k++) mac_row(t0, t1, t2, t3, t4, t5, t6, t7, t8, a[k].v[i], b[k].v);
+        uint32_t q = t0 * M::inv;
+        mac_row(t0, t1, t2, t3, t4, t5, t6, t7, t8, q, mm);
+        t0 = t1; t1 = t2; t2 = t3; t3 = t4; t4 = t5; t5 = t6; t6 = t7; t7 = t8; t8 = 0;
+    }
+    uint32_t t[8] = {t0, t1, t2, t3, t4, t5, t6, t7};
+    cond_sub<M>(r.v, t);
+}
+
 // r = a b - c d = a b + (m - c) d, one reduction
 template <class M>
 __device__ __forceinline__ void fmulsub(Fe<M>& r, const Fe<M>& a, const Fe<M>& b, const Fe<M>& c, const Fe<M>& d) {

@@ -181,6 +181,30 @@ namespace zk {
 static thread_local zk_prove_stats g_prove_stats;
 
 // ------------------------------------------------------------------ kernels
+// acc += sum_{j = a, a + step, ... < b} val_j w[col_j], four products per
+// Montgomery reduction (a dot product is a sum of products)
+__device__ __forceinline__ void row_dot(Fr& acc, const Fr* __restrict__ val, const int32_t* __restrict__ col, const Fr* __restrict__ w,
+                                        int a, int b, int step) {
+    int j = a;
+    for (; j + 3 * step < b; j += 4 * step) {
+        Fr v[4], x[4], s;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            fload_nc(v[k], val + j + k * step);
+            fload_nc(x[k], w + col[j + k * step]);
+        }
+        fmulsum_inline<ModR, 4>(s, v, x);
+        fadd(acc, acc, s);
+    }
+    for (; j < b; j += step) {
+        Fr v, x;
+        fload_nc(v, val + j);
+        fload_nc(x, w + col[j]);
+        fmul(v, v, x);
+        fadd(acc, acc, v);
+    }
+}
+
 // rows [lo, hi) of M w into out[r - lo]; rows at or beyond `rows` (the
 // constraint count) are zero.  Rows with at most kShortRow entries: one thread
 // per row; long rows are skipped here and done by r1cs_matvec_long_kernel.
@@ -192,13 +216,7 @@ __global__ void r1cs_matvec_short_kernel(const int32_t* __restrict__ row_ptr, co
         if (r < (uint64_t)rows) {
             const int a = row_ptr[r], b = row_ptr[r + 1];
             if (b - a <= kShortRow) {
-                for (int j = a; j < b; j++) {
-                    Fr v, x;
-                    fload_nc(v, val + j);
-                    fload_nc(x, w + col[j]);
-                    fmul(v, v, x);
-                    fadd(acc, acc, v);
-                }
+                row_dot(acc, val, col, w, a, b, 1);
             } else {
                 continue;  // written by the warp or block kernel
             }
@@ -219,13 +237,7 @@ __global__ void __launch_bounds__(256) r1cs_matvec_warp_kernel(const int32_t* __
     const int a = row_ptr[r], b = row_ptr[r + 1];
     Fr acc;
     fset_zero(acc);
-    for (int j = a + (int)lane; j < b; j += 32) {
-        Fr v, x;
-        fload_nc(v, val + j);
-        fload_nc(x, w + col[j]);
-        fmul(v, v, x);
-        fadd(acc, acc, v);
-    }
+    row_dot(acc, val, col, w, a + (int)lane, b, 32);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         Fr t;
@@ -245,13 +257,7 @@ __global__ void __launch_bounds__(256) r1cs_matvec_long_kernel(const int32_t* __
     const int a = row_ptr[r], b = row_ptr[r + 1];
     Fr acc;
     fset_zero(acc);
-    for (int j = a + threadIdx.x; j < b; j += blockDim.x) {
-        Fr v, x;
-        fload_nc(v, val + j);
-        fload_nc(x, w + col[j]);
-        fmul(v, v, x);
-        fadd(acc, acc, v);
-    }
+    row_dot(acc, val, col, w, a + (int)threadIdx.x, b, (int)blockDim.x);
     part[threadIdx.x] = acc;
     __syncthreads();
     for (int s = blockDim.x / 2; s > 0; s >>= 1) {
