@@ -305,13 +305,16 @@ def run_b200(args):
     adds = stats[-1]["bucket_adds"]
     launches = stats[-1]["kernel_launches"] * args.steps
     # algorithmic IMAD of the accumulate kernel: bucket_adds mixed XYZZ additions,
-    # each 8M + 2S = 10 Fp products of which two (Y3 = R (Q - X3) - Y1 PPP) share one
-    # Montgomery reduction: 9.5 x 256 IMAD (8 x 32-bit limbs: 128 product and 128
-    # reduction multiply-adds per product; a shared reduction saves 128)
-    achieved = adds * 9.5 * 256 / (acc_ms / 1e3)
+    # each 8M + 2S.  On 8 x 32-bit limbs a product is 128 product + 128 reduction
+    # multiply-adds; a squaring 72 + 128 (each cross product once); the two products
+    # of Y3 = R (Q - X3) - Y1 PPP share one reduction (256 + 128).  Per addition:
+    # 6 x 256 + 2 x 200 + 384 = 2320 IMAD.
+    imad_per_add = 6 * 256 + 2 * 200 + 384
+    achieved = adds * imad_per_add / (acc_ms / 1e3)
     roofline = {"bound": "int32", "kernel": "msm_accumulate_kernel<G1>", "achieved": achieved / 1e12,
                 "peak": imad / 1e12, "unit": "TIMAD/s", "frac": achieved / imad, "traffic": None,
-                "algorithmic": f"{adds} mixed additions x 9.5 Fp products (10, two sharing a reduction) x 256 IMAD per launch",
+                "algorithmic": f"{adds} mixed additions x {imad_per_add} IMAD (6 products x 256, 2 squarings x 200, "
+                               f"Y3's two products sharing a reduction 384) per launch",
                 "peak_source": "zk_probe_imad_rate, measured in this run (the Montgomery multiplication itself on 4 independent chains per thread, counted as 256 IMAD)",
                 "msm_whole_frac_ref_ops": 256 * msm_ref_ops(n) / (stats[-1]["total_device_ms"] / 1e3) / imad}
     prof = os.path.join(ROOT, "profiles", "msm_accumulate_g1_traffic.json")

@@ -170,8 +170,189 @@ __device__ __forceinline__ void fmul(Fe<M>& r, const Fe<M>& a, const Fe<M>& b) {
 #endif
 }
 
+// r = a^2 (Montgomery): the product part computes each off-diagonal a_i a_j once
+// (28 products, doubled) plus the 8 diagonal squares into a 16-word T, then a
+// separate reduction slides a 10-word window over T (8 reduction rows; a carry
+// word catches the window's overflow).  616 instead of 784 FMA-heavy cycles per
+// warp for a Montgomery product.  Every carry chain ends in a word the partial
+// value provably does not overflow: after off-diagonal row i the sum is below
+// 2^(32 (i + 9)), a^2 < 2^512, and the result (a^2 + Q m) / R < 2 m.
 template <class M>
-__device__ __forceinline__ void fsqr(Fe<M>& r, const Fe<M>& a) { fmul(r, a, a); }
+__device__ __forceinline__ void fsqr_inline(Fe<M>& r, const Fe<M>& a) {
+    uint32_t T[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) T[k] = 0;
+    // off-diagonal row 0: T[1..8] += a_0 * a[1..7]
+    asm("mad.lo.cc.u32  %0, %8, %9, %0;\n\t"
+        "madc.lo.cc.u32 %1, %8, %10, %1;\n\t"
+        "madc.lo.cc.u32 %2, %8, %11, %2;\n\t"
+        "madc.lo.cc.u32 %3, %8, %12, %3;\n\t"
+        "madc.lo.cc.u32 %4, %8, %13, %4;\n\t"
+        "madc.lo.cc.u32 %5, %8, %14, %5;\n\t"
+        "madc.lo.cc.u32 %6, %8, %15, %6;\n\t"
+        "addc.u32       %7, %7, 0;\n\t"
+        "mad.hi.cc.u32  %1, %8, %9, %1;\n\t"
+        "madc.hi.cc.u32 %2, %8, %10, %2;\n\t"
+        "madc.hi.cc.u32 %3, %8, %11, %3;\n\t"
+        "madc.hi.cc.u32 %4, %8, %12, %4;\n\t"
+        "madc.hi.cc.u32 %5, %8, %13, %5;\n\t"
+        "madc.hi.cc.u32 %6, %8, %14, %6;\n\t"
+        "madc.hi.u32    %7, %8, %15, %7;"
+        : "+r"(T[1]), "+r"(T[2]), "+r"(T[3]), "+r"(T[4]), "+r"(T[5]), "+r"(T[6]), "+r"(T[7]), "+r"(T[8])
+        : "r"(a.v[0]), "r"(a.v[1]), "r"(a.v[2]), "r"(a.v[3]), "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]), "r"(a.v[7]));
+    // off-diagonal row 1: T[3..9] += a_1 * a[2..7]
+    asm("mad.lo.cc.u32  %0, %7, %8, %0;\n\t"
+        "madc.lo.cc.u32 %1, %7, %9, %1;\n\t"
+        "madc.lo.cc.u32 %2, %7, %10, %2;\n\t"
+        "madc.lo.cc.u32 %3, %7, %11, %3;\n\t"
+        "madc.lo.cc.u32 %4, %7, %12, %4;\n\t"
+        "madc.lo.cc.u32 %5, %7, %13, %5;\n\t"
+        "addc.u32       %6, %6, 0;\n\t"
+        "mad.hi.cc.u32  %1, %7, %8, %1;\n\t"
+        "madc.hi.cc.u32 %2, %7, %9, %2;\n\t"
+        "madc.hi.cc.u32 %3, %7, %10, %3;\n\t"
+        "madc.hi.cc.u32 %4, %7, %11, %4;\n\t"
+        "madc.hi.cc.u32 %5, %7, %12, %5;\n\t"
+        "madc.hi.u32    %6, %7, %13, %6;"
+        : "+r"(T[3]), "+r"(T[4]), "+r"(T[5]), "+r"(T[6]), "+r"(T[7]), "+r"(T[8]), "+r"(T[9])
+        : "r"(a.v[1]), "r"(a.v[2]), "r"(a.v[3]), "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]), "r"(a.v[7]));
+    // off-diagonal row 2: T[5..10] += a_2 * a[3..7]
+    asm("mad.lo.cc.u32  %0, %6, %7, %0;\n\t"
+        "madc.lo.cc.u32 %1, %6, %8, %1;\n\t"
+        "madc.lo.cc.u32 %2, %6, %9, %2;\n\t"
+        "madc.lo.cc.u32 %3, %6, %10, %3;\n\t"
+        "madc.lo.cc.u32 %4, %6, %11, %4;\n\t"
+        "addc.u32       %5, %5, 0;\n\t"
+        "mad.hi.cc.u32  %1, %6, %7, %1;\n\t"
+        "madc.hi.cc.u32 %2, %6, %8, %2;\n\t"
+        "madc.hi.cc.u32 %3, %6, %9, %3;\n\t"
+        "madc.hi.cc.u32 %4, %6, %10, %4;\n\t"
+        "madc.hi.u32    %5, %6, %11, %5;"
+        : "+r"(T[5]), "+r"(T[6]), "+r"(T[7]), "+r"(T[8]), "+r"(T[9]), "+r"(T[10])
+        : "r"(a.v[2]), "r"(a.v[3]), "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]), "r"(a.v[7]));
+    // off-diagonal row 3: T[7..11] += a_3 * a[4..7]
+    asm("mad.lo.cc.u32  %0, %5, %6, %0;\n\t"
+        "madc.lo.cc.u32 %1, %5, %7, %1;\n\t"
+        "madc.lo.cc.u32 %2, %5, %8, %2;\n\t"
+        "madc.lo.cc.u32 %3, %5, %9, %3;\n\t"
+        "addc.u32       %4, %4, 0;\n\t"
+        "mad.hi.cc.u32  %1, %5, %6, %1;\n\t"
+        "madc.hi.cc.u32 %2, %5, %7, %2;\n\t"
+        "madc.hi.cc.u32 %3, %5, %8, %3;\n\t"
+        "madc.hi.u32    %4, %5, %9, %4;"
+        : "+r"(T[7]), "+r"(T[8]), "+r"(T[9]), "+r"(T[10]), "+r"(T[11])
+        : "r"(a.v[3]), "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]), "r"(a.v[7]));
+    // off-diagonal row 4: T[9..12] += a_4 * a[5..7]
+    asm("mad.lo.cc.u32  %0, %4, %5, %0;\n\t"
+        "madc.lo.cc.u32 %1, %4, %6, %1;\n\t"
+        "madc.lo.cc.u32 %2, %4, %7, %2;\n\t"
+        "addc.u32       %3, %3, 0;\n\t"
+        "mad.hi.cc.u32  %1, %4, %5, %1;\n\t"
+        "madc.hi.cc.u32 %2, %4, %6, %2;\n\t"
+        "madc.hi.u32    %3, %4, %7, %3;"
+        : "+r"(T[9]), "+r"(T[10]), "+r"(T[11]), "+r"(T[12])
+        : "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]), "r"(a.v[7]));
+    // off-diagonal row 5: T[11..13] += a_5 * a[6..7]
+    asm("mad.lo.cc.u32  %0, %3, %4, %0;\n\t"
+        "madc.lo.cc.u32 %1, %3, %5, %1;\n\t"
+        "addc.u32       %2, %2, 0;\n\t"
+        "mad.hi.cc.u32  %1, %3, %4, %1;\n\t"
+        "madc.hi.u32    %2, %3, %5, %2;"
+        : "+r"(T[11]), "+r"(T[12]), "+r"(T[13])
+        : "r"(a.v[5]), "r"(a.v[6]), "r"(a.v[7]));
+    // off-diagonal row 6: T[13..14] += a_6 * a[7..7]
+    asm("mad.lo.cc.u32  %0, %2, %3, %0;\n\t"
+        "addc.u32       %1, %1, 0;\n\t"
+        "mad.hi.cc.u32  %1, %2, %3, %1;"
+        : "+r"(T[13]), "+r"(T[14])
+        : "r"(a.v[6]), "r"(a.v[7]));
+    // T = 2 T
+    asm("add.cc.u32  %0, %0, %0;\n\t"
+        "addc.cc.u32 %1, %1, %1;\n\t"
+        "addc.cc.u32 %2, %2, %2;\n\t"
+        "addc.cc.u32 %3, %3, %3;\n\t"
+        "addc.cc.u32 %4, %4, %4;\n\t"
+        "addc.cc.u32 %5, %5, %5;\n\t"
+        "addc.cc.u32 %6, %6, %6;\n\t"
+        "addc.cc.u32 %7, %7, %7;\n\t"
+        "addc.cc.u32 %8, %8, %8;\n\t"
+        "addc.cc.u32 %9, %9, %9;\n\t"
+        "addc.cc.u32 %10, %10, %10;\n\t"
+        "addc.cc.u32 %11, %11, %11;\n\t"
+        "addc.cc.u32 %12, %12, %12;\n\t"
+        "addc.cc.u32 %13, %13, %13;\n\t"
+        "addc.cc.u32 %14, %14, %14;\n\t"
+        "addc.u32    %15, %15, %15;"
+        : "+r"(T[0]), "+r"(T[1]), "+r"(T[2]), "+r"(T[3]), "+r"(T[4]), "+r"(T[5]), "+r"(T[6]), "+r"(T[7]), "+r"(T[8]), "+r"(T[9]), "+r"(T[10]), "+r"(T[11]), "+r"(T[12]), "+r"(T[13]), "+r"(T[14]), "+r"(T[15]));
+    // T += sum a_i^2 2^(64 i)
+    asm("mad.lo.cc.u32  %0, %16, %16, %0;\n\t"
+        "madc.hi.cc.u32 %1, %16, %16, %1;\n\t"
+        "madc.lo.cc.u32 %2, %17, %17, %2;\n\t"
+        "madc.hi.cc.u32 %3, %17, %17, %3;\n\t"
+        "madc.lo.cc.u32 %4, %18, %18, %4;\n\t"
+        "madc.hi.cc.u32 %5, %18, %18, %5;\n\t"
+        "madc.lo.cc.u32 %6, %19, %19, %6;\n\t"
+        "madc.hi.cc.u32 %7, %19, %19, %7;\n\t"
+        "madc.lo.cc.u32 %8, %20, %20, %8;\n\t"
+        "madc.hi.cc.u32 %9, %20, %20, %9;\n\t"
+        "madc.lo.cc.u32 %10, %21, %21, %10;\n\t"
+        "madc.hi.cc.u32 %11, %21, %21, %11;\n\t"
+        "madc.lo.cc.u32 %12, %22, %22, %12;\n\t"
+        "madc.hi.cc.u32 %13, %22, %22, %13;\n\t"
+        "madc.lo.cc.u32 %14, %23, %23, %14;\n\t"
+        "madc.hi.u32    %15, %23, %23, %15;"
+        : "+r"(T[0]), "+r"(T[1]), "+r"(T[2]), "+r"(T[3]), "+r"(T[4]), "+r"(T[5]), "+r"(T[6]), "+r"(T[7]), "+r"(T[8]), "+r"(T[9]), "+r"(T[10]), "+r"(T[11]), "+r"(T[12]), "+r"(T[13]), "+r"(T[14]), "+r"(T[15])
+        : "r"(a.v[0]), "r"(a.v[1]), "r"(a.v[2]), "r"(a.v[3]), "r"(a.v[4]), "r"(a.v[5]), "r"(a.v[6]), "r"(a.v[7]));
+    // reduction: window t0..t8 over T, t9 catches its carry
+    uint32_t t0 = T[0], t1 = T[1], t2 = T[2], t3 = T[3], t4 = T[4], t5 = T[5], t6 = T[6], t7 = T[7], t8 = T[8], t9 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t q = t0 * M::inv;
+        asm("mad.lo.cc.u32  %0, %10, %11, %0;\n\t"
+            "madc.hi.cc.u32 %1, %10, %11, %1;\n\t"
+            "madc.lo.cc.u32 %2, %10, %13, %2;\n\t"
+            "madc.hi.cc.u32 %3, %10, %13, %3;\n\t"
+            "madc.lo.cc.u32 %4, %10, %15, %4;\n\t"
+            "madc.hi.cc.u32 %5, %10, %15, %5;\n\t"
+            "madc.lo.cc.u32 %6, %10, %17, %6;\n\t"
+            "madc.hi.cc.u32 %7, %10, %17, %7;\n\t"
+            "addc.cc.u32    %8, %8, 0;\n\t"
+            "addc.u32       %9, %9, 0;\n\t"
+            "mad.lo.cc.u32  %1, %10, %12, %1;\n\t"
+            "madc.hi.cc.u32 %2, %10, %12, %2;\n\t"
+            "madc.lo.cc.u32 %3, %10, %14, %3;\n\t"
+            "madc.hi.cc.u32 %4, %10, %14, %4;\n\t"
+            "madc.lo.cc.u32 %5, %10, %16, %5;\n\t"
+            "madc.hi.cc.u32 %6, %10, %16, %6;\n\t"
+            "madc.lo.cc.u32 %7, %10, %18, %7;\n\t"
+            "madc.hi.cc.u32 %8, %10, %18, %8;\n\t"
+            "addc.u32       %9, %9, 0;"
+            : "+r"(t0), "+r"(t1), "+r"(t2), "+r"(t3), "+r"(t4), "+r"(t5), "+r"(t6), "+r"(t7), "+r"(t8), "+r"(t9)
+            : "r"(q), "r"(M::m(0)), "r"(M::m(1)), "r"(M::m(2)), "r"(M::m(3)), "r"(M::m(4)), "r"(M::m(5)), "r"(M::m(6)),
+              "r"(M::m(7)));
+        // t0 == 0: shift down one word and bring in T[i + 9]
+        t0 = t1; t1 = t2; t2 = t3; t3 = t4; t4 = t5; t5 = t6; t6 = t7; t7 = t8; t8 = t9; t9 = 0;
+        if (i + 9 <= 15) asm("add.cc.u32 %0, %0, %2;\n\taddc.u32 %1, 0, 0;" : "+r"(t8), "=r"(t9) : "r"(T[i + 9]));
+    }
+    uint32_t t[8] = {t0, t1, t2, t3, t4, t5, t6, t7};
+    cond_sub<M>(r.v, t);
+}
+
+template <class M>
+__device__ __noinline__ Fe<M> fsqr_outline(Fe<M> a) {
+    Fe<M> r;
+    fsqr_inline(r, a);
+    return r;
+}
+
+template <class M>
+__device__ __forceinline__ void fsqr(Fe<M>& r, const Fe<M>& a) {
+#if ZK_FMUL_OUTLINE
+    r = fsqr_outline<M>(a);
+#else
+    fsqr_inline(r, a);
+#endif
+}
 
 // r = a b + c d with one Montgomery reduction: each CIOS step adds the rows a_i b
 // and c_i d before its reduction row, 48 instead of 2 x 32 multiply-adds a step.

@@ -337,7 +337,7 @@ __device__ __forceinline__ void load_signed_point(Affine<typename Cv::F>& a, boo
 }
 
 template <class Cv>
-__global__ void __launch_bounds__(128) msm_accumulate_kernel(
+__global__ void __launch_bounds__(128, Cv::kAccumulateMinBlocks) msm_accumulate_kernel(
     const uint32_t* __restrict__ keys, const uint32_t* __restrict__ offsets, uint32_t nb, const uint8_t* __restrict__ points,
     uint32_t seg, uint8_t* __restrict__ bucket_sums, uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last,
     uint32_t* __restrict__ first_bucket, uint32_t* __restrict__ last_bucket, uint32_t idx_lo, uint32_t idx_hi,
