@@ -1,5 +1,5 @@
-"""bench.py -- G1 MSM points/s at 2^24 points per GPU (BASELINE.json metric,
-configs[1]) on B200, one process per GPU.
+"""bench.py -- G1 MSM points/s at 2^24 points per GPU (the headline metric, on
+the standalone-MSM benchmark configuration) on B200, one process per GPU.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--log-n L] [--impl b200|reference]
 
@@ -147,9 +147,10 @@ def run_reference(args):
 
 # ---------------------------------------------------------------- Groth16 prove
 def bench_prove(Z, args, dev, world=1, rank=0):
-    """Groth16 prove of a synthetic CONV2D/ReLU circuit with SURVEY config 5's
-    shape (2 x [CONV 3x3, 32 ch, 32x32, exact ReLU with bit-decomposed range
-    checks] + dense 32768 -> 10; domain 2^22), proving key from the device
+    """Groth16 prove of the synthetic statement of the large prove configuration
+    (2 x [CONV 3x3, 32 ch, 32x32, RELU_EXACT with bit-decomposed range checks,
+    widths 24 then 23, shift 10] + dense 32768 -> 10 with public outputs;
+    4,128,789 constraints, domain 2^22), proving key from the device
     setup under the reference's deterministic toxic waste, key and circuit
     resident; a step is one prove from the host witness to the 256-byte proof.
     With world > 1 every rank holds the key and the proof is split over the
@@ -178,7 +179,7 @@ def bench_prove(Z, args, dev, world=1, rank=0):
         pk.prove(r1, w, 12345, 67890)
         times.append(time.perf_counter() - t0)
     st = Z.prove_last_stats()
-    return {"config": f"synthetic CONV 2 x {args.prove_channels}ch x {args.prove_hw}x{args.prove_hw} + dense 10 (config 5 shape)",
+    return {"config": f"synthetic statement: 2 x CONV2D 3x3 {args.prove_channels}ch {args.prove_hw}x{args.prove_hw} + RELU_EXACT, dense 10 (config 5)",
             "constraints": c["num_constraints"], "variables": c["num_variables"], "public": c["num_public"],
             "nnz": [len(c["A"]), len(c["B"]), len(c["C"])], "log_n": r1.log_n,
             "prove_ms": 1e3 * statistics.median(times), "prove_ms_min": 1e3 * min(times), "steps": args.prove_steps,
@@ -228,7 +229,7 @@ def bench_prove_sharded(Z, args, dev, world, rank):
     mine = {marks[i][0]: round(1e3 * (marks[i][1] - marks[i - 1][1]), 3) for i in range(1, len(marks))}
     per_rank = [None] * world
     dist.all_gather_object(per_rank, mine)
-    return {"config": f"synthetic CONV 2 x {args.prove_channels}ch x {args.prove_hw}x{args.prove_hw} + dense 10 (config 5 shape)",
+    return {"config": f"synthetic statement: 2 x CONV2D 3x3 {args.prove_channels}ch {args.prove_hw}x{args.prove_hw} + RELU_EXACT, dense 10 (config 5)",
             "phase_ms_per_rank": per_rank,
             "constraints": c["num_constraints"], "variables": c["num_variables"], "public": c["num_public"],
             "nnz": [len(c["A"]), len(c["B"]), len(c["C"])], "log_n": r1.log_n,

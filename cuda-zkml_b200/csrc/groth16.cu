@@ -25,6 +25,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <string>
 #include <thread>
 #include <vector>
 
@@ -174,6 +175,9 @@ struct zk_groth16_pk {
     uint8_t* h_tab = nullptr;
     int h_c = 0, h_W = 0;
     std::mutex h_mu;
+    // private device context of the witness MSMs inside prove (created on first
+    // use), so that they run beside compute_h and the H MSM on the shared one
+    zk::DeviceContext* wctx = nullptr;
 };
 
 namespace zk {
@@ -644,7 +648,7 @@ static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, s
 // the witness slice [lo, hi): A, B (G2) and B1 over its points [lo, hi), L over
 // the private part of the slice (L_j pairs with w_{1 + pub + j}).  One
 // histogram and one counting sort serve the four.  *all_ms: device time.
-static int witness_msms(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_w, size_t lo, size_t hi, uint64_t a[8], uint64_t b[16],
+static int witness_msms(zk_groth16_pk* pk, DeviceContext* ctx, cudaStream_t st, const Fr* d_w, size_t lo, size_t hi, uint64_t a[8], uint64_t b[16],
                         uint64_t b1[8], uint64_t l[8], float set_ms[4], float* all_ms) {
     const size_t m = (size_t)pk->m, pub = (size_t)pk->num_public;
     const size_t num_priv = (size_t)std::max(0, std::min(pk->l, pk->m - 1 - pk->num_public));
@@ -667,7 +671,7 @@ static int witness_msms(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_w, size_
     ZK_TRY_CUDA(cudaEventCreate(&s0.e));
     ZK_TRY_CUDA(cudaEventCreate(&s1.e));
     ZK_TRY_CUDA(cudaEventRecord(s0.e, st));
-    ZK_TRY(msm_shared_scalars_run(pk->device, st, d_w + lo, hi - lo, sets, pts, g2, range, outs, set_ms));
+    ZK_TRY(msm_shared_scalars_run(ctx, st, d_w + lo, hi - lo, sets, pts, g2, range, outs, set_ms));
     ZK_TRY_CUDA(cudaEventRecord(s1.e, st));
     ZK_TRY_CUDA(cudaEventSynchronize(s1.e));
     cudaEventElapsedTime(all_ms, s0.e, s1.e);
@@ -689,11 +693,38 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     const uint64_t n = R.n;
     const int m = R.m, pub = R.num_public;
     ZK_TRY(ensure_prover_buffers(pk, n, m));
-    ScopedEvent evs[4];
+    if (!pk->wctx) ZK_TRY(create_context(pk->device, &pk->wctx));
+    ScopedEvent evs[5];
     for (auto& e : evs) ZK_TRY_CUDA(cudaEventCreate(&e.e));
-    cudaEvent_t ev[4] = {evs[0].e, evs[1].e, evs[2].e, evs[3].e};
+    cudaEvent_t ev[5] = {evs[0].e, evs[1].e, evs[2].e, evs[3].e, evs[4].e};
     ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
     ZK_TRY_CUDA(cudaMemcpyAsync(pk->w, h_witness, (size_t)m * 32, cudaMemcpyHostToDevice, st));
+    ZK_TRY_CUDA(cudaEventRecord(ev[4], st));
+
+    // A, B (G2), B1 and L need only the witness: a worker thread runs them on
+    // the key's private context as soon as the witness lands, beside the
+    // matvec, compute_h and the H MSM on `st`.  Over a witness (mostly 0/1
+    // range-check bits) their bucket fixups and reductions are chains of
+    // dependent point additions over few, very full buckets that leave most
+    // SMs idle; the NTTs and the H MSM fill them.  One counting sort of the
+    // witness serves the four.
+    uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm_out[8] = {0}, b_msm[16];
+    float set_ms[4] = {0, 0, 0, 0}, wit_all = 0;
+    int wit_rc = ZK_OK;
+    std::string wit_err;
+    struct Joiner {
+        std::thread t;
+        ~Joiner() {
+            if (t.joinable()) t.join();
+        }
+    } worker;  // joined on every return path, before the results above go out of scope
+    DeviceContext* wctx = pk->wctx;
+    ZK_TRY_CUDA(cudaStreamWaitEvent(wctx->stream, ev[4], 0));
+    worker.t = std::thread([&, wctx]() {
+        wit_rc = witness_msms(pk, wctx, wctx->stream, pk->w, 0, (size_t)m, a_msm, b_msm, b1_msm, l_msm, set_ms, &wit_all);
+        if (wit_rc != ZK_OK) wit_err = zk_last_error();
+    });
+
     ZK_TRY(r1cs_matvec(R, st, pk->w, pk->abc, ctx->num_sms));
     const bool check = witness_check_enabled();
     if (check) {
@@ -716,24 +747,24 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     cudaEventElapsedTime(&ms, ev[1], ev[2]);
     stats.compute_h_ms = ms;
 
-    uint64_t a_msm[8], b1_msm[8], l_msm[8] = {0}, h_msm_out[8] = {0}, b_msm[16];
-    const size_t g1A = 0, g1B1 = (size_t)m, g1L = 2 * (size_t)m;
     zk_msm_stats ms_st;
-    {  // A, B (G2), B1 and L share the witness as scalars: one counting sort
-        float set_ms[4] = {0, 0, 0, 0}, all = 0;
-        ZK_TRY(witness_msms(pk, st, pk->w, 0, (size_t)m, a_msm, b_msm, b1_msm, l_msm, set_ms, &all));
-        // the shared histogram and sort are charged to A
-        stats.msm_ms[0] = all - set_ms[1] - set_ms[2] - set_ms[3];
-        stats.msm_ms[1] = set_ms[1];
-        stats.msm_ms[4] = set_ms[2];
-        stats.msm_ms[2] = set_ms[3];
-    }
     const int n_h = std::min<int>((int)n, pk->n_h);
     if (n_h > 0) {
         ZK_TRY(h_msm(pk, st, pk->h, 0, (size_t)n_h, h_msm_out));
         zk_msm_last_stats(&ms_st);
         stats.msm_ms[3] = ms_st.total_device_ms;
     }
+    worker.t.join();
+    if (wit_rc != ZK_OK) {
+        set_error("%s", wit_err.c_str());
+        return wit_rc;
+    }
+    // device time of each witness MSM on its own stream (overlapping the work
+    // above); the shared histogram and sort are charged to A
+    stats.msm_ms[0] = wit_all - set_ms[1] - set_ms[2] - set_ms[3];
+    stats.msm_ms[1] = set_ms[1];
+    stats.msm_ms[4] = set_ms[2];
+    stats.msm_ms[2] = set_ms[3];
 
     assemble(pk, r, s, a_msm, b_msm, l_msm, h_msm_out, b1_msm, outA, outB, outC);
     ZK_TRY_CUDA(cudaEventRecord(ev[3], st));
@@ -1081,6 +1112,7 @@ extern "C" void zk_groth16_pk_destroy(zk_groth16_pk* pk) {
     cudaFree(pk->d_bad);
     cudaFreeHost(pk->h_bad);
     cudaFree(pk->h_tab);
+    zk::destroy_context(pk->wctx);
     delete pk;
 }
 
@@ -1249,5 +1281,5 @@ extern "C" int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, c
     ZK_TRY(get_context(pk->device, &ctx));
     uint64_t* q = (uint64_t*)sums;  // A (8) | B2 (16) | L (8) | H (8, untouched) | B1 (8) words
     float set_ms[4], all = 0;
-    return witness_msms(pk, (cudaStream_t)stream, (const Fr*)d_witness, lo, hi, q, q + 8, q + 40, q + 24, set_ms, &all);
+    return witness_msms(pk, ctx, (cudaStream_t)stream, (const Fr*)d_witness, lo, hi, q, q + 8, q + 40, q + 24, set_ms, &all);
 }

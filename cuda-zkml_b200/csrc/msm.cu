@@ -1192,7 +1192,7 @@ int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t
 // counting sort, then an accumulate + reduce per point set (G1 or G2 packed
 // affine).  idx_range (optional, 2 per set): set k uses the scalars
 // [lo, hi) only, against its points 0 .. hi - lo.
-int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
+int msm_shared_scalars_run(DeviceContext* ctx, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
                            const int* is_g2, const uint32_t* idx_range, uint64_t* const* outs, float* set_ms) {
     MsmStats& stats = msm_stats();
     stats = MsmStats();
@@ -1205,8 +1205,7 @@ int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, s
         set_error("msm: %zu points or %d point sets out of range", n, n_sets);
         return ZK_ERR_RANGE;
     }
-    DeviceContext* ctx;
-    ZK_TRY(get_context(device, &ctx));
+    ZK_TRY_CUDA(cudaSetDevice(ctx->device));
     std::lock_guard<std::mutex> lock(ctx->mu);
     const double sms = (double)std::max(ctx->num_sms, 1);
     ZK_TRY(ensure_pinned(ctx, 4096));

@@ -70,6 +70,21 @@ struct NttTables {
     std::map<std::vector<uint64_t>, CosetTables> coset;  // key: L, kind, g limbs
 };
 
+void release_ntt_tables(DeviceContext* ctx) {
+    if (!ctx->ntt) return;
+    for (auto& kv : ctx->ntt->dir) {
+        cudaFree(kv.second.roots);
+        cudaFree(kv.second.tw_lo);
+        cudaFree(kv.second.tw_hi);
+    }
+    for (auto& kv : ctx->ntt->coset) {
+        cudaFree(kv.second.lo);
+        cudaFree(kv.second.hi);
+    }
+    delete ctx->ntt;
+    ctx->ntt = nullptr;
+}
+
 static void host_fr_pow_u64(zkh::Fe& r, const zkh::Fe& a, uint64_t e) {
     uint64_t ee[4] = {e, 0, 0, 0};
     zkh::pow(zkh::kR, r, a, ee);

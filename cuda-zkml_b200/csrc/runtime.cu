@@ -23,7 +23,36 @@ MsmStats& msm_stats() { return g_msm_stats; }
 static std::mutex g_ctx_mu;
 static DeviceContext* g_ctx[64];
 
-int get_context(int device, DeviceContext** out) {
+// Streams, events and device properties of a new context on `device`.
+static int init_context(DeviceContext* c, int device) {
+    c->device = device;
+    cudaDeviceProp prop;
+    ZK_TRY_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) {
+        set_error("device %d is sm_%d%d; this library is built for sm_100a only", device, prop.major, prop.minor);
+        return ZK_ERR_NODEV;
+    }
+    c->num_sms = prop.multiProcessorCount;
+    // keep stream-ordered allocations cached in the device's default pool
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+    ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_a, cudaEventDisableTiming));
+    ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_b, cudaEventDisableTiming));
+    ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_c, cudaEventDisableTiming));
+    ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->scratch_done, cudaEventDisableTiming));
+    ZK_TRY_CUDA(cudaEventRecord(c->scratch_done, c->stream));
+    for (int i = 0; i < 9; i++) ZK_TRY_CUDA(cudaEventCreate(&c->phase[i]));
+    ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->aux_stream, cudaStreamNonBlocking));
+    for (int i = 0; i < 12; i++) ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->batch_ev[i], cudaEventDisableTiming));
+    return ZK_OK;
+}
+
+static int check_device(int& device) {
     int count = 0;
     cudaError_t e = cudaGetDeviceCount(&count);
     if (e != cudaSuccess || count == 0) {
@@ -36,38 +65,56 @@ int get_context(int device, DeviceContext** out) {
         return ZK_ERR_INVALID;
     }
     ZK_TRY_CUDA(cudaSetDevice(device));
+    return ZK_OK;
+}
+
+int get_context(int device, DeviceContext** out) {
+    ZK_TRY(check_device(device));
     std::lock_guard<std::mutex> lock(g_ctx_mu);
     if (!g_ctx[device]) {
         DeviceContext* c = new DeviceContext();
-        c->device = device;
-        cudaDeviceProp prop;
-        ZK_TRY_CUDA(cudaGetDeviceProperties(&prop, device));
-        if (prop.major < 10) {
-            set_error("device %d is sm_%d%d; this library is built for sm_100a only", device, prop.major, prop.minor);
-            delete c;
-            return ZK_ERR_NODEV;
+        const int rc = init_context(c, device);
+        if (rc != ZK_OK) {
+            destroy_context(c);
+            return rc;
         }
-        c->num_sms = prop.multiProcessorCount;
-        // keep stream-ordered allocations cached in the device's default pool
-        cudaMemPool_t pool;
-        if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
-            uint64_t keep = UINT64_MAX;
-            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
-        }
-        ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
-        ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
-        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_a, cudaEventDisableTiming));
-        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_b, cudaEventDisableTiming));
-        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->ev_c, cudaEventDisableTiming));
-        ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->scratch_done, cudaEventDisableTiming));
-        ZK_TRY_CUDA(cudaEventRecord(c->scratch_done, c->stream));
-        for (int i = 0; i < 9; i++) ZK_TRY_CUDA(cudaEventCreate(&c->phase[i]));
-        ZK_TRY_CUDA(cudaStreamCreateWithFlags(&c->aux_stream, cudaStreamNonBlocking));
-        for (int i = 0; i < 12; i++) ZK_TRY_CUDA(cudaEventCreateWithFlags(&c->batch_ev[i], cudaEventDisableTiming));
         g_ctx[device] = c;
     }
     *out = g_ctx[device];
     return ZK_OK;
+}
+
+int create_context(int device, DeviceContext** out) {
+    ZK_TRY(check_device(device));
+    DeviceContext* c = new DeviceContext();
+    const int rc = init_context(c, device);
+    if (rc != ZK_OK) {
+        destroy_context(c);
+        return rc;
+    }
+    *out = c;
+    return ZK_OK;
+}
+
+void destroy_context(DeviceContext* c) {
+    if (!c) return;
+    if (c->device >= 0) cudaSetDevice(c->device);
+    cudaStream_t streams[3] = {c->stream, c->copy_stream, c->aux_stream};
+    for (cudaStream_t s : streams)
+        if (s) cudaStreamSynchronize(s);
+    release_ntt_tables(c);
+    if (c->scratch) cudaFree(c->scratch);
+    if (c->pinned) cudaFreeHost(c->pinned);
+    cudaEvent_t evs[4] = {c->ev_a, c->ev_b, c->ev_c, c->scratch_done};
+    for (cudaEvent_t e : evs)
+        if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : c->phase)
+        if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : c->batch_ev)
+        if (e) cudaEventDestroy(e);
+    for (cudaStream_t s : streams)
+        if (s) cudaStreamDestroy(s);
+    delete c;
 }
 
 int ensure_scratch(DeviceContext* ctx, size_t bytes) {

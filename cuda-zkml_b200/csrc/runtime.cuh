@@ -97,6 +97,13 @@ struct DeviceContext {
 // Lazily created context of `device` (-1 = the calling thread's current device).
 // Makes `device` current on the calling thread.
 int get_context(int device, DeviceContext** out);
+// A private context on `device` (its own streams, scratch and lock), for work
+// that runs beside calls on the device's shared context; freed by
+// destroy_context after its streams drain.
+int create_context(int device, DeviceContext** out);
+void destroy_context(DeviceContext* ctx);
+// Frees the NTT tables cached in a context (ntt.cu).
+void release_ntt_tables(DeviceContext* ctx);
 // Ensure the scratch arena holds at least `bytes` (synchronises on growth).
 int ensure_scratch(DeviceContext* ctx, size_t bytes);
 int ensure_pinned(DeviceContext* ctx, size_t bytes);
@@ -122,8 +129,9 @@ MsmStats& msm_stats();
 void g1_window_tables_shape(size_t n, int* c, int* W);
 int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out);
 // Several MSMs (G1 or G2 point sets) over the same device scalars with one
-// shared counting sort (msm.cu); outs[k]: 64 or 128 host bytes.
-int msm_shared_scalars_run(int device, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
+// shared counting sort (msm.cu), in the scratch of `ctx`; outs[k]: 64 or 128
+// host bytes.
+int msm_shared_scalars_run(DeviceContext* ctx, cudaStream_t st, const void* d_scalars, size_t n, int n_sets, const void* const* d_points,
                            const int* is_g2, const uint32_t* idx_range, uint64_t* const* outs, float* set_ms);
 int g1_window_tables_msm(int device, cudaStream_t st, const void* tables, size_t n_total, int c, int W, size_t lo, size_t hi,
                          const void* d_scalars, uint64_t* out_affine);

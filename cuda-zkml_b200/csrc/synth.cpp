@@ -1,21 +1,31 @@
-// synth.cpp -- seeded synthetic R1CS workloads shaped like the reference's
-// quantised-CNN statements (SURVEY configs 4/5): CONV2D 3x3 layers (pad 1)
-// whose outputs go through an exact ReLU with a bit-decomposed range check and
-// a right shift, then a dense layer.  The circuit comes with a satisfying
-// witness, in the reference's data layout: constraints as
-// zkml::SparseEntry records {int row; int col; Fr value} (40 bytes,
-// src/prover/circuit.cuh:31-35) and the witness as Fr[num_variables] laid out
-// [1, public..., private...] (src/prover/circuit.cuh:22-24).
+// synth.cpp -- seeded synthetic R1CS workloads with the constraint structure
+// of the reference's quantised-CNN statements (statement v2 with fixed model
+// weights, src/prover/statement_v2.cuh:98-240, gadgets from
+// src/prover/gadgets.cuh): CONV2D 3x3 layers (pad 1) whose outputs go through
+// RELU_EXACT (an exact ReLU plus a range-checked rescale), then a dense layer
+// whose outputs are public.  The circuit comes with a satisfying witness, in the
+// reference's data layout: constraints as zkml::SparseEntry records
+// {int row; int col; Fr value} (40 bytes, src/prover/circuit.cuh:31-35) and the
+// witness as Fr[num_variables] laid out [1, public..., private...]
+// (src/prover/circuit.cuh:22-24).
 //
-// Constraint families (all coefficients small integers, converted to Montgomery
-// form):
-//   dot      sum_k W_k x_k + bias            * 1 = acc
-//   bit      t_i                             * (t_i - 1) = 0        (b rows)
-//   recomp   sum_i 2^i t_i - 2^(b-1)         * 1 = acc
-//   relu     t_(b-1)                         * sum_{i=s}^{b-2} 2^(i-s) t_i = q
-//   range    bits of q (o rows) and their recomposition
-//   dense    sum_j V_kj q_j                  * 1 = out_k   (public outputs)
-// The input feature map and the dense outputs are the public inputs.
+// Variables, in allocation order (statement_v2.cuh:111-128): the constant 1,
+// the public dense outputs, the public model tag, the public input feature
+// map; then per layer the conv outputs, then per neuron the ReLU and rescale
+// variables; last the dense outputs' private copies.  Rows, in order, with
+// k the layer's range width and s the shift:
+//   tag       tag * 1 = tag_var                                 (1 row)
+//   conv      sum_taps W x + bias * 1 = z    (add_fixed_conv2d, gadgets.cuh:281-311;
+//             taps with a zero weight are skipped, the bias term is always kept)
+//   ReLU      b_i * (b_i - 1) = 0, i < k; sum 2^i b_i - z - 2^(k-1) = 0;
+//             b_(k-1) * z = y                 (add_relu_exact, gadgets.cuh:197-204)
+//   rescale   bits of r (s rows + recomposition), signed bits of q (k rows +
+//             recomposition), q 2^s + r - y = 0   (add_rescale, gadgets.cuh:207-220)
+//   dense     sum_j V_kj q_j + bias * 1 = out_k             (add_fixed_linear)
+//   outputs   pub_k - out_k = 0                        (statement_v2.cuh:216-218)
+// A config-5 shape (2 layers of 32 x 32 x 32, k = 24 then 23, s = 10, 10 dense
+// outputs) gives 4,128,789 constraints and 4,030,486 variables (32,779 public),
+// the counts of the reference's own statement for that model.
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -73,138 +83,157 @@ struct Builder {
     }
 };
 
-int bitlen(uint64_t x) {
-    int b = 0;
-    while (x) { b++; x >>= 1; }
-    return b;
-}
 
 }  // namespace
 
 extern "C" int zk_synth_conv_circuit(int layers, int channels, int height, int width, int bits, int shift, int out_bits,
                                      int dense_outputs, uint64_t seed, zk_synth_circuit* out) {
-    if (!out || layers < 1 || channels < 1 || height < 1 || width < 1 || bits < 4 || shift < 0 || out_bits < 0 ||
-        dense_outputs < 0)
+    if (!out || layers < 1 || channels < 1 || height < 1 || width < 1 || bits < 2 || bits > 60 || shift < 0 ||
+        shift > 60 || out_bits < 0 || out_bits == 1 || out_bits > 60 || dense_outputs < 0)
         return ZK_ERR_INVALID;
     std::memset(out, 0, sizeof *out);
     std::mt19937_64 rng(seed);
     auto i8 = [&]() { return (int64_t)(rng() % 255) - 127; };
     Builder B;
     const int C = channels, H = height, Wd = width, fm = C * H * Wd;
-    const int num_public = fm + dense_outputs;
+    // public: [dense outputs, model tag, input feature map]
+    const int num_public = dense_outputs + 1 + fm;
     B.wit.assign((size_t)1 + num_public, 0);
     B.wit[0] = 1;
+    const int tag = 1 + dense_outputs;
+    const int64_t tag_value = (int64_t)(rng() >> 2);
+    B.wit[(size_t)tag] = tag_value;
     std::vector<int> X(fm);
     for (int i = 0; i < fm; i++) {
-        X[i] = 1 + i;
+        X[i] = tag + 1 + i;
         B.wit[(size_t)X[i]] = (int64_t)(rng() % 17);  // inputs in [0, 16]
     }
+    int row = B.rows++;
+    B.put(0, row, 0, tag_value);
+    B.put(1, row, 0, 1);
+    B.put(2, row, tag, 1);
+
+    // k boolean variables for v + offset (LSB first), their b (b - 1) = 0 rows and
+    // the recomposition row sum 2^i b_i - v - offset = 0 (no offset term when 0)
+    auto range_bits = [&](int v, int64_t offset, int k) -> int {
+        const uint64_t t = (uint64_t)(B.wit[(size_t)v] + offset);
+        int first = -1;
+        for (int i = 0; i < k; i++) {
+            const int bv = B.var((int64_t)((t >> i) & 1));
+            if (i == 0) first = bv;
+            const int r = B.rows++;
+            B.put(0, r, bv, 1);
+            B.put(1, r, bv, 1);
+            B.put(1, r, 0, -1);
+        }
+        const int r = B.rows++;
+        for (int i = 0; i < k; i++) B.put(0, r, first + i, (int64_t)1 << i);
+        B.put(0, r, v, -1);
+        if (offset) B.put(0, r, 0, -offset);
+        B.put(1, r, 0, 1);
+        return first;
+    };
+
     for (int l = 0; l < layers; l++) {
+        const int k = (l == 0 || out_bits == 0) ? bits : out_bits;
+        const int64_t half = (int64_t)1 << (k - 1);
         std::vector<int64_t> Wt((size_t)C * C * 9), bias(C);
         for (auto& w : Wt) w = i8();
         for (auto& b : bias) b = i8();
-        // accumulators first, to size the range check of this layer
-        std::vector<int64_t> acc(fm);
-        int64_t amax = 0;
-        for (int co = 0; co < C; co++)
-            for (int y = 0; y < H; y++)
-                for (int x = 0; x < Wd; x++) {
-                    int64_t a = bias[co];
-                    for (int ci = 0; ci < C; ci++)
-                        for (int dy = 0; dy < 3; dy++)
-                            for (int dx = 0; dx < 3; dx++) {
-                                int yy = y + dy - 1, xx = x + dx - 1;
-                                if (yy < 0 || yy >= H || xx < 0 || xx >= Wd) continue;
-                                a += Wt[((size_t)co * C + ci) * 9 + dy * 3 + dx] * B.wit[(size_t)X[((size_t)ci * H + yy) * Wd + xx]];
-                            }
-                    acc[((size_t)co * H + y) * Wd + x] = a;
-                    amax = std::max<int64_t>(amax, a < 0 ? -a : a);
-                }
-        const int b = std::max(bits, bitlen((uint64_t)amax) + 2);
-        std::vector<int> Y(fm);
+        std::vector<int> Z(fm);
         for (int co = 0; co < C; co++)
             for (int y = 0; y < H; y++)
                 for (int x = 0; x < Wd; x++) {
                     const size_t o = ((size_t)co * H + y) * Wd + x;
-                    const int64_t a = acc[o];
-                    const int av = B.var(a);
-                    // dot: sum W x + bias = acc
-                    int row = B.rows++;
+                    row = B.rows++;
+                    int64_t a = bias[co];
                     for (int ci = 0; ci < C; ci++)
                         for (int dy = 0; dy < 3; dy++)
                             for (int dx = 0; dx < 3; dx++) {
-                                int yy = y + dy - 1, xx = x + dx - 1;
+                                const int yy = y + dy - 1, xx = x + dx - 1;
                                 if (yy < 0 || yy >= H || xx < 0 || xx >= Wd) continue;
-                                B.put(0, row, X[((size_t)ci * H + yy) * Wd + xx], Wt[((size_t)co * C + ci) * 9 + dy * 3 + dx]);
+                                const int64_t w = Wt[((size_t)co * C + ci) * 9 + dy * 3 + dx];
+                                if (!w) continue;
+                                const int xv = X[((size_t)ci * H + yy) * Wd + xx];
+                                B.put(0, row, xv, w);
+                                a += w * B.wit[(size_t)xv];
                             }
                     B.put(0, row, 0, bias[co]);
                     B.put(1, row, 0, 1);
-                    B.put(2, row, av, 1);
-                    // bit decomposition of t = acc + 2^(b-1)
-                    const uint64_t t = (uint64_t)(a + ((int64_t)1 << (b - 1)));
-                    std::vector<int> tv(b);
-                    for (int i = 0; i < b; i++) {
-                        tv[i] = B.var((int64_t)((t >> i) & 1));
-                        row = B.rows++;
-                        B.put(0, row, tv[i], 1);
-                        B.put(1, row, tv[i], 1);
-                        B.put(1, row, 0, -1);
-                    }
-                    row = B.rows++;
-                    for (int i = 0; i < b; i++) B.put(0, row, tv[i], (int64_t)1 << i);
-                    B.put(0, row, 0, -((int64_t)1 << (b - 1)));
-                    B.put(1, row, 0, 1);
-                    B.put(2, row, av, 1);
-                    // relu + shift: q = sign * floor(t_low / 2^s)
-                    const int64_t q = a > 0 ? (a >> shift) : 0;
-                    const int qv = B.var(q);
-                    row = B.rows++;
-                    B.put(0, row, tv[b - 1], 1);
-                    for (int i = shift; i <= b - 2; i++) B.put(1, row, tv[i], (int64_t)1 << (i - shift));
-                    B.put(2, row, qv, 1);
-                    // range check of q (at least as many bits as q can have)
-                    const int ob = out_bits > 0 ? std::max(out_bits, b - 1 - shift) : 0;
-                    if (ob > 0) {
-                        std::vector<int> uv(ob);
-                        for (int i = 0; i < ob; i++) {
-                            uv[i] = B.var((int64_t)(((uint64_t)q >> i) & 1));
-                            row = B.rows++;
-                            B.put(0, row, uv[i], 1);
-                            B.put(1, row, uv[i], 1);
-                            B.put(1, row, 0, -1);
-                        }
-                        row = B.rows++;
-                        for (int i = 0; i < ob; i++) B.put(0, row, uv[i], (int64_t)1 << i);
-                        B.put(1, row, 0, 1);
-                        B.put(2, row, qv, 1);
-                    }
-                    Y[o] = qv;
+                    Z[o] = B.var(a);
+                    B.put(2, row, Z[o], 1);
+                    if (a < -half || a >= half) return ZK_ERR_INVALID;  // outside the layer's range
                 }
-        X.swap(Y);
+        std::vector<int> Q(fm);
+        for (size_t o = 0; o < (size_t)fm; o++) {
+            const int z = Z[o];
+            const int64_t a = B.wit[(size_t)z];
+            // exact ReLU: the top bit of z + 2^(k-1) is [z >= 0]; y = s z
+            const int b0 = range_bits(z, half, k);
+            const int s = b0 + k - 1;
+            const int yv = B.var(B.wit[(size_t)s] * a);
+            row = B.rows++;
+            B.put(0, row, s, 1);
+            B.put(1, row, z, 1);
+            B.put(2, row, yv, 1);
+            if (shift == 0) {
+                Q[o] = yv;
+                continue;
+            }
+            // rescale: y = q 2^s + r with 0 <= r < 2^s and q in the signed k-bit range
+            const int64_t y = B.wit[(size_t)yv];
+            const int64_t q = y >> shift, r = y - (q << shift);
+            if (q < -half || q >= half) return ZK_ERR_INVALID;
+            const int qv = B.var(q), rv = B.var(r);
+            range_bits(rv, 0, shift);
+            range_bits(qv, half, k);
+            row = B.rows++;
+            B.put(0, row, qv, (int64_t)1 << shift);
+            B.put(0, row, rv, 1);
+            B.put(0, row, yv, -1);
+            B.put(1, row, 0, 1);
+            Q[o] = qv;
+        }
+        X.swap(Q);
     }
-    for (int k = 0; k < dense_outputs; k++) {
-        const int ov = 1 + fm + k;
+    std::vector<int> dense(dense_outputs);
+    for (int kk = 0; kk < dense_outputs; kk++) {
+        row = B.rows++;
         int64_t s = 0;
-        const int row = B.rows++;
         for (int j = 0; j < fm; j++) {
             const int64_t v = i8();
             if (!v) continue;
             B.put(0, row, X[j], v);
             s += v * B.wit[(size_t)X[j]];
         }
+        const int64_t b = i8();
+        B.put(0, row, 0, b);
+        s += b;
         B.put(1, row, 0, 1);
-        B.put(2, row, ov, 1);
-        B.wit[(size_t)ov] = s;
+        dense[kk] = B.var(s);
+        B.put(2, row, dense[kk], 1);
+    }
+    for (int kk = 0; kk < dense_outputs; kk++) {
+        const int pv = 1 + kk;
+        B.wit[(size_t)pv] = B.wit[(size_t)dense[kk]];
+        row = B.rows++;
+        B.put(0, row, pv, 1);
+        B.put(0, row, dense[kk], -1);
+        B.put(1, row, 0, 1);
     }
     const size_t m = B.wit.size();
     zkh::Fe* w = (zkh::Fe*)std::malloc(m * 32);
     if (!w) return ZK_ERR_NOMEM;
     for (size_t i = 0; i < m; i++) w[i] = B.fr_of(B.wit[i]);
-    for (int k = 0; k < 3; k++) {
-        out->nnz[k] = B.m[k].size();
-        out->entries[k] = std::malloc(std::max<size_t>(1, B.m[k].size()) * sizeof(Entry));
-        if (!out->entries[k]) return ZK_ERR_NOMEM;
-        std::memcpy(out->entries[k], B.m[k].data(), B.m[k].size() * sizeof(Entry));
+    for (int kk = 0; kk < 3; kk++) {
+        out->nnz[kk] = B.m[kk].size();
+        out->entries[kk] = std::malloc(std::max<size_t>(1, B.m[kk].size()) * sizeof(Entry));
+        if (!out->entries[kk]) {
+            std::free(w);
+            zk_synth_free(out);
+            return ZK_ERR_NOMEM;
+        }
+        std::memcpy(out->entries[kk], B.m[kk].data(), B.m[kk].size() * sizeof(Entry));
     }
     out->witness = w;
     out->num_constraints = B.rows;

@@ -327,11 +327,15 @@ typedef struct {
     void* witness;     /* malloc'd Fr array */
 } zk_synth_circuit;
 
-/* `layers` CONV2D 3x3 (pad 1) layers of channels x height x width with int8
- * weights, each output through an exact ReLU (bit decomposition of
- * acc + 2^(b-1), b >= `bits` wide enough for the layer), a right shift by
- * `shift` and an `out_bits` range check, then `dense_outputs` dense outputs.
- * Public inputs: the input feature map (values 0..16) and the dense outputs. */
+/* `layers` CONV2D 3x3 (pad 1) layers of channels x height x width with
+ * seeded int8 weights and biases, each output through RELU_EXACT with the
+ * reference's gadgets (src/prover/gadgets.cuh:197-220: a signed range check
+ * of `bits` bits whose top bit selects y = z, then y = q 2^shift + r with r
+ * in `shift` bits and q in the same signed range), `out_bits` replacing
+ * `bits` from the second layer on (0: same), then `dense_outputs` int8 dense
+ * outputs made public through equality rows.  Public inputs, in order: the
+ * dense outputs, a model tag, the input feature map (values 0..16).
+ * ZK_ERR_INVALID when a value leaves its layer's range. */
 int zk_synth_conv_circuit(int layers, int channels, int height, int width, int bits, int shift,
                           int out_bits, int dense_outputs, uint64_t seed, zk_synth_circuit* out);
 void zk_synth_free(zk_synth_circuit* c);

@@ -32,7 +32,7 @@ def test_parse_reference_proving_key(case):
 
 
 def test_p160_size_formula():
-    # SURVEY: p160 (n = 1024, m = 716, pub = 75, L = 640) is 294,496 bytes
+    # p160 (n = 1024, m = 716, pub = 75, L = 640) is 294,496 bytes
     assert zkmlpk3.pk_size(1024, 716, 640) == 294496
 
 

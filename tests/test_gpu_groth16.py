@@ -111,10 +111,10 @@ def test_mismatched_key_is_refused(small):
 
 
 def test_prove_2_16_config4_shape():
-    """A ~60k-constraint circuit (domain 2^16, the size of SURVEY config 4):
+    """A ~60k-constraint circuit (domain 2^16, the size of the reference's config-4 statement):
     the proof passes the trapdoor check (the oracle prove would be slow here,
     so validity rather than byte equality is checked)."""
-    c = Z.synth_conv_circuit(2, 4, 12, 12, 24, 10, 23, 10, 4)
+    c = Z.synth_conv_circuit(2, 4, 11, 11, 24, 10, 23, 10, 4)
     assert 1 << 15 < c["num_constraints"] <= 1 << 16
     r1 = Z.R1cs(c)
     assert r1.log_n == 16

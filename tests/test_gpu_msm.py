@@ -114,8 +114,8 @@ def test_g1_window_sizes_agree(c, monkeypatch):
 
 def test_g1_skewed_scalars():
     """Bucket skew: 40% zeros, 30% one repeated scalar, 20% values < 2^16,
-    plus duplicated points and P, -P pairs (the SURVEY's 10%/10% variant is a
-    milder version of this)."""
+    plus duplicated points and P, -P pairs (the benchmark's 10% zero / 10% small
+    variant is a milder version of this)."""
     n = 20000
     rng = O.Rng(21)
     k = rng.fr_vector(n)

@@ -67,7 +67,7 @@ def parse_pk(buf):
 
 
 def pk_size(n_h, m, l, tau_g2=2, tau_g1=0):
-    """Byte size of a ZKMLPK3 file (SURVEY's check: p160 = 294,496 bytes)."""
+    """Byte size of a ZKMLPK3 file (worked check: p160 = 294,496 bytes)."""
     return 24 + 3 * 65 + 3 * 129 + (4 + tau_g1 * 65) + (4 + tau_g2 * 129) + 2 * (4 + m * 65) + (4 + m * 129) + (4 + l * 65) + (4 + n_h * 65)
 
 
