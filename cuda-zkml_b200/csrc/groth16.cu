@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -178,6 +179,16 @@ struct zk_groth16_pk {
     // private device context of the witness MSMs inside prove (created on first
     // use), so that they run beside compute_h and the H MSM on the shared one
     zk::DeviceContext* wctx = nullptr;
+    // per (log_parts, part): that part's H points in the "blocks" order of a
+    // proof split over 2^log_parts parts, and window tables over them; built on
+    // first use and kept until the key is destroyed (a process proving one part
+    // holds one entry; ranks emulated as threads on one device hold several)
+    struct HBlocks {
+        uint8_t* pts = nullptr;
+        uint8_t* tab = nullptr;
+        int c = 0, W = 0;
+    };
+    std::map<std::pair<int, int>, HBlocks> hb;
 };
 
 namespace zk {
@@ -642,6 +653,57 @@ static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, s
     }
     const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
     return zk_msm_g1_device(pk->device, st, hq + lo * 64, d_h + lo, hi - lo, out);
+}
+
+// One part's share of the H MSM of a proof split over N = 2^log_parts parts,
+// its coefficients in the "blocks" layout of the split transforms (local
+// k q + v is global k m + part q + v, m = n / N, q = m / N).  The part's H
+// points are gathered once into that order (points at or beyond n_h stay the
+// identity, all-zero), with window tables over them from 2^16 points when
+// the query covers the whole domain.
+static int h_msm_blocks(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h_part, int log_parts, int part, uint64_t out[8]) {
+    const uint64_t n = (uint64_t)pk->num_constraints;
+    if (log_parts < 0 || log_parts > 3 || (n >> (2 * log_parts)) == 0 || part < 0 || part >= (1 << log_parts)) {
+        set_error("H MSM blocks: %d parts of a %llu-point domain, part %d out of range", 1 << log_parts, (unsigned long long)n, part);
+        return ZK_ERR_RANGE;
+    }
+    const uint64_t m = n >> log_parts, q = m >> log_parts;
+    zk_groth16_pk::HBlocks hb;
+    {
+        std::lock_guard<std::mutex> lock(pk->h_mu);
+        auto it = pk->hb.find({log_parts, part});
+        if (it != pk->hb.end()) {
+            hb = it->second;
+        } else {
+            int rc = ZK_OK;
+            if (cudaMalloc(&hb.pts, m * 64) != cudaSuccess) rc = ZK_ERR_CUDA;
+            if (rc == ZK_OK && cudaMemsetAsync(hb.pts, 0, m * 64, st) != cudaSuccess) rc = ZK_ERR_CUDA;
+            const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
+            for (uint64_t k = 0; rc == ZK_OK && k < (1ull << log_parts); k++) {
+                const uint64_t g0 = k * m + (uint64_t)part * q;
+                if (g0 >= (uint64_t)pk->n_h) continue;
+                const uint64_t cnt = std::min<uint64_t>(q, (uint64_t)pk->n_h - g0);
+                if (cudaMemcpyAsync(hb.pts + k * q * 64, hq + g0 * 64, cnt * 64, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+                    rc = ZK_ERR_CUDA;
+            }
+            // tables need every base on the curve: none when identities fill missing points
+            if (rc == ZK_OK && m >= (uint64_t)kHTablesMin && (uint64_t)pk->n_h >= n) {
+                g1_window_tables_shape(m, &hb.c, &hb.W);
+                if (cudaMalloc(&hb.tab, (size_t)hb.W * m * 64) != cudaSuccess) rc = ZK_ERR_CUDA;
+                if (rc == ZK_OK) rc = g1_window_tables_build(pk->device, st, hb.pts, m, hb.c, hb.W, hb.tab);
+            }
+            if (rc == ZK_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = ZK_ERR_CUDA;
+            if (rc != ZK_OK) {
+                if (rc == ZK_ERR_CUDA) set_error("H MSM blocks: %s", cudaGetErrorString(cudaGetLastError()));
+                cudaFree(hb.pts);
+                cudaFree(hb.tab);
+                return rc;
+            }
+            pk->hb[{log_parts, part}] = hb;
+        }
+    }
+    if (hb.tab) return g1_window_tables_msm(pk->device, st, hb.tab, m, hb.c, hb.W, 0, m, d_h_part, out);
+    return zk_msm_g1_device(pk->device, st, hb.pts, d_h_part, m, out);
 }
 
 // The MSMs of a proof whose scalars are the witness (groth16.cu:776-827), over
@@ -1112,6 +1174,10 @@ extern "C" void zk_groth16_pk_destroy(zk_groth16_pk* pk) {
     cudaFree(pk->d_bad);
     cudaFreeHost(pk->h_bad);
     cudaFree(pk->h_tab);
+    for (auto& kv : pk->hb) {
+        cudaFree(kv.second.pts);
+        cudaFree(kv.second.tab);
+    }
     zk::destroy_context(pk->wctx);
     delete pk;
 }
@@ -1271,6 +1337,15 @@ extern "C" int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const vo
     DeviceContext* ctx;
     ZK_TRY(get_context(pk->device, &ctx));
     return h_msm(pk, (cudaStream_t)stream, (const Fr*)d_h, lo, hi, (uint64_t*)out_affine);
+}
+
+extern "C" int zk_groth16_h_msm_blocks_device(zk_groth16_pk* pk, void* stream, const void* d_h_part, int log_parts, int part,
+                                              void* out_affine) {
+    clear_error();
+    if (!pk || !d_h_part || !out_affine) return ZK_ERR_INVALID;
+    DeviceContext* ctx;
+    ZK_TRY(get_context(pk->device, &ctx));
+    return h_msm_blocks(pk, (cudaStream_t)stream, (const Fr*)d_h_part, log_parts, part, (uint64_t*)out_affine);
 }
 
 extern "C" int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, const void* d_witness, uint64_t lo, uint64_t hi,

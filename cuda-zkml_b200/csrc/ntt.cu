@@ -161,6 +161,7 @@ static int get_dir_tables(DeviceContext* ctx, int L, bool inverse, const NttDirT
 // kind 0: g^i          (forward coset pre-multiplication)
 // kind 1: n^-1 g^-i    (inverse coset post-multiplication)
 // kind 2: n^-1 g^i     (INTT followed by the coset shift, fused)
+// kind 3: g^-i         (inverse coset factor without the n^-1)
 static int get_coset_tables(DeviceContext* ctx, int L, int kind, const zkh::Fe& g, const CosetTables** out) {
     if (!ctx->ntt) ctx->ntt = new NttTables();
     std::vector<uint64_t> key = {(uint64_t)L, (uint64_t)kind, g.v[0], g.v[1], g.v[2], g.v[3]};
@@ -172,8 +173,8 @@ static int get_coset_tables(DeviceContext* ctx, int L, int kind, const zkh::Fe& 
     CosetTables t;
     t.h = (L + 1) / 2;
     zkh::Fe one = zkh::one(zkh::kR), step = g, start = one;
-    if (kind == 1) zkh::inv(zkh::kR, step, g);
-    if (kind >= 1) {
+    if (kind == 1 || kind == 3) zkh::inv(zkh::kR, step, g);
+    if (kind == 1 || kind == 2) {
         zkh::Fe two, ninv;
         uint64_t s2[4] = {2, 0, 0, 0};
         zkh::from_std(zkh::kR, two, s2);
@@ -561,6 +562,140 @@ __global__ void h_pointwise_kernel(Fr* out, const Fr* a, const Fr* b, const Fr* 
     }
 }
 
+// ------------------------------------------------------------------ transforms split over parts
+// A 2^L-point transform split over N = 2^s parts (one per GPU), m = n / N,
+// q = m / N, with two layouts of a part p's m elements:
+//   cyclic   local t          <-> global p + N t
+//   blocks   local k q + v    <-> global k m + p q + v      (k < N, v < q)
+// cyclic -> blocks:  X[k1 m + k2] = sum_j1 w_N^(j1 k1) w^(j1 k2) sum_j2 x[j1 + N j2] w_m^(j2 k2):
+//   each part runs the m-point transform of its cyclic elements, an all-to-all
+//   sends the k2 in [p' q, p' q + q) to part p', and ntt_cross_kernel mode 0
+//   applies w^(j1 k2) to what part j1 sent and the N-point transform over j1.
+// blocks -> cyclic:  X[k1 + N k2] = sum_j2 w_m^(j2 k2) w^(j2 k1) sum_j1 w_N^(j1 k1) x[j1 m + j2]:
+//   ntt_cross_kernel mode 1 runs the N-point transforms over the local blocks
+//   and applies w^(j2 k1); an all-to-all sends block k1 to part k1, which runs
+//   the m-point transform of what it gathered (j2 in order).
+// One all-to-all per transform; the layouts chain (an INTT from cyclic to
+// blocks feeds a coset NTT from blocks back to cyclic).  An optional factor
+// f(global index) is applied to the outputs (mode 0) or inputs (mode 1), and
+// `scale` (N^-1 for an inverse transform) to the outputs.
+struct RootsN {
+    Fr w[4];  // w_N^t, t < N / 2
+};
+
+template <int LOGN>
+__global__ void __launch_bounds__(256) ntt_cross_kernel(const Fr* __restrict__ in, Fr* __restrict__ out, uint64_t q, uint64_t m,
+                                                        uint64_t part, int mode, const Fr* __restrict__ tw_lo,
+                                                        const Fr* __restrict__ tw_hi, int tw_h, const Fr* __restrict__ f_lo,
+                                                        const Fr* __restrict__ f_hi, int f_h, RootsN roots, Fr scale, int has_scale) {
+    constexpr int N = 1 << LOGN;
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < q; v += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t j = part * q + v;  // k2 (mode 0) or j2 (mode 1)
+        Fr x[N];
+#pragma unroll
+        for (int a = 0; a < N; a++) fload_nc(x[a], in + a * q + v);
+#pragma unroll
+        for (int a = 0; a < N; a++) {
+            Fr t;
+            if (mode == 0) {
+                if (a) {  // w^(j1 k2), j1 k2 < N m = n
+                    table_factor(t, tw_lo, tw_hi, tw_h, (uint64_t)a * j);
+                    fmul(x[a], x[a], t);
+                }
+            } else if (f_lo) {
+                table_factor(t, f_lo, f_hi, f_h, (uint64_t)a * m + j);
+                fmul(x[a], x[a], t);
+            }
+        }
+        // N-point DIF over the parts: half sizes N/2 .. 1, outputs in bit-reversed order
+#pragma unroll
+        for (int h = N / 2; h >= 1; h >>= 1) {
+#pragma unroll
+            for (int i = 0; i < N; i++) {
+                if (i & h) continue;
+                Fr s, d;
+                fadd(s, x[i], x[i + h]);
+                fsub(d, x[i], x[i + h]);
+                const int t = (i & (h - 1)) * (N / (2 * h));
+                if (t) fmul(d, d, roots.w[t]);
+                x[i] = s;
+                x[i + h] = d;
+            }
+        }
+#pragma unroll
+        for (int pos = 0; pos < N; pos++) {
+            const int k = LOGN ? (int)(__brev((unsigned)pos) >> (32 - LOGN)) : 0;
+            Fr y = x[pos], t;
+            if (mode == 0) {
+                if (f_lo) {
+                    table_factor(t, f_lo, f_hi, f_h, (uint64_t)k * m + j);
+                    fmul(y, y, t);
+                }
+            } else if (k) {  // w^(j2 k1), j2 k1 < m N = n
+                table_factor(t, tw_lo, tw_hi, tw_h, j * (uint64_t)k);
+                fmul(y, y, t);
+            }
+            if (has_scale) fmul(y, y, scale);
+            fstore(out + (uint64_t)k * q + v, y);
+        }
+    }
+}
+
+int ntt_cross_run(int device, cudaStream_t st, void* d_out, const void* d_in, int L, int log_parts, int part, bool inverse, int mode,
+                  const void* factor_g, bool factor_inverse) {
+    if (!d_out || !d_in) { set_error("ntt_cross: null pointer"); return ZK_ERR_INVALID; }
+    if (log_parts < 0 || log_parts > 3 || 2 * log_parts > L || L > ZK_NTT_MAX_LOG || part < 0 || part >= (1 << log_parts) ||
+        mode < 0 || mode > 1) {
+        set_error("ntt_cross: log_n %d, log_parts %d, part %d, mode %d out of range", L, log_parts, part, mode);
+        return ZK_ERR_RANGE;
+    }
+    if (d_out == d_in) { set_error("ntt_cross: d_out must not alias d_in"); return ZK_ERR_INVALID; }
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const NttDirTables* T;
+    ZK_TRY(get_dir_tables(ctx, L, inverse, &T));
+    const CosetTables* F = nullptr;
+    if (factor_g) {
+        zkh::Fe g;
+        std::memcpy(g.v, factor_g, 32);
+        ZK_TRY(get_coset_tables(ctx, L, factor_inverse ? 3 : 0, g, &F));
+    }
+    const int N = 1 << log_parts;
+    const uint64_t m = 1ull << (L - log_parts), q = m >> log_parts;
+    RootsN roots;
+    const zkh::Fe w = host_root(L, inverse);
+    for (int t = 0; t < 4; t++) {
+        zkh::Fe r;
+        host_fr_pow_u64(r, w, (uint64_t)t * m);  // w_N = w^m
+        std::memcpy(roots.w[t].v, r.v, 32);
+    }
+    Fr scale{};
+    int has_scale = 0;
+    if (inverse && N > 1) {
+        scale = n_inverse_dev(log_parts);
+        has_scale = 1;
+    }
+    const unsigned grid = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>((q + 255) / 256, (uint64_t)ctx->num_sms * 8));
+    const Fr* fl = F ? F->lo : nullptr;
+    const Fr* fh = F ? F->hi : nullptr;
+    const int fhh = F ? F->h : 0;
+    switch (log_parts) {
+#define ZK_CROSS(S)                                                                                                                    \
+    case S:                                                                                                                            \
+        ntt_cross_kernel<S><<<grid, 256, 0, st>>>((const Fr*)d_in, (Fr*)d_out, q, m, (uint64_t)part, mode, T->tw_lo, T->tw_hi, T->h, \
+                                                  fl, fh, fhh, roots, scale, has_scale);                                              \
+        break;
+        ZK_CROSS(0)
+        ZK_CROSS(1)
+        ZK_CROSS(2)
+        ZK_CROSS(3)
+#undef ZK_CROSS
+    }
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
 // compute_h after the matvec (src/prover/groth16.cu:322-383)
 int compute_h_run(int device, cudaStream_t user_stream, void* d_h, const void* d_a, const void* d_b, const void* d_c, int L) {
     if (!d_h || !d_a || !d_b || !d_c) { set_error("compute_h: null pointer"); return ZK_ERR_INVALID; }
@@ -854,6 +989,13 @@ extern "C" int zk_ntt_device_noalloc(int device, void* stream, void* d_out, cons
     return ntt_noalloc_run(device, (cudaStream_t)stream, d_out, d_in, log_n, inverse != 0, coset_shift);
 }
 
+extern "C" int zk_ntt_cross_device(int device, void* stream, void* d_out, const void* d_in, int log_n, int log_parts, int part,
+                                   int inverse, int mode, const void* factor_g, int factor_inverse) {
+    clear_error();
+    return ntt_cross_run(device, (cudaStream_t)stream, d_out, d_in, log_n, log_parts, part, inverse != 0, mode, factor_g,
+                         factor_inverse != 0);
+}
+
 extern "C" int zk_compute_h_coset_shift(int log_n, void* out_g) {
     clear_error();
     if (!out_g) return ZK_ERR_INVALID;
@@ -865,17 +1007,19 @@ extern "C" int zk_compute_h_coset_shift(int log_n, void* out_g) {
 }
 
 extern "C" int zk_compute_h_pointwise_device(int device, void* stream, void* d_out, const void* d_a, const void* d_b, const void* d_c,
-                                             int log_n) {
+                                             int log_n, uint64_t count) {
     clear_error();
     if (!d_out || !d_a || !d_b || !d_c) return ZK_ERR_INVALID;
     if (log_n < 0 || log_n > ZK_NTT_MAX_LOG) { set_error("compute_h: log_n = %d out of range", log_n); return ZK_ERR_RANGE; }
+    if (count > (1ull << log_n)) { set_error("compute_h: %llu values exceed the 2^%d-point domain", (unsigned long long)count, log_n); return ZK_ERR_RANGE; }
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     zkh::Fe g, zinv;
     ZK_TRY(coset_shift(log_n, g, zinv));
     Fr zi;
     std::memcpy(zi.v, zinv.v, 32);
-    const uint64_t n = 1ull << log_n;
+    const uint64_t n = count;
+    if (n == 0) return ZK_OK;
     const unsigned grid = (unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)ctx->num_sms * 16);
     h_pointwise_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((Fr*)d_out, (const Fr*)d_a, (const Fr*)d_b, (const Fr*)d_c, n, zi);
     ZK_TRY_CUDA(cudaGetLastError());

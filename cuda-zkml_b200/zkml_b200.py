@@ -76,11 +76,13 @@ _SIGS = {
     "zk_r1cs_matvec_rows_device": [_vp, _vp, _vp, ctypes.c_uint64, ctypes.c_uint64, _vp],
     "zk_fr_hadamard_check_device": [_i, _vp, _vp, _vp, _vp, _sz, ctypes.c_uint64, ctypes.POINTER(ctypes.c_longlong)],
     "zk_compute_h_coset_shift": [_i, _vp],
-    "zk_compute_h_pointwise_device": [_i, _vp, _vp, _vp, _vp, _vp, _i],
+    "zk_compute_h_pointwise_device": [_i, _vp, _vp, _vp, _vp, _vp, _i, ctypes.c_uint64],
+    "zk_ntt_cross_device": [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i],
     "zk_groth16_pk_arrays": [_vp, ctypes.POINTER(Groth16Arrays)],
     "zk_groth16_assemble": [_vp, _vp, _vp, _vp, _vp, _vp],
     "zk_groth16_assemble_parts": [_vp, _vp, _vp, _vp, _i, _vp, _vp],
     "zk_groth16_h_msm_device": [_vp, _vp, _vp, ctypes.c_uint64, ctypes.c_uint64, _vp],
+    "zk_groth16_h_msm_blocks_device": [_vp, _vp, _vp, _i, _i, _vp],
     "zk_groth16_precompute": [_vp, _vp],
     "zk_groth16_witness_msms_device": [_vp, _vp, _vp, ctypes.c_uint64, ctypes.c_uint64, _vp],
 }
@@ -308,12 +310,31 @@ def compute_h_coset_shift(log_n):
 
 
 def compute_h_pointwise(a, b, c, log_n, out=None):
-    """(a b - c) / (g^n - 1) elementwise over coset evaluations (CUDA tensors)."""
+    """(a b - c) / (g^n - 1) elementwise over coset evaluations of the 2^log_n
+    domain (CUDA tensors: all of them, or one part's share)."""
     torch = _torch()
     if out is None:
         out = torch.empty_like(a)
     check(lib.zk_compute_h_pointwise_device(a.device.index, _stream(a), _dev_ptr(out), _dev_ptr(a), _dev_ptr(b), _dev_ptr(c),
-                                            log_n))
+                                            log_n, a.shape[0]))
+    return out
+
+
+def ntt_cross(x, log_n, log_parts, part, inverse, mode, factor=None, factor_inverse=False, out=None):
+    """One part's cross-part step of a 2^log_n-point transform split over
+    2^log_parts parts (zk_ntt_cross_device): mode 0 cyclic -> blocks (after the
+    size-m transform and the all-to-all), mode 1 blocks -> cyclic (before them).
+    factor: None or a (4,) uint64 Montgomery g, applied as g^i (g^-i with
+    factor_inverse) at global index i."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(x)
+    g = None
+    if factor is not None:
+        gc = np.ascontiguousarray(factor, dtype=np.uint64)
+        g = _np_ptr(gc)
+    check(lib.zk_ntt_cross_device(x.device.index, _stream(x), _dev_ptr(out), _dev_ptr(x), log_n, log_parts, part, int(inverse),
+                                  mode, g, int(factor_inverse)))
     return out
 
 
@@ -500,6 +521,13 @@ class ProvingKey:
         coefficients on the device); packed affine (8,) uint64."""
         out = np.zeros(8, np.uint64)
         check(lib.zk_groth16_h_msm_device(self.h, _stream(d_h), _dev_ptr(d_h), lo, hi, _np_ptr(out)))
+        return out
+
+    def h_msm_blocks(self, d_h_part, log_parts, part):
+        """This part's share of the H MSM of a proof split over 2^log_parts parts:
+        its coefficients (CUDA tensor) in the "blocks" layout of ntt_cross."""
+        out = np.zeros(8, np.uint64)
+        check(lib.zk_groth16_h_msm_blocks_device(self.h, _stream(d_h_part), _dev_ptr(d_h_part), log_parts, part, _np_ptr(out)))
         return out
 
     def assemble_parts(self, r, s, parts):

@@ -1,10 +1,17 @@
-"""Point-sharded MSM across ranks (one process per GPU, torch.distributed).
+"""Work split across ranks (one process per GPU, torch.distributed).
 
-Each rank owns a contiguous slice of the points and scalars (its proving-key
-slice stays resident on its GPU), runs the whole Pippenger pipeline locally,
-and the ranks exchange only their partial sums: one affine point per rank
-(64 B for G1, 128 B for G2) through an all-gather, which every rank then
-folds with the host point addition.  The data path carries no collective.
+MSM: each rank owns a contiguous slice of the points and scalars (its
+proving-key slice stays resident on its GPU), runs the whole Pippenger
+pipeline locally, and the ranks exchange only their partial sums: one affine
+point per rank (64 B for G1, 128 B for G2) through an all-gather, which every
+rank then folds with the host point addition.  The data path carries no
+collective.
+
+Groth16 prove (sharded_prove): rows of the matvec per rank; compute_h with
+every transform split over the ranks (a size-n/N transform on each rank, one
+all-to-all, a cross-rank step: split_compute_h); the H MSM over each rank's
+own coefficients and the witness MSMs over witness slices; the partial sums
+all-gathered and folded.
 """
 import numpy as np
 
@@ -141,6 +148,60 @@ def balance_shares(poly_s, msm_s, shares, damping=0.5, floor=0.02):
     return [float(x) for x in new]
 
 
+def split_log(world, n):
+    """log2(world) when compute_h's transforms split over the ranks (world a
+    power of two up to 8, with world^2 <= n), else None."""
+    if world < 2 or world > 8 or world & (world - 1):
+        return None
+    s = world.bit_length() - 1
+    return s if (n >> (2 * s)) > 0 else None
+
+
+def _a2a_blocks(comm, t, world):
+    """All-to-all of a (k, m, 4) stack whose rows split into `world` equal
+    chunks: chunk j of every vector goes to rank j; returns (k, m, 4) with the
+    chunks received from rank 0, 1, ... in order."""
+    k, m = t.shape[0], t.shape[1]
+    send = t.reshape(k, world, m // world, 4).permute(1, 0, 2, 3).contiguous()
+    recv = comm.all_to_all(send)
+    return recv.permute(1, 0, 2, 3).reshape(k, m, 4).contiguous()
+
+
+def _to_cyclic(comm, t, world):
+    """(k, m, 4) stack of this rank's consecutive rows [rank m, rank m + m) ->
+    the rows i = rank (mod world), in order (the split transforms' cyclic layout)."""
+    k, m = t.shape[0], t.shape[1]
+    strided = t.reshape(k, m // world, world, 4).permute(0, 2, 1, 3).contiguous()  # [k, residue, i // world]
+    return _a2a_blocks(comm, strided.reshape(k, m, 4), world)
+
+
+def split_compute_h(prover, comm, abc, s_log):
+    """compute_h (groth16.cu:263-390) with every transform split over the
+    2^s_log ranks: abc holds this rank's rows [rank m, rank m + m) of A w, B w,
+    C w (m = n / world); returns this rank's m coefficients of h in the
+    "blocks" layout (local k q + v = global k m + rank q + v, q = m / world).
+    Each transform is a size-m transform on every rank, one all-to-all, and a
+    cross-rank step (zk_ntt_cross_device); the three polynomials travel together."""
+    world, rank = comm.world, comm.rank
+    L = prover.log_n
+    g = prover.g
+    x = _to_cyclic(comm, abc, world)                                   # evaluations, cyclic
+    for k in range(3):
+        prover.local_ntt(x[k], L - s_log, inverse=True)
+    y = _a2a_blocks(comm, x, world)
+    coeffs = [prover.cross(y[k], L, s_log, rank, True, 0, g, False) for k in range(3)]    # n^-1 g^i coefficients, blocks
+    z = prover.stack([prover.cross(c, L, s_log, rank, False, 1, None, False) for c in coeffs])
+    del coeffs, y
+    ev = _a2a_blocks(comm, z, world)                                   # coset evaluations, cyclic
+    for k in range(3):
+        prover.local_ntt(ev[k], L - s_log, inverse=False)
+    q = prover.pointwise(ev[0], ev[1], ev[2])                          # (a b - c) / (g^n - 1), cyclic
+    del ev, z
+    prover.local_ntt(q, L - s_log, inverse=True)
+    qb = _a2a_blocks(comm, q.reshape((1,) + tuple(q.shape)), world)[0]
+    return prover.cross(qb, L, s_log, rank, True, 0, g, True)          # n^-1 g^-i coefficients, blocks
+
+
 def sharded_prove(prover, comm, witness, r, s, marks=None):
     """One Groth16 proof with the work of `prover` (this rank's device) shared
     over `comm`'s ranks.  witness: (m, 4) uint64 Montgomery (host); r, s ints.
@@ -170,6 +231,23 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     mark("check")
     if bad != _NO_ROW:
         raise prover.error(f"[Prove] Witness does not satisfy R1CS constraints (constraint {bad} failed)")
+    s_log = split_log(world, n)
+    if s_log is not None:
+        # every transform of compute_h split over the ranks, then the H MSM over
+        # each rank's own coefficients
+        t_poly = prover.timer()
+        h_part = split_compute_h(prover, comm, prover.stack([prover.pad_rows(abc[k], S) for k in range(3)]), s_log)
+        t_poly = prover.elapsed(t_poly)
+        del abc
+        mark("h")
+        t_msm = prover.timer()
+        a, b = weighted_bounds(m, shares, rank)
+        sums = unpack_sums(prover.witness_msms(w, a, b))
+        t_msm = prover.elapsed(t_msm)
+        mark("witness_msms")
+        sums["h"] = prover.h_msm_blocks(h_part, s_log, rank) if sizes["h"] > 0 else np.zeros(8, np.uint64)
+        mark("h_msm")
+        return _finish(prover, comm, r, s, sums, shares, t_poly, t_msm, mark)
     full = [comm.all_gather_rows(prover.pad_rows(abc[k], S), S)[:n] for k in range(3)]
     mark("gather")
     owners = [k % world for k in range(3)]
@@ -195,6 +273,12 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     a, b = shard_bounds(sizes["h"], rank, world)
     sums["h"] = prover.msm("h", a, b, h, 0)
     mark("h_msm")
+    return _finish(prover, comm, r, s, sums, shares, t_poly, t_msm, mark)
+
+
+def _finish(prover, comm, r, s, sums, shares, t_poly, t_msm, mark):
+    """All-gather the partial sums (and timings), rebalance the witness slices
+    for the next proof, assemble."""
     recs = comm.all_gather_points(pack_sums(sums, (t_poly(), t_msm())))
     parts = [unpack_sums(p) for p in recs]
     prover.witness_shares = balance_shares([p["times"][0] for p in parts], [p["times"][1] for p in parts], shares)
@@ -226,6 +310,13 @@ class TorchComm:
     def broadcast(self, t, src):
         self.dist.broadcast(t, src, group=self.group)
         return t
+
+    def all_to_all(self, t):
+        """t: (world, ...) contiguous; slice j goes to rank j; returns the
+        slices received, in rank order."""
+        out = t.new_empty(t.shape)
+        self.dist.all_to_all_single(out, t.contiguous(), group=self.group)
+        return out
 
     def all_gather_points(self, rec):
         import torch
@@ -284,6 +375,15 @@ class ThreadComm:
 
     def all_gather_points(self, rec):
         return self._exchange(np.array(rec, copy=True))
+
+    def all_to_all(self, t):
+        import torch
+        self._sync(t)
+        items = self._exchange(t)
+        out = torch.stack([x[self.rank].to(t.device) for x in items])
+        self._sync(out)  # the other ranks' buffers stay untouched until this copy is done
+        self.sh.barrier.wait()
+        return out
 
 
 class CudaProver:
@@ -373,6 +473,23 @@ class CudaProver:
 
     def witness_msms(self, w, lo, hi):
         return self.pk.witness_msms(w, lo, hi)
+
+    def stack(self, vs):
+        import torch
+        return torch.stack(list(vs))
+
+    def local_ntt(self, v, log_m, inverse):
+        """In place: this rank's size-2^log_m share of a split transform."""
+        self.Z.ntt(v, log_m, inverse=inverse, out=v)
+
+    def cross(self, v, log_n, s_log, part, inverse, mode, factor, factor_inverse):
+        return self.Z.ntt_cross(v, log_n, s_log, part, inverse, mode, factor, factor_inverse)
+
+    def pointwise(self, a, b, c):
+        return self.Z.compute_h_pointwise(a, b, c, self.log_n)
+
+    def h_msm_blocks(self, h_part, s_log, part):
+        return self.pk.h_msm_blocks(h_part, s_log, part)
 
     def msm(self, key, lo, hi, scalars, scalar_offset):
         import ctypes

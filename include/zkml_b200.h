@@ -241,10 +241,14 @@ int zk_groth16_last_stats(zk_prove_stats* out);
  * Pieces of zk_groth16_prove for a prove split across devices (one process
  * per GPU).  The reference proves on device 0 only; these entry points let a
  * host driver shard every step and get the same proof bytes:
- *   rows of the matvec and the witness check -> all-gather of A w, B w, C w
- *   -> per polynomial INTT + coset NTT (zk_ntt_device) -> broadcast
- *   -> zk_compute_h_pointwise_device + coset INTT (h) -> point-sharded MSMs
- *   over zk_groth16_pk_arrays -> fold the partial sums -> zk_groth16_assemble.
+ *   rows of the matvec and the witness check -> A w, B w, C w re-laid out
+ *   cyclically over the parts -> each transform of compute_h split over the
+ *   parts (zk_ntt_device on the part's share + one all-to-all +
+ *   zk_ntt_cross_device) -> zk_compute_h_pointwise_device on each part ->
+ *   the H MSM over each part's coefficients (zk_groth16_h_msm_blocks_device)
+ *   and the witness MSMs over witness slices -> fold the partial sums ->
+ *   zk_groth16_assemble.  (Part counts that are not powers of two: each
+ *   polynomial's INTT + coset NTT on one part, then broadcasts.)
  * zk_groth16_prove runs the witness check too: unless ZKML_SKIP_WITNESS_CHECK
  * is "1" it fails with ZK_ERR_INVALID naming the first constraint whose
  * (A w)(B w) != (C w), like Groth16Prover::prove (groth16.cu:691-697) with
@@ -262,10 +266,27 @@ int zk_fr_hadamard_check_device(int device, void* stream, const void* d_a, const
                                 const void* d_c, size_t count, uint64_t row0, long long* first_bad);
 /* compute_h's coset shift g (5, or 7 when 5^n = 1; groth16.cu:329-342). */
 int zk_compute_h_coset_shift(int log_n, void* out_g);
-/* d_out = (a b - c) / (g^n - 1) elementwise over the 2^log_n coset
- * evaluations (groth16.cu:364-371); d_out may alias an input. */
+/* d_out = (a b - c) / (g^n - 1) elementwise over `count` (<= 2^log_n) coset
+ * evaluations of the 2^log_n-point domain (groth16.cu:364-371): all of them,
+ * or one part's share; d_out may alias an input. */
 int zk_compute_h_pointwise_device(int device, void* stream, void* d_out, const void* d_a,
-                                  const void* d_b, const void* d_c, int log_n);
+                                  const void* d_b, const void* d_c, int log_n, uint64_t count);
+/* One part's step of a 2^log_n-point (I)NTT split over 2^log_parts parts
+ * (log_parts <= 3, 2 log_parts <= log_n), replacing ntt_gpu (src/ntt/ntt.cu:
+ * 354-478) inside compute_h (groth16.cu:306-383) on several GPUs.  With
+ * m = n / N, q = m / N, part p holds m values either "cyclic" (local t is
+ * global p + N t) or in "blocks" (local k q + v is global k m + p q + v).
+ * mode 0 (cyclic -> blocks, after zk_ntt_device of size m on each part's
+ * cyclic values and an all-to-all sending local [p' q, p' q + q) to part p'):
+ * d_in holds what the parts sent, in part order; d_out gets this part's
+ * blocks of the transform, times factor(global index) if factor_g is given.
+ * mode 1 (blocks -> cyclic, before the all-to-all sending local block k to
+ * part k and zk_ntt_device of size m on what each part gathered): d_in holds
+ * this part's blocks, times factor(global index) if given.  factor = g^i, or
+ * g^-i with factor_inverse; an inverse transform's N^-1 is applied here (the
+ * size-m INTT applies m^-1).  d_out must not alias d_in. */
+int zk_ntt_cross_device(int device, void* stream, void* d_out, const void* d_in, int log_n, int log_parts,
+                        int part, int inverse, int mode, const void* factor_g, int factor_inverse);
 
 /* Device-resident query arrays of a proving key (packed affine, Montgomery). */
 typedef struct {
@@ -296,6 +317,14 @@ int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, c
  * one bucket set and one reduce.  Smaller slices run the plain MSM. */
 int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const void* d_h, uint64_t lo, uint64_t hi,
                             void* out_affine);
+/* One part's share of the H MSM of a proof split over 2^log_parts parts:
+ * sum h_i H_i over the part's coefficients in the "blocks" layout of
+ * zk_ntt_cross_device (d_h_part: its n / 2^log_parts local values; global
+ * indices at or beyond n_h are skipped).  The part's H points, gathered in
+ * that order, and window tables over them are built on first use and kept
+ * with the key (one part per key). */
+int zk_groth16_h_msm_blocks_device(zk_groth16_pk* pk, void* stream, const void* d_h_part, int log_parts,
+                                   int part, void* out_affine);
 /* The MSMs of a proof whose scalars are the witness, over the witness slice
  * [lo, hi) (d_witness: all num_variables device Fr): sum w_i A_i, w_i B2_i and
  * w_i B1_i for i in the slice, and w_i L_{i - 1 - pub} for the private i in it,

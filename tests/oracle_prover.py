@@ -81,6 +81,65 @@ class OracleProver:
                       for i in range(self.n)])
         return _t(O.coset_ntt(q, self.log_n, True, self.g))
 
+    def stack(self, vs):
+        return torch.stack(list(vs))
+
+    def local_ntt(self, v, log_m, inverse):
+        v.copy_(_t(O.ntt(_np(v), log_m, inverse)))
+
+    def cross(self, v, log_n, s_log, part, inverse, mode, factor, factor_inverse):
+        """The cross-part step of a split transform as its defining sums
+        (zkml_dist.split_compute_h): the N-point DFT over the parts, written
+        directly, with the twiddles w^(j1 k2) / w^(j2 k1) and the factor."""
+        R = G.R
+        N, n = 1 << s_log, 1 << log_n
+        m = n >> s_log
+        q = m >> s_log
+        w = O.fr_to_int(O.compute_omega(log_n, inverse))
+        wN = pow(w, m, R)
+        x = [O.fr_to_int(e) for e in _np(v)]
+        g = O.fr_to_int(factor) if factor is not None else None
+        if g is not None and factor_inverse:
+            g = pow(g, -1, R)
+        ninv = pow(N, -1, R) if inverse else 1
+        out = [0] * m
+        for vv in range(q):
+            j = part * q + vv
+            xs = []
+            for a in range(N):
+                t = x[a * q + vv]
+                if mode == 0:
+                    t = t * pow(w, a * j, R) % R
+                elif g is not None:
+                    t = t * pow(g, a * m + j, R) % R
+                xs.append(t)
+            for k in range(N):
+                y = sum(xs[a] * pow(wN, a * k, R) for a in range(N)) % R
+                if mode == 0:
+                    if g is not None:
+                        y = y * pow(g, k * m + j, R) % R
+                else:
+                    y = y * pow(w, j * k, R) % R
+                out[k * q + vv] = y * ninv % R
+        return _t(np.stack([O.fr_from_int(y) for y in out]))
+
+    def pointwise(self, a, b, c):
+        a, b, c = _np(a), _np(b), _np(c)
+        return _t(np.stack([O.fr_from_int((O.fr_to_int(a[i]) * O.fr_to_int(b[i]) - O.fr_to_int(c[i])) * self.zinv % G.R)
+                            for i in range(a.shape[0])]))
+
+    def h_msm_blocks(self, h_part, s_log, part):
+        N = 1 << s_log
+        m = self.n >> s_log
+        q = m >> s_log
+        idx = [k * m + part * q + v for k in range(N) for v in range(q)]
+        sc = _np(h_part)
+        keep = [i for i, g in enumerate(idx) if g < self.n_h]
+        if not keep:
+            return np.zeros(8, np.uint64)
+        pts = np.stack([self.pk["H"][idx[i]] for i in keep])
+        return O.msm_g1(pts, sc[keep])
+
     def msm(self, key, lo, hi, scalars, off):
         pts = self.pk[_KEYS[key]][lo:hi]
         words = 16 if key == "b2" else 8

@@ -59,7 +59,7 @@ def _worker(rank, world, port, corrupt, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_sharded_prove_matches_one_device(tmp_path, world):
     import groth16_oracle as G
     mp.spawn(_worker, args=(world, _free_port(), None, str(tmp_path)), nprocs=world, join=True)
@@ -122,3 +122,55 @@ def test_balance_shares_moves_work_off_polynomial_owners():
         s = D.balance_shares([2.9] * 3 + [0.0] * 5, [7.7 * x for x in s], s)
     assert max(s[:3]) < 0.01 and abs(sum(s) - 1) < 1e-9
     assert D.balance_shares([0.0], [1.0], [1.0]) == [1.0]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_split_compute_h_matches_one_device(world):
+    """compute_h with every transform split over `world` thread ranks (cyclic
+    re-layout, size-m transforms, all-to-alls, cross-rank steps) gives the
+    one-device coefficients of h, each rank holding its blocks."""
+    import threading
+
+    import torch
+
+    import groth16_oracle as G
+    import pyoracle as O
+    import zkml_dist as D
+    from oracle_prover import OracleProver
+
+    L = 8
+    n = 1 << L
+    rng = O.Rng(40 + world)
+    abc = np.stack([rng.fr_vector(n) for _ in range(3)])
+    exp = O.compute_h_from_evals(abc[0], abc[1], abc[2], L)
+    pk = {"n": n, "log_n": L, "m": 1, "num_public": 0, "l": 0}
+    s_log = D.split_log(world, n)
+    assert s_log == world.bit_length() - 1
+    m, q = n // world, n // world // world
+    shared = D.ThreadComm.Shared(world, timeout=60)
+    got, errs = [None] * world, []
+
+    def run(rank):
+        try:
+            comm = D.ThreadComm(shared, rank)
+            t = torch.from_numpy(abc[:, rank * m:(rank + 1) * m].copy().view(np.int64))
+            got[rank] = D.split_compute_h(OracleProver(pk, []), comm, t, s_log).numpy().view(np.uint64)
+        except Exception as e:  # surfaced below
+            errs.append(e)
+            shared.barrier.abort()
+
+    ts = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errs, errs
+    for rank in range(world):
+        idx = [k * m + rank * q + v for k in range(world) for v in range(q)]
+        assert np.array_equal(got[rank], exp[idx]), rank
+
+
+def test_split_log():
+    import zkml_dist as D
+    assert D.split_log(1, 1 << 10) is None and D.split_log(3, 1 << 10) is None and D.split_log(16, 1 << 20) is None
+    assert D.split_log(2, 4) == 1 and D.split_log(2, 2) is None and D.split_log(8, 1 << 6) == 3 and D.split_log(8, 1 << 5) is None

@@ -145,3 +145,28 @@ def test_prove_2_16_config4_shape():
                                            ctypes.c_void_p(d_h.data_ptr() + lo * 32), hi - lo, exp.ctypes.data_as(ctypes.c_void_p)))
         assert np.array_equal(got, exp), (lo, hi)
     torch.cuda.synchronize()
+
+
+def test_h_msm_blocks_sum_to_the_whole_query():
+    """The per-part H MSMs of a split proof (each part's coefficients in the
+    blocks layout, over its gathered H points: window tables from 2^16 points
+    per part, the plain MSM below) add up to the H MSM over the whole query."""
+    import torch
+    c = Z.synth_conv_circuit(2, 4, 16, 16, 24, 10, 23, 10, 6)
+    r1 = Z.R1cs(c)
+    assert r1.log_n == 17
+    pk = Z.ProvingKey.setup(r1, G.toxic_deterministic())
+    n = 1 << r1.log_n
+    d_h = Z.to_device(Z.random_fr(n, 78))
+    d_h[11] = 0
+    whole = pk.h_msm(d_h, 0, n)
+    for s_log in (1, 3):
+        N = 1 << s_log
+        m, q = n // N, n // N // N
+        acc = np.zeros(8, np.uint64)
+        for part in range(N):
+            idx = torch.tensor([k * m + part * q + v for k in range(N) for v in range(q)], device=d_h.device)
+            got = pk.h_msm_blocks(d_h[idx].contiguous(), s_log, part)
+            acc = Z.g1_add_affine(acc, got)
+        assert np.array_equal(acc, whole), s_log
+    torch.cuda.synchronize()

@@ -98,3 +98,35 @@ def test_compute_h_satisfied_divides_at_2_16():
     rhs_i = O.fr_to_int(O.fr_poly_eval(h, tau)) * (pow(O.fr_to_int(tau), n, O.R) - 1) % O.R
     assert lhs_i == rhs_i
     assert not h[n - 1].any()
+
+
+@pytest.mark.parametrize("s_log", [0, 1, 2, 3])
+def test_ntt_cross_matches_oracle(s_log):
+    """The cross-part step of a transform split over 2^s_log parts
+    (zk_ntt_cross_device) against the oracle's direct sums, every mode,
+    direction and factor, first and last part."""
+    from oracle_prover import OracleProver
+    L = 10
+    n = 1 << L
+    m = n >> s_log
+    orc = OracleProver({"n": n, "log_n": L, "m": 1, "num_public": 0, "l": 0}, [])
+    x = O.Rng(70 + s_log).fr_vector(m)
+    g = O.fr_from_int(5)
+    for part in sorted({0, (1 << s_log) - 1}):
+        for mode in (0, 1):
+            for inverse in (False, True):
+                for factor, finv in ((None, False), (g, False), (g, True)):
+                    got = Z.to_host(Z.ntt_cross(dev(x), L, s_log, part, inverse, mode, factor, finv))
+                    exp = orc.cross(torch.from_numpy(x.view(np.int64).copy()), L, s_log, part, inverse, mode, factor,
+                                    finv).numpy().view(np.uint64)
+                    assert np.array_equal(got, exp), (part, mode, inverse, factor is not None, finv)
+
+
+def test_ntt_cross_refuses_bad_arguments():
+    x = dev(O.Rng(9).fr_vector(256))
+    for args in ((8, 4, 0, 0), (8, 5, 0, 0), (8, 2, 4, 0), (8, 2, 0, 2), (8, -1, 0, 0)):
+        L, s_log, part, mode = args
+        with pytest.raises(Z.ZkError):
+            Z.ntt_cross(x, L, s_log, part, False, mode)
+    with pytest.raises(Z.ZkError):
+        Z.ntt_cross(x, 8, 1, 0, False, 0, out=x)  # in place is refused
