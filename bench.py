@@ -235,8 +235,12 @@ def bench_prove_sharded(Z, args, dev, world, rank):
             "nnz": [len(c["A"]), len(c["B"]), len(c["C"])], "log_n": r1.log_n,
             "prove_ms": 1e3 * statistics.median(times), "prove_ms_min": 1e3 * min(times), "steps": args.prove_steps,
             "setup_s": setup_s, "n_gpus": world, "proof_equals_one_device": bool(flag.item()),
-            "parallelism": "matvec rows + witness check sharded, A/B/C polynomials task-parallel, coset "
-                           "evaluations broadcast, every MSM point-sharded, partial sums all-gathered",
+            "parallelism": ("matvec rows + witness check sharded, every compute_h transform split over the ranks "
+                            "(size-n/N NTT + one NCCL all-to-all + cross-rank N-point step), H MSM over each rank's "
+                            "coefficients, witness MSMs over witness slices, partial sums all-gathered")
+            if D.split_log(world, 1 << r1.log_n) is not None else
+            ("matvec rows + witness check sharded, A/B/C polynomials task-parallel, coset "
+             "evaluations broadcast, every MSM point-sharded, partial sums all-gathered"),
             "timed": "host witness in -> 256-byte proof out on every rank; max over ranks of CUDA-event time"}
 
 

@@ -729,6 +729,7 @@ static int witness_msms(zk_groth16_pk* pk, DeviceContext* ctx, cudaStream_t st, 
                                (uint32_t)(has_l ? l_hi - lo : 0)};
     std::memset(l, 0, 64);
     uint64_t* outs[4] = {a, b, b1, l};
+    ZK_TRY_CUDA(cudaSetDevice(ctx->device));  // the events below belong to the context's device
     ScopedEvent s0, s1;
     ZK_TRY_CUDA(cudaEventCreate(&s0.e));
     ZK_TRY_CUDA(cudaEventCreate(&s1.e));
@@ -737,6 +738,13 @@ static int witness_msms(zk_groth16_pk* pk, DeviceContext* ctx, cudaStream_t st, 
     ZK_TRY_CUDA(cudaEventRecord(s1.e, st));
     ZK_TRY_CUDA(cudaEventSynchronize(s1.e));
     cudaEventElapsedTime(all_ms, s0.e, s1.e);
+    return ZK_OK;
+}
+
+// The key's private device context of the witness MSMs (created on first use).
+static int ensure_witness_context(zk_groth16_pk* pk) {
+    std::lock_guard<std::mutex> lock(pk->h_mu);
+    if (!pk->wctx) ZK_TRY(create_context(pk->device, &pk->wctx));
     return ZK_OK;
 }
 
@@ -755,7 +763,7 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     const uint64_t n = R.n;
     const int m = R.m, pub = R.num_public;
     ZK_TRY(ensure_prover_buffers(pk, n, m));
-    if (!pk->wctx) ZK_TRY(create_context(pk->device, &pk->wctx));
+    ZK_TRY(ensure_witness_context(pk));
     ScopedEvent evs[5];
     for (auto& e : evs) ZK_TRY_CUDA(cudaEventCreate(&e.e));
     cudaEvent_t ev[5] = {evs[0].e, evs[1].e, evs[2].e, evs[3].e, evs[4].e};
@@ -783,6 +791,12 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     DeviceContext* wctx = pk->wctx;
     ZK_TRY_CUDA(cudaStreamWaitEvent(wctx->stream, ev[4], 0));
     worker.t = std::thread([&, wctx]() {
+        // a new thread starts on device 0: everything it creates must live on the key's device
+        if (cudaSetDevice(wctx->device) != cudaSuccess) {
+            wit_rc = ZK_ERR_CUDA;
+            wit_err = std::string("witness MSMs: cudaSetDevice: ") + cudaGetErrorString(cudaGetLastError());
+            return;
+        }
         wit_rc = witness_msms(pk, wctx, wctx->stream, pk->w, 0, (size_t)m, a_msm, b_msm, b1_msm, l_msm, set_ms, &wit_all);
         if (wit_rc != ZK_OK) wit_err = zk_last_error();
     });
@@ -1354,7 +1368,9 @@ extern "C" int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, c
     if (!pk || !sums || (hi > lo && !d_witness)) return ZK_ERR_INVALID;
     DeviceContext* ctx;
     ZK_TRY(get_context(pk->device, &ctx));
+    ZK_TRY(ensure_witness_context(pk));
     uint64_t* q = (uint64_t*)sums;  // A (8) | B2 (16) | L (8) | H (8, untouched) | B1 (8) words
     float set_ms[4], all = 0;
-    return witness_msms(pk, ctx, (cudaStream_t)stream, (const Fr*)d_witness, lo, hi, q, q + 8, q + 40, q + 24, set_ms, &all);
+    return witness_msms(pk, pk->wctx, (cudaStream_t)stream, (const Fr*)d_witness, lo, hi, q, q + 8, q + 40, q + 24, set_ms,
+                        &all);
 }

@@ -234,19 +234,22 @@ def sharded_prove(prover, comm, witness, r, s, marks=None):
     s_log = split_log(world, n)
     if s_log is not None:
         # every transform of compute_h split over the ranks, then the H MSM over
-        # each rank's own coefficients
+        # each rank's own coefficients; the witness MSMs need only the witness and
+        # run beside them (their bucket fixups and reductions are chains of
+        # dependent additions that leave most of the device idle)
+        a, b = weighted_bounds(m, shares, rank)
+        side = prover.start_witness_msms(w, a, b, overlap=marks is None)
         t_poly = prover.timer()
         h_part = split_compute_h(prover, comm, prover.stack([prover.pad_rows(abc[k], S) for k in range(3)]), s_log)
         t_poly = prover.elapsed(t_poly)
         del abc
         mark("h")
-        t_msm = prover.timer()
-        a, b = weighted_bounds(m, shares, rank)
-        sums = unpack_sums(prover.witness_msms(w, a, b))
-        t_msm = prover.elapsed(t_msm)
-        mark("witness_msms")
-        sums["h"] = prover.h_msm_blocks(h_part, s_log, rank) if sizes["h"] > 0 else np.zeros(8, np.uint64)
+        h_sum = prover.h_msm_blocks(h_part, s_log, rank) if sizes["h"] > 0 else np.zeros(8, np.uint64)
         mark("h_msm")
+        rec, t_msm = side()
+        sums = unpack_sums(rec)
+        sums["h"] = h_sum
+        mark("witness_msms")
         return _finish(prover, comm, r, s, sums, shares, t_poly, t_msm, mark)
     full = [comm.all_gather_rows(prover.pad_rows(abc[k], S), S)[:n] for k in range(3)]
     mark("gather")
@@ -473,6 +476,48 @@ class CudaProver:
 
     def witness_msms(self, w, lo, hi):
         return self.pk.witness_msms(w, lo, hi)
+
+    def start_witness_msms(self, w, lo, hi, overlap=True):
+        """The witness MSMs over [lo, hi) from a host thread on a side stream
+        (ordered after the work already queued for w), beside the caller's
+        work on its own stream; returns a callable giving (sums record, device
+        seconds) once they are done.  overlap=False runs them here and now."""
+        import threading
+
+        import torch
+        if not overlap:
+            t = self.timer()
+            rec = self.witness_msms(w, lo, hi)
+            el = self.elapsed(t)
+            return lambda: (rec, el)
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        ready = torch.cuda.Event()
+        ready.record()
+        box = {}
+
+        def body():
+            try:
+                torch.cuda.set_device(self.device)
+                with torch.cuda.stream(self._side):
+                    self._side.wait_event(ready)
+                    t = self.timer()
+                    box["rec"] = self.witness_msms(w, lo, hi)
+                    box["el"] = self.elapsed(t)
+            except BaseException as e:  # re-raised by the caller
+                box["err"] = e
+
+        th = threading.Thread(target=body)
+        th.start()
+
+        def finish():
+            th.join()
+            if "err" in box:
+                raise box["err"]
+            torch.cuda.current_stream(self.device).wait_stream(self._side)
+            w.record_stream(self._side)
+            return box["rec"], box["el"]
+        return finish
 
     def stack(self, vs):
         import torch

@@ -329,7 +329,10 @@ int zk_groth16_h_msm_blocks_device(zk_groth16_pk* pk, void* stream, const void* 
  * [lo, hi) (d_witness: all num_variables device Fr): sum w_i A_i, w_i B2_i and
  * w_i B1_i for i in the slice, and w_i L_{i - 1 - pub} for the private i in it,
  * with one shared counting sort.  Writes A, B2, L and B1 into a 384-byte sums
- * record (the layout of zk_groth16_assemble; H is left untouched). */
+ * record (the layout of zk_groth16_assemble; H is left untouched).  Runs in
+ * the key's private device context (its own scratch and lock), so a host
+ * thread may run it on its own stream while another runs the transforms and
+ * MSMs of the device's shared context; calls on one key run one at a time. */
 int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, const void* d_witness, uint64_t lo,
                                    uint64_t hi, void* sums);
 /* Build the key's precomputed tables now instead of at the first proof. */

@@ -159,6 +159,10 @@ class OracleProver:
         sums["l"] = self.msm("l", l_lo - 1 - pub, l_hi - 1 - pub, w, 1 + pub) if l_hi > l_lo else np.zeros(8, np.uint64)
         return D.pack_sums(sums)
 
+    def start_witness_msms(self, w, lo, hi, overlap=True):
+        rec = self.witness_msms(w, lo, hi)
+        return lambda: (rec, lambda: 0.0)
+
     def add_g1(self, a, b):
         one = O.fr_from_int(1)
         return O.msm_g1_naive(np.stack([a, b]), np.stack([one, one]))

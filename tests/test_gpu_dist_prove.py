@@ -156,6 +156,8 @@ def _nccl_worker(rank, world, port, out_dir):
         r, s = G.blinding_deterministic()
         proof = D.sharded_prove(D.CudaProver(pk, r1), D.TorchComm(), c["witness"], r, s)[0]
         open(os.path.join(out_dir, f"proof{rank}.bin"), "wb").write(proof)
+        # the one-device prove on this rank's own GPU (device 1 for rank 1)
+        open(os.path.join(out_dir, f"single{rank}.bin"), "wb").write(pk.prove(r1, c["witness"], r, s)[0])
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -168,3 +170,4 @@ def test_nccl_ranks_match_one_device(key, tmp_path):
     mp.spawn(_nccl_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     for rank in range(2):
         assert open(tmp_path / f"proof{rank}.bin", "rb").read() == proof[0], rank
+        assert open(tmp_path / f"single{rank}.bin", "rb").read() == proof[0], rank
