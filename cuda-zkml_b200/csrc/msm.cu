@@ -1108,9 +1108,10 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
         ZK_TRY(msm_sort_phase<Cv>(ctx, as, d_sc + off[k], nk[k], Pb[k], S[k], lc));
         ZK_TRY_CUDA(cudaEventRecord(ev[3 * k + 2], as));
     }
+    // empty buckets must read as the identity (all-zero XYZZ) for the merge;
+    // cleared while the work stream still waits for the first batch
+    for (int k = 0; k < kBatches; k++) ZK_TRY_CUDA(cudaMemsetAsync(buckets[k], 0, bucket_bytes, st));
     for (int k = 0; k < kBatches; k++) {  // accumulates, on the work stream
-        // empty buckets must read as the identity (all-zero XYZZ) for the merge
-        ZK_TRY_CUDA(cudaMemsetAsync(buckets[k], 0, bucket_bytes, st));
         ZK_TRY_CUDA(cudaStreamWaitEvent(st, ev[3 * k + 2], 0));
         ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, d_pts + off[k] * Cv::kAffineBytes, Pb[k], S[k], buckets[k], ev[3 * k + 1], lc));
         ZK_TRY_CUDA(cudaMemcpyAsync(keys_total + k, S[k].offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
