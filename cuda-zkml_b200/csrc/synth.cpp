@@ -242,6 +242,149 @@ extern "C" int zk_synth_conv_circuit(int layers, int channels, int height, int w
     return ZK_OK;
 }
 
+// A quantised MLP statement (statement v2 with fixed weights and a context
+// binding, src/prover/statement_v2.cuh:98-240): `batch` samples of
+// n_in -> n_hidden (LINEAR, then RELU_EXACT with `bits` and `shift`) -> n_out
+// (LINEAR), one seeded int8 model for all samples, inputs in 0..16.  Public, in
+// order: the batch x n_out outputs, the model tag, the context (when `context`),
+// the batch x n_in inputs.  Rows: the tag, the context binding ctx * ctx = ctx^2
+// (add_context_binding, gadgets.cuh:152-158), then per sample the linear rows,
+// each hidden neuron's ReLU and rescale rows, the output rows and the
+// output-equality rows.  Batch 4 of 64 -> 32 -> 10 with bits 24, shift 6 gives
+// 7,762 constraints, 7,764 variables and 298 public, the counts of the
+// reference's own statement for that model.
+extern "C" int zk_synth_mlp_circuit(int batch, int n_in, int n_hidden, int n_out, int bits, int shift, int context, uint64_t seed,
+                                    zk_synth_circuit* out) {
+    if (!out || batch < 1 || n_in < 1 || n_hidden < 1 || n_out < 1 || bits < 2 || bits > 60 || shift < 0 || shift > 60)
+        return ZK_ERR_INVALID;
+    std::memset(out, 0, sizeof *out);
+    std::mt19937_64 rng(seed);
+    auto i8 = [&]() { return (int64_t)(rng() % 255) - 127; };
+    std::vector<int64_t> W1((size_t)n_hidden * n_in), b1(n_hidden), W2((size_t)n_out * n_hidden), b2(n_out);
+    for (auto& w : W1) w = i8();
+    for (auto& b : b1) b = i8();
+    for (auto& w : W2) w = i8();
+    for (auto& b : b2) b = i8();
+    Builder B;
+    const int outs = 1, tag = outs + batch * n_out, ctx = tag + 1, ins = ctx + (context ? 1 : 0);
+    const int num_public = batch * n_out + 1 + (context ? 1 : 0) + batch * n_in;
+    B.wit.assign((size_t)1 + num_public, 0);
+    B.wit[0] = 1;
+    const int64_t tag_value = (int64_t)(rng() >> 2);
+    B.wit[(size_t)tag] = tag_value;
+    int row = B.rows++;
+    B.put(0, row, 0, tag_value);
+    B.put(1, row, 0, 1);
+    B.put(2, row, tag, 1);
+    if (context) {
+        const int64_t c = (int64_t)(rng() >> 33);  // c^2 stays an exact int64
+        B.wit[(size_t)ctx] = c;
+        const int sq = B.var(c * c);
+        row = B.rows++;
+        B.put(0, row, ctx, 1);
+        B.put(1, row, ctx, 1);
+        B.put(2, row, sq, 1);
+    }
+    for (int i = 0; i < batch * n_in; i++) B.wit[(size_t)(ins + i)] = (int64_t)(rng() % 17);
+    const int64_t half = (int64_t)1 << (bits - 1);
+    auto range_bits = [&](int v, int64_t offset, int k) -> int {
+        const uint64_t t = (uint64_t)(B.wit[(size_t)v] + offset);
+        int first = -1;
+        for (int i = 0; i < k; i++) {
+            const int bv = B.var((int64_t)((t >> i) & 1));
+            if (i == 0) first = bv;
+            const int r = B.rows++;
+            B.put(0, r, bv, 1);
+            B.put(1, r, bv, 1);
+            B.put(1, r, 0, -1);
+        }
+        const int r = B.rows++;
+        for (int i = 0; i < k; i++) B.put(0, r, first + i, (int64_t)1 << i);
+        B.put(0, r, v, -1);
+        if (offset) B.put(0, r, 0, -offset);
+        B.put(1, r, 0, 1);
+        return first;
+    };
+    // y = W x + b, one row per output (add_fixed_linear; zero weights skipped, the bias kept)
+    auto linear = [&](const std::vector<int>& x, const std::vector<int64_t>& W, const std::vector<int64_t>& bias, int n_o) {
+        std::vector<int> y(n_o);
+        for (int o = 0; o < n_o; o++) {
+            const int r = B.rows++;
+            int64_t acc = bias[o];
+            for (size_t j = 0; j < x.size(); j++) {
+                const int64_t w = W[(size_t)o * x.size() + j];
+                if (!w) continue;
+                B.put(0, r, x[j], w);
+                acc += w * B.wit[(size_t)x[j]];
+            }
+            B.put(0, r, 0, bias[o]);
+            B.put(1, r, 0, 1);
+            y[o] = B.var(acc);
+            B.put(2, r, y[o], 1);
+        }
+        return y;
+    };
+    for (int b = 0; b < batch; b++) {
+        std::vector<int> x(n_in);
+        for (int i = 0; i < n_in; i++) x[i] = ins + b * n_in + i;
+        std::vector<int> h = linear(x, W1, b1, n_hidden);
+        for (auto& z : h) {
+            const int64_t a = B.wit[(size_t)z];
+            if (a < -half || a >= half) return ZK_ERR_INVALID;  // outside the ReLU's range
+            const int s = range_bits(z, half, bits) + bits - 1;
+            const int yv = B.var(B.wit[(size_t)s] * a);
+            row = B.rows++;
+            B.put(0, row, s, 1);
+            B.put(1, row, z, 1);
+            B.put(2, row, yv, 1);
+            if (shift == 0) {
+                z = yv;
+                continue;
+            }
+            const int64_t y = B.wit[(size_t)yv];
+            const int64_t q = y >> shift, r = y - (q << shift);
+            if (q < -half || q >= half) return ZK_ERR_INVALID;
+            const int qv = B.var(q), rv = B.var(r);
+            range_bits(rv, 0, shift);
+            range_bits(qv, half, bits);
+            row = B.rows++;
+            B.put(0, row, qv, (int64_t)1 << shift);
+            B.put(0, row, rv, 1);
+            B.put(0, row, yv, -1);
+            B.put(1, row, 0, 1);
+            z = qv;
+        }
+        std::vector<int> y = linear(h, W2, b2, n_out);
+        for (int o = 0; o < n_out; o++) {
+            const int pv = outs + b * n_out + o;
+            B.wit[(size_t)pv] = B.wit[(size_t)y[o]];
+            row = B.rows++;
+            B.put(0, row, pv, 1);
+            B.put(0, row, y[o], -1);
+            B.put(1, row, 0, 1);
+        }
+    }
+    const size_t m = B.wit.size();
+    zkh::Fe* w = (zkh::Fe*)std::malloc(m * 32);
+    if (!w) return ZK_ERR_NOMEM;
+    for (size_t i = 0; i < m; i++) w[i] = B.fr_of(B.wit[i]);
+    for (int kk = 0; kk < 3; kk++) {
+        out->nnz[kk] = B.m[kk].size();
+        out->entries[kk] = std::malloc(std::max<size_t>(1, B.m[kk].size()) * sizeof(Entry));
+        if (!out->entries[kk]) {
+            std::free(w);
+            zk_synth_free(out);
+            return ZK_ERR_NOMEM;
+        }
+        std::memcpy(out->entries[kk], B.m[kk].data(), B.m[kk].size() * sizeof(Entry));
+    }
+    out->witness = w;
+    out->num_constraints = B.rows;
+    out->num_variables = (int)m;
+    out->num_public = num_public;
+    return ZK_OK;
+}
+
 extern "C" void zk_synth_free(zk_synth_circuit* c) {
     if (!c) return;
     for (int k = 0; k < 3; k++) std::free(c->entries[k]);

@@ -388,6 +388,8 @@ class ProveStats(ctypes.Structure):
 
 lib.zk_synth_conv_circuit.argtypes = [_i, _i, _i, _i, _i, _i, _i, _i, ctypes.c_uint64, ctypes.POINTER(_Synth)]
 lib.zk_synth_conv_circuit.restype = _i
+lib.zk_synth_mlp_circuit.argtypes = [_i, _i, _i, _i, _i, _i, _i, ctypes.c_uint64, ctypes.POINTER(_Synth)]
+lib.zk_synth_mlp_circuit.restype = _i
 lib.zk_synth_free.argtypes = [ctypes.POINTER(_Synth)]
 lib.zk_synth_free.restype = None
 lib.zk_r1cs_create.argtypes = [_i, _i, _i, _i, _vp, _sz, _vp, _sz, _vp, _sz, ctypes.POINTER(_vp)]
@@ -410,6 +412,18 @@ def synth_conv_circuit(layers=2, channels=32, height=32, width=32, bits=24, shif
     """Seeded CONV/ReLU R1CS with a satisfying witness (host numpy copies)."""
     c = _Synth()
     check(lib.zk_synth_conv_circuit(layers, channels, height, width, bits, shift, out_bits, dense, seed, ctypes.byref(c)))
+    return _synth_copy(c)
+
+
+def synth_mlp_circuit(batch=4, n_in=64, n_hidden=32, n_out=10, bits=24, shift=6, context=True, seed=1):
+    """Seeded MLP statement (LINEAR, RELU_EXACT, LINEAR over a batch, context-bound)
+    with a satisfying witness (host numpy copies)."""
+    c = _Synth()
+    check(lib.zk_synth_mlp_circuit(batch, n_in, n_hidden, n_out, bits, shift, int(context), seed, ctypes.byref(c)))
+    return _synth_copy(c)
+
+
+def _synth_copy(c):
     try:
         mats = []
         for k in range(3):

@@ -370,6 +370,15 @@ typedef struct {
  * ZK_ERR_INVALID when a value leaves its layer's range. */
 int zk_synth_conv_circuit(int layers, int channels, int height, int width, int bits, int shift,
                           int out_bits, int dense_outputs, uint64_t seed, zk_synth_circuit* out);
+/* A quantised MLP statement: `batch` samples of n_in -> n_hidden (LINEAR +
+ * RELU_EXACT with `bits`, `shift`, the gadgets above) -> n_out (LINEAR), one
+ * seeded int8 model, inputs 0..16; public: the outputs, a model tag, the
+ * context when `context` (bound by ctx * ctx = ctx^2, src/prover/gadgets.cuh:
+ * 152-158) and the inputs.  Batch 4 of 64 -> 32 -> 10, bits 24, shift 6 has
+ * the reference statement's counts for that model: 7,762 constraints, 7,764
+ * variables, 298 public.  ZK_ERR_INVALID when a value leaves its range. */
+int zk_synth_mlp_circuit(int batch, int n_in, int n_hidden, int n_out, int bits, int shift, int context,
+                         uint64_t seed, zk_synth_circuit* out);
 void zk_synth_free(zk_synth_circuit* c);
 
 #ifdef __cplusplus

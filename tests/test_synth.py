@@ -76,3 +76,42 @@ def test_config5_shape_matches_the_reference_statement():
     assert len(c["B"]) == 7_864_341 and len(c["C"]) == 131_083
     assert abs(len(c["A"]) - 26_480_000) < 0.005 * 26_480_000
     assert c["num_constraints"] <= 1 << 22 < 2 * c["num_constraints"]
+
+
+def _mlp_rows(batch, n_in, n_hidden, n_out, bits, shift, context):
+    per_neuron = 1 + (bits + 2) + ((shift + 1) + (bits + 1) + 1 if shift else 0)
+    return 1 + (1 if context else 0) + batch * (n_hidden * per_neuron + 2 * n_out)
+
+
+@pytest.mark.parametrize("args", [(4, 64, 32, 10, 24, 6, True, 1), (1, 8, 5, 3, 20, 4, False, 2), (2, 6, 4, 2, 24, 0, True, 3)])
+def test_mlp_statements_are_satisfied(args):
+    batch, n_in, n_hidden, n_out, bits, shift, context, seed = args
+    c = Z.synth_mlp_circuit(*args)
+    assert c["num_public"] == batch * n_out + 1 + (1 if context else 0) + batch * n_in
+    assert c["num_constraints"] == _mlp_rows(*args[:7])
+    n = 1 << max(1, (c["num_constraints"] - 1).bit_length())
+    assert G.first_failing_constraint([c[k] for k in "ABC"], G._ints(c["witness"]), c["num_constraints"], n,
+                                      c["num_variables"]) == -1
+
+
+def test_mlp_config1_matches_the_reference_statement():
+    # the reference's statement v2 for the config-1 model (batch 4 of 64 -> 32 RELU_EXACT
+    # (bits 24, shift 6) -> 10, context-bound): 7,762 constraints, 7,764 variables,
+    # 298 public (40 outputs, the model tag, the context, 256 inputs), domain 2^13
+    c = Z.synth_mlp_circuit(4, 64, 32, 10, 24, 6, True, 1)
+    assert (c["num_constraints"], c["num_variables"], c["num_public"]) == (7762, 7764, 298)
+    assert 1 << 12 < c["num_constraints"] <= 1 << 13
+    mats = [c[k] for k in "ABC"]
+    n = 1 << 13
+    # the context (public index 1 + 40 + 1) appears only in its binding row, row 1;
+    # sample 0's first output only in its equality row, after the tag and context
+    # rows and that sample's 32 x 60 hidden and 10 output rows
+    for var, row in ((42, 1), (1, 2 + 32 * 60 + 10)):
+        w = G._ints(c["witness"])
+        w[var] = (w[var] + 1) % G.R
+        assert G.first_failing_constraint(mats, w, c["num_constraints"], n, c["num_variables"]) == row, var
+
+
+def test_mlp_out_of_range_is_refused():
+    with pytest.raises(Exception):
+        Z.synth_mlp_circuit(1, 64, 4, 2, 8, 2, False, 1)
