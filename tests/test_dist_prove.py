@@ -23,12 +23,14 @@ def _free_port():
     return p
 
 
-def _circuit():
+def _circuit(kind="conv"):
     import zkml_b200 as Z
+    if kind == "mlp":  # config 1's statement (7,762 constraints, domain 2^13)
+        return Z.synth_mlp_circuit()
     return Z.synth_conv_circuit(*CIRCUIT)
 
 
-def _worker(rank, world, port, corrupt, out_dir):
+def _worker(rank, world, port, corrupt, out_dir, kind="conv"):
     import sys
     for sub in ("oracle", "cuda-zkml_b200", "tests"):
         sys.path.insert(0, os.path.join(ROOT, sub))
@@ -42,7 +44,7 @@ def _worker(rank, world, port, corrupt, out_dir):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        c = _circuit()
+        c = _circuit(kind)
         mats = [c["A"], c["B"], c["C"]]
         pk = G.setup(mats, c["num_constraints"], c["num_variables"], c["num_public"], G.toxic_deterministic())
         w = np.array(c["witness"], copy=True)
@@ -69,6 +71,26 @@ def test_sharded_prove_matches_one_device(tmp_path, world):
     r, s = G.blinding_deterministic()
     exp = G.prove(pk, mats, c["witness"], r, s)[0]
     for rank in range(world):
+        assert open(tmp_path / f"proof{rank}.bin", "rb").read() == exp, rank
+
+
+def test_sharded_prove_mlp_statement(tmp_path):
+    """Config 1's MLP statement split over two gloo ranks (the split transforms at
+    n = 2^13) proves to the one-device oracle proof, which verifies with the
+    toxic waste known."""
+    import groth16_oracle as G
+    mp.spawn(_worker, args=(2, _free_port(), None, str(tmp_path), "mlp"), nprocs=2, join=True)
+    c = _circuit("mlp")
+    mats = [c["A"], c["B"], c["C"]]
+    tox = G.toxic_deterministic()
+    pk = G.setup(mats, c["num_constraints"], c["num_variables"], c["num_public"], tox)
+    r, s = G.blinding_deterministic()
+    exp, A, B, C, h = G.prove(pk, mats, c["witness"], r, s)
+    n, log_n = G.domain(c["num_constraints"])
+    at, vanish = G.qap_at_tau(mats, n, log_n, c["num_variables"], tox[0])
+    pk_o = {"m": c["num_variables"], "num_public": c["num_public"], "_at": at, "_vanish": vanish, "_toxic": tox}
+    assert G.trapdoor_verify(pk_o, c["witness"], r, s, h, A, B, C)
+    for rank in range(2):
         assert open(tmp_path / f"proof{rank}.bin", "rb").read() == exp, rank
 
 
