@@ -75,6 +75,28 @@ def test_compute_calls_fail_without_device():
     assert e.value.status == Z.ZK_ERR_NODEV
 
 
+def test_split_transform_and_pointwise_arguments_checked_first():
+    """zk_ntt_cross_device and zk_compute_h_pointwise_device refuse bad shapes
+    before they look for a device: ZK_ERR_RANGE / ZK_ERR_INVALID here, and
+    ZK_ERR_NODEV (no CPU fallback) for valid shapes when no GPU is visible."""
+    import ctypes
+    buf = (ctypes.c_uint8 * 64)()
+    other = (ctypes.c_uint8 * 64)()
+    p, q = ctypes.cast(buf, ctypes.c_void_p), ctypes.cast(other, ctypes.c_void_p)
+    cross = Z.lib.zk_ntt_cross_device
+    for log_n, s_log, part, mode in ((8, 4, 0, 0), (8, 5, 0, 0), (8, 2, 4, 0), (8, 2, 0, 2), (8, -1, 0, 0), (3, 2, 0, 0)):
+        assert cross(0, None, p, q, log_n, s_log, part, 0, mode, None, 0) == Z.ZK_ERR_RANGE, (log_n, s_log, part, mode)
+    assert cross(0, None, p, p, 8, 1, 0, 0, 0, None, 0) == Z.ZK_ERR_INVALID  # in place
+    assert cross(0, None, None, q, 8, 1, 0, 0, 0, None, 0) == Z.ZK_ERR_INVALID
+    pw = Z.lib.zk_compute_h_pointwise_device
+    assert pw(0, None, p, p, p, p, 4, 17) == Z.ZK_ERR_RANGE  # more values than the domain
+    assert pw(0, None, None, p, p, p, 4, 4) == Z.ZK_ERR_INVALID
+    if Z.device_count() == 0:
+        assert cross(0, None, p, q, 8, 1, 0, 0, 0, None, 0) == Z.ZK_ERR_NODEV
+        assert pw(0, None, p, p, p, p, 4, 16) == Z.ZK_ERR_NODEV
+    assert Z.lib.zk_groth16_h_msm_blocks_device(None, None, p, 1, 0, p) == Z.ZK_ERR_INVALID
+
+
 REF = os.environ.get("REF", "/root/reference")
 
 
