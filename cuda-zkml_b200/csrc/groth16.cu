@@ -489,18 +489,25 @@ static int setup(const R1cs& R, const zkh::Fe toxic[5], zk_groth16_pk* pk) {
 
     DeviceContext* ctx;
     ZK_TRY(get_context(R.device, &ctx));
-    Fr* d_sc;
-    ZK_TRY_CUDA(cudaMalloc(&d_sc, std::max(nG1, s2.size()) * 32));
-    uint8_t *g1_all, *g2_all;
-    ZK_TRY_CUDA(cudaMalloc(&g1_all, nG1 * 64));
-    ZK_TRY_CUDA(cudaMalloc(&g2_all, s2.size() * 128));
+    // freed on every exit path; the two point arrays pass to the key on success
+    DeviceBuffer sc_buf, g1_buf, g2_buf;
+    ZK_TRY_CUDA(sc_buf.alloc(std::max(nG1, s2.size()) * 32));
+    ZK_TRY_CUDA(g1_buf.alloc(nG1 * 64));
+    ZK_TRY_CUDA(g2_buf.alloc(s2.size() * 128));
+    Fr* d_sc = (Fr*)sc_buf.p;
+    uint8_t* g1_all = (uint8_t*)g1_buf.p;
+    uint8_t* g2_all = (uint8_t*)g2_buf.p;
     ZK_TRY_CUDA(cudaMemcpy(d_sc, s1.data(), nG1 * 32, cudaMemcpyHostToDevice));
     ZK_TRY(zk_g1_fixed_base_device(R.device, nullptr, g1_all, d_sc, nG1));
     ZK_TRY_CUDA(cudaDeviceSynchronize());
     ZK_TRY_CUDA(cudaMemcpy(d_sc, s2.data(), s2.size() * 32, cudaMemcpyHostToDevice));
     ZK_TRY(zk_g2_fixed_base_device(R.device, nullptr, g2_all, d_sc, s2.size()));
     ZK_TRY_CUDA(cudaDeviceSynchronize());
-    cudaFree(d_sc);
+    std::vector<uint64_t> t1((size_t)(pub + 1 + 3) * 8);
+    const size_t tail1 = 2 * (size_t)m + l + n;
+    ZK_TRY_CUDA(cudaMemcpy(t1.data(), g1_all + tail1 * 64, t1.size() * 8, cudaMemcpyDeviceToHost));
+    std::vector<uint64_t> t2(5 * 16);
+    ZK_TRY_CUDA(cudaMemcpy(t2.data(), g2_all + (size_t)m * 128, t2.size() * 8, cudaMemcpyDeviceToHost));
 
     pk->device = R.device;
     pk->num_constraints = (int)n;
@@ -508,17 +515,12 @@ static int setup(const R1cs& R, const zkh::Fe toxic[5], zk_groth16_pk* pk) {
     pk->num_public = pub;
     pk->l = l;
     pk->n_h = (int)n;
-    pk->g1 = g1_all;  // A | B1 | L | H | IC | alpha beta delta (the tail is copied out below)
-    pk->g2 = g2_all;  // B2 | beta gamma delta tau G2
-    const size_t tail1 = 2 * (size_t)m + l + n;
-    std::vector<uint64_t> t1((size_t)(pub + 1 + 3) * 8);
-    ZK_TRY_CUDA(cudaMemcpy(t1.data(), g1_all + tail1 * 64, t1.size() * 8, cudaMemcpyDeviceToHost));
+    pk->g1 = (uint8_t*)g1_buf.release();  // A | B1 | L | H | IC | alpha beta delta (the tail copied out above)
+    pk->g2 = (uint8_t*)g2_buf.release();  // B2 | beta gamma delta tau G2
     pk->ic.assign(t1.begin(), t1.begin() + (size_t)(pub + 1) * 8);
     std::memcpy(pk->alpha1, &t1[(size_t)(pub + 1) * 8], 64);
     std::memcpy(pk->beta1, &t1[(size_t)(pub + 2) * 8], 64);
     std::memcpy(pk->delta1, &t1[(size_t)(pub + 3) * 8], 64);
-    std::vector<uint64_t> t2(5 * 16);
-    ZK_TRY_CUDA(cudaMemcpy(t2.data(), g2_all + (size_t)m * 128, t2.size() * 8, cudaMemcpyDeviceToHost));
     std::memcpy(pk->beta2, &t2[0], 128);
     std::memcpy(pk->gamma2, &t2[16], 128);
     std::memcpy(pk->delta2, &t2[32], 128);
@@ -627,6 +629,7 @@ static int ensure_h_tables(zk_groth16_pk* pk, cudaStream_t st) {
     if (pk->h_tab || pk->n_h < kHTablesMin) return ZK_OK;
     int c, W;
     g1_window_tables_shape((size_t)pk->n_h, &c, &W);
+    if ((size_t)W * pk->n_h > 0x7fffffffull) return ZK_OK;  // keys index 32 bits: the plain MSM runs in passes
     uint8_t* tab = nullptr;
     ZK_TRY_CUDA(cudaMalloc(&tab, (size_t)W * pk->n_h * 64));
     const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
@@ -689,8 +692,10 @@ static int h_msm_blocks(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h_part, 
             // tables need every base on the curve: none when identities fill missing points
             if (rc == ZK_OK && m >= (uint64_t)kHTablesMin && (uint64_t)pk->n_h >= n) {
                 g1_window_tables_shape(m, &hb.c, &hb.W);
-                if (cudaMalloc(&hb.tab, (size_t)hb.W * m * 64) != cudaSuccess) rc = ZK_ERR_CUDA;
-                if (rc == ZK_OK) rc = g1_window_tables_build(pk->device, st, hb.pts, m, hb.c, hb.W, hb.tab);
+                if ((size_t)hb.W * m <= 0x7fffffffull) {  // keys index 32 bits: else the plain MSM, in passes
+                    if (cudaMalloc(&hb.tab, (size_t)hb.W * m * 64) != cudaSuccess) rc = ZK_ERR_CUDA;
+                    if (rc == ZK_OK) rc = g1_window_tables_build(pk->device, st, hb.pts, m, hb.c, hb.W, hb.tab);
+                }
             }
             if (rc == ZK_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = ZK_ERR_CUDA;
             if (rc != ZK_OK) {

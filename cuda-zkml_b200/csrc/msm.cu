@@ -142,6 +142,38 @@ static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist, int num_sms) {
     return p;
 }
 
+// The counting sort counts, offsets and indexes keys in 32 bits (bucket
+// offsets, segment starts, sign << 31 | point index), so a pass may hold at
+// most 2^31 - 1 keys.  With the widest window the cost model picks for
+// full-width scalars (c = 21, W = 13) kMaxPassPoints points give 1.74e9 keys;
+// larger MSMs run in passes of at most that many points.
+static constexpr size_t kMaxKeys = 0x7fffffffull;
+static constexpr size_t kMaxPassPoints = (size_t)1 << 27;
+
+// A window width forced by ZK_MSM_WINDOW_BITS fixes W, and with it the worst
+// case n W, before any device work: refuse a pass that cannot fit.
+static int check_forced_window(size_t n, bool g2) {
+    const char* env = getenv(g2 ? "ZK_MSM_G2_WINDOW_BITS" : "ZK_MSM_WINDOW_BITS");
+    if (!env || atoi(env) < 2 || atoi(env) > 22) return ZK_OK;
+    const int c = atoi(env);
+    const size_t W = (255 + c - 1) / c;
+    if (n * W > kMaxKeys) {
+        set_error("msm: %zu points with the forced window width %d (%zu windows) exceed 2^31 - 1 keys", n, c, W);
+        return ZK_ERR_RANGE;
+    }
+    return ZK_OK;
+}
+
+// The plan's proven key bound (from the scalars' bit lengths) must fit too.
+static int check_key_bound(const MsmPlan& p, const uint32_t* hist) {
+    const size_t bound = plan_key_bound(p, hist);
+    if (bound > kMaxKeys) {
+        set_error("msm: up to %zu keys with window width %d exceed 2^31 - 1", bound, p.c);
+        return ZK_ERR_RANGE;
+    }
+    return ZK_OK;
+}
+
 // ------------------------------------------------------------------ digits
 // Signed-digit recoding of a standard-form scalar held in v[0..7], consumed
 // c bits at a time from the bottom (the 256-bit value is shifted in place).
@@ -1074,7 +1106,13 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     uint32_t hist[256];
     for (int b = 0; b < 256; b++) hist[b] = (uint32_t)std::min<double>(4e9, (double)hist_host[b] * (double)n / (double)nk[0]);
-    const MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
+    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
+    // The batches are sized by the trivial key bound below: a narrow window
+    // chosen from small first-batch scalars (many windows) could push that past
+    // the 32-bit key space, so such a plan gives way to the full-width one.
+    bool fits = true;
+    for (int k = 0; k < kBatches; k++) fits = fits && nk[k] * (size_t)P.W <= kMaxKeys;
+    if (!fits) P = make_plan(n, std::is_same<Cv, G2>::value, nullptr, ctx->num_sms);
     // per batch, any scalar may have all W digits nonzero: the later batches'
     // histograms are not looked at, so their key bound is the trivial one
     MsmPlan Pb[kBatches];
@@ -1263,10 +1301,11 @@ int msm_shared_scalars_run(DeviceContext* ctx, cudaStream_t st, const void* d_sc
         if (set_ms) set_ms[k] = 0.f;
     }
     if (n == 0 || n_sets == 0) return ZK_OK;
-    if (n > 0x7fffffffull || n_sets > 8) {
-        set_error("msm: %zu points or %d point sets out of range", n, n_sets);
+    if (n > kMaxPassPoints || n_sets > 8) {
+        set_error("msm: %zu points (at most %zu) or %d point sets (at most 8) out of range", n, kMaxPassPoints, n_sets);
         return ZK_ERR_RANGE;
     }
+    ZK_TRY(check_forced_window(n, false));
     ZK_TRY_CUDA(cudaSetDevice(ctx->device));
     std::lock_guard<std::mutex> lock(ctx->mu);
     const double sms = (double)std::max(ctx->num_sms, 1);
@@ -1285,7 +1324,8 @@ int msm_shared_scalars_run(DeviceContext* ctx, cudaStream_t st, const void* d_sc
     uint32_t hist[256];
     std::memcpy(hist, hist_host, sizeof hist);
     const MsmPlan P = make_plan(n, false, hist, ctx->num_sms);  // the sort, and the G1 accumulates
-    MsmPlan P2 = P;                                             // G2 accumulates: shorter segments
+    ZK_TRY(check_key_bound(P, hist));
+    MsmPlan P2 = P;                                           // G2 accumulates: shorter segments
     P2.seg = pow2_clamp((double)plan_key_bound(P, hist) / (sms * 512.0), 8, 64);
     P2.max_segs = std::max<size_t>(1, (plan_key_bound(P, hist) + P2.seg - 1) / P2.seg);
     stats.window_bits = P.c;
@@ -1341,9 +1381,14 @@ int msm_shared_scalars_run(DeviceContext* ctx, cudaStream_t st, const void* d_sc
     return ZK_OK;
 }
 
+template <class Cv>
+static void host_add_affine(const uint64_t* a, const uint64_t* b, uint64_t* out);
+
 // Full MSM.  src_points / src_scalars are device pointers (host_inputs == 0)
 // or host pointers (host_inputs == 1, copied in chunks on the copy stream).
 // ref_layout: points are reference records (72 / 136 B) rather than packed.
+// More than kMaxPassPoints points run as consecutive passes whose affine
+// results are added on the host, so that no pass outgrows the 32-bit key space.
 template <class Cv>
 static int msm_run(int device, cudaStream_t user_stream, const void* src_points, const void* src_scalars, size_t n,
                    bool host_inputs, bool ref_layout, uint64_t* out_affine) {
@@ -1354,10 +1399,29 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
         std::memset(out_affine, 0, 2 * kw * 8);
         return ZK_OK;
     }
-    if (n > 0x7fffffffull) {
-        set_error("msm: n = %zu exceeds 2^31 - 1 points", n);
-        return ZK_ERR_RANGE;
+    if (n > kMaxPassPoints) {
+        const size_t rec = ref_layout ? Cv::kAffineBytes + 8 : Cv::kAffineBytes;
+        uint64_t acc[2 * kw] = {}, part[2 * kw];
+        MsmStats sum;
+        for (size_t off = 0; off < n; off += kMaxPassPoints) {
+            const size_t cnt = std::min(kMaxPassPoints, n - off);
+            ZK_TRY(msm_run<Cv>(device, user_stream, (const uint8_t*)src_points + off * rec, (const uint8_t*)src_scalars + off * 32,
+                               cnt, host_inputs, ref_layout, part));
+            host_add_affine<Cv>(acc, part, acc);
+            const MsmStats& s = msm_stats();
+            sum.kernel_launches += s.kernel_launches;
+            sum.accumulate_ms += s.accumulate_ms;
+            sum.total_device_ms += s.total_device_ms;
+            sum.bucket_adds += s.bucket_adds;
+            sum.window_bits = s.window_bits;
+            sum.num_windows = s.num_windows;
+            for (int i = 0; i < 8; i++) sum.phase_ms[i] += s.phase_ms[i];
+        }
+        stats = sum;
+        std::memcpy(out_affine, acc, sizeof acc);
+        return ZK_OK;
     }
+    ZK_TRY(check_forced_window(n, std::is_same<Cv, G2>::value));
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     std::lock_guard<std::mutex> lock(ctx->mu);
@@ -1387,6 +1451,7 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     uint32_t hist[256];
     std::memcpy(hist, hist_host, sizeof hist);
     MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
+    ZK_TRY(check_key_bound(P, hist));
     stats.window_bits = P.c;
     stats.num_windows = P.W;
 

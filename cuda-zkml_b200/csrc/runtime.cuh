@@ -60,6 +60,24 @@ struct PoolBuffer {
     }
 };
 
+// A cudaMalloc allocation owned by a scope: freed on every exit path unless
+// release() hands it on.
+struct DeviceBuffer {
+    void* p = nullptr;
+    DeviceBuffer() = default;
+    DeviceBuffer(const DeviceBuffer&) = delete;
+    DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+    ~DeviceBuffer() {
+        if (p) cudaFree(p);
+    }
+    cudaError_t alloc(size_t bytes) { return cudaMalloc(&p, bytes); }
+    void* release() {
+        void* q = p;
+        p = nullptr;
+        return q;
+    }
+};
+
 // bump allocator over one device buffer; all offsets 256-byte aligned
 struct Arena {
     char* base = nullptr;

@@ -22,10 +22,16 @@ _REFLIB = os.path.join(HERE, "_ref", "libzkref.so")
 _u64p = ctypes.POINTER(ctypes.c_uint64)
 
 
+def reference_tree():
+    """The reference checkout: $REF, else a directory named `reference` beside
+    this repository (absent on machines that only run the prebuilt checkers)."""
+    return os.environ.get("REF") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
 def build():
     """Compile liboracle.so (and _ref/ when the reference tree is present)."""
     targets = ["liboracle.so"]
-    if os.path.isdir(os.environ.get("REF", "/root/reference")):
+    if os.path.isdir(reference_tree()):
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
 

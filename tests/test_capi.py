@@ -97,7 +97,7 @@ def test_split_transform_and_pointwise_arguments_checked_first():
     assert Z.lib.zk_groth16_h_msm_blocks_device(None, None, p, 1, 0, p) == Z.ZK_ERR_INVALID
 
 
-REF = os.environ.get("REF", "/root/reference")
+REF = O.reference_tree()
 
 
 @pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "src")), reason="reference tree not present")
@@ -129,3 +129,25 @@ def test_reference_code_links_against_library(tmp_path):
         w, v = out[ln].split()
         assert int(w, 16) == O.to_int(g["fwd"][ln])
         assert int(v, 16) == O.to_int(g["inv"][ln])
+
+
+def test_msm_key_space_refused_before_device_work(monkeypatch):
+    """Keys of the counting sort are counted and indexed in 32 bits.  A window
+    width forced by ZK_MSM_WINDOW_BITS fixes the worst case n W before any
+    device work, and a pass whose n W exceeds 2^31 - 1 is refused with
+    ZK_ERR_RANGE (here, without a GPU, before the device lookup).  Larger MSMs
+    with the automatic window run in passes of at most 2^27 points."""
+    import ctypes
+    buf = (ctypes.c_uint8 * 128)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    monkeypatch.setenv("ZK_MSM_WINDOW_BITS", "3")   # W = 85
+    assert Z.lib.zk_msm_g1_device(0, None, p, p, (1 << 27), p) == Z.ZK_ERR_RANGE
+    assert Z.lib.zk_msm_g1_host(0, None, p, p, (1 << 27) + 5, p) == Z.ZK_ERR_RANGE   # the first pass is refused
+    assert "2^31" in Z.last_error()
+    monkeypatch.setenv("ZK_MSM_G2_WINDOW_BITS", "4")  # W = 64
+    assert Z.lib.zk_msm_g2_device(0, None, p, p, 1 << 25, p) == Z.ZK_ERR_RANGE   # 2^31 keys
+    if Z.device_count() == 0:
+        # within the key space the call goes on to the device lookup
+        assert Z.lib.zk_msm_g2_device(0, None, p, p, (1 << 25) - 1, p) == Z.ZK_ERR_NODEV
+        monkeypatch.delenv("ZK_MSM_WINDOW_BITS")
+        assert Z.lib.zk_msm_g1_device(0, None, p, p, (1 << 27) + 5, p) == Z.ZK_ERR_NODEV

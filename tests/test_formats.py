@@ -5,9 +5,10 @@ import os
 
 import pytest
 
+import pyoracle
 import zkmlpk3
 
-REF = os.environ.get("REF", "/root/reference")
+REF = pyoracle.reference_tree()
 ART = os.path.join(REF, "results", "gpu_validation_2026", "artifacts")
 
 
