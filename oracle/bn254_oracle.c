@@ -657,43 +657,96 @@ static uint32_t bitrev(uint32_t x, int bits) {
 }
 
 /* bit-reverse, radix-2 DIT stages with t = w^(pos << (log_n-1-s)) * b,
- * (a+t, a-t), then the n^-1 scale for the inverse (ntt.cu:354-465) */
-void orc_ntt(uint64_t* out, const uint64_t* in, int log_n, int inverse) {
+ * (a+t, a-t), then the n^-1 scale for the inverse (ntt.cu:354-465).
+ * The multi-threaded form splits each stage's butterflies (and the stage's
+ * twiddle table) into contiguous ranges: every value is computed exactly as in
+ * the single-threaded loop. */
+typedef struct {
+    uint64_t* buf; const uint64_t* in; orc_fe* tw; orc_fe ws; orc_fe sc;
+    size_t n, lo, hi; int log_n, stage, phase;
+} ntt_job;
+
+static void ntt_job_run(ntt_job* J) {
+    const size_t stride = (size_t)1 << J->stage;
+    if (J->phase == 0) {          /* bit-reversed copy of elements [lo, hi) */
+        for (size_t i = J->lo; i < J->hi; i++) memcpy(J->buf + 4 * bitrev((uint32_t)i, J->log_n), J->in + 4 * i, 32);
+    } else if (J->phase == 1) {   /* twiddles tw[k] = ws^k, k in [lo, hi) */
+        uint64_t e[4] = {J->lo, 0, 0, 0};
+        mpow_(&MR, J->tw[J->lo].v, J->ws.v, e);
+        for (size_t k = J->lo + 1; k < J->hi; k++) mmul_(&MR, J->tw[k].v, J->tw[k - 1].v, J->ws.v);
+    } else if (J->phase == 2) {   /* butterflies j in [lo, hi): group j / stride, offset j % stride */
+        for (size_t j = J->lo; j < J->hi; j++) {
+            const size_t k = j & (stride - 1), g = (j >> J->stage) << (J->stage + 1);
+            uint64_t* a = J->buf + 4 * (g + k);
+            uint64_t* b = J->buf + 4 * (g + k + stride);
+            uint64_t t[4], s0[4];
+            mmul_(&MR, t, J->tw[k].v, b);
+            madd_(&MR, s0, a, t);
+            msub_(&MR, b, a, t);
+            memcpy(a, s0, 32);
+        }
+    } else {                      /* n^-1 scale of [lo, hi) */
+        for (size_t i = J->lo; i < J->hi; i++) mmul_(&MR, J->buf + 4 * i, J->buf + 4 * i, J->sc.v);
+    }
+}
+
+static void* ntt_worker(void* arg) { ntt_job_run((ntt_job*)arg); return NULL; }
+
+/* run `proto` over [0, count) split into nthreads ranges */
+static void ntt_parallel(const ntt_job* proto, size_t count, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    if ((size_t)nthreads > count) nthreads = count ? (int)count : 1;
+    if (nthreads == 1 || count < 4096) {
+        ntt_job J = *proto;
+        J.lo = 0; J.hi = count;
+        ntt_job_run(&J);
+        return;
+    }
+    pthread_t th[256];
+    ntt_job jobs[256];
+    if (nthreads > 256) nthreads = 256;
+    for (int t = 0; t < nthreads; t++) {
+        jobs[t] = *proto;
+        jobs[t].lo = count * t / nthreads;
+        jobs[t].hi = count * (t + 1) / nthreads;
+        pthread_create(&th[t], NULL, ntt_worker, &jobs[t]);
+    }
+    for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
+}
+
+void orc_ntt_mt(uint64_t* out, const uint64_t* in, int log_n, int inverse, int nthreads) {
     INIT();
     size_t n = (size_t)1 << log_n;
     uint64_t* buf = (uint64_t*)malloc(n * 32);
-    for (size_t i = 0; i < n; i++) memcpy(buf + 4 * bitrev((uint32_t)i, log_n), in + 4 * i, 32);
+    orc_fe* tw = (orc_fe*)malloc((n / 2 + 1) * sizeof(orc_fe));
+    ntt_job P;
+    memset(&P, 0, sizeof P);
+    P.buf = buf; P.in = in; P.tw = tw; P.n = n; P.log_n = log_n;
+    P.phase = 0;
+    ntt_parallel(&P, n, nthreads);
     orc_fe w;
     orc_compute_omega(&w, log_n, inverse);
-    orc_fe* tw = (orc_fe*)malloc((n / 2 + 1) * sizeof(orc_fe));
     for (int s = 0; s < log_n; s++) {
-        size_t stride = (size_t)1 << s;
         orc_fe ws = w;
         for (int i = 0; i < log_n - 1 - s; i++) mmul_(&MR, ws.v, ws.v, ws.v);
-        memcpy(tw[0].v, MR.one, 32);
-        for (size_t k = 1; k < stride; k++) mmul_(&MR, tw[k].v, tw[k - 1].v, ws.v);
-        for (size_t g = 0; g < n; g += 2 * stride) {
-            for (size_t k = 0; k < stride; k++) {
-                uint64_t* a = buf + 4 * (g + k);
-                uint64_t* b = buf + 4 * (g + k + stride);
-                uint64_t t[4];
-                mmul_(&MR, t, tw[k].v, b);
-                uint64_t s0[4];
-                madd_(&MR, s0, a, t);
-                msub_(&MR, b, a, t);
-                memcpy(a, s0, 32);
-            }
-        }
+        P.stage = s;
+        P.ws = ws;
+        P.phase = 1;
+        ntt_parallel(&P, (size_t)1 << s, nthreads);
+        P.phase = 2;
+        ntt_parallel(&P, n / 2, nthreads);
     }
     if (inverse) {
-        orc_fe sc;
-        memcpy(sc.v, MR.one, 32);
-        for (int i = 0; i < log_n; i++) mmul_(&MR, sc.v, sc.v, FR_HALF.v);
-        for (size_t i = 0; i < n; i++) mmul_(&MR, buf + 4 * i, buf + 4 * i, sc.v);
+        memcpy(P.sc.v, MR.one, 32);
+        for (int i = 0; i < log_n; i++) mmul_(&MR, P.sc.v, P.sc.v, FR_HALF.v);
+        P.phase = 3;
+        ntt_parallel(&P, n, nthreads);
     }
     memcpy(out, buf, n * 32);
     free(buf); free(tw);
 }
+
+void orc_ntt(uint64_t* out, const uint64_t* in, int log_n, int inverse) { orc_ntt_mt(out, in, log_n, inverse, 1); }
 
 /* O(n^2) DFT, tests/test_ntt.cu:19-37 */
 void orc_ntt_naive(uint64_t* out, const uint64_t* in, int log_n, int inverse) {
@@ -724,7 +777,7 @@ void orc_ntt_naive(uint64_t* out, const uint64_t* in, int log_n, int inverse) {
     free(buf);
 }
 
-void orc_coset_ntt(uint64_t* out, const uint64_t* in, int log_n, int inverse, const orc_fe* g) {
+void orc_coset_ntt_mt(uint64_t* out, const uint64_t* in, int log_n, int inverse, const orc_fe* g, int nthreads) {
     INIT();
     size_t n = (size_t)1 << log_n;
     orc_fe gp, gs = *g;
@@ -735,17 +788,21 @@ void orc_coset_ntt(uint64_t* out, const uint64_t* in, int log_n, int inverse, co
             mmul_(&MR, tmp + 4 * i, in + 4 * i, gp.v);
             mmul_(&MR, gp.v, gp.v, gs.v);
         }
-        orc_ntt(out, tmp, log_n, 0);
+        orc_ntt_mt(out, tmp, log_n, 0, nthreads);
         free(tmp);
     } else {
         orc_fe gi;
         minv_(&MR, gi.v, gs.v);
-        orc_ntt(out, in, log_n, 1);
+        orc_ntt_mt(out, in, log_n, 1, nthreads);
         for (size_t i = 0; i < n; i++) {
             mmul_(&MR, out + 4 * i, out + 4 * i, gp.v);
             mmul_(&MR, gp.v, gp.v, gi.v);
         }
     }
+}
+
+void orc_coset_ntt(uint64_t* out, const uint64_t* in, int log_n, int inverse, const orc_fe* g) {
+    orc_coset_ntt_mt(out, in, log_n, inverse, g, 1);
 }
 
 /* compute_h after the sparse matvec (groth16.cu:322-383): 3 INTT, coset shift

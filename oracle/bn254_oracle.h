@@ -92,11 +92,14 @@ void orc_msm_config(size_t n, int g2, int* window_bits, int* num_windows);
 void orc_compute_omega(orc_fe* r, int log_n, int inverse);
 /* natural order in/out; inverse scales by n^-1; in and out may alias. */
 void orc_ntt(uint64_t* out, const uint64_t* in, int log_n, int inverse);
+/* the same transform with each stage split over nthreads threads */
+void orc_ntt_mt(uint64_t* out, const uint64_t* in, int log_n, int inverse, int nthreads);
 void orc_ntt_naive(uint64_t* out, const uint64_t* in, int log_n, int inverse);
 /* coset forms used by compute_h (src/prover/groth16.cu:329-383):
  * coset forward  : out = NTT(a_i * g^i)
  * coset inverse  : out_i = INTT(a)_i * g^-i                               */
 void orc_coset_ntt(uint64_t* out, const uint64_t* in, int log_n, int inverse, const orc_fe* g);
+void orc_coset_ntt_mt(uint64_t* out, const uint64_t* in, int log_n, int inverse, const orc_fe* g, int nthreads);
 
 /* ---- quotient polynomial (src/prover/groth16.cu:263-390) ----
  * Input: the three evaluation vectors A*w, B*w, C*w on the size-n domain.

@@ -234,10 +234,10 @@ def g2_on_curve(pt):
 
 
 # ---------------------------------------------------------------- NTT
-def ntt(a, log_n, inverse=False):
+def ntt(a, log_n, inverse=False, nthreads=1):
     a = np.ascontiguousarray(a, np.uint64)
     out = np.zeros_like(a)
-    lib.orc_ntt(_p(out), _p(a), ctypes.c_int(log_n), ctypes.c_int(int(inverse)))
+    lib.orc_ntt_mt(_p(out), _p(a), ctypes.c_int(log_n), ctypes.c_int(int(inverse)), ctypes.c_int(nthreads))
     return out
 
 
@@ -248,11 +248,11 @@ def ntt_naive(a, log_n, inverse=False):
     return out
 
 
-def coset_ntt(a, log_n, inverse, g):
+def coset_ntt(a, log_n, inverse, g, nthreads=1):
     a = np.ascontiguousarray(a, np.uint64)
     out = np.zeros_like(a)
     gg = np.ascontiguousarray(g, np.uint64)
-    lib.orc_coset_ntt(_p(out), _p(a), ctypes.c_int(log_n), ctypes.c_int(int(inverse)), _p(gg))
+    lib.orc_coset_ntt_mt(_p(out), _p(a), ctypes.c_int(log_n), ctypes.c_int(int(inverse)), _p(gg), ctypes.c_int(nthreads))
     return out
 
 

@@ -15,6 +15,8 @@
 
 #include <unistd.h>
 
+#include <chrono>
+
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -77,6 +79,58 @@ int ref_g16_verify(int nc, int m, int pub, const void* a, size_t na, const void*
     ProvingKey pk;
     VerificationKey vk;
     Groth16Prover::setup(r, pk, vk);
+    char path[] = "/tmp/zkref_proof_XXXXXX";
+    int fd = mkstemp(path);
+    if (fd < 0) return 4;
+    bool wrote = write(fd, proof_bytes, 256) == 256;
+    close(fd);
+    if (!wrote) { unlink(path); return 4; }
+    Groth16Proof proof = load_proof(path);
+    unlink(path);
+    std::vector<bn254::Fr> pubs((size_t)pub);
+    std::memcpy(pubs.data(), public_inputs, (size_t)pub * sizeof(bn254::Fr));
+    *verified = Groth16Verifier::verify(vk, proof, pubs) ? 1 : 0;
+    return 0;
+}
+
+// The reference's Groth16Prover::prove from key files: a ZKMLPK3 proving key
+// read by ProvingKey::load_streaming (src/prover/groth16.cu:1190-1314) and a
+// vk.bin read by load_vk (src/verifier/verifier.cu:103-148), both written by
+// the library under test (its setup is byte-identical to the reference's, and
+// the reference's own host setup would take minutes to hours at the larger
+// configurations).  Deterministic blinding (ZKML_DETERMINISTIC_PROVE=1).
+// Writes the 256-byte proof, the reference verifier's verdict on it, and the
+// wall time of prove() in milliseconds.
+int ref_g16_prove_keys(const char* pk_path, const char* vk_path, int nc, int m, int pub, const void* a, size_t na, const void* b,
+                       size_t nb, const void* c, size_t ncc, const void* witness, uint8_t* proof_out, int* verified,
+                       double* prove_ms) {
+    setenv("ZKML_DETERMINISTIC_PROVE", "1", 1);
+    R1CS r = make_r1cs(nc, m, pub, a, na, b, nb, c, ncc);
+    Witness w;
+    w.values.resize(m);
+    std::memcpy(w.values.data(), witness, (size_t)m * sizeof(bn254::Fr));
+    w.num_public = pub;
+    w.num_private = m - 1 - pub;
+    ProvingKey pk;
+    if (!pk.load_streaming(pk_path)) return 2;
+    VerificationKey vk = load_vk(vk_path);
+    if ((int)vk.ic.size() != pub + 1) return 5;
+    auto t0 = std::chrono::steady_clock::now();
+    Groth16Proof proof = Groth16Prover::prove(pk, r, w);
+    auto t1 = std::chrono::steady_clock::now();
+    if (prove_ms) *prove_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
+    if (!proof.valid) return 3;
+    std::vector<uint8_t> bytes = proof.serialize();
+    std::memcpy(proof_out, bytes.data(), 256);
+    *verified = Groth16Verifier::verify(vk, proof, w.get_public()) ? 1 : 0;
+    return 0;
+}
+
+// The reference verifier on externally produced proof bytes with a vk.bin
+// (load_vk) instead of a setup: reads the proof through load_proof as the CLI does.
+int ref_g16_verify_vk(const char* vk_path, int pub, const void* public_inputs, const uint8_t* proof_bytes, int* verified) {
+    VerificationKey vk = load_vk(vk_path);
+    if ((int)vk.ic.size() != pub + 1) return 5;
     char path[] = "/tmp/zkref_proof_XXXXXX";
     int fd = mkstemp(path);
     if (fd < 0) return 4;
