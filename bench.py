@@ -14,11 +14,16 @@ e2e   : the same MSM through the host-buffer entry point zk_msm_g1_host, with
         the points and scalars copied from pinned host memory every step and
         the result read back to the host.
 roofline: the bucket-accumulation kernel (the dominant one) against the
-        measured INT32 multiply-add (IMAD) rate of this GPU.
+        hardware issue rate of mad.lo.u32 on this GPU, measured in the run
+        (zk_probe_int_pipe); the fractions against a lo/hi product pair and
+        against the library's own Montgomery multiplication ride along.
 cpu_baseline: the oracle's multi-threaded Pippenger (a CPU restatement of the
         reference's algorithm) on a 2^18-point sample of the same inputs.
---impl reference: the reference's own CPU MSM path (its host arithmetic,
-        compiled from its sources into oracle/_ref) on all host cores.
+--impl reference: the reference's Pippenger schedule (src/msm/msm.cu) with its
+        own host arithmetic (compiled from its sources into oracle/_ref) on all
+        host cores, over a 2^18-point sample per step; beside it, the
+        reference's own GPU NTT (bn254::ntt_gpu built for sm_100a) at 2^16,
+        2^20 and 2^24 on the same B200.
 """
 import argparse
 import json
@@ -98,7 +103,44 @@ def emit(obj):
 
 
 # ---------------------------------------------------------------- reference arm
+def reference_gpu_ntt(ref, sizes, reps=3):
+    """The reference's own GPU NTT entry point bn254::ntt_gpu (src/ntt/ntt.cu:
+    354-465, compiled for sm_100a from its source into oracle/_ref/libzkref.so)
+    on this B200: wall time of the synchronous call (it allocates, builds each
+    global stage's twiddles on the host and copies them, as a reference user
+    gets it), device buffers allocated here.  No lock or wait in its kernels."""
+    import torch
+    out = {}
+    dev = torch.device("cuda", 0)
+    for ln in sizes:
+        n = 1 << ln
+        x = torch.randint(0, 1 << 62, (n, 4), dtype=torch.int64, device=dev)
+        x[:, 3] &= (1 << 60) - 1  # below r
+        y = torch.empty_like(x)
+        ref.ref_ntt_gpu(ctypes_ptr(y), ctypes_ptr(x), ln, 0)  # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            ref.ref_ntt_gpu(ctypes_ptr(y), ctypes_ptr(x), ln, 0)
+        torch.cuda.synchronize()
+        out[f"2^{ln}"] = {"ms": 1e3 * (time.perf_counter() - t0) / reps, "reps": reps}
+        del x, y
+    return out
+
+
+def ctypes_ptr(t):
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr())
+
+
 def run_reference(args):
+    """The reference's CPU MSM path at this workload: its Pippenger schedule
+    (src/msm/msm.cu:320-442: MSMConfig windows, unsigned digits, add_affine
+    buckets, running-sum reduce, host combine) executed on the host cores with
+    its own host arithmetic (src/field, src/curve compiled from its sources into
+    oracle/_ref), on a bounded sample of the 2^L points per step.  Its GPU MSM
+    is not run (unbounded atomicCAS spin locks, msm.cu:63-72); its GPU NTT is
+    timed beside it on the same B200."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
@@ -115,13 +157,23 @@ def run_reference(args):
     sc = rng.fr_vector(n)
     out = np.zeros(8, np.uint64)
     inf = ctypes.c_int()
+    gpu_ntt = None
     if O.ref_available():
         ref = O.ref()
         kind = "reference"
 
         def step():
-            ref.ref_msm_g1_naive_mt(O._p(out), ctypes.byref(inf), O._p(pts), O._p(sc), n, cores)
-        what = "reference host arithmetic (src/field, src/curve) and CPU MSM path (src/msm/msm.cu:330-339)"
+            ref.ref_msm_g1_pippenger_mt(O._p(out), ctypes.byref(inf), O._p(pts), O._p(sc), n, cores)
+        what = ("reference Pippenger schedule (src/msm/msm.cu:320-442) with the reference's own host arithmetic "
+                "(src/field, src/curve), windows split over the host threads")
+        if not args.no_ntt:
+            try:
+                import torch
+                if torch.cuda.is_available():
+                    ref.ref_ntt_gpu.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+                    gpu_ntt = reference_gpu_ntt(ref, (16, 20, 24))
+            except Exception as e:  # reported, not fatal: the MSM arm stands alone
+                gpu_ntt = {"error": str(e)[:200]}
     else:
         kind = "port"
 
@@ -142,7 +194,8 @@ def run_reference(args):
           "config": {"workload": f"G1 MSM, 2^{args.log_n} points per GPU (configs[1])", "log_n": args.log_n,
                      "sample_points": n},
           "cpu_baseline": {"value": value, "unit": "points/s", "cores": cores, "kind": kind, "sample": sample},
-          "e2e": {"value": value, "unit": "points/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+          "e2e": {"value": value, "unit": "points/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+          "reference_gpu_ntt": gpu_ntt})
 
 
 # ---------------------------------------------------------------- Groth16 prove
@@ -283,7 +336,9 @@ def run_b200(args):
             part = D.combine(D.gather_partials(part, device=dev), Z.g1_add_affine)
         return part
 
-    imad = max(Z.probe_imad_rate(local) for _ in range(3))
+    imad = max(Z.probe_imad_rate(local) for _ in range(3))  # the library's own multiplication, 256 IMAD each
+    pipe = max((Z.probe_int_pipe(local) for _ in range(2)), key=lambda r: r["mad_lo_per_s"])
+    hw_peak = pipe["mad_lo_per_s"]  # hardware mad.lo.u32 issue rate at the clock this run sees
 
     for _ in range(args.warmup):
         step_device()
@@ -317,11 +372,18 @@ def run_b200(args):
     imad_per_add = 6 * 256 + 2 * 200 + 384
     achieved = adds * imad_per_add / (acc_ms / 1e3)
     roofline = {"bound": "int32", "kernel": "msm_accumulate_kernel<G1>", "achieved": achieved / 1e12,
-                "peak": imad / 1e12, "unit": "TIMAD/s", "frac": achieved / imad, "traffic": None,
+                "peak": hw_peak / 1e12, "unit": "TIMAD/s", "frac": achieved / hw_peak, "traffic": None,
                 "algorithmic": f"{adds} mixed additions x {imad_per_add} IMAD (6 products x 256, 2 squarings x 200, "
                                f"Y3's two products sharing a reduction 384) per launch",
-                "peak_source": "zk_probe_imad_rate, measured in this run (the Montgomery multiplication itself on 4 independent chains per thread, counted as 256 IMAD)",
-                "msm_whole_frac_ref_ops": 256 * msm_ref_ops(n) / (stats[-1]["total_device_ms"] / 1e3) / imad}
+                "peak_source": (f"zk_probe_int_pipe, measured in this run: the hardware issue rate of plain mad.lo.u32 "
+                                f"({pipe['mad_lo_per_clk_sm']:.1f}/clk/SM x {pipe['num_sms']} SMs x {pipe['sm_clock_ghz']:.3f} GHz "
+                                f"measured by the probe); every one of the counted IMAD is a mad.lo or mad.hi half of a product"),
+                "pipe_rates": {"mad_lo_per_clk_sm": pipe["mad_lo_per_clk_sm"], "mad_hi_per_clk_sm": pipe["mad_hi_per_clk_sm"],
+                               "mad_lo_hi_pair_per_clk_sm": pipe["mad_pair_per_clk_sm"], "sm_clock_ghz": pipe["sm_clock_ghz"]},
+                "frac_vs_lo_hi_pairs": achieved / pipe["mad_pair_per_s"],
+                "frac_vs_own_multiply": achieved / imad,
+                "own_multiply_timad": imad / 1e12,
+                "msm_whole_frac_ref_ops": 256 * msm_ref_ops(n) / (stats[-1]["total_device_ms"] / 1e3) / hw_peak}
     prof = os.path.join(ROOT, "profiles", "msm_accumulate_g1_traffic.json")
     if os.path.exists(prof):
         # DRAM bytes per addition from one ncu capture of the accumulate kernel,
@@ -387,9 +449,25 @@ def run_b200(args):
         ntt = {"log_n": ln, "ms": t * 1e3, "elements_per_s": nn / t,
                "hbm": {"achieved_gbs": alg_bytes / t / 1e9, "peak_gbs": args.hbm_peak,
                        "frac": alg_bytes / t / 1e9 / args.hbm_peak, "algorithmic": "128 B per element"},
-               "int32": {"achieved_timad": alg_imad / t / 1e12, "peak_timad": imad / 1e12, "frac": alg_imad / t / imad,
-                         "algorithmic": "(n/2) log2 n Montgomery multiplications x 256 IMAD"}}
+               "int32": {"achieved_timad": alg_imad / t / 1e12, "peak_timad": hw_peak / 1e12, "frac": alg_imad / t / hw_peak,
+                         "frac_vs_own_multiply": alg_imad / t / imad,
+                         "algorithmic": "(n/2) log2 n Montgomery multiplications x 256 IMAD, against the mad.lo issue rate"}}
         del x, y
+        # the reference-shaped entry point zk_ntt (synchronous, device pointers: the
+        # call bn254::ntt_gpu makes), wall time per call at config 3's sizes; the
+        # reference arm times the reference's own ntt_gpu the same way on this GPU
+        ntt["zk_ntt_wall_ms"] = {}
+        for lr in (16, 20, 24):
+            xr = Z.to_device(Z.random_fr(1 << lr, 0xA1A1 + lr), dev)
+            yr = torch.empty_like(xr)
+            Z.ntt_ref(yr, xr, lr, False)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(3):
+                Z.ntt_ref(yr, xr, lr, False)
+            torch.cuda.synchronize()
+            ntt["zk_ntt_wall_ms"][f"2^{lr}"] = 1e3 * (time.perf_counter() - t0) / 3
+            del xr, yr
 
     prove = None
     if not args.no_prove and (rank == 0 or world > 1):
@@ -420,6 +498,8 @@ def run_b200(args):
                          "parallelism": f"points sharded over {world} GPU(s), partial sums all-gathered",
                          "l2": "inputs 1.5 GiB per GPU > 126 MB L2 (no flush needed)"},
               "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "ntt": ntt, "prove": prove,
+              "vs_cpu_baseline": ({"device": value / cpu["value"], "e2e": e2e["value"] / cpu["value"] if e2e else None}
+                                  if cpu else None),
               "clocks": sampler.summary(), "accumulate_ms": acc_ms,
               "phase_ms": {k: round(v, 3) for k, v in stats[-1]["phase_ms"].items()}})
     if world > 1:
@@ -437,7 +517,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-log-n", type=int, default=18)
-    ap.add_argument("--ref-sample", type=int, default=1 << 13)
+    ap.add_argument("--ref-sample", type=int, default=1 << 18)
     ap.add_argument("--no-ntt", action="store_true")
     ap.add_argument("--no-prove", action="store_true")
     ap.add_argument("--prove-channels", type=int, default=32)

@@ -5,6 +5,7 @@
 
 #include <cstring>
 #include <string>
+#include <vector>
 
 namespace zk {
 
@@ -190,9 +191,110 @@ __global__ void __launch_bounds__(256) imad_probe_kernel(uint32_t* out, uint32_t
     out[blockIdx.x * blockDim.x + threadIdx.x] = acc;
 }
 
+// ------------------------------------------------------------------ INT32 pipe probe
+// The hardware issue rate of the 32-bit integer multiply-add, independent of
+// any field code: 8 independent chains per thread at full occupancy, each step
+// one instruction of the probed form (kMode 0: mad.lo.u32; 1: mad.hi.u32;
+// 2: a mad.lo.cc.u32 / madc.hi.u32 pair, the two halves of one 32 x 32-bit
+// product with carry, counted as 2 instructions).  Thread 0 of each block
+// records clock64 and the global timer around its loop, giving the SM clock
+// the probe ran at.
+template <int kMode>
+__global__ void __launch_bounds__(256) int_pipe_probe_kernel(uint32_t* out, unsigned long long* clk, uint32_t seed, int iters) {
+    uint32_t a[8];
+    const uint32_t m = seed | 1u;
+#pragma unroll
+    for (int k = 0; k < 8; k++) a[k] = seed * (k + 1) + threadIdx.x + blockIdx.x;
+    unsigned long long c0 = 0, t0 = 0;
+    if (threadIdx.x == 0) {
+        c0 = clock64();
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    }
+    for (int i = 0; i < iters; i++) {
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (kMode == 0) {
+                    asm volatile("mad.lo.u32 %0, %0, %1, %2;" : "+r"(a[k]) : "r"(m), "r"((uint32_t)k));
+                } else if (kMode == 1) {
+                    asm volatile("mad.hi.u32 %0, %0, %1, %2;" : "+r"(a[k]) : "r"(m), "r"((uint32_t)k));
+                } else {
+                    asm volatile("{\n\t.reg .u32 t;\n\t"
+                                 "mad.lo.cc.u32 t, %0, %1, %2;\n\t"
+                                 "madc.hi.u32 %0, %0, %1, t;\n\t}"
+                                 : "+r"(a[k]) : "r"(m), "r"((uint32_t)k));
+                }
+            }
+        }
+    }
+    if (threadIdx.x == 0) {
+        unsigned long long c1 = clock64(), t1;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+        clk[2 * blockIdx.x] = c1 - c0;
+        clk[2 * blockIdx.x + 1] = t1 - t0;
+    }
+    uint32_t acc = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc ^= a[k];
+    out[blockIdx.x * blockDim.x + threadIdx.x] = acc;
+}
+
+template <int kMode>
+static int run_int_pipe_probe(DeviceContext* ctx, uint32_t* buf, unsigned long long* clk_dev, double* per_s, double* ghz) {
+    const int threads = 256, blocks = ctx->num_sms * 8, iters = 512;
+    ScopedEvent a, b;
+    ZK_TRY_CUDA(cudaEventCreate(&a.e));
+    ZK_TRY_CUDA(cudaEventCreate(&b.e));
+    int_pipe_probe_kernel<kMode><<<blocks, threads, 0, ctx->stream>>>(buf, clk_dev, 12345u, 64);  // warm-up
+    ZK_TRY_CUDA(cudaEventRecord(a.e, ctx->stream));
+    int_pipe_probe_kernel<kMode><<<blocks, threads, 0, ctx->stream>>>(buf, clk_dev, 777u, iters);
+    ZK_TRY_CUDA(cudaEventRecord(b.e, ctx->stream));
+    ZK_TRY_CUDA(cudaEventSynchronize(b.e));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a.e, b.e);
+    const double per_step = kMode == 2 ? 2.0 : 1.0;
+    *per_s = (double)threads * blocks * iters * 4 * 8 * per_step / (ms * 1e-3);
+    std::vector<unsigned long long> clk((size_t)2 * blocks);
+    ZK_TRY_CUDA(cudaMemcpy(clk.data(), clk_dev, clk.size() * 8, cudaMemcpyDeviceToHost));
+    double cyc = 0, ns = 0;
+    for (int i = 0; i < blocks; i++) {
+        cyc += (double)clk[(size_t)2 * i];
+        ns += (double)clk[(size_t)2 * i + 1];
+    }
+    *ghz = ns > 0 ? cyc / ns : 0.0;
+    return ZK_OK;
+}
+
 }  // namespace zk
 
 using namespace zk;
+
+extern "C" int zk_probe_int_pipe(int device, zk_int_pipe_rates* out) {
+    clear_error();
+    if (!out) return ZK_ERR_INVALID;
+    std::memset(out, 0, sizeof *out);
+    DeviceContext* ctx;
+    ZK_TRY(get_context(device, &ctx));
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const int blocks = ctx->num_sms * 8;
+    PoolBuffer ob, cb;
+    ZK_TRY_CUDA(ob.alloc((size_t)256 * blocks * 4, ctx->stream));
+    ZK_TRY_CUDA(cb.alloc((size_t)2 * blocks * 8, ctx->stream));
+    double ghz[3] = {0, 0, 0};
+    ZK_TRY(run_int_pipe_probe<0>(ctx, (uint32_t*)ob.p, (unsigned long long*)cb.p, &out->mad_lo_per_s, &ghz[0]));
+    ZK_TRY(run_int_pipe_probe<1>(ctx, (uint32_t*)ob.p, (unsigned long long*)cb.p, &out->mad_hi_per_s, &ghz[1]));
+    ZK_TRY(run_int_pipe_probe<2>(ctx, (uint32_t*)ob.p, (unsigned long long*)cb.p, &out->mad_pair_per_s, &ghz[2]));
+    out->num_sms = ctx->num_sms;
+    out->sm_clock_ghz = (ghz[0] + ghz[1] + ghz[2]) / 3.0;
+    const double per_clk = (double)ctx->num_sms * out->sm_clock_ghz * 1e9;
+    if (per_clk > 0) {
+        out->mad_lo_per_clk_sm = out->mad_lo_per_s / per_clk;
+        out->mad_hi_per_clk_sm = out->mad_hi_per_s / per_clk;
+        out->mad_pair_per_clk_sm = out->mad_pair_per_s / per_clk;
+    }
+    return ZK_OK;
+}
 
 extern "C" const char* zk_last_error(void) { return g_err; }
 

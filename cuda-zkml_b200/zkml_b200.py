@@ -372,6 +372,23 @@ def probe_imad_rate(device=0):
     return r.value
 
 
+class IntPipeRates(ctypes.Structure):
+    _fields_ = [("mad_lo_per_s", ctypes.c_double), ("mad_hi_per_s", ctypes.c_double), ("mad_pair_per_s", ctypes.c_double),
+                ("sm_clock_ghz", ctypes.c_double), ("mad_lo_per_clk_sm", ctypes.c_double),
+                ("mad_hi_per_clk_sm", ctypes.c_double), ("mad_pair_per_clk_sm", ctypes.c_double), ("num_sms", ctypes.c_int)]
+
+
+lib.zk_probe_int_pipe.argtypes = [ctypes.c_int, ctypes.POINTER(IntPipeRates)]
+
+
+def probe_int_pipe(device=0):
+    """Hardware issue rates of mad.lo / mad.hi / lo+hi pairs (instructions/s and
+    per clock per SM at the SM clock the probe measured)."""
+    r = IntPipeRates()
+    check(lib.zk_probe_int_pipe(device, ctypes.byref(r)))
+    return {f: getattr(r, f) for f, _ in IntPipeRates._fields_}
+
+
 # ------------------------------------------------------------------ Groth16
 ENTRY_DTYPE = np.dtype([("row", "<i4"), ("col", "<i4"), ("v", "<u8", (4,))])  # zkml::SparseEntry
 

@@ -169,6 +169,21 @@ int zk_g2_add_affine(const void* a, const void* b, void* out);
  * the MSM and NTT rooflines. */
 int zk_probe_imad_rate(int device, double* imad_per_second);
 
+/* Hardware issue rate of the 32-bit integer multiply-add on `device`, measured
+ * with no field code: independent chains of one instruction form at full
+ * occupancy.  mad_lo: mad.lo.u32; mad_hi: mad.hi.u32; mad_pair: the two halves
+ * of one 32 x 32-bit product with carry (mad.lo.cc.u32 + madc.hi.u32, counted
+ * as 2 instructions), the form every Montgomery product here is made of.  The
+ * per-clock figures use the SM clock the probe itself measured (clock64 over
+ * the global timer).  The hardware denominators of the MSM and NTT rooflines. */
+typedef struct {
+    double mad_lo_per_s, mad_hi_per_s, mad_pair_per_s;
+    double sm_clock_ghz;
+    double mad_lo_per_clk_sm, mad_hi_per_clk_sm, mad_pair_per_clk_sm;
+    int num_sms;
+} zk_int_pipe_rates;
+int zk_probe_int_pipe(int device, zk_int_pipe_rates* out);
+
 /* Statistics of the most recent MSM on the calling thread: launches of this
  * library's kernels and the device time of the bucket-accumulation kernel. */
 typedef struct {

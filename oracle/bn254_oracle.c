@@ -204,6 +204,10 @@ void orc_fr_add(orc_fe* r, const orc_fe* a, const orc_fe* b) { INIT(); madd_(&MR
 void orc_fr_sub(orc_fe* r, const orc_fe* a, const orc_fe* b) { INIT(); msub_(&MR, r->v, a->v, b->v); }
 void orc_fr_inv(orc_fe* r, const orc_fe* a) { INIT(); minv_(&MR, r->v, a->v); }
 void orc_fr_from_std(orc_fe* r, const uint64_t s[4]) { INIT(); mmul_(&MR, r->v, s, MR.r2); }
+void orc_fr_from_std_vec(uint64_t* out, const uint64_t* in, size_t n) {
+    INIT();
+    for (size_t i = 0; i < n; i++) mmul_(&MR, out + 4 * i, in + 4 * i, MR.r2);
+}
 void orc_fr_to_std(uint64_t s[4], const orc_fe* a) { INIT(); uint64_t one[4] = {1, 0, 0, 0}; mmul_(&MR, s, a->v, one); }
 void orc_fr_from_u64(orc_fe* r, uint64_t v) { uint64_t s[4] = {v, 0, 0, 0}; orc_fr_from_std(r, s); }
 void orc_fr_one(orc_fe* r) { INIT(); memcpy(r->v, MR.one, 32); }

@@ -51,6 +51,8 @@ void orc_fr_add(orc_fe* r, const orc_fe* a, const orc_fe* b);
 void orc_fr_sub(orc_fe* r, const orc_fe* a, const orc_fe* b);
 void orc_fr_inv(orc_fe* r, const orc_fe* a);
 void orc_fr_from_std(orc_fe* r, const uint64_t s[4]);
+/* n standard-form values (4 limbs each, < r) to Montgomery form */
+void orc_fr_from_std_vec(uint64_t* out, const uint64_t* in, size_t n);
 void orc_fr_to_std(uint64_t s[4], const orc_fe* a);
 void orc_fr_from_u64(orc_fe* r, uint64_t v);
 void orc_fr_one(orc_fe* r);

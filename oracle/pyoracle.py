@@ -109,6 +109,14 @@ def fp_mul(a, b):
     return o
 
 
+def fr_from_std_vector(a):
+    """(n, 4) standard-form values below r -> Montgomery form."""
+    a = np.ascontiguousarray(a, np.uint64).reshape(-1, 4)
+    out = np.zeros_like(a)
+    lib.orc_fr_from_std_vec(_p(out), _p(a), ctypes.c_size_t(a.shape[0]))
+    return out
+
+
 def fr_from_int(x):
     o = np.zeros(4, dtype=np.uint64)
     lib.orc_fr_from_std(_p(o), _p(u64(x % R)))

@@ -178,3 +178,76 @@ extern "C" void ref_msm_g1_naive_mt(uint64_t* o, int* oinf, const uint64_t* pts,
     }
     st_g1(o, oinf, acc.to_affine());
 }
+
+namespace bn254 {
+void ntt_gpu(Fr* d_out, const Fr* d_in, int log_n, bool inverse);  // src/ntt/ntt.cuh:49 (ntt_ref.o)
+}
+
+// The reference's Pippenger MSM (src/msm/msm.cu:320-442) run on the host cores
+// with the reference's own arithmetic: MSMConfig::for_size windows
+// (src/msm/msm.cuh:46-63), unsigned c-bit digits of the standard-form scalar
+// (msm.cu:122-142), zero digits and infinity points skipped, each nonzero digit
+// added into its Jacobian bucket with G1Jacobian::add_affine (msm.cu:150-152),
+// the per-window running-sum reduce (msm.cu:284-307) and the host combine with
+// c doublings per window (msm.cu:423-430).  The windows are split over
+// `nthreads` threads; the result is the canonical affine point.  This is the
+// CPU baseline of bench.py's reference arm: the reference's algorithm and
+// arithmetic without its GPU (whose buckets accumulate under unbounded spin
+// locks, msm.cu:63-72, and are not run here).
+extern "C" void ref_msm_g1_pippenger_mt(uint64_t* o, int* oinf, const uint64_t* pts, const uint64_t* sc, int n, int nthreads) {
+    const int c = n <= (1 << 10) ? 10 : n <= (1 << 14) ? 12 : n <= (1 << 18) ? 14 : n <= (1 << 22) ? 15 : 16;
+    const int W = (253 + c) / c;
+    const int nb = (1 << c) - 1;
+    std::vector<uint64_t> std_sc((size_t)n * 4);
+    for (int i = 0; i < n; i++) ld_fr(sc + 4 * i).to_standard(&std_sc[(size_t)4 * i]);
+    std::vector<G1Affine> P((size_t)n);
+    for (int i = 0; i < n; i++) {
+        const uint64_t* p = pts + 8 * i;
+        int inf = 1;
+        for (int k = 0; k < 8; k++) if (p[k]) inf = 0;
+        P[(size_t)i] = ld_g1(p, inf);
+    }
+    std::vector<G1Jacobian> win((size_t)W, G1Jacobian::identity());
+    if (nthreads < 1) nthreads = 1;
+    std::vector<std::thread> th;
+    for (int t = 0; t < nthreads; t++) {
+        th.emplace_back([&, t]() {
+            std::vector<G1Jacobian> bucket((size_t)nb);
+            const uint64_t mask = ((uint64_t)1 << c) - 1;
+            for (int w = t; w < W; w += nthreads) {
+                std::fill(bucket.begin(), bucket.end(), G1Jacobian::identity());
+                const int off = w * c, limb = off / 64, sh = off % 64;
+                for (int i = 0; i < n; i++) {
+                    if (P[(size_t)i].is_infinity()) continue;
+                    const uint64_t* s = &std_sc[(size_t)4 * i];
+                    uint64_t bits;
+                    if (limb >= 4) bits = 0;
+                    else if (sh + c <= 64) bits = (s[limb] >> sh) & mask;
+                    else if (limb + 1 < 4) bits = ((s[limb] >> sh) | (s[limb + 1] << (64 - sh))) & mask;
+                    else bits = (s[limb] >> sh) & mask;
+                    if (bits == 0) continue;
+                    bucket[(size_t)bits - 1] = bucket[(size_t)bits - 1].add_affine(P[(size_t)i]);
+                }
+                G1Jacobian running = G1Jacobian::identity(), sum = G1Jacobian::identity();
+                for (int b = nb - 1; b >= 0; b--) {
+                    if (!bucket[(size_t)b].is_infinity()) running = running + bucket[(size_t)b];
+                    sum = sum + running;
+                }
+                win[(size_t)w] = sum;
+            }
+        });
+    }
+    for (auto& x : th) x.join();
+    G1Jacobian r = G1Jacobian::identity();
+    for (int w = W - 1; w >= 0; w--) {
+        for (int i = 0; i < c; i++) r = r.dbl();
+        r = r + win[(size_t)w];
+    }
+    st_g1(o, oinf, r.to_affine());
+}
+
+// The reference's own GPU NTT entry point bn254::ntt_gpu (src/ntt/ntt.cu:354-465,
+// compiled for sm_100a from its source): device pointers, synchronous.
+extern "C" void ref_ntt_gpu(void* d_out, const void* d_in, int log_n, int inverse) {
+    bn254::ntt_gpu((bn254::Fr*)d_out, (const bn254::Fr*)d_in, log_n, inverse != 0);
+}

@@ -146,6 +146,28 @@ def test_g1_survey_variant_10pct_zero_10pct_small():
 
 
 @pytest.mark.parametrize("log_n", [20, 24])
+def test_g1_survey_variant_full_size_identity(log_n):
+    """Config 2's skewed variant (10 % zero, 10 % uniform below 2^16, the rest
+    uniform, positions shuffled) at 2^20 and 2^24 points: the identity
+    sum_i s_i (k_i G) = (sum_i s_i k_i) G, device and host entry points."""
+    n = 1 << log_n
+    k = Z.random_fr(n, 0x5EED2000 + log_n)
+    sc = Z.random_fr(n, 0x5EED3000 + log_n)
+    rng = np.random.default_rng(0x5EED0000 + log_n)
+    perm = rng.permutation(n)
+    sc[perm[: n // 10]] = 0
+    small = perm[n // 10: n // 5]
+    sc[small] = 0
+    sc[small, 0] = rng.integers(0, 1 << 16, small.size).astype(np.uint64)
+    sc[small] = O.fr_from_std_vector(sc[small])  # the small values as Montgomery Fr
+    pts = Z.g1_fixed_base(dev(k))
+    got = Z.msm_g1(pts, dev(sc))
+    exp = O.g1_fixed_base(O.fr_dot(k, sc)[None, :])[0]
+    assert np.array_equal(got, exp)
+    assert np.array_equal(Z.msm_g1(Z.to_host(pts), sc), exp)
+
+
+@pytest.mark.parametrize("log_n", [20, 24])
 def test_g1_full_size_identity(log_n):
     """sum_i s_i (k_i G) == (sum_i s_i k_i) G at the benchmark sizes."""
     n = 1 << log_n
@@ -209,6 +231,31 @@ def test_g2_full_size_identity():
     n = 1 << 18
     k = Z.random_fr(n, 41)
     sc = Z.random_fr(n, 42)
+    pts = Z.g2_fixed_base(dev(k))
+    got = Z.msm_g2(pts, dev(sc))
+    exp = O.g2_fixed_base(O.fr_dot(k, sc)[None, :])[0]
+    assert np.array_equal(got, exp)
+
+
+@pytest.mark.parametrize("scalars", ["uniform", "witness"])
+def test_g2_witness_size_identity(scalars):
+    """The G2 (B) MSM at config 5's witness size, 4,030,486 points, with
+    uniform scalars and with a witness-like mix (69 % zero, 26 % one, the
+    rest spread over small and full-width values): the identity
+    sum_i s_i (k_i G2) = (sum_i s_i k_i) G2."""
+    n = 4030486
+    k = Z.random_fr(n, 61)
+    sc = Z.random_fr(n, 62)
+    if scalars == "witness":
+        rng = np.random.default_rng(63)
+        u = rng.random(n)
+        sc[u < 0.69] = 0
+        ones = (u >= 0.69) & (u < 0.95)
+        sc[ones] = Z.fr_from_int(1)
+        small = np.flatnonzero((u >= 0.95) & (u < 0.99))
+        sc[small] = 0
+        sc[small, 0] = rng.integers(2, 1 << 20, small.size).astype(np.uint64)
+        sc[small] = O.fr_from_std_vector(sc[small])
     pts = Z.g2_fixed_base(dev(k))
     got = Z.msm_g2(pts, dev(sc))
     exp = O.g2_fixed_base(O.fr_dot(k, sc)[None, :])[0]

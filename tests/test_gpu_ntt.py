@@ -51,17 +51,22 @@ def test_coset_matches_oracle(ln):
 
 
 @pytest.mark.parametrize("ln", [20, 22, 24])
-def test_full_size_round_trip_and_spot_values(ln):
+def test_full_size_bit_exact(ln):
+    """Config 3's sizes: forward, inverse, coset forward and coset inverse
+    (g = 5) over whole vectors, bit-exact against the oracle's restatement of
+    the reference's radix-2 transform (its stages split over the host cores),
+    plus the round trip INTT(NTT(x)) = x on the device."""
     n = 1 << ln
+    cores = os.cpu_count() or 1
     x = Z.random_fr(n, 0xA000 + ln)
     d = dev(x)
     y = Z.ntt(d, ln, False)
-    back = Z.ntt(y, ln, True)
-    assert torch.equal(back, d)
-    yh = Z.to_host(y)
-    w = O.compute_omega(ln, False)
-    for k in (0, 1, n // 2 + 3, n - 1):
-        assert np.array_equal(yh[k], O.fr_poly_eval(x, O.fr_pow(w, k))), k
+    assert np.array_equal(Z.to_host(y), O.ntt(x, ln, False, nthreads=cores)), "forward"
+    assert torch.equal(Z.ntt(y, ln, True), d), "round trip"
+    assert np.array_equal(Z.to_host(Z.ntt(d, ln, True)), O.ntt(x, ln, True, nthreads=cores)), "inverse"
+    g = Z.fr_from_int(5)
+    assert np.array_equal(Z.to_host(Z.ntt(d, ln, False, coset=g)), O.coset_ntt(x, ln, False, g, nthreads=cores)), "coset forward"
+    assert np.array_equal(Z.to_host(Z.ntt(d, ln, True, coset=g)), O.coset_ntt(x, ln, True, g, nthreads=cores)), "coset inverse"
 
 
 def test_in_place_and_ranges():
