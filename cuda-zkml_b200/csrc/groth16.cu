@@ -16,9 +16,7 @@
 // evaluations at tau and the query scalars on the host, then every query point
 // k * G by the device fixed-base kernel; the points are canonical, so the key is
 // byte-identical to the reference's for the same toxic waste.
-#include "field.cuh"
-#include "host_field.hpp"
-#include "runtime.cuh"
+#include "prover.hpp"
 
 #include <algorithm>
 #include <cstdio>
@@ -111,85 +109,7 @@ static void store_aff(uint64_t* r, const zkh::Xyzz<zkh::Fp2>& p) {
     std::memcpy(r + 12, y.c1.v, 32);
 }
 
-// ------------------------------------------------------------------ R1CS
-struct SparseEntry {  // zkml::SparseEntry (src/prover/circuit.cuh:31-35)
-    int32_t row;
-    int32_t col;
-    uint64_t v[4];
-};
-static_assert(sizeof(SparseEntry) == 40, "SparseEntry layout");
-
-struct Csr {
-    std::vector<int32_t> row_ptr, col;
-    std::vector<zkh::Fe> val;
-    std::vector<int32_t> mid_rows;   // rows with kShortRow < entries <= kMidRow (ascending)
-    std::vector<int32_t> long_rows;  // rows with > kMidRow entries (ascending)
-};
-// Row lengths: up to kShortRow entries one thread per row, up to kMidRow one
-// warp per row (the 289-entry rows of a 3x3x32 convolution), beyond that one
-// block per row (dense layers).  A block per 289-entry row left most of its
-// threads idle through a synchronised shared-memory tree.
-static constexpr int kShortRow = 16;
-static constexpr int kMidRow = 2048;
-
-struct R1cs {
-    int device = -1;
-    int num_constraints = 0, m = 0, num_public = 0, log_n = 0;
-    uint64_t n = 0;
-    Csr host[3];
-    int32_t* d_row_ptr[3] = {};
-    int32_t* d_col[3] = {};
-    Fr* d_val[3] = {};
-    int32_t* d_mid[3] = {};
-    int32_t* d_long[3] = {};
-    size_t nnz[3] = {};
-};
-
 }  // namespace zk
-
-struct zk_r1cs {
-    zk::R1cs r;
-};
-
-struct zk_groth16_pk {
-    int device = -1;
-    int num_constraints = 0;  // padded domain size n, as the reference stores it (groth16.cu:621)
-    int m = 0, num_public = 0, l = 0, n_h = 0;
-    uint8_t* g1 = nullptr;  // device: A[m] | B1[m] | L[l] | H[n_h]   (64-B packed)
-    uint8_t* g2 = nullptr;  // device: B2[m]                          (128-B packed)
-    uint64_t alpha1[8], beta1[8], delta1[8];
-    uint64_t beta2[16], gamma2[16], delta2[16], g2gen[16], tau2[16];
-    std::vector<uint64_t> ic;  // (num_public + 1) x 8
-    // prover buffers
-    zk::Fr* w = nullptr;
-    zk::Fr* abc = nullptr;  // 3 n
-    zk::Fr* h = nullptr;    // n
-    unsigned long long* d_bad = nullptr;  // first failing constraint of the witness check
-    unsigned long long* h_bad = nullptr;  // pinned host copy
-    uint64_t n_buf = 0;
-    // 2^i delta1 and 2^i delta2 (i < 256), built on first use: r delta1 and
-    // s delta2 of every proof as sums of table entries
-    mutable std::mutex tab_mu;
-    mutable std::vector<zkh::Xyzz<zkh::Fe>> d1_pow;
-    mutable std::vector<zkh::Xyzz<zkh::Fp2>> d2_pow;
-    // window tables of the H query (2^(c j) H_i, j < h_W), built on first use
-    uint8_t* h_tab = nullptr;
-    int h_c = 0, h_W = 0;
-    std::mutex h_mu;
-    // private device context of the witness MSMs inside prove (created on first
-    // use), so that they run beside compute_h and the H MSM on the shared one
-    zk::DeviceContext* wctx = nullptr;
-    // per (log_parts, part): that part's H points in the "blocks" order of a
-    // proof split over 2^log_parts parts, and window tables over them; built on
-    // first use and kept until the key is destroyed (a process proving one part
-    // holds one entry; ranks emulated as threads on one device hold several)
-    struct HBlocks {
-        uint8_t* pts = nullptr;
-        uint8_t* tab = nullptr;
-        int c = 0, W = 0;
-    };
-    std::map<std::pair<int, int>, HBlocks> hb;
-};
 
 namespace zk {
 
@@ -377,7 +297,7 @@ static int r1cs_create(int device, int num_constraints, int num_variables, int n
 }
 
 // rows [lo, hi) of A w, B w, C w into out3 (three vectors of hi - lo elements)
-static int r1cs_matvec_rows(const R1cs& R, cudaStream_t st, const Fr* w, uint64_t lo, uint64_t hi, Fr* out3, int num_sms) {
+int r1cs_matvec_rows(const R1cs& R, cudaStream_t st, const Fr* w, uint64_t lo, uint64_t hi, Fr* out3, int num_sms) {
     const int rows = (int)std::min<uint64_t>(R.n, (uint64_t)R.num_constraints);
     const uint64_t len = hi - lo;
     if (len == 0) return ZK_OK;
@@ -411,14 +331,14 @@ static int r1cs_matvec(const R1cs& R, cudaStream_t st, const Fr* w, Fr* out3, in
 // constraint row r satisfies (A w)_r (B w)_r = (C w)_r.  Enqueues the check of
 // rows [row0, row0 + count) on `st`; *first_bad (device) must start at
 // 0xff..ff and ends as the first failing row, if any.
-static void enqueue_hadamard_check(cudaStream_t st, const Fr* a, const Fr* b, const Fr* c, uint64_t count, uint64_t row0,
+void enqueue_hadamard_check(cudaStream_t st, const Fr* a, const Fr* b, const Fr* c, uint64_t count, uint64_t row0,
                                    unsigned long long* first_bad, int num_sms) {
     if (!count) return;
     const unsigned grid = (unsigned)std::min<uint64_t>((count + 255) / 256, (uint64_t)num_sms * 16);
     hadamard_check_kernel<<<grid, 256, 0, st>>>(a, b, c, count, row0, first_bad);
 }
 
-static bool witness_check_enabled() {
+bool witness_check_enabled() {
     // ZKML_SKIP_WITNESS_CHECK=1 turns the check off, as in Groth16Prover::prove (groth16.cu:691-697)
     const char* e = std::getenv("ZKML_SKIP_WITNESS_CHECK");
     return !(e && std::strcmp(e, "1") == 0);
@@ -664,7 +584,7 @@ static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, s
 // points are gathered once into that order (points at or beyond n_h stay the
 // identity, all-zero), with window tables over them from 2^16 points when
 // the query covers the whole domain.
-static int h_msm_blocks(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h_part, int log_parts, int part, uint64_t out[8]) {
+int h_msm_blocks(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h_part, int log_parts, int part, uint64_t out[8]) {
     const uint64_t n = (uint64_t)pk->num_constraints;
     if (log_parts < 0 || log_parts > 3 || (n >> (2 * log_parts)) == 0 || part < 0 || part >= (1 << log_parts)) {
         set_error("H MSM blocks: %d parts of a %llu-point domain, part %d out of range", 1 << log_parts, (unsigned long long)n, part);
@@ -715,7 +635,7 @@ static int h_msm_blocks(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h_part, 
 // the witness slice [lo, hi): A, B (G2) and B1 over its points [lo, hi), L over
 // the private part of the slice (L_j pairs with w_{1 + pub + j}).  One
 // histogram and one counting sort serve the four.  *all_ms: device time.
-static int witness_msms(zk_groth16_pk* pk, DeviceContext* ctx, cudaStream_t st, const Fr* d_w, size_t lo, size_t hi, uint64_t a[8], uint64_t b[16],
+int witness_msms(zk_groth16_pk* pk, DeviceContext* ctx, cudaStream_t st, const Fr* d_w, size_t lo, size_t hi, uint64_t a[8], uint64_t b[16],
                         uint64_t b1[8], uint64_t l[8], float set_ms[4], float* all_ms) {
     const size_t m = (size_t)pk->m, pub = (size_t)pk->num_public;
     const size_t num_priv = (size_t)std::max(0, std::min(pk->l, pk->m - 1 - pk->num_public));
@@ -747,7 +667,7 @@ static int witness_msms(zk_groth16_pk* pk, DeviceContext* ctx, cudaStream_t st, 
 }
 
 // The key's private device context of the witness MSMs (created on first use).
-static int ensure_witness_context(zk_groth16_pk* pk) {
+int ensure_witness_context(zk_groth16_pk* pk) {
     std::lock_guard<std::mutex> lock(pk->h_mu);
     if (!pk->wctx) ZK_TRY(create_context(pk->device, &pk->wctx));
     return ZK_OK;
@@ -1197,6 +1117,7 @@ extern "C" void zk_groth16_pk_destroy(zk_groth16_pk* pk) {
         cudaFree(kv.second.pts);
         cudaFree(kv.second.tab);
     }
+    zk::destroy_split_states(pk);
     zk::destroy_context(pk->wctx);
     delete pk;
 }

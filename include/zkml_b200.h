@@ -357,6 +357,69 @@ int zk_groth16_precompute(zk_groth16_pk* pk, void* stream);
 int zk_groth16_assemble_parts(const zk_groth16_pk* pk, const void* r, const void* s,
                               const void* parts, int nparts, void* proof256, void* points);
 
+/* ------------------------------------------------------------------
+ * The whole prove split over several devices, in C (no counterpart in the
+ * reference, which proves on device 0 only; its caller is the zkml-prove CLI,
+ * src/cli/prove.cu:1286 -> Groth16Prover::prove, src/prover/groth16.cu:
+ * 655-920).  Every rank holds the whole proving key and R1CS on its own
+ * device and ends with the same proof bytes as zk_groth16_prove:
+ *   witness slices uploaded and all-gathered -> rows of the matvec and of the
+ *   witness check per rank -> compute_h with every transform split over the
+ *   ranks (size-n/N transform, one all-to-all, cross-rank N-point step) -> the
+ *   H MSM over each rank's coefficients, the witness MSMs over witness slices
+ *   beside it -> partial sums all-gathered, folded and assembled on every rank.
+ * N (the rank count) is a power of two up to 8 with N^2 <= n.  Peer data
+ * always lands in the receiving device's own memory before a kernel reads it.
+ * ------------------------------------------------------------------ */
+typedef struct zk_comm zk_comm;  /* one rank's communicator */
+
+/* NCCL is loaded at run time (libnccl.so.2, or $ZKML_NCCL_LIB); without it
+ * these return ZK_ERR_NODEV.  One process per GPU: rank 0 makes an id
+ * (128 bytes), every rank receives it out of band and joins. */
+int zk_comm_unique_id(void* id128);
+int zk_comm_init_rank(int device, const void* id128, int nranks, int rank, zk_comm** out);
+/* One process driving ndev devices: comms[i] is rank i on devices[i]. */
+int zk_comm_init_all(const int* devices, int ndev, zk_comm** comms);
+/* nranks ranks as host threads sharing one device (copies on the device,
+ * host barriers; no NCCL): the split prove where one GPU is at hand. */
+int zk_comm_init_local(int device, int nranks, zk_comm** comms);
+/* Ends the communicator's pending collectives (they fail); it cannot be used again. */
+int zk_comm_abort(zk_comm* comm);
+void zk_comm_destroy(zk_comm* comm);
+
+/* This rank's part of one proof (every rank calls it with the same whole host
+ * witness, r and s; each returns the proof).  pk and r1cs on the rank's
+ * device.  A rank whose call lasts longer than ZKML_SPLIT_TIMEOUT_S seconds
+ * (default 300) aborts its communicator and returns ZK_ERR_CUDA.  A witness
+ * that does not satisfy the R1CS fails on every rank with ZK_ERR_INVALID, as
+ * zk_groth16_prove does. */
+int zk_groth16_prove_split(zk_groth16_pk* pk, const zk_r1cs* r1cs, zk_comm* comm, const void* h_witness, const void* r,
+                           const void* s, void* proof256, void* points);
+
+typedef struct {
+    int nranks, rank;
+    float witness_ms;       /* this rank's witness slice upload + the all-gather (device) */
+    float matvec_ms;        /* its rows of A w, B w, C w, their check and its all-reduce */
+    float compute_h_ms;     /* the split transforms, all-to-alls included */
+    float all_to_all_ms;    /* the four all-to-alls inside compute_h_ms */
+    float h_msm_ms;         /* the H MSM over its coefficients */
+    float witness_msms_ms;  /* A, B2, B1, L over its witness slice (side stream, overlapped) */
+    float witness_wait_ms;  /* host time spent waiting for them after the H MSM */
+    float gather_ms;        /* partial sums all-gather */
+    float assemble_ms;      /* fold, blinding and serialisation on the host */
+    float total_ms;         /* the whole call, host wall time */
+} zk_split_stats;
+/* Statistics of the calling thread's last zk_groth16_prove_split. */
+int zk_groth16_split_last_stats(zk_split_stats* out);
+
+/* All ranks from one call: pks[i], r1cs[i] on comms[i]'s device (comms from
+ * zk_comm_init_all or zk_comm_init_local), one host thread per rank.  A rank
+ * that fails aborts every communicator; after timeout_s seconds (<= 0: 600)
+ * the communicators are aborted as well.  stats: NULL or nranks records. */
+int zk_groth16_prove_multi(zk_groth16_pk* const* pks, const zk_r1cs* const* r1cs, zk_comm* const* comms, int nranks,
+                           const void* h_witness, const void* r, const void* s, void* proof256, void* points,
+                           double timeout_s, zk_split_stats* stats);
+
 /* ==================================================================
  * Synthetic workloads (seeded, for benchmarks and tests)
  * ================================================================== */
