@@ -1,0 +1,567 @@
+// pairing.cpp -- the BN254 optimal ate pairing and the Groth16 verifier
+// (Groth16Verifier::verify, src/prover/groth16.cu:967-1022, over
+// verify_pairing_product, src/curve/pairing.cuh:198-282), host code with the
+// public-input sum vk_x = IC[0] + sum_i x_i IC[i+1] as an MSM on the GPU.
+//
+// Tower (the reference's, src/field/fp6.cuh, fp12.cuh): Fp2 = Fp[u]/(u^2 + 1),
+// Fp6 = Fp2[v]/(v^3 - xi) with xi = 9 + u, Fp12 = Fp6[w]/(w^2 - v).  G2 is the
+// D-type sextic twist E': y^2 = x^3 + 3/xi, untwisted by (x, y) -> (x w^2, y w^3).
+//
+// Miller loop (the optimal ate pairing of Vercauteren, "Optimal pairings",
+// 2010, for BN curves): f_{6t+2, Q}(P) over the signed binary expansion of
+// 6t + 2 (t = 4965661367192848881, the BN parameter), then the lines through
+// [6t+2]Q and pi(Q), and through that sum and -pi^2(Q), pi the p-power
+// Frobenius.  Points of the loop are kept affine (one Fp2 inversion per step:
+// a verifier runs four loops per proof, so clarity wins over speed here).  The
+// line through T with slope l (on the twist), evaluated at P = (xP, yP), is
+//   yP - l xP w + (l xT - yT) w^3,
+// vertical lines omitted (they lie in a proper subfield and vanish under the
+// final exponentiation).
+//
+// Final exponentiation f^((p^12 - 1)/r) = f^((p^6 - 1)(p^2 + 1) d) with the
+// hard part d = (p^4 - p^2 + 1)/r written in base p (Scott, Benger, Charlemagne,
+// Dominguez Perez, Kachisa, "On the final exponentiation for calculating
+// pairings on ordinary elliptic curves", 2009):
+//   d = l0 + l1 p + l2 p^2 + p^3,  l2 = 6t^2 + 1,
+//   l1 = -36t^3 - 18t^2 - 12t + 1,  l0 = -36t^3 - 30t^2 - 18t - 2,
+// checked at start-up against d r = p^4 - p^2 + 1.  The result is exactly the
+// reduced pairing value (the reference raises to the same exponent in one
+// chain), so pairing values compare bit for bit.  Every constant (the Frobenius
+// coefficients xi^(i (p - 1)/6), the loop digits, the l_i) is derived here
+// from p, xi and t.
+#include "host_field.hpp"
+#include "runtime.cuh"
+
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+namespace zkp {
+
+using zkh::Fe;
+using zkh::Fp2;
+
+// ---------------------------------------------------------------- Fp2 extras
+static Fp2 f2(const Fe& a, const Fe& b) { Fp2 r; r.c0 = a; r.c1 = b; return r; }
+static Fp2 add(const Fp2& a, const Fp2& b) { Fp2 r; zkh::fadd(r, a, b); return r; }
+static Fp2 sub(const Fp2& a, const Fp2& b) { Fp2 r; zkh::fsub(r, a, b); return r; }
+static Fp2 mul(const Fp2& a, const Fp2& b) { Fp2 r; zkh::fmul(r, a, b); return r; }
+static Fp2 sqr(const Fp2& a) { return mul(a, a); }
+static Fp2 neg(const Fp2& a) { Fp2 z; zkh::fset_zero(z); return sub(z, a); }
+static Fp2 inv(const Fp2& a) { Fp2 r; zkh::finv(r, a); return r; }
+static Fp2 conj(const Fp2& a) { Fp2 r; r.c0 = a.c0; zkh::fsub(r.c1, zkh::zero(), a.c1); return r; }
+static Fp2 mul_fp(const Fp2& a, const Fe& s) { Fp2 r; zkh::fmul(r.c0, a.c0, s); zkh::fmul(r.c1, a.c1, s); return r; }
+static Fp2 one2() { Fp2 r; zkh::fset_one(r); return r; }
+static Fp2 zero2() { Fp2 r; zkh::fset_zero(r); return r; }
+static bool eq(const Fp2& a, const Fp2& b) { return zkh::eq(a.c0, b.c0) && zkh::eq(a.c1, b.c1); }
+static Fe fp_small(uint64_t v) {
+    uint64_t s[4] = {v, 0, 0, 0};
+    Fe r;
+    zkh::from_std(zkh::kP, r, s);
+    return r;
+}
+// xi = 9 + u
+static Fp2 xi() { return f2(fp_small(9), fp_small(1)); }
+static Fp2 mul_xi(const Fp2& a) { return mul(a, xi()); }
+static Fp2 pow2(const Fp2& a, const uint64_t e[4]) {
+    Fp2 acc = one2();
+    for (int bit = 255; bit >= 0; bit--) {
+        acc = sqr(acc);
+        if ((e[bit >> 6] >> (bit & 63)) & 1) acc = mul(acc, a);
+    }
+    return acc;
+}
+
+// ---------------------------------------------------------------- Fp6, Fp12
+struct Fp6 {
+    Fp2 c0, c1, c2;
+};
+static Fp6 add(const Fp6& a, const Fp6& b) { return {add(a.c0, b.c0), add(a.c1, b.c1), add(a.c2, b.c2)}; }
+static Fp6 sub(const Fp6& a, const Fp6& b) { return {sub(a.c0, b.c0), sub(a.c1, b.c1), sub(a.c2, b.c2)}; }
+static Fp6 neg(const Fp6& a) { return {neg(a.c0), neg(a.c1), neg(a.c2)}; }
+static Fp6 mul(const Fp6& a, const Fp6& b) {
+    // v^3 = xi
+    const Fp2 a0b0 = mul(a.c0, b.c0), a1b1 = mul(a.c1, b.c1), a2b2 = mul(a.c2, b.c2);
+    const Fp2 r0 = add(a0b0, mul_xi(add(mul(a.c1, b.c2), mul(a.c2, b.c1))));
+    const Fp2 r1 = add(add(mul(a.c0, b.c1), mul(a.c1, b.c0)), mul_xi(a2b2));
+    const Fp2 r2 = add(add(mul(a.c0, b.c2), a1b1), mul(a.c2, b.c0));
+    return {r0, r1, r2};
+}
+static Fp6 mul_v(const Fp6& a) { return {mul_xi(a.c2), a.c0, a.c1}; }
+static Fp6 one6() { return {one2(), zero2(), zero2()}; }
+static Fp6 inv(const Fp6& a) {
+    const Fp2 A = sub(sqr(a.c0), mul_xi(mul(a.c1, a.c2)));
+    const Fp2 B = sub(mul_xi(sqr(a.c2)), mul(a.c0, a.c1));
+    const Fp2 C = sub(sqr(a.c1), mul(a.c0, a.c2));
+    const Fp2 F = add(mul(a.c0, A), mul_xi(add(mul(a.c2, B), mul(a.c1, C))));
+    const Fp2 Fi = inv(F);
+    return {mul(A, Fi), mul(B, Fi), mul(C, Fi)};
+}
+
+struct Fp12 {
+    Fp6 c0, c1;
+};
+static Fp12 mul(const Fp12& a, const Fp12& b) {  // w^2 = v
+    return {add(mul(a.c0, b.c0), mul_v(mul(a.c1, b.c1))), add(mul(a.c0, b.c1), mul(a.c1, b.c0))};
+}
+static Fp12 sqr(const Fp12& a) { return mul(a, a); }
+static Fp12 conj(const Fp12& a) { return {a.c0, neg(a.c1)}; }
+static Fp12 one12() { return {one6(), {zero2(), zero2(), zero2()}}; }
+static Fp12 inv(const Fp12& a) {  // (c0 - c1 w) / (c0^2 - v c1^2)
+    const Fp6 d = inv(sub(mul(a.c0, a.c0), mul_v(mul(a.c1, a.c1))));
+    return {mul(a.c0, d), neg(mul(a.c1, d))};
+}
+static bool eq(const Fp12& a, const Fp12& b) {
+    const Fp2* x = &a.c0.c0;
+    const Fp2* y = &b.c0.c0;
+    for (int i = 0; i < 6; i++)
+        if (!eq(x[i], y[i])) return false;
+    return true;
+}
+
+// ---------------------------------------------------------------- derived constants
+struct Consts {
+    Fp2 gamma[6];          // xi^(i (p - 1)/6): (w^i)^p = w^i gamma[i]
+    std::vector<int> naf;  // signed digits of 6t + 2, least significant first
+    uint64_t l0[4], l1[4], l2[4];  // |l0|, |l1|, l2 (l0, l1 < 0)
+    bool ok = false;
+};
+
+// little helpers on multi-limb unsigned integers (up to 17 limbs)
+static void mul_small(uint64_t* r, const uint64_t* a, int n, uint64_t k) {
+    unsigned __int128 c = 0;
+    for (int i = 0; i < n; i++) {
+        c += (unsigned __int128)a[i] * k;
+        r[i] = (uint64_t)c;
+        c >>= 64;
+    }
+}
+static void add_n(uint64_t* r, const uint64_t* a, const uint64_t* b, int n) {
+    unsigned __int128 c = 0;
+    for (int i = 0; i < n; i++) {
+        c += (unsigned __int128)a[i] + b[i];
+        r[i] = (uint64_t)c;
+        c >>= 64;
+    }
+}
+static void sub_n(uint64_t* r, const uint64_t* a, const uint64_t* b, int n) {
+    uint64_t br = 0;
+    for (int i = 0; i < n; i++) {
+        unsigned __int128 d = (unsigned __int128)a[i] - b[i] - br;
+        r[i] = (uint64_t)d;
+        br = (uint64_t)(d >> 64) & 1;
+    }
+}
+static void mul_n(uint64_t* r, const uint64_t* a, int na, const uint64_t* b, int nb) {  // r: na + nb limbs
+    std::memset(r, 0, (size_t)(na + nb) * 8);
+    for (int i = 0; i < na; i++) {
+        unsigned __int128 c = 0;
+        for (int j = 0; j < nb; j++) {
+            c += (unsigned __int128)a[i] * b[j] + r[i + j];
+            r[i + j] = (uint64_t)c;
+            c >>= 64;
+        }
+        r[i + nb] = (uint64_t)c;
+    }
+}
+
+static const uint64_t kT = 4965661367192848881ull;  // the BN parameter of BN254
+
+static Consts make_consts() {
+    Consts C;
+    // gamma[i] = xi^(i (p - 1)/6)
+    uint64_t e[4];
+    std::memcpy(e, zkh::kP.m, 32);
+    e[0] -= 1;  // p - 1 (p odd)
+    // divide by 6
+    unsigned __int128 rem = 0;
+    for (int i = 3; i >= 0; i--) {
+        unsigned __int128 cur = (rem << 64) | e[i];
+        e[i] = (uint64_t)(cur / 6);
+        rem = cur % 6;
+    }
+    if (rem != 0) return C;
+    const Fp2 g1 = pow2(xi(), e);
+    C.gamma[0] = one2();
+    for (int i = 1; i < 6; i++) C.gamma[i] = mul(C.gamma[i - 1], g1);
+    // NAF of 6t + 2
+    {
+        uint64_t s[2];
+        unsigned __int128 v = (unsigned __int128)kT * 6 + 2;
+        s[0] = (uint64_t)v;
+        s[1] = (uint64_t)(v >> 64);
+        unsigned __int128 k = ((unsigned __int128)s[1] << 64) | s[0];
+        while (k) {
+            int d = 0;
+            if (k & 1) {
+                d = 2 - (int)(k & 3);  // 1 or -1
+                if (d == 1) k -= 1; else k += 1;
+            }
+            C.naf.push_back(d);
+            k >>= 1;
+        }
+    }
+    // l2 = 6t^2 + 1, |l1| = 36t^3 + 18t^2 + 12t - 1, |l0| = 36t^3 + 30t^2 + 18t + 2
+    uint64_t t[4] = {kT, 0, 0, 0}, t2[8], t3[8], a[4], b[4];
+    mul_n(t2, t, 1, t, 1);  // 2 limbs
+    mul_n(t3, t2, 2, t, 1); // 3 limbs
+    for (int i = 2; i < 4; i++) t2[i] = 0;
+    t3[3] = 0;
+    uint64_t one[4] = {1, 0, 0, 0}, two[4] = {2, 0, 0, 0};
+    mul_small(C.l2, t2, 4, 6);
+    add_n(C.l2, C.l2, one, 4);
+    mul_small(a, t3, 4, 36);
+    mul_small(b, t2, 4, 18);
+    add_n(a, a, b, 4);
+    mul_small(b, t, 4, 12);
+    add_n(a, a, b, 4);
+    sub_n(C.l1, a, one, 4);
+    mul_small(a, t3, 4, 36);
+    mul_small(b, t2, 4, 30);
+    add_n(a, a, b, 4);
+    mul_small(b, t, 4, 18);
+    add_n(a, a, b, 4);
+    add_n(C.l0, a, two, 4);
+    // check d r = p^4 - p^2 + 1 with d = p^3 + l2 p^2 - |l1| p - |l0| (p^4 < 2^1016: 17 limbs)
+    const int W = 17;
+    uint64_t p1[W] = {}, p2[W] = {}, p3[W] = {}, p4[W] = {}, tmp[2 * W];
+    std::memcpy(p1, zkh::kP.m, 32);
+    mul_n(tmp, p1, 4, p1, 4);
+    std::memcpy(p2, tmp, 8 * 8);
+    mul_n(tmp, p2, 8, p1, 4);
+    std::memcpy(p3, tmp, 12 * 8);
+    mul_n(tmp, p2, 8, p2, 8);
+    std::memcpy(p4, tmp, 16 * 8);
+    uint64_t d[W] = {}, u[W] = {};
+    std::memcpy(d, p3, sizeof d);
+    mul_n(tmp, p2, 8, C.l2, 4);
+    std::memcpy(u, tmp, 12 * 8);
+    add_n(d, d, u, W);
+    mul_n(tmp, p1, 4, C.l1, 4);
+    std::memset(u, 0, sizeof u);
+    std::memcpy(u, tmp, 8 * 8);
+    sub_n(d, d, u, W);
+    std::memset(u, 0, sizeof u);
+    std::memcpy(u, C.l0, 32);
+    sub_n(d, d, u, W);
+    uint64_t r[W] = {}, lhs[2 * W], rhs[W];
+    std::memcpy(r, zkh::kR.m, 32);
+    mul_n(lhs, d, W, r, 4);  // d r (fits in 13 limbs)
+    std::memcpy(rhs, p4, sizeof rhs);
+    sub_n(rhs, rhs, p2, W);
+    uint64_t o[W] = {1};
+    add_n(rhs, rhs, o, W);
+    C.ok = std::memcmp(lhs, rhs, sizeof rhs) == 0;
+    for (int i = W; i < W + 4; i++) C.ok = C.ok && lhs[i] == 0;
+    return C;
+}
+
+static const Consts& consts() {
+    static std::once_flag once;
+    static Consts C;
+    std::call_once(once, [] { C = make_consts(); });
+    return C;
+}
+
+// ---------------------------------------------------------------- Frobenius, exponentiation
+static Fp12 frob(const Fp12& a) {
+    const Consts& C = consts();
+    // coefficient of w^i: i = 0, 2, 4 in c0 (c0, c1, c2), i = 1, 3, 5 in c1
+    Fp12 r;
+    r.c0.c0 = mul(conj(a.c0.c0), C.gamma[0]);
+    r.c0.c1 = mul(conj(a.c0.c1), C.gamma[2]);
+    r.c0.c2 = mul(conj(a.c0.c2), C.gamma[4]);
+    r.c1.c0 = mul(conj(a.c1.c0), C.gamma[1]);
+    r.c1.c1 = mul(conj(a.c1.c1), C.gamma[3]);
+    r.c1.c2 = mul(conj(a.c1.c2), C.gamma[5]);
+    return r;
+}
+static Fp12 pow12(const Fp12& a, const uint64_t e[4]) {
+    Fp12 acc = one12();
+    int top = 255;
+    while (top >= 0 && !((e[top >> 6] >> (top & 63)) & 1)) top--;
+    for (int bit = top; bit >= 0; bit--) {
+        acc = sqr(acc);
+        if ((e[bit >> 6] >> (bit & 63)) & 1) acc = mul(acc, a);
+    }
+    return acc;
+}
+static Fp12 final_exp(const Fp12& f) {
+    const Consts& C = consts();
+    Fp12 m = mul(conj(f), inv(f));  // f^(p^6 - 1)
+    m = mul(frob(frob(m)), m);       // ^(p^2 + 1)
+    const Fp12 a = conj(pow12(m, C.l0));
+    const Fp12 b = conj(pow12(frob(m), C.l1));
+    const Fp12 c = pow12(frob(frob(m)), C.l2);
+    const Fp12 d = frob(frob(frob(m)));
+    return mul(mul(a, b), mul(c, d));
+}
+
+// ---------------------------------------------------------------- Miller loop
+struct G1a {
+    Fe x, y;
+    bool inf;
+};
+struct G2a {
+    Fp2 x, y;
+    bool inf;
+};
+
+// the line with slope l through (xT, yT) on the twist, at P
+static Fp12 line(const Fp2& l, const Fp2& xT, const Fp2& yT, const G1a& P) {
+    Fp12 r = {{zero2(), zero2(), zero2()}, {zero2(), zero2(), zero2()}};
+    r.c0.c0 = f2(P.y, zkh::zero());
+    r.c1.c0 = neg(mul_fp(l, P.x));
+    r.c1.c1 = sub(mul(l, xT), yT);
+    return r;
+}
+// T <- 2T, returns the tangent line at T
+static Fp12 dbl_step(G2a& T, const G1a& P) {
+    const Fp2 x2 = sqr(T.x);
+    const Fp2 l = mul(add(add(x2, x2), x2), inv(add(T.y, T.y)));
+    const Fp12 ln = line(l, T.x, T.y, P);
+    const Fp2 x3 = sub(sub(sqr(l), T.x), T.x);
+    T.y = sub(mul(l, sub(T.x, x3)), T.y);
+    T.x = x3;
+    return ln;
+}
+// T <- T + Q, returns the line through T and Q
+static Fp12 add_step(G2a& T, const G2a& Q, const G1a& P) {
+    const Fp2 l = mul(sub(Q.y, T.y), inv(sub(Q.x, T.x)));
+    const Fp12 ln = line(l, T.x, T.y, P);
+    const Fp2 x3 = sub(sub(sqr(l), T.x), Q.x);
+    T.y = sub(mul(l, sub(T.x, x3)), T.y);
+    T.x = x3;
+    return ln;
+}
+static G2a frob_g2(const G2a& Q) {
+    const Consts& C = consts();
+    return {mul(conj(Q.x), C.gamma[2]), mul(conj(Q.y), C.gamma[3]), Q.inf};
+}
+
+// prod_k f_{6t+2, Q_k}(P_k) (with the two Frobenius lines), pairs with an
+// infinite point skipped (their pairing is 1)
+static Fp12 multi_miller(const G1a* P, const G2a* Q, int n) {
+    const Consts& C = consts();
+    std::vector<G2a> T;
+    std::vector<int> idx;
+    for (int k = 0; k < n; k++)
+        if (!P[k].inf && !Q[k].inf) {
+            T.push_back(Q[k]);
+            idx.push_back(k);
+        }
+    Fp12 f = one12();
+    const int top = (int)C.naf.size() - 1;
+    for (int i = top - 1; i >= 0; i--) {
+        f = sqr(f);
+        for (size_t j = 0; j < T.size(); j++) f = mul(f, dbl_step(T[j], P[idx[j]]));
+        if (C.naf[(size_t)i] != 0) {
+            for (size_t j = 0; j < T.size(); j++) {
+                G2a q = Q[idx[j]];
+                if (C.naf[(size_t)i] < 0) q.y = neg(q.y);
+                f = mul(f, add_step(T[j], q, P[idx[j]]));
+            }
+        }
+    }
+    for (size_t j = 0; j < T.size(); j++) {
+        const G2a q1 = frob_g2(Q[idx[j]]);
+        G2a q2 = frob_g2(q1);
+        q2.y = neg(q2.y);
+        f = mul(f, add_step(T[j], q1, P[idx[j]]));
+        f = mul(f, add_step(T[j], q2, P[idx[j]]));
+    }
+    return f;
+}
+
+static G1a load_g1(const uint64_t* w) {
+    G1a p;
+    std::memcpy(p.x.v, w, 32);
+    std::memcpy(p.y.v, w + 4, 32);
+    p.inf = zkh::is_zero(p.x) && zkh::is_zero(p.y);
+    return p;
+}
+static G2a load_g2(const uint64_t* w) {
+    G2a q;
+    std::memcpy(q.x.c0.v, w, 32);
+    std::memcpy(q.x.c1.v, w + 4, 32);
+    std::memcpy(q.y.c0.v, w + 8, 32);
+    std::memcpy(q.y.c1.v, w + 12, 32);
+    q.inf = zkh::fis_zero(q.x) && zkh::fis_zero(q.y);
+    return q;
+}
+
+}  // namespace zkp
+
+// ================================================================== C ABI (pairing, verifier)
+using namespace zk;
+
+struct zk_groth16_vk {
+    int num_public = 0;
+    uint64_t alpha1[8], beta2[16], gamma2[16], delta2[16];
+    std::vector<uint64_t> ic;  // (num_public + 1) x 8 packed affine, Montgomery
+};
+
+static int consts_ok() {
+    if (!zkp::consts().ok) {
+        set_error("pairing: derived final-exponentiation constants failed their check");
+        return ZK_ERR_INVALID;
+    }
+    return ZK_OK;
+}
+
+extern "C" int zk_bn254_pairing(const void* p64, const void* q128, void* out_fp12) {
+    clear_error();
+    if (!p64 || !q128 || !out_fp12) return ZK_ERR_INVALID;
+    ZK_TRY(consts_ok());
+    const zkp::G1a P = zkp::load_g1((const uint64_t*)p64);
+    const zkp::G2a Q = zkp::load_g2((const uint64_t*)q128);
+    const zkp::Fp12 e = zkp::final_exp(zkp::multi_miller(&P, &Q, 1));
+    std::memcpy(out_fp12, &e, sizeof e);  // c0.c0 c0.c1 c0.c2 c1.c0 c1.c1 c1.c2, each Fp2 (c0, c1)
+    return ZK_OK;
+}
+
+extern "C" int zk_bn254_pairing_check(const void* p64s, const void* q128s, int n, int* holds) {
+    clear_error();
+    if (!holds || n < 0 || (n && (!p64s || !q128s))) return ZK_ERR_INVALID;
+    ZK_TRY(consts_ok());
+    std::vector<zkp::G1a> P((size_t)n);
+    std::vector<zkp::G2a> Q((size_t)n);
+    for (int i = 0; i < n; i++) {
+        P[(size_t)i] = zkp::load_g1((const uint64_t*)p64s + (size_t)i * 8);
+        Q[(size_t)i] = zkp::load_g2((const uint64_t*)q128s + (size_t)i * 16);
+    }
+    *holds = zkp::eq(zkp::final_exp(zkp::multi_miller(P.data(), Q.data(), n)), zkp::one12()) ? 1 : 0;
+    return ZK_OK;
+}
+
+static void std_to_mont_fp(uint64_t* w, int fe_count) {
+    for (int i = 0; i < fe_count; i++) {
+        zkh::Fe f;
+        zkh::from_std(zkh::kP, f, w + 4 * i);
+        std::memcpy(w + 4 * i, f.v, 32);
+    }
+}
+
+extern "C" int zk_groth16_vk_load(const char* path, zk_groth16_vk** out) {
+    clear_error();
+    if (!path || !out) return ZK_ERR_INVALID;
+    *out = nullptr;
+    FILE* f = fopen(path, "rb");
+    if (!f) { set_error("vk_load: cannot open %s", path); return ZK_ERR_INVALID; }
+    auto rd = [&](void* p, size_t n) { return fread(p, 1, n, f) == n; };
+    zk_groth16_vk* vk = new zk_groth16_vk();
+    int32_t pub = 0, nic = 0;
+    bool ok = rd(&pub, 4) && pub >= 0 && pub < (1 << 28) && rd(vk->alpha1, 64) && rd(vk->beta2, 128) && rd(vk->gamma2, 128) &&
+              rd(vk->delta2, 128) && rd(&nic, 4) && nic >= 0 && nic < (1 << 28);
+    if (ok) {
+        vk->ic.resize((size_t)nic * 8);
+        ok = rd(vk->ic.data(), (size_t)nic * 64);
+    }
+    fclose(f);
+    if (!ok) {
+        set_error("vk_load: %s is not a complete vk.bin", path);
+        delete vk;
+        return ZK_ERR_INVALID;
+    }
+    vk->num_public = pub;
+    std_to_mont_fp(vk->alpha1, 2);
+    std_to_mont_fp(vk->beta2, 4);
+    std_to_mont_fp(vk->gamma2, 4);
+    std_to_mont_fp(vk->delta2, 4);
+    std_to_mont_fp(vk->ic.data(), 2 * nic);
+    *out = vk;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_vk_from_pk(const zk_groth16_pk* pk, zk_groth16_vk** out) {
+    clear_error();
+    if (!pk || !out) return ZK_ERR_INVALID;
+    *out = nullptr;
+    const int nic = zk_groth16_vk_points(pk, nullptr, nullptr, nullptr, nullptr, nullptr, 0);
+    if (nic <= 0) {
+        set_error("vk_from_pk: this proving key carries no verification key (loaded from a file)");
+        return ZK_ERR_INVALID;
+    }
+    zk_groth16_vk* vk = new zk_groth16_vk();
+    vk->ic.resize((size_t)nic * 8);
+    zk_groth16_vk_points(pk, vk->alpha1, vk->beta2, vk->gamma2, vk->delta2, vk->ic.data(), nic);
+    vk->num_public = nic - 1;
+    *out = vk;
+    return ZK_OK;
+}
+
+extern "C" void zk_groth16_vk_destroy(zk_groth16_vk* vk) { delete vk; }
+
+extern "C" int zk_groth16_vk_num_public(const zk_groth16_vk* vk) { return vk ? vk->num_public : -1; }
+
+// 256-byte proof -> packed Montgomery A (8 words), B (16), C (8)
+static void parse_proof(const uint8_t* in, uint64_t A[8], uint64_t B[16], uint64_t C[8]) {
+    uint64_t* dst[8] = {A, A + 4, B, B + 4, B + 8, B + 12, C, C + 4};
+    for (int k = 0; k < 8; k++) {
+        uint64_t s[4];
+        std::memcpy(s, in + 32 * k, 32);
+        zkh::Fe f;
+        zkh::from_std(zkh::kP, f, s);
+        std::memcpy(dst[k], f.v, 32);
+    }
+}
+
+extern "C" int zk_groth16_verify(const zk_groth16_vk* vk, int device, const void* public_inputs, int num_public, const void* proof256,
+                                 int* valid) {
+    clear_error();
+    if (!vk || !valid || !proof256 || num_public < 0 || (num_public && !public_inputs)) return ZK_ERR_INVALID;
+    *valid = 0;
+    ZK_TRY(consts_ok());
+    if (num_public != vk->num_public || vk->ic.size() != (size_t)(num_public + 1) * 8) return ZK_OK;  // groth16.cu:976-980
+    // vk_x = IC[0] + sum_i x_i IC[i + 1]
+    uint64_t sum[8] = {0};
+    if (num_public > 0) {
+        if (device >= 0) {
+            ZK_TRY(zk_msm_g1_host(device, nullptr, vk->ic.data() + 8, public_inputs, (size_t)num_public, sum));
+        } else {  // host: the reference's own loop (scalar multiplications one by one)
+            zkh::Xyzz<zkh::Fe> acc, t, p;
+            zkh::set_identity(acc);
+            for (int i = 0; i < num_public; i++) {
+                const uint64_t* q = vk->ic.data() + (size_t)(i + 1) * 8;
+                bool inf = true;
+                for (int k = 0; k < 8; k++) if (q[k]) inf = false;
+                if (inf) continue;
+                zkh::Fe x, y, s;
+                std::memcpy(x.v, q, 32);
+                std::memcpy(y.v, q + 4, 32);
+                zkh::from_affine(p, x, y);
+                std::memcpy(s.v, (const uint64_t*)public_inputs + 4 * i, 32);
+                uint64_t k_std[4];
+                zkh::to_std(zkh::kR, k_std, s);
+                zkh::smul(t, p, k_std);
+                zkh::add(acc, t);
+            }
+            zkh::Fe x, y;
+            if (zkh::to_affine(x, y, acc)) {
+                std::memcpy(sum, x.v, 32);
+                std::memcpy(sum + 4, y.v, 32);
+            }
+        }
+    }
+    uint64_t vkx[8];
+    ZK_TRY(zk_g1_add_affine(vk->ic.data(), sum, vkx));
+    uint64_t A[8], B[16], C[8];
+    parse_proof((const uint8_t*)proof256, A, B, C);
+    // e(-A, B) e(alpha, beta) e(vk_x, gamma) e(C, delta) == 1
+    uint64_t P[4][8], Q[4][16];
+    std::memcpy(P[0], A, 64);
+    {
+        zkh::Fe y;
+        std::memcpy(y.v, A + 4, 32);
+        if (!zkh::is_zero(y)) zkh::fsub(y, zkh::zero(), y);
+        std::memcpy(P[0] + 4, y.v, 32);
+    }
+    std::memcpy(P[1], vk->alpha1, 64);
+    std::memcpy(P[2], vkx, 64);
+    std::memcpy(P[3], C, 64);
+    std::memcpy(Q[0], B, 128);
+    std::memcpy(Q[1], vk->beta2, 128);
+    std::memcpy(Q[2], vk->gamma2, 128);
+    std::memcpy(Q[3], vk->delta2, 128);
+    return zk_bn254_pairing_check(P, Q, 4, valid);
+}

@@ -24,8 +24,8 @@
 // driving several GPUs with a host thread each), or ranks as host threads
 // sharing one device (copies on the device, host barriers) for testing the
 // split where only one GPU is at hand.  No kernel waits on another rank: every
-// exchange is an NCCL operation or a stream-ordered copy, and no TMA multicast
-// exists in this library.
+// exchange is an NCCL operation or a stream-ordered copy into the receiving
+// device's own memory, and no kernel reads a peer's memory.
 #include "prover.hpp"
 
 #include <dlfcn.h>

@@ -586,6 +586,171 @@ class ProvingKey:
             self.h = None
 
 
+# ------------------------------------------------------------------ split prove (C, several devices)
+class SplitStats(ctypes.Structure):
+    _fields_ = [("nranks", ctypes.c_int), ("rank", ctypes.c_int), ("witness_ms", ctypes.c_float), ("matvec_ms", ctypes.c_float),
+                ("compute_h_ms", ctypes.c_float), ("all_to_all_ms", ctypes.c_float), ("h_msm_ms", ctypes.c_float),
+                ("witness_msms_ms", ctypes.c_float), ("witness_wait_ms", ctypes.c_float), ("gather_ms", ctypes.c_float),
+                ("assemble_ms", ctypes.c_float), ("total_ms", ctypes.c_float)]
+
+    def as_dict(self):
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
+
+lib.zk_comm_unique_id.argtypes = [_vp]
+lib.zk_comm_init_rank.argtypes = [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]
+lib.zk_comm_init_all.argtypes = [_vp, ctypes.c_int, _vp]
+lib.zk_comm_init_local.argtypes = [ctypes.c_int, ctypes.c_int, _vp]
+lib.zk_comm_abort.argtypes = [_vp]
+lib.zk_comm_destroy.argtypes = [_vp]
+lib.zk_comm_destroy.restype = None
+lib.zk_groth16_prove_split.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
+lib.zk_groth16_split_last_stats.argtypes = [ctypes.POINTER(SplitStats)]
+lib.zk_groth16_prove_multi.argtypes = [_vp, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, ctypes.c_double, _vp]
+
+
+class Comm:
+    """One rank's communicator for zk_groth16_prove_split (zk_comm)."""
+
+    def __init__(self, handle, keep=None):
+        self.h = handle
+        self._keep = keep
+
+    @staticmethod
+    def unique_id():
+        """128-byte NCCL id (rank 0 makes it; the others receive it out of band)."""
+        buf = (ctypes.c_uint8 * 128)()
+        check(lib.zk_comm_unique_id(ctypes.cast(buf, _vp)))
+        return bytes(buf)
+
+    @classmethod
+    def init_rank(cls, device, uid, nranks, rank):
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+        h = _vp()
+        check(lib.zk_comm_init_rank(device, ctypes.cast(buf, _vp), nranks, rank, ctypes.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def init_all(cls, devices):
+        arr = (ctypes.c_int * len(devices))(*devices)
+        hs = (_vp * len(devices))()
+        check(lib.zk_comm_init_all(ctypes.cast(arr, _vp), len(devices), ctypes.cast(hs, _vp)))
+        return [cls(_vp(h)) for h in hs]
+
+    @classmethod
+    def init_local(cls, device, nranks):
+        """nranks ranks as host threads sharing one device (no NCCL)."""
+        hs = (_vp * nranks)()
+        check(lib.zk_comm_init_local(device, nranks, ctypes.cast(hs, _vp)))
+        return [cls(_vp(h)) for h in hs]
+
+    def abort(self):
+        check(lib.zk_comm_abort(self.h))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.zk_comm_destroy(self.h)
+            self.h = None
+
+
+def prove_split(pk, r1cs, comm, witness, r, s):
+    """This rank's part of a proof split over comm's ranks (zk_groth16_prove_split):
+    (proof bytes, A, B, C, per-phase statistics)."""
+    witness = np.ascontiguousarray(witness, dtype=np.uint64)
+    rr, ss = fr_from_int(r), fr_from_int(s)
+    proof = np.zeros(256, np.uint8)
+    pts = np.zeros(32, np.uint64)
+    check(lib.zk_groth16_prove_split(pk.h, r1cs.h, comm.h, _np_ptr(witness), _np_ptr(rr), _np_ptr(ss), _np_ptr(proof), _np_ptr(pts)))
+    st = SplitStats()
+    lib.zk_groth16_split_last_stats(ctypes.byref(st))
+    return proof.tobytes(), pts[:8], pts[8:24], pts[24:32], st.as_dict()
+
+
+def prove_multi(pks, r1css, comms, witness, r, s, timeout_s=600.0):
+    """All ranks from this thread (zk_groth16_prove_multi): (proof bytes, A, B, C,
+    list of per-rank statistics)."""
+    n = len(comms)
+    witness = np.ascontiguousarray(witness, dtype=np.uint64)
+    rr, ss = fr_from_int(r), fr_from_int(s)
+    proof = np.zeros(256, np.uint8)
+    pts = np.zeros(32, np.uint64)
+    pk_arr = (_vp * n)(*[p.h for p in pks])
+    r1_arr = (_vp * n)(*[x.h for x in r1css])
+    cm_arr = (_vp * n)(*[c.h for c in comms])
+    stats = (SplitStats * n)()
+    check(lib.zk_groth16_prove_multi(ctypes.cast(pk_arr, _vp), ctypes.cast(r1_arr, _vp), ctypes.cast(cm_arr, _vp), n,
+                                     _np_ptr(witness), _np_ptr(rr), _np_ptr(ss), _np_ptr(proof), _np_ptr(pts), timeout_s,
+                                     ctypes.cast(stats, _vp)))
+    return proof.tobytes(), pts[:8], pts[8:24], pts[24:32], [x.as_dict() for x in stats]
+
+
+# ------------------------------------------------------------------ verifier
+lib.zk_bn254_pairing.argtypes = [_vp, _vp, _vp]
+lib.zk_bn254_pairing_check.argtypes = [_vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+lib.zk_groth16_vk_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
+lib.zk_groth16_vk_from_pk.argtypes = [_vp, ctypes.POINTER(_vp)]
+lib.zk_groth16_vk_destroy.argtypes = [_vp]
+lib.zk_groth16_vk_destroy.restype = None
+lib.zk_groth16_vk_num_public.argtypes = [_vp]
+lib.zk_groth16_verify.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.POINTER(ctypes.c_int)]
+
+
+def bn254_pairing(p, q):
+    """e(P, Q): packed G1 (8 words) and G2 (16 words) Montgomery -> (12, 4) uint64 Fp12."""
+    p = np.ascontiguousarray(p, np.uint64)
+    q = np.ascontiguousarray(q, np.uint64)
+    out = np.zeros((12, 4), np.uint64)
+    check(lib.zk_bn254_pairing(_np_ptr(p), _np_ptr(q), _np_ptr(out)))
+    return out
+
+
+def pairing_check(ps, qs):
+    """prod_i e(P_i, Q_i) == 1 ?"""
+    ps = np.ascontiguousarray(ps, np.uint64).reshape(-1, 8)
+    qs = np.ascontiguousarray(qs, np.uint64).reshape(-1, 16)
+    ok = ctypes.c_int(-1)
+    check(lib.zk_bn254_pairing_check(_np_ptr(ps), _np_ptr(qs), ps.shape[0], ctypes.byref(ok)))
+    return ok.value == 1
+
+
+class VerifyingKey:
+    """Groth16 verification key on the host (zk_groth16_vk)."""
+
+    def __init__(self, handle):
+        self.h = handle
+
+    @classmethod
+    def load(cls, path):
+        h = _vp()
+        check(lib.zk_groth16_vk_load(path.encode(), ctypes.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def from_pk(cls, pk):
+        h = _vp()
+        check(lib.zk_groth16_vk_from_pk(pk.h, ctypes.byref(h)))
+        return cls(h)
+
+    @property
+    def num_public(self):
+        return lib.zk_groth16_vk_num_public(self.h)
+
+    def verify(self, public_inputs, proof, device=0):
+        """Groth16 verification of 256 proof bytes against (n, 4) Montgomery public
+        inputs; the public-input MSM on `device` (-1: on the host)."""
+        pub = np.ascontiguousarray(public_inputs, np.uint64).reshape(-1, 4)
+        pb = np.frombuffer(bytes(proof), dtype=np.uint8).copy()
+        ok = ctypes.c_int(-1)
+        check(lib.zk_groth16_verify(self.h, device, _np_ptr(pub) if pub.shape[0] else None, pub.shape[0], _np_ptr(pb),
+                                    ctypes.byref(ok)))
+        return ok.value == 1
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.zk_groth16_vk_destroy(self.h)
+            self.h = None
+
+
 def prove_last_stats():
     s = ProveStats()
     check(lib.zk_groth16_last_stats(ctypes.byref(s)))

@@ -420,6 +420,41 @@ int zk_groth16_prove_multi(zk_groth16_pk* const* pks, const zk_r1cs* const* r1cs
                            const void* h_witness, const void* r, const void* s, void* proof256, void* points,
                            double timeout_s, zk_split_stats* stats);
 
+/* ------------------------------------------------------------------
+ * Verifier: the BN254 optimal ate pairing and the Groth16 check, host code
+ * with the public-input MSM on a GPU.
+ * ------------------------------------------------------------------ */
+typedef struct zk_groth16_vk zk_groth16_vk;  /* verification key (host) */
+
+/* vk.bin (save_vk / load_vk, src/verifier/verifier.cu:103-148). */
+int zk_groth16_vk_load(const char* path, zk_groth16_vk** out);
+/* The verification key of a proving key made by zk_groth16_setup. */
+int zk_groth16_vk_from_pk(const zk_groth16_pk* pk, zk_groth16_vk** out);
+void zk_groth16_vk_destroy(zk_groth16_vk* vk);
+/* Number of public inputs the key expects (-1 for NULL). */
+int zk_groth16_vk_num_public(const zk_groth16_vk* vk);
+
+/* Replaces Groth16Verifier::verify (src/prover/groth16.cu:967-1022):
+ * e(-A, B) e(alpha, beta) e(vk_x, gamma) e(C, delta) == 1 with
+ * vk_x = IC[0] + sum_i x_i IC[i + 1] (x: num_public Montgomery Fr) and the
+ * pairing product of verify_pairing_product (src/curve/pairing.cuh:278-282).
+ * proof256: Groth16Proof::serialize bytes.  vk_x is an MSM on `device`
+ * (>= 0), or summed on the host with device = -1 (the reference's loop).
+ * *valid = 1 when the proof verifies, 0 otherwise (a public-input count other
+ * than the key's included, as the reference returns false). */
+int zk_groth16_verify(const zk_groth16_vk* vk, int device, const void* public_inputs, int num_public,
+                      const void* proof256, int* valid);
+
+/* Replaces bn254::pairing (src/curve/pairing.cuh:226-230): e(P, Q) for a packed
+ * G1 point (64 B) and G2 point (128 B), written as 12 Montgomery Fp (384 B) in
+ * the reference's Fp12 layout (c0.c0.c0, c0.c0.c1, c0.c1.c0, ..., c1.c2.c1;
+ * Fp6 = Fp2[v]/(v^3 - (9 + u)), Fp12 = Fp6[w]/(w^2 - v)); the reduced value
+ * f^((p^12 - 1)/r), equal bit for bit to the reference's. */
+int zk_bn254_pairing(const void* p64, const void* q128, void* out_fp12);
+/* Replaces bn254::verify_pairing_product (src/curve/pairing.cuh:278-282):
+ * *holds = 1 when prod_i e(P_i, Q_i) == 1 (n packed pairs). */
+int zk_bn254_pairing_check(const void* p64s, const void* q128s, int n, int* holds);
+
 /* ==================================================================
  * Synthetic workloads (seeded, for benchmarks and tests)
  * ================================================================== */

@@ -251,3 +251,18 @@ extern "C" void ref_msm_g1_pippenger_mt(uint64_t* o, int* oinf, const uint64_t* 
 extern "C" void ref_ntt_gpu(void* d_out, const void* d_in, int log_n, int inverse) {
     bn254::ntt_gpu((bn254::Fr*)d_out, (const bn254::Fr*)d_in, log_n, inverse != 0);
 }
+
+// The reference's pairing e(P, Q) (src/curve/pairing.cuh:226-230) on its own
+// host arithmetic: 12 Montgomery Fp in the Fp12 layout (c0.c0.c0 ... c1.c2.c1).
+#include "curve/pairing.cuh"
+extern "C" void ref_pairing(uint64_t* out48, const uint64_t* p, int pinf, const uint64_t* q, int qinf) {
+    Fp12 e = pairing(ld_g1(p, pinf), ld_g2(q, qinf));
+    const Fp6* h[2] = {&e.c0, &e.c1};
+    for (int a = 0; a < 2; a++) {
+        const Fp2* c[3] = {&h[a]->c0, &h[a]->c1, &h[a]->c2};
+        for (int b = 0; b < 3; b++) {
+            st(out48 + 4 * (a * 6 + b * 2), c[b]->c0.val);
+            st(out48 + 4 * (a * 6 + b * 2 + 1), c[b]->c1.val);
+        }
+    }
+}

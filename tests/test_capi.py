@@ -151,3 +151,20 @@ def test_msm_key_space_refused_before_device_work(monkeypatch):
         assert Z.lib.zk_msm_g2_device(0, None, p, p, (1 << 25) - 1, p) == Z.ZK_ERR_NODEV
         monkeypatch.delenv("ZK_MSM_WINDOW_BITS")
         assert Z.lib.zk_msm_g1_device(0, None, p, p, (1 << 27) + 5, p) == Z.ZK_ERR_NODEV
+
+
+def test_split_prove_entry_points_check_arguments():
+    """The C split prove's entry points refuse bad arguments before any device
+    work; NCCL loads at run time (an id is made without a GPU); without a
+    device the local communicator reports ZK_ERR_NODEV (no CPU fallback)."""
+    import ctypes
+    assert Z.lib.zk_groth16_prove_split(None, None, None, None, None, None, None, None) == Z.ZK_ERR_INVALID
+    assert Z.lib.zk_groth16_prove_multi(None, None, None, 2, None, None, None, None, None, 1.0, None) == Z.ZK_ERR_INVALID
+    hs = (ctypes.c_void_p * 2)()
+    assert Z.lib.zk_comm_init_local(0, 0, ctypes.cast(hs, ctypes.c_void_p)) == Z.ZK_ERR_INVALID
+    assert Z.lib.zk_comm_init_rank(0, None, 2, 0, None) == Z.ZK_ERR_INVALID
+    assert Z.lib.zk_comm_abort(None) == Z.ZK_ERR_INVALID
+    uid = Z.Comm.unique_id()
+    assert len(uid) == 128 and uid != Z.Comm.unique_id()
+    if Z.device_count() == 0:
+        assert Z.lib.zk_comm_init_local(0, 2, ctypes.cast(hs, ctypes.c_void_p)) == Z.ZK_ERR_NODEV

@@ -75,6 +75,13 @@ def test_statement_proof_equals_reference(libs, name, tmp_path):
     bad[200] ^= 1
     assert not RS.verify_with_vk(ref_cpu, vk_path, c, bytes(bad)), "the reference verifier accepted a tampered proof"
 
+    # this library's verifier (public-input MSM on the GPU), from the key and from vk.bin
+    pub = np.ascontiguousarray(c["witness"][1:1 + c["num_public"]])
+    for vk in (Z.VerifyingKey.from_pk(pk), Z.VerifyingKey.load(vk_path)):
+        assert vk.verify(pub, proof, device=0)
+        assert not vk.verify(pub, bytes(bad), device=0)
+        assert vk.verify(pub, proof, device=-1)
+
 
 def test_statement_witness_refused_when_tampered(libs):
     """Flipping config 4's public route flag (the reference host test's
