@@ -18,6 +18,11 @@
 // byte-identical to the reference's for the same toxic waste.
 #include "prover.hpp"
 
+#include <unistd.h>
+
+#include <atomic>
+#include <chrono>
+
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
@@ -222,17 +227,6 @@ __global__ void hadamard_check_kernel(const Fr* __restrict__ a, const Fr* __rest
     }
 }
 
-// x -> x * R^2 * R^-1 = Montgomery form of a standard-form Fp value
-__global__ void fp_to_mont_kernel(uint64_t* __restrict__ v, size_t count) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
-        Fp x, r2;
-        fload(x, v + 4 * i);
-#pragma unroll
-        for (int k = 0; k < 8; k++) r2.v[k] = ModP::r2(k);
-        fmul(x, x, r2);
-        fstore(v + 4 * i, x);
-    }
-}
 
 // ------------------------------------------------------------------ R1CS upload
 static int r1cs_create(int device, int num_constraints, int num_variables, int num_public, const SparseEntry* const* ent,
@@ -902,61 +896,110 @@ static void std_to_mont_host(uint64_t* v, size_t fe_count) {
     }
 }
 
+// ZKMLPK3 records: u8 infinity flag + x (+ y) in standard form, 65 B (G1) or
+// 129 B (G2).  One thread per record: the record's bytes from aligned 32-bit
+// words (funnel shifts), then x R^2 R^-1 per coordinate (Montgomery form);
+// a set flag gives the all-zero record.  raw must extend 8 bytes past the
+// last record (the loader pads it).
+template <int kCoords>
+__global__ void unpack_records_kernel(const uint8_t* __restrict__ raw, size_t count, uint64_t* __restrict__ out) {
+    constexpr int kRec = 1 + 32 * kCoords;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t start = i * kRec;
+        const uint8_t flag = raw[start];
+        const size_t s = start + 1;
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(raw + (s & ~size_t(3)));
+        const uint32_t sh = (uint32_t)(s & 3) * 8;
+        Fp r2;
+#pragma unroll
+        for (int k = 0; k < 8; k++) r2.v[k] = ModP::r2(k);
+#pragma unroll
+        for (int c = 0; c < kCoords; c++) {
+            Fp x;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t lo = w[c * 8 + k], hi = w[c * 8 + k + 1];
+                x.v[k] = sh ? __funnelshift_r(lo, hi, sh) : lo;
+            }
+            if (flag) {
+                fset_zero(x);
+            } else {
+                fmul(x, x, r2);
+            }
+            fstore(reinterpret_cast<Fp*>(out) + i * kCoords + c, x);
+        }
+    }
+}
+
+static thread_local zk_pk_load_stats g_load_stats;
+
+// ZKMLPK3 (ProvingKey::save / load_streaming, groth16.cu:1104-1314) straight
+// into device memory: the header and vector counts are read first (fixed-size
+// records give every offset), the five query vectors' bytes are read in 64 MiB
+// chunks by several threads into pinned buffers and copied to the device while
+// the next chunk is read, and one kernel per vector unpacks the records and
+// converts them to Montgomery form.  Fail-closed as the reference's loader:
+// bad magic or version, bad counts, truncation, incomplete query vectors.
 static int pk_load(int device, const char* path, zk_groth16_pk* pk) {
+    zk_pk_load_stats& st = g_load_stats;
+    std::memset(&st, 0, sizeof st);
+    const auto t0 = std::chrono::steady_clock::now();
     FILE* f = fopen(path, "rb");
     if (!f) { set_error("pk_load: cannot open %s", path); return ZK_ERR_INVALID; }
+    struct Closer {
+        FILE* f;
+        ~Closer() { fclose(f); }
+    } closer{f};
     fseek(f, 0, SEEK_END);
-    const long size = ftell(f);
+    const long long size = ftell(f);
     fseek(f, 0, SEEK_SET);
-    std::vector<uint8_t> buf((size_t)std::max(0L, size));
-    const bool rd = fread(buf.data(), 1, buf.size(), f) == buf.size();
-    fclose(f);
-    if (!rd) { set_error("pk_load: read failed for %s", path); return ZK_ERR_INVALID; }
-    Reader R{buf.data(), buf.size()};
+    auto rd = [&](void* p, size_t n) { return fread(p, 1, n, f) == n; };
+    auto skip = [&](long long n) { return fseek(f, (long)n, SEEK_CUR) == 0; };
+    auto rd_i32 = [&](int32_t& v) { return rd(&v, 4); };
+    auto rd_rec = [&](uint64_t* rec, int coords) {
+        uint8_t inf = 0;
+        if (!rd(&inf, 1) || !rd(rec, (size_t)32 * coords)) return false;
+        if (inf) std::memset(rec, 0, (size_t)32 * coords);
+        return true;
+    };
     char magic[8];
-    R.raw(magic, 8);
     uint32_t version = 0;
-    R.raw(&version, 4);
-    if (!R.ok || std::memcmp(magic, "ZKMLPK3", 7) != 0 || version != 3) {
+    if (!rd(magic, 8) || !rd(&version, 4) || std::memcmp(magic, "ZKMLPK3", 7) != 0 || version != 3) {
         set_error("pk_load: %s is not a ZKMLPK3 v3 proving key", path);
         return ZK_ERR_INVALID;
     }
-    pk->num_constraints = R.i32();
-    pk->m = R.i32();
-    pk->num_public = R.i32();
-    if (!R.ok || pk->num_constraints < 0 || pk->m <= 0 || pk->num_public < 0) {
+    if (!rd_i32(pk->num_constraints) || !rd_i32(pk->m) || !rd_i32(pk->num_public) || pk->num_constraints < 0 || pk->m <= 0 ||
+        pk->num_public < 0) {
         set_error("pk_load: invalid metadata in %s", path);
         return ZK_ERR_INVALID;
     }
     uint64_t small1[3][8], small2[3][16];
-    for (int k = 0; k < 3; k++) get_g1(R, small1[k]);
-    for (int k = 0; k < 3; k++) get_g2(R, small2[k]);
-    const int32_t ntg1 = R.i32();
-    if (!R.ok || ntg1 < 0 || ntg1 > (1 << 28)) { set_error("pk_load: bad tau_g1 count"); return ZK_ERR_INVALID; }
-    for (int32_t i = 0; i < ntg1; i++) { uint64_t t[8]; get_g1(R, t); }
-    const int32_t ntg2 = R.i32();
-    if (!R.ok || ntg2 < 0 || ntg2 > (1 << 28)) { set_error("pk_load: bad tau_g2 count"); return ZK_ERR_INVALID; }
+    bool ok = true;
+    for (int k = 0; k < 3; k++) ok = ok && rd_rec(small1[k], 2);
+    for (int k = 0; k < 3; k++) ok = ok && rd_rec(small2[k], 4);
+    int32_t ntg1 = -1, ntg2 = -1;
+    ok = ok && rd_i32(ntg1) && ntg1 >= 0 && ntg1 <= (1 << 28) && skip((long long)ntg1 * 65);
+    if (!ok) { set_error("pk_load: bad header or tau_g1 vector in %s", path); return ZK_ERR_INVALID; }
+    ok = rd_i32(ntg2) && ntg2 >= 0 && ntg2 <= (1 << 28);
     uint64_t tg2[2][16] = {};
-    for (int32_t i = 0; i < ntg2; i++) {
-        uint64_t t[16];
-        get_g2(R, t);
-        if (i < 2) std::memcpy(tg2[i], t, 128);
-    }
-    std::vector<uint64_t> g1h, g2h;
+    for (int32_t i = 0; ok && i < std::min(ntg2, 2); i++) ok = rd_rec(tg2[i], 4);
+    ok = ok && (ntg2 <= 2 || skip((long long)(ntg2 - 2) * 129));
+    if (!ok) { set_error("pk_load: bad tau_g2 vector in %s", path); return ZK_ERR_INVALID; }
+    // the five query vectors: A, B1 (G1), B2 (G2), L, H (G1)
     int32_t counts[5];
+    long long off[5];
     for (int v = 0; v < 5; v++) {
-        const bool g2 = v == 2;
-        counts[v] = R.i32();
-        if (!R.ok || counts[v] < 0 || counts[v] > (1 << 28)) { set_error("pk_load: bad vector count in %s", path); return ZK_ERR_INVALID; }
-        std::vector<uint64_t>& dst = g2 ? g2h : g1h;
-        const size_t base = dst.size();
-        dst.resize(base + (size_t)counts[v] * (g2 ? 16 : 8));
-        for (int32_t i = 0; i < counts[v]; i++) {
-            if (g2) get_g2(R, &dst[base + (size_t)i * 16]);
-            else get_g1(R, &dst[base + (size_t)i * 8]);
+        const int rec = v == 2 ? 129 : 65;
+        if (!rd_i32(counts[v]) || counts[v] < 0 || counts[v] > (1 << 28)) {
+            set_error("pk_load: bad vector count in %s", path);
+            return ZK_ERR_INVALID;
+        }
+        off[v] = ftell(f);
+        if (off[v] + (long long)counts[v] * rec > size || !skip((long long)counts[v] * rec)) {
+            set_error("pk_load: truncated file %s", path);
+            return ZK_ERR_INVALID;
         }
     }
-    if (!R.ok) { set_error("pk_load: truncated file %s", path); return ZK_ERR_INVALID; }
     if (counts[0] < pk->m || counts[1] < pk->m || counts[2] < pk->m) {
         set_error("pk_load: incomplete v3 proving key in %s", path);  // groth16.cu:1300-1305
         return ZK_ERR_INVALID;
@@ -978,18 +1021,85 @@ static int pk_load(int device, const char* path, zk_groth16_pk* pk) {
     std::memcpy(pk->delta2, small2[2], 128);
     std::memcpy(pk->g2gen, tg2[0], 128);
     std::memcpy(pk->tau2, tg2[1], 128);
+
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     pk->device = ctx->device;
-    ZK_TRY_CUDA(cudaMalloc(&pk->g1, std::max<size_t>(g1h.size(), 8) * 8));
-    ZK_TRY_CUDA(cudaMalloc(&pk->g2, std::max<size_t>(g2h.size(), 16) * 8));
-    ZK_TRY_CUDA(cudaMemcpy(pk->g1, g1h.data(), g1h.size() * 8, cudaMemcpyHostToDevice));
-    ZK_TRY_CUDA(cudaMemcpy(pk->g2, g2h.data(), g2h.size() * 8, cudaMemcpyHostToDevice));
-    // standard -> Montgomery on the device; all-zero (infinity) stays zero because 0 * R^2 = 0
-    fp_to_mont_kernel<<<ctx->num_sms * 8, 256>>>((uint64_t*)pk->g1, g1h.size() / 4);
-    fp_to_mont_kernel<<<ctx->num_sms * 8, 256>>>((uint64_t*)pk->g2, g2h.size() / 4);
+    const long long first = off[0], last = off[4] + (long long)counts[4] * 65;  // the vectors are contiguous
+    const size_t raw_bytes = (size_t)(last - first);
+    const size_t g1_count = (size_t)counts[0] + counts[1] + counts[3] + counts[4];
+    DeviceBuffer raw_buf, g1_buf, g2_buf;
+    ZK_TRY_CUDA(raw_buf.alloc(raw_bytes + 64));
+    ZK_TRY_CUDA(g1_buf.alloc(std::max<size_t>(g1_count, 1) * 64));
+    ZK_TRY_CUDA(g2_buf.alloc(std::max<size_t>(counts[2], 1) * 128));
+    uint8_t* raw = (uint8_t*)raw_buf.p;
+    cudaStream_t cs = ctx->copy_stream;
+    ZK_TRY_CUDA(cudaMemsetAsync(raw + raw_bytes, 0, 64, cs));
+    // chunked read: kThreads readers fill one pinned chunk while the previous one
+    // is copied; ZKML_PK_LOAD_CHUNK_MB overrides the 64 MiB chunk
+    const char* ce = getenv("ZKML_PK_LOAD_CHUNK_MB");
+    const size_t kChunk = (ce && atoi(ce) > 0 && atoi(ce) <= 4096 ? (size_t)atoi(ce) : (size_t)64) << 20;
+    constexpr int kBufs = 3, kThreads = 8;
+    uint8_t* pin[kBufs] = {};
+    cudaEvent_t pin_free[kBufs] = {};
+    struct PinnedSet {
+        uint8_t** p;
+        cudaEvent_t* e;
+        ~PinnedSet() {
+            for (int i = 0; i < kBufs; i++) {
+                if (e[i]) { cudaEventSynchronize(e[i]); cudaEventDestroy(e[i]); }
+                if (p[i]) cudaFreeHost(p[i]);
+            }
+        }
+    } pinned_set{pin, pin_free};
+    for (int i = 0; i < kBufs; i++) {
+        ZK_TRY_CUDA(cudaMallocHost(&pin[i], std::min(kChunk, std::max<size_t>(raw_bytes, 1))));
+        ZK_TRY_CUDA(cudaEventCreateWithFlags(&pin_free[i], cudaEventDisableTiming));
+        ZK_TRY_CUDA(cudaEventRecord(pin_free[i], cs));
+    }
+    const int fd = fileno(f);
+    double read_s = 0;
+    for (size_t pos = 0, c = 0; pos < raw_bytes; pos += kChunk, c++) {
+        const size_t len = std::min(kChunk, raw_bytes - pos);
+        const int b = (int)(c % kBufs);
+        ZK_TRY_CUDA(cudaEventSynchronize(pin_free[b]));
+        const auto r0 = std::chrono::steady_clock::now();
+        std::atomic<bool> bad{false};
+        {
+            std::vector<std::thread> th;
+            for (int t = 0; t < kThreads; t++)
+                th.emplace_back([&, t]() {
+                    size_t a = len * t / kThreads, e = len * (t + 1) / kThreads;
+                    while (a < e) {
+                        const ssize_t got = pread(fd, pin[b] + a, e - a, (off_t)(first + (long long)(pos + a)));
+                        if (got <= 0) { bad = true; return; }
+                        a += (size_t)got;
+                    }
+                });
+            for (auto& x : th) x.join();
+        }
+        read_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - r0).count();
+        if (bad) { set_error("pk_load: read failed for %s", path); return ZK_ERR_INVALID; }
+        ZK_TRY_CUDA(cudaMemcpyAsync(raw + pos, pin[b], len, cudaMemcpyHostToDevice, cs));
+        ZK_TRY_CUDA(cudaEventRecord(pin_free[b], cs));
+    }
+    // unpack: A | B1 | L | H into g1, B2 into g2
+    uint8_t* g1 = (uint8_t*)g1_buf.p;
+    const int grid = ctx->num_sms * 8;
+    size_t o1 = 0;
+    for (int v : {0, 1, 3, 4}) {
+        if (counts[v] > 0)
+            unpack_records_kernel<2><<<grid, 256, 0, cs>>>(raw + (off[v] - first), (size_t)counts[v], (uint64_t*)(g1 + o1 * 64));
+        o1 += (size_t)counts[v];
+    }
+    if (counts[2] > 0) unpack_records_kernel<4><<<grid, 256, 0, cs>>>(raw + (off[2] - first), (size_t)counts[2], (uint64_t*)g2_buf.p);
     ZK_TRY_CUDA(cudaGetLastError());
-    ZK_TRY_CUDA(cudaDeviceSynchronize());
+    ZK_TRY_CUDA(cudaStreamSynchronize(cs));
+    pk->g1 = (uint8_t*)g1_buf.release();
+    pk->g2 = (uint8_t*)g2_buf.release();
+    st.bytes = (double)raw_bytes;
+    st.read_ms = read_s * 1e3;
+    st.total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     return ZK_OK;
 }
 
@@ -1073,6 +1183,12 @@ extern "C" int zk_groth16_pk_load(int device, const char* path, zk_groth16_pk** 
     int st = pk_load(device, path, pk);
     if (st != ZK_OK) { zk_groth16_pk_destroy(pk); return st; }
     *out = pk;
+    return ZK_OK;
+}
+
+extern "C" int zk_groth16_pk_last_load_stats(zk_pk_load_stats* out) {
+    if (!out) return ZK_ERR_INVALID;
+    *out = g_load_stats;
     return ZK_OK;
 }
 

@@ -486,6 +486,13 @@ class R1cs:
             self.h = None
 
 
+class PkLoadStats(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_double), ("read_ms", ctypes.c_double), ("total_ms", ctypes.c_double)]
+
+
+lib.zk_groth16_pk_last_load_stats.argtypes = [ctypes.POINTER(PkLoadStats)]
+
+
 class ProvingKey:
     """Proving key resident on one device (zk_groth16_pk)."""
 
@@ -505,6 +512,14 @@ class ProvingKey:
         h = _vp()
         check(lib.zk_groth16_pk_load(device, path.encode(), ctypes.byref(h)))
         return cls(h)
+
+    @staticmethod
+    def last_load_stats():
+        """Bytes of query records, host read time and whole-call time of this
+        thread's last load (zk_groth16_pk_last_load_stats)."""
+        st = PkLoadStats()
+        check(lib.zk_groth16_pk_last_load_stats(ctypes.byref(st)))
+        return {"bytes": st.bytes, "read_ms": st.read_ms, "total_ms": st.total_ms}
 
     def save(self, path):
         check(lib.zk_groth16_pk_save(self.h, path.encode()))

@@ -226,6 +226,15 @@ int zk_groth16_setup(zk_r1cs* r1cs, const void* toxic, zk_groth16_pk** out);
 /* ZKMLPK3 proving-key files (ProvingKey::save / load_streaming,
  * groth16.cu:1104-1314), loaded straight into device memory. */
 int zk_groth16_pk_load(int device, const char* path, zk_groth16_pk** out);
+/* The calling thread's last zk_groth16_pk_load: bytes of query records read,
+ * host time spent reading them (parallel reads into pinned chunks, overlapped
+ * with the copies to the device), and the whole call. */
+typedef struct {
+    double bytes;
+    double read_ms;
+    double total_ms;
+} zk_pk_load_stats;
+int zk_groth16_pk_last_load_stats(zk_pk_load_stats* out);
 int zk_groth16_pk_save(const zk_groth16_pk* pk, const char* path);
 /* vk.bin (save_vk, src/verifier/verifier.cu:103-148); keys from setup only. */
 int zk_groth16_vk_save(const zk_groth16_pk* pk, const char* path);

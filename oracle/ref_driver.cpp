@@ -266,3 +266,18 @@ extern "C" void ref_pairing(uint64_t* out48, const uint64_t* p, int pinf, const 
         }
     }
 }
+
+// The ceremony's random linear combination sum_i rho_i P_i (src/prover/
+// ceremony.cuh:242-246), the reference's own loop of scalar multiplications.
+#include "prover/ceremony.cuh"
+extern "C" void ref_random_combination(uint64_t* o, int* oinf, const uint64_t* pts, const uint64_t* rho, int n) {
+    std::vector<G1Affine> p((size_t)n);
+    std::vector<Fr> r((size_t)n);
+    for (int i = 0; i < n; i++) {
+        int inf = 1;
+        for (int k = 0; k < 8; k++) if (pts[8 * i + k]) inf = 0;
+        p[(size_t)i] = ld_g1(pts + 8 * i, inf);
+        r[(size_t)i] = ld_fr(rho + 4 * i);
+    }
+    st_g1(o, oinf, zkml::ceremony::random_combination(p, r));
+}

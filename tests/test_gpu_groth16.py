@@ -85,6 +85,30 @@ def test_pk_file_round_trip(small, tmp_path):
         Z.ProvingKey.load(bad)
 
 
+def test_pk_load_in_chunks_config4(tmp_path, monkeypatch):
+    """A 59 MB key (129,034 variables, domain 2^18) through the chunked loader
+    with 1 MiB chunks (about 60 reads overlapped with their copies):
+    the loaded key proves the same bytes, records at infinity included; a file
+    cut inside the last query vector is refused."""
+    c = Z.synth_conv_circuit(1, 8, 16, 16, 24, 10, 0, 4, 9)
+    r1 = Z.R1cs(c)
+    pk = Z.ProvingKey.setup(r1, G.toxic_deterministic())
+    path = str(tmp_path / "pk.bin")
+    pk.save(path)
+    monkeypatch.setenv("ZKML_PK_LOAD_CHUNK_MB", "1")
+    pk2 = Z.ProvingKey.load(path)
+    st = Z.ProvingKey.last_load_stats()
+    assert st["bytes"] > (1 << 20) and st["total_ms"] > 0
+    r, s = G.blinding_deterministic()
+    assert pk2.prove(r1, c["witness"], r, s)[0] == pk.prove(r1, c["witness"], r, s)[0]
+    raw = open(path, "rb").read()
+    bad = str(tmp_path / "cut.bin")
+    open(bad, "wb").write(raw[:-100])
+    with pytest.raises(Z.ZkError) as e:
+        Z.ProvingKey.load(bad)
+    assert "truncated" in str(e.value)
+
+
 def test_wrong_witness_does_not_verify(small, monkeypatch):
     """With the witness check off (ZKML_SKIP_WITNESS_CHECK=1, as the reference
     allows) a wrong witness still proves, to the oracle's bytes, and the proof
@@ -170,3 +194,43 @@ def test_h_msm_blocks_sum_to_the_whole_query():
             acc = Z.g1_add_affine(acc, got)
         assert np.array_equal(acc, whole), s_log
     torch.cuda.synchronize()
+
+
+def _device_view(ptr, rows, words):
+    """A (rows, words) int64 CUDA tensor over existing device memory."""
+    import torch
+
+    class _Cai:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (rows, words), "typestr": "<i8", "data": (int(ptr), False),
+                                             "version": 3, "strides": None}
+    return torch.as_tensor(_Cai(), device="cuda").clone()
+
+
+def test_ceremony_random_combination_is_the_msm():
+    """The phase-2 ceremony's random linear combination sum_i rho_i P_i over a
+    proving key's query points (src/prover/ceremony.cuh:242-246, run here as
+    the reference's own host loop from oracle/_ref) equals the MSM through the
+    reference-shaped drop-in (bn254::msm_g1 records, zk_msm_g1) and through
+    the device entry point, over the L and H queries of a key."""
+    import ctypes
+
+    import pyoracle as O
+    if not O.ref_available():
+        pytest.skip("reference arithmetic not built")
+    c = Z.synth_conv_circuit(1, 2, 8, 8, 24, 10, 0, 2, 31)
+    r1 = Z.R1cs(c)
+    pk = Z.ProvingKey.setup(r1, G.toxic_deterministic())
+    arr = pk.arrays()
+    ref = O.ref()
+    for name, count in (("l_query", arr["l"]), ("h_query", arr["n_h"])):
+        n = min(count, 1500)
+        pts = Z.to_host(_device_view(arr[name], n, 8))
+        rho = O.Rng(55 + n).fr_vector(n)
+        out = np.zeros(8, np.uint64)
+        inf = ctypes.c_int()
+        ref.ref_random_combination(O._p(out), ctypes.byref(inf), O._p(pts), O._p(rho), n)
+        exp = np.zeros(8, np.uint64) if inf.value else out
+        jac = Z.msm_g1_ref(Z.packed_to_ref_g1(pts), rho)
+        assert np.array_equal(jac[:8] if exp.any() else np.zeros(8, np.uint64), exp), name
+        assert np.array_equal(Z.msm_g1(Z.to_device(pts), Z.to_device(rho)), exp), name
