@@ -417,11 +417,26 @@ def run_b200(args):
     # of Y3 = R (Q - X3) - Y1 PPP share one reduction (256 + 128).  Per addition:
     # 6 x 256 + 2 x 200 + 384 = 2320 IMAD.
     imad_per_add = 6 * 256 + 2 * 200 + 384
-    achieved = adds * imad_per_add / (acc_ms / 1e3)
+    # With the batch-affine rounds (G1, full buckets) most of the additions are
+    # affine pair additions sharing one inversion per round: 5 products + 1
+    # squaring each (3 for the shared inversion, the slope, y3; the squared
+    # slope): 5 x 256 + 200 = 1480 IMAD; the elements they leave go through the
+    # mixed XYZZ additions above (counted as if every one were an addition).
+    imad_per_pair = 5 * 256 + 200
+    ba_pairs = stats[-1].get("batch_affine_pairs", 0)
+    ba_left = stats[-1].get("batch_affine_left", 0)
+    acc_imad = ba_pairs * imad_per_pair + ba_left * imad_per_add if ba_pairs else adds * imad_per_add
+    achieved = acc_imad / (acc_ms / 1e3)
     roofline = {"bound": "int32", "kernel": "msm_accumulate_kernel<G1>", "achieved": achieved / 1e12,
                 "peak": hw_peak / 1e12, "unit": "TIMAD/s", "frac": achieved / hw_peak, "traffic": None,
-                "algorithmic": f"{adds} mixed additions x {imad_per_add} IMAD (6 products x 256, 2 squarings x 200, "
-                               f"Y3's two products sharing a reduction 384) per launch",
+                "algorithmic": (f"{ba_pairs} batch-affine pair additions x {imad_per_pair} IMAD (5 products x 256 + 1 squaring x 200) "
+                                f"+ {ba_left} remaining elements x {imad_per_add} IMAD (mixed XYZZ: 6 products x 256, 2 squarings "
+                                f"x 200, Y3's two products sharing a reduction 384), {adds} keys in all"
+                                if ba_pairs else
+                                f"{adds} mixed additions x {imad_per_add} IMAD (6 products x 256, 2 squarings x 200, "
+                                f"Y3's two products sharing a reduction 384) per launch"),
+                "kernels": ("ba_pass_a/ba_pass_b x 3 rounds + product-tree batch inversions + msm_accumulate_kernel<G1, direct>"
+                            if ba_pairs else "msm_accumulate_kernel<G1>"),
                 "peak_source": (f"zk_probe_int_pipe, measured in this run: the hardware issue rate of plain mad.lo.u32 "
                                 f"({pipe['mad_lo_per_clk_sm']:.1f}/clk/SM x {pipe['num_sms']} SMs x {pipe['sm_clock_ghz']:.3f} GHz "
                                 f"measured by the probe); every one of the counted IMAD is a mad.lo or mad.hi half of a product"),
@@ -431,15 +446,16 @@ def run_b200(args):
                 "frac_vs_own_multiply": achieved / imad,
                 "own_multiply_timad": imad / 1e12,
                 "msm_whole_frac_ref_ops": 256 * msm_ref_ops(n) / (stats[-1]["total_device_ms"] / 1e3) / hw_peak}
-    prof = os.path.join(ROOT, "profiles", "msm_accumulate_g1_traffic.json")
+    prof = os.path.join(ROOT, "profiles", "msm_batch_affine_g1_traffic.json" if ba_pairs else "msm_accumulate_g1_traffic.json")
     if os.path.exists(prof):
-        # DRAM bytes per addition from one ncu capture of the accumulate kernel,
-        # scaled by this launch's additions (the capture's points exceed L2 too)
+        # DRAM bytes per key of the accumulation phase from one ncu capture of
+        # its kernels at a smaller size, scaled by this launch's keys (the
+        # capture's points exceed L2 too)
         try:
             tr = json.load(open(prof))
             roofline["traffic"] = tr["bytes_per_addition"] * adds
-            roofline["traffic_source"] = (f"ncu dram__bytes_read+write of one 2^{tr['capture_log_n']} launch "
-                                          f"({tr['bytes_per_addition']:.1f} B per addition) x {adds} additions")
+            roofline["traffic_source"] = (f"ncu dram__bytes_read+write of the accumulation kernels at 2^{tr['capture_log_n']} "
+                                          f"({tr['bytes_per_addition']:.1f} B per key) x {adds} keys")
         except (OSError, ValueError, KeyError):
             pass
 

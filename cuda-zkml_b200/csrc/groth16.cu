@@ -907,9 +907,11 @@ __global__ void unpack_records_kernel(const uint8_t* __restrict__ raw, size_t co
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
         const size_t start = i * kRec;
         const uint8_t flag = raw[start];
-        const size_t s = start + 1;
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(raw + (s & ~size_t(3)));
-        const uint32_t sh = (uint32_t)(s & 3) * 8;
+        // the coordinates' bytes from 4-byte aligned words (alignment of the
+        // absolute address: a vector's records need not start on a word)
+        const uintptr_t a = reinterpret_cast<uintptr_t>(raw + start + 1);
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+        const uint32_t sh = (uint32_t)(a & 3) * 8;
         Fp r2;
 #pragma unroll
         for (int k = 0; k < 8; k++) r2.v[k] = ModP::r2(k);

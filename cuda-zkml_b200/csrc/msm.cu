@@ -30,6 +30,7 @@
 //                 normalisation.
 #include "curve.cuh"
 #include "host_field.hpp"
+#include "msm_affine.cuh"
 #include "runtime.cuh"
 
 #include <algorithm>
@@ -59,6 +60,13 @@ struct MsmPlan {
     // where the point of (i, w) is 2^(c w) P_i, stored at index i + w n
     uint32_t wstride = 0;
     size_t kstride = 0;
+    // batch-affine rounds before the XYZZ accumulation (msm_affine.cuh): 0 or
+    // kBaRounds; bound of the elements left after them, and the accumulation's
+    // segment length over those
+    int ba = 0;
+    size_t ba_left = 0;
+    uint32_t ba_seg = 0;
+    size_t key_bound = 0;
 };
 
 static constexpr int kScanTile = 4096;  // 1024 threads x 4
@@ -368,7 +376,9 @@ __device__ __forceinline__ void load_signed_point(Affine<typename Cv::F>& a, boo
     if (key >> 31) { F t; fneg(t, a.y); a.y = t; }
 }
 
-template <class Cv>
+// kDirect: element p of a bucket is the point stored at position p (the level
+// left by the batch-affine rounds: no key, no sign, all-zero = infinity).
+template <class Cv, bool kDirect = false>
 __global__ void __launch_bounds__(128, Cv::kAccumulateMinBlocks) msm_accumulate_kernel(
     const uint32_t* __restrict__ keys, const uint32_t* __restrict__ offsets, uint32_t nb, const uint8_t* __restrict__ points,
     uint32_t seg, uint8_t* __restrict__ bucket_sums, uint8_t* __restrict__ part_first, uint8_t* __restrict__ part_last,
@@ -421,7 +431,12 @@ __global__ void __launch_bounds__(128, Cv::kAccumulateMinBlocks) msm_accumulate_
         }
         Affine<F> a;
         bool inf;
-        load_signed_point<Cv>(a, inf, points, keys[p], idx_lo, idx_hi);
+        if (kDirect) {
+            load_affine(a, points + (size_t)p * Cv::kAffineBytes);
+            inf = fis_zero(a.x) && fis_zero(a.y);
+        } else {
+            load_signed_point<Cv>(a, inf, points, keys[p], idx_lo, idx_hi);
+        }
         if (!inf) madd(acc, a);
     }
     flush();
@@ -986,6 +1001,159 @@ static int msm_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void*
     return ZK_OK;
 }
 
+// ------------------------------------------------------------------ batch-affine accumulation (G1)
+// Rounds of pairwise affine additions (msm_affine.cuh) when the buckets are
+// full enough to pay for them: at least 8 keys per bucket on average and 2^20
+// keys.  ZK_MSM_BATCH_AFFINE=0 turns them off, =1 forces them.
+static constexpr bool kBaDefault = false;  // on only when ZK_MSM_BATCH_AFFINE=1 until it beats the serial accumulation
+static void ba_plan(MsmPlan& P, size_t key_bound, bool g2, int num_sms) {
+    P.ba = 0;
+    P.key_bound = key_bound;
+    if (g2) return;
+    const char* env = getenv("ZK_MSM_BATCH_AFFINE");
+    const bool want = env && *env ? atoi(env) != 0 : (kBaDefault && key_bound >= ((size_t)1 << 20) && key_bound >= 8 * (size_t)P.nb);
+    if (!want || key_bound == 0) return;
+    P.ba = kBaRounds;
+    P.ba_left = (key_bound >> kBaRounds) + P.nb + 1;
+    P.ba_seg = pow2_clamp((double)P.ba_left / ((double)std::max(num_sms, 1) * 512.0), 16, 128);
+    P.max_segs = std::max(P.max_segs, (P.ba_left + P.ba_seg - 1) / P.ba_seg);
+}
+
+struct BaScratch {
+    uint32_t* off[2];         // level offsets (nb + 1), alternating
+    uint8_t* pts[2];          // level points: levels 1 and 3 in pts[0], level 2 in pts[1]
+    Fp* prefix;               // running products before each regular pair
+    Fp* totals;               // per-thread products, turned into their inverses
+    Fp* tree;                 // product-tree nodes and upper levels
+    unsigned long long* pairs;  // regular pair additions per round, then the elements left (4 words)
+};
+static size_t ba_bound(const MsmPlan& P, size_t key_bound, int level) { return (key_bound >> level) + P.nb + 1; }
+static size_t ba_threads(size_t outputs) { return (outputs + kBaItems - 1) / kBaItems; }
+static size_t ba_tree_elems(size_t n) {  // nodes of every level plus the upper levels' values
+    size_t e = 0;
+    while (n > 1) {
+        const size_t blocks = (n + kTreeLeaves - 1) / kTreeLeaves;
+        e += blocks * 2 * kTreeLeaves + blocks;
+        n = blocks;
+    }
+    return e + 1;
+}
+static size_t ba_scratch_bytes(const MsmPlan& P, size_t key_bound) {
+    if (!P.ba) return 0;
+    const size_t b1 = ba_bound(P, key_bound, 1), b2 = ba_bound(P, key_bound, 2), nt = ba_threads(b1);
+    return 2 * Arena::round((size_t)(P.nb + 1) * 4) + Arena::round(b1 * 64) + Arena::round(b2 * 64) + Arena::round(b1 * 32) +
+           Arena::round(nt * 32) + Arena::round(ba_tree_elems(nt) * 32) + Arena::round(4 * 8);
+}
+static BaScratch take_ba_scratch(Arena& ar, const MsmPlan& P, size_t key_bound) {
+    BaScratch B{};
+    if (!P.ba) return B;
+    const size_t b1 = ba_bound(P, key_bound, 1), b2 = ba_bound(P, key_bound, 2), nt = ba_threads(b1);
+    B.off[0] = ar.take<uint32_t>(P.nb + 1);
+    B.off[1] = ar.take<uint32_t>(P.nb + 1);
+    B.pts[0] = ar.take<uint8_t>(b1 * 64);
+    B.pts[1] = ar.take<uint8_t>(b2 * 64);
+    B.prefix = ar.take<Fp>(b1);
+    B.totals = ar.take<Fp>(nt);
+    B.tree = ar.take<Fp>(ba_tree_elems(nt));
+    B.pairs = ar.take<unsigned long long>(4);
+    return B;
+}
+
+// vals[0 .. n) <- their inverses (all nonzero): product tree, one inversion, back down
+static int batch_invert(cudaStream_t st, Fp* vals, size_t n, Fp* tree, LaunchCounter& lc) {
+    struct Level { Fp* vals; Fp* nodes; size_t n; };
+    Level lv[8];
+    int L = 0;
+    lv[0].vals = vals;
+    lv[0].n = n;
+    Fp* cur = tree;
+    while (lv[L].n > 1) {
+        const size_t blocks = (lv[L].n + kTreeLeaves - 1) / kTreeLeaves;
+        lv[L].nodes = cur;
+        cur += blocks * 2 * kTreeLeaves;
+        lv[L + 1].vals = cur;
+        lv[L + 1].n = blocks;
+        cur += blocks;
+        bt_up_kernel<<<(unsigned)blocks, 256, 0, st>>>(lv[L].vals, lv[L].n, lv[L].nodes, lv[L + 1].vals);
+        lc++;
+        L++;
+        if (L >= 7) { set_error("batch inversion: %zu values exceed the tree depth", n); return ZK_ERR_RANGE; }
+    }
+    bt_invert_kernel<<<1, 32, 0, st>>>(lv[L].vals);
+    lc++;
+    for (int l = L - 1; l >= 0; l--) {
+        bt_down_kernel<<<(unsigned)lv[l + 1].n, 256, 0, st>>>(lv[l].nodes, lv[l + 1].vals, lv[l].n, lv[l].vals);
+        lc++;
+    }
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
+// Batch-affine rounds over the sorted keys, then the XYZZ accumulation and
+// fixup over the level they leave (G1).  Same contract as
+// msm_accumulate_phase; phase event 3..4 spans the rounds and the accumulation.
+static int ba_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const MsmPlan& P, const SortScratch& S,
+                               const BaScratch& B, size_t key_bound, uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
+    cudaEvent_t* ph = ctx->phase;
+    ZK_TRY_CUDA(cudaMemsetAsync(S.first_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(S.last_bucket, 0xff, P.max_segs * sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(S.max_span, 0, sizeof(uint32_t), st));
+    ZK_TRY_CUDA(cudaMemsetAsync(B.pairs, 0, 4 * 8, st));
+    if (points_ready) ZK_TRY_CUDA(cudaStreamWaitEvent(st, points_ready, 0));
+    ZK_TRY_CUDA(cudaEventRecord(ph[3], st));
+    const uint32_t* off_in = S.offsets;
+    const uint8_t* pts_in = (const uint8_t*)d_points;
+    for (int r = 0; r < P.ba; r++) {
+        uint32_t* off_out = B.off[r & 1];
+        uint8_t* pts_out = B.pts[r & 1];
+        // the next level's offsets: exclusive scan of ceil(c_g / 2^(r + 1))
+        ba_level_counts_kernel<<<grid_for(P.nb, 256, ctx->num_sms * 8), 256, 0, st>>>(S.offsets, P.nb, r + 1, S.counts);
+        scan_tile_sums_kernel<<<P.tiles, 1024, 0, st>>>(S.counts, P.nb, S.tile_sums);
+        scan_tiles_kernel<<<1, 1024, 0, st>>>(S.tile_sums, P.tiles);
+        scan_finish_kernel<<<P.tiles, 1024, 0, st>>>(S.counts, P.nb, S.tile_sums, off_out, S.cursors);
+        for (int k = 0; k < 4; k++) lc++;
+        const size_t nt = ba_threads(ba_bound(P, key_bound, r + 1));
+        const unsigned blocks = (unsigned)((nt + kBaThreads - 1) / kBaThreads);
+        if (r == 0)
+            ba_pass_a_kernel<true><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, B.pairs + r);
+        else
+            ba_pass_a_kernel<false><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, B.pairs + r);
+        lc++;
+        ZK_TRY(batch_invert(st, B.totals, nt, B.tree, lc));
+        if (r == 0)
+            ba_pass_b_kernel<true><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, pts_out);
+        else
+            ba_pass_b_kernel<false><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, pts_out);
+        lc++;
+        off_in = off_out;
+        pts_in = pts_out;
+    }
+    ZK_TRY_CUDA(cudaMemcpyAsync(B.pairs + 3, off_in + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));  // elements left
+    {
+        const size_t segs = (P.ba_left + P.ba_seg - 1) / P.ba_seg;
+        const unsigned blocks = (unsigned)std::max<size_t>(1, (segs + 127) / 128);
+        msm_accumulate_kernel<G1, true><<<blocks, 128, 0, st>>>(nullptr, off_in, P.nb, pts_in, P.ba_seg, buckets, S.part_first,
+                                                                 S.part_last, S.first_bucket, S.last_bucket, 0, 0xffffffffu,
+                                                                 S.max_span);
+        lc++;
+    }
+    ZK_TRY_CUDA(cudaEventRecord(ph[4], st));
+    {
+        const size_t segs = (P.ba_left + P.ba_seg - 1) / P.ba_seg;
+        const unsigned blocks = grid_for(segs, 128, ctx->num_sms * 16);
+        for (uint64_t stride = 1; stride < segs; stride <<= 1) {
+            msm_fixup_round_kernel<G1><<<blocks, 128, 0, st>>>(off_in, S.first_bucket, S.last_bucket, segs, P.ba_seg, stride,
+                                                                S.part_first, S.part_last, S.max_span);
+            lc++;
+        }
+        msm_fixup_final_kernel<G1><<<(P.nb + 255) / 256, 256, 0, st>>>(off_in, P.nb, P.ba_seg, S.part_first, S.part_last, buckets);
+        lc++;
+    }
+    ZK_TRY_CUDA(cudaEventRecord(ph[5], st));
+    ZK_TRY_CUDA(cudaGetLastError());
+    return ZK_OK;
+}
+
 template <class Cv>
 static int msm_bucket_phase(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
                             const MsmPlan& P, const SortScratch& S, uint8_t* buckets, cudaEvent_t points_ready, LaunchCounter& lc) {
@@ -1031,18 +1199,25 @@ static int msm_reduce_phase(DeviceContext* ctx, cudaStream_t st, const MsmPlan& 
 template <class Cv>
 static int msm_pipeline(DeviceContext* ctx, cudaStream_t st, const void* d_points, const void* d_scalars, size_t n,
                         const MsmPlan& P, Arena& ar, uint8_t* windows_dev, cudaEvent_t points_ready, LaunchCounter& lc,
-                        uint32_t** total_keys_dev) {
+                        uint32_t** total_keys_dev, unsigned long long** ba_stats_dev = nullptr) {
     const SortScratch S = take_sort_scratch<Cv>(ar, P);
     *total_keys_dev = S.offsets + P.nb;
     uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
     const ReduceScratch R = take_reduce_scratch<Cv>(ar, P);
-    ZK_TRY(msm_bucket_phase<Cv>(ctx, st, d_points, d_scalars, n, P, S, buckets, points_ready, lc));
+    const BaScratch B = take_ba_scratch(ar, P, P.key_bound);
+    if (ba_stats_dev) *ba_stats_dev = P.ba ? B.pairs : nullptr;
+    ZK_TRY(msm_sort_phase<Cv>(ctx, st, d_scalars, n, P, S, lc));
+    if (P.ba && std::is_same<Cv, G1>::value)
+        ZK_TRY(ba_accumulate_phase(ctx, st, d_points, P, S, B, P.key_bound, buckets, points_ready, lc));
+    else
+        ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, d_points, P, S, buckets, points_ready, lc));
     return msm_reduce_phase<Cv>(ctx, st, P, S.offsets, buckets, R, windows_dev, lc);
 }
 
 template <class Cv>
 static size_t pipeline_bytes(const MsmPlan& P) {
-    return sort_scratch_bytes<Cv>(P) + Arena::round((size_t)P.nb * Cv::kXyzzBytes) + reduce_scratch_bytes<Cv>(P);
+    return sort_scratch_bytes<Cv>(P) + Arena::round((size_t)P.nb * Cv::kXyzzBytes) + reduce_scratch_bytes<Cv>(P) +
+           ba_scratch_bytes(P, P.key_bound);
 }
 
 // Host inputs from n >= kPipelineMinPoints: kBatches batches of points (a short
@@ -1116,10 +1291,13 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     // per batch, any scalar may have all W digits nonzero: the later batches'
     // histograms are not looked at, so their key bound is the trivial one
     MsmPlan Pb[kBatches];
+    int kmax = 0;  // the batch with the most keys: the batch-affine scratch (shared, work stream) is sized for it
     for (int k = 0; k < kBatches; k++) {
         Pb[k] = P;
         Pb[k].max_keys = nk[k] * (size_t)P.W;
         Pb[k].max_segs = std::max<size_t>(1, (Pb[k].max_keys + P.seg - 1) / P.seg);
+        ba_plan(Pb[k], Pb[k].max_keys, std::is_same<Cv, G2>::value, ctx->num_sms);
+        if (Pb[k].max_keys > Pb[kmax].max_keys) kmax = k;
     }
     stats.window_bits = P.c;
     stats.num_windows = P.W;
@@ -1127,6 +1305,7 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     const size_t bucket_bytes = (size_t)P.nb * Cv::kXyzzBytes;
     size_t need = Arena::round((size_t)P.W * Cv::kXyzzBytes) + Arena::round(kBatches * sizeof(uint32_t)) + reduce_scratch_bytes<Cv>(P);
     for (int k = 0; k < kBatches; k++) need += sort_scratch_bytes<Cv>(Pb[k]) + Arena::round(bucket_bytes);
+    need += ba_scratch_bytes(Pb[kmax], Pb[kmax].key_bound);
     ZK_TRY(ensure_scratch(ctx, need));  // may synchronise the device (growth only)
     ZK_TRY(ensure_pinned(ctx, (size_t)P.W * Cv::kXyzzBytes + 64));
     Arena ar;
@@ -1140,6 +1319,7 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
         buckets[k] = ar.take<uint8_t>(bucket_bytes);
     }
     const ReduceScratch R = take_reduce_scratch<Cv>(ar, P);
+    const BaScratch B = take_ba_scratch(ar, Pb[kmax], Pb[kmax].key_bound);
     LaunchCounter lc;
     for (int k = 0; k < kBatches; k++) {  // sorts, on the auxiliary stream
         ZK_TRY_CUDA(cudaStreamWaitEvent(as, ev[3 * k], 0));
@@ -1151,7 +1331,11 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     for (int k = 0; k < kBatches; k++) ZK_TRY_CUDA(cudaMemsetAsync(buckets[k], 0, bucket_bytes, st));
     for (int k = 0; k < kBatches; k++) {  // accumulates, on the work stream
         ZK_TRY_CUDA(cudaStreamWaitEvent(st, ev[3 * k + 2], 0));
-        ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, d_pts + off[k] * Cv::kAffineBytes, Pb[k], S[k], buckets[k], ev[3 * k + 1], lc));
+        if (Pb[k].ba && std::is_same<Cv, G1>::value)
+            ZK_TRY(ba_accumulate_phase(ctx, st, d_pts + off[k] * Cv::kAffineBytes, Pb[k], S[k], B, Pb[k].key_bound, buckets[k],
+                                       ev[3 * k + 1], lc));
+        else
+            ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, d_pts + off[k] * Cv::kAffineBytes, Pb[k], S[k], buckets[k], ev[3 * k + 1], lc));
         ZK_TRY_CUDA(cudaMemcpyAsync(keys_total + k, S[k].offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
     }
     for (int k = 1; k < kBatches; k++) {
@@ -1222,8 +1406,9 @@ static int msm_tables_run(int device, cudaStream_t st, const uint8_t* tables, si
     Pr.tw2 = Pr.tw / Pr.chunk2;
     stats.window_bits = c;
     stats.num_windows = W;
+    ba_plan(P, P.max_keys, std::is_same<Cv, G2>::value, ctx->num_sms);
     const size_t need = Arena::round(Cv::kXyzzBytes) + sort_scratch_bytes<Cv>(P) + Arena::round((size_t)P.nb * Cv::kXyzzBytes) +
-                        reduce_scratch_bytes<Cv>(Pr);
+                        reduce_scratch_bytes<Cv>(Pr) + ba_scratch_bytes(P, P.key_bound);
     ZK_TRY(ensure_scratch(ctx, need));
     ZK_TRY(ensure_pinned(ctx, Cv::kXyzzBytes + 64));
     Arena ar;
@@ -1232,6 +1417,7 @@ static int msm_tables_run(int device, cudaStream_t st, const uint8_t* tables, si
     const SortScratch S = take_sort_scratch<Cv>(ar, P);
     uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * Cv::kXyzzBytes);
     const ReduceScratch R = take_reduce_scratch<Cv>(ar, Pr);
+    const BaScratch B = take_ba_scratch(ar, P, P.key_bound);
     LaunchCounter lc;
     ScopedEvent t0, t1;
     ZK_TRY_CUDA(cudaEventCreate(&t0.e));
@@ -1239,7 +1425,10 @@ static int msm_tables_run(int device, cudaStream_t st, const uint8_t* tables, si
     ZK_TRY(scratch_begin(ctx, st));
     ZK_TRY_CUDA(cudaEventRecord(t0.e, st));
     ZK_TRY(msm_sort_phase<Cv>(ctx, st, d_scalars, n, P, S, lc));
-    ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, tables + lo * Cv::kAffineBytes, P, S, buckets, nullptr, lc));
+    if (P.ba && std::is_same<Cv, G1>::value)
+        ZK_TRY(ba_accumulate_phase(ctx, st, tables + lo * Cv::kAffineBytes, P, S, B, P.key_bound, buckets, nullptr, lc));
+    else
+        ZK_TRY(msm_accumulate_phase<Cv>(ctx, st, tables + lo * Cv::kAffineBytes, P, S, buckets, nullptr, lc));
     ZK_TRY(msm_reduce_phase<Cv>(ctx, st, Pr, S.offsets, buckets, R, windows_dev, lc));
     ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows_dev, Cv::kXyzzBytes, cudaMemcpyDeviceToHost, st));
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + Cv::kXyzzBytes);
@@ -1413,6 +1602,8 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
             sum.accumulate_ms += s.accumulate_ms;
             sum.total_device_ms += s.total_device_ms;
             sum.bucket_adds += s.bucket_adds;
+            sum.ba_pairs += s.ba_pairs;
+            sum.ba_left += s.ba_left;
             sum.window_bits = s.window_bits;
             sum.num_windows = s.num_windows;
             for (int i = 0; i < 8; i++) sum.phase_ms[i] += s.phase_ms[i];
@@ -1452,6 +1643,7 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     std::memcpy(hist, hist_host, sizeof hist);
     MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
     ZK_TRY(check_key_bound(P, hist));
+    ba_plan(P, plan_key_bound(P, hist), std::is_same<Cv, G2>::value, ctx->num_sms);
     stats.window_bits = P.c;
     stats.num_windows = P.W;
 
@@ -1462,7 +1654,7 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     if (own_points) need += Arena::round(pt_bytes);
     if (ref_layout) need += Arena::round(ref_bytes);
     ZK_TRY(ensure_scratch(ctx, need));
-    ZK_TRY(ensure_pinned(ctx, (size_t)P.W * Cv::kXyzzBytes + 64));
+    ZK_TRY(ensure_pinned(ctx, (size_t)P.W * Cv::kXyzzBytes + 128));
     Arena ar;
     ar.base = (char*)ctx->scratch;
     uint8_t* windows_dev = ar.take<uint8_t>((size_t)P.W * Cv::kXyzzBytes);
@@ -1503,10 +1695,13 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     }
 
     uint32_t* total_keys_dev = nullptr;
-    ZK_TRY(msm_pipeline<Cv>(ctx, st, d_points, d_scalars, n, P, ar, windows_dev, points_ready, lc, &total_keys_dev));
+    unsigned long long* ba_dev = nullptr;
+    ZK_TRY(msm_pipeline<Cv>(ctx, st, d_points, d_scalars, n, P, ar, windows_dev, points_ready, lc, &total_keys_dev, &ba_dev));
     ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows_dev, (size_t)P.W * Cv::kXyzzBytes, cudaMemcpyDeviceToHost, st));
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes);
     ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, total_keys_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    unsigned long long* ba_host = (unsigned long long*)((char*)ctx->pinned + (size_t)P.W * Cv::kXyzzBytes + 64);
+    if (ba_dev) ZK_TRY_CUDA(cudaMemcpyAsync(ba_host, ba_dev, 4 * 8, cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaEventRecord(ctx->phase[8], st));
     ZK_TRY_CUDA(cudaEventRecord(t1.e, st));
     ZK_TRY(scratch_end(ctx, st));
@@ -1518,6 +1713,10 @@ static int msm_run(int device, cudaStream_t user_stream, const void* src_points,
     stats.accumulate_ms = stats.phase_ms[3];
     stats.total_device_ms = ms_all;
     stats.bucket_adds = *keys_host;
+    if (ba_dev) {
+        stats.ba_pairs = (long long)(ba_host[0] + ba_host[1] + ba_host[2]);
+        stats.ba_left = (long long)(ba_host[3] & 0xffffffffull);
+    }
     host_combine<Cv>((const uint64_t*)ctx->pinned, P.W, P.c, out_affine);
     return ZK_OK;
 }
@@ -1717,6 +1916,8 @@ extern "C" int zk_msm_last_stats(zk_msm_stats* out) {
     out->window_bits = s.window_bits;
     out->num_windows = s.num_windows;
     out->bucket_adds = s.bucket_adds;
+    out->batch_affine_pairs = s.ba_pairs;
+    out->batch_affine_left = s.ba_left;
     for (int i = 0; i < 8; i++) out->phase_ms[i] = s.phase_ms[i];
     return ZK_OK;
 }

@@ -139,6 +139,8 @@ struct MsmStats {
     int num_windows = 0;
     long long bucket_adds = 0;
     float phase_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    long long ba_pairs = 0;  // affine pair additions of the batch-affine rounds
+    long long ba_left = 0;   // elements left after them for the XYZZ accumulation
 };
 MsmStats& msm_stats();
 

@@ -45,7 +45,8 @@ class MsmStats(ctypes.Structure):
     _fields_ = [("kernel_launches", ctypes.c_int), ("accumulate_ms", ctypes.c_float),
                 ("total_device_ms", ctypes.c_float), ("window_bits", ctypes.c_int),
                 ("num_windows", ctypes.c_int), ("bucket_adds", ctypes.c_longlong),
-                ("phase_ms", ctypes.c_float * 8)]
+                ("phase_ms", ctypes.c_float * 8), ("batch_affine_pairs", ctypes.c_longlong),
+                ("batch_affine_left", ctypes.c_longlong)]
 
 
 class Groth16Arrays(ctypes.Structure):

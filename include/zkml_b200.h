@@ -196,6 +196,11 @@ typedef struct {
     /* device time per phase: count, scan, scatter, accumulate, fixup, reduce,
      * window sums, result copy */
     float phase_ms[8];
+    /* G1 MSMs with enough keys per bucket first add each bucket's points in
+     * affine pairs sharing one inversion per round: the pair additions made,
+     * and the elements left for the mixed XYZZ accumulation (0 when unused) */
+    long long batch_affine_pairs;
+    long long batch_affine_left;
 } zk_msm_stats;
 int zk_msm_last_stats(zk_msm_stats* out);
 

@@ -268,3 +268,51 @@ def test_stats_and_probe():
     st = Z.msm_last_stats()
     assert st["kernel_launches"] >= 8 and st["accumulate_ms"] > 0
     assert Z.probe_imad_rate(0) > 1e12
+
+
+@pytest.mark.parametrize("mode", ["1", "0"])
+def test_g1_batch_affine_rounds_on_edge_cases(mode, monkeypatch):
+    """The batch-affine rounds of the G1 accumulation (pairwise affine additions
+    sharing one inversion per round) forced on (1) and off (0) for every case:
+    the golden vectors (zero scalars, points at infinity, duplicates, P and -P,
+    r - 1, all-zero inputs), a skewed mix with repeated points and opposite
+    points in one bucket, and the oracle at several sizes."""
+    monkeypatch.setenv("ZK_MSM_BATCH_AFFINE", mode)
+    gz = g("g1_msm.npz")
+    for name in cases(gz):
+        pts, sc, res = gz[name + "_points"], gz[name + "_scalars"], gz[name + "_result"]
+        assert np.array_equal(Z.msm_g1(dev(pts), dev(sc)), res), name
+    n = 5000
+    k, pts, sc = _random_instance(n, 0xBA00)
+    ph = Z.to_host(pts)
+    ph[100:200] = ph[300:400]                 # repeated points with repeated scalars: doublings
+    sc[100:200] = sc[300:400]
+    for i in range(500, 600):                 # -P beside P with the same scalar: P + (-P) in one bucket
+        ph[i] = ph[i + 100]
+        y = (O.P - O.to_int(ph[i + 100][4:8])) % O.P
+        ph[i][4:8] = [(y >> (64 * w)) & (2**64 - 1) for w in range(4)]
+    sc[500:600] = sc[600:700]
+    ph[800:900] = 0                           # points at infinity
+    sc[900:1000] = sc[7]                      # one hot bucket
+    exp = O.msm_g1(ph, sc, nthreads=os.cpu_count())
+    assert np.array_equal(Z.msm_g1(dev(ph), dev(sc)), exp)
+    for n in (1, 2, 3, 255, 4097, 1 << 14):
+        _, p2, s2 = _random_instance(n, 0xBA10 + n)
+        assert np.array_equal(Z.msm_g1(p2, dev(s2)), O.msm_g1(Z.to_host(p2), s2, nthreads=os.cpu_count())), n
+
+
+def test_g1_batch_affine_matches_serial_at_2_22():
+    """2^22 uniform points: the default plan (batch-affine rounds, then the XYZZ
+    accumulation) equals the serial XYZZ accumulation and the identity."""
+    n = 1 << 22
+    k = Z.random_fr(n, 0xBA22)
+    sc = Z.random_fr(n, 0xBA23)
+    pts = Z.g1_fixed_base(dev(k))
+    got = Z.msm_g1(pts, dev(sc))
+    exp = O.g1_fixed_base(O.fr_dot(k, sc)[None, :])[0]
+    assert np.array_equal(got, exp)
+    os.environ["ZK_MSM_BATCH_AFFINE"] = "0"
+    try:
+        assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
+    finally:
+        del os.environ["ZK_MSM_BATCH_AFFINE"]
