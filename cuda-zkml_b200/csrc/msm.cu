@@ -1021,14 +1021,15 @@ static void ba_plan(MsmPlan& P, size_t key_bound, bool g2, int num_sms) {
 
 struct BaScratch {
     uint32_t* off[2];         // level offsets (nb + 1), alternating
-    uint8_t* pts[2];          // level points: levels 1 and 3 in pts[0], level 2 in pts[1]
+    uint8_t* pts[2];          // level points: levels 1 and 3 in pts[0]; the dense level 0 and level 2 in pts[1]
     Fp* prefix;               // running products before each regular pair
     Fp* totals;               // per-thread products, turned into their inverses
     Fp* tree;                 // product-tree nodes and upper levels
     unsigned long long* pairs;  // regular pair additions per round, then the elements left (4 words)
 };
 static size_t ba_bound(const MsmPlan& P, size_t key_bound, int level) { return (key_bound >> level) + P.nb + 1; }
-static size_t ba_threads(size_t outputs) { return (outputs + kBaItems - 1) / kBaItems; }
+// threads of a pass over `outputs` positions: whole warps of 32 kBaItems positions
+static size_t ba_threads(size_t outputs) { return (outputs + 32 * kBaItems - 1) / (32 * kBaItems) * 32; }
 static size_t ba_tree_elems(size_t n) {  // nodes of every level plus the upper levels' values
     size_t e = 0;
     while (n > 1) {
@@ -1040,18 +1041,18 @@ static size_t ba_tree_elems(size_t n) {  // nodes of every level plus the upper 
 }
 static size_t ba_scratch_bytes(const MsmPlan& P, size_t key_bound) {
     if (!P.ba) return 0;
-    const size_t b1 = ba_bound(P, key_bound, 1), b2 = ba_bound(P, key_bound, 2), nt = ba_threads(b1);
-    return 2 * Arena::round((size_t)(P.nb + 1) * 4) + Arena::round(b1 * 64) + Arena::round(b2 * 64) + Arena::round(b1 * 32) +
+    const size_t b1 = ba_bound(P, key_bound, 1), b0 = std::max(key_bound, ba_bound(P, key_bound, 2)), nt = ba_threads(b1);
+    return 2 * Arena::round((size_t)(P.nb + 1) * 4) + Arena::round(b1 * 64) + Arena::round(b0 * 64) + Arena::round(b1 * 32) +
            Arena::round(nt * 32) + Arena::round(ba_tree_elems(nt) * 32) + Arena::round(4 * 8);
 }
 static BaScratch take_ba_scratch(Arena& ar, const MsmPlan& P, size_t key_bound) {
     BaScratch B{};
     if (!P.ba) return B;
-    const size_t b1 = ba_bound(P, key_bound, 1), b2 = ba_bound(P, key_bound, 2), nt = ba_threads(b1);
+    const size_t b1 = ba_bound(P, key_bound, 1), b0 = std::max(key_bound, ba_bound(P, key_bound, 2)), nt = ba_threads(b1);
     B.off[0] = ar.take<uint32_t>(P.nb + 1);
     B.off[1] = ar.take<uint32_t>(P.nb + 1);
     B.pts[0] = ar.take<uint8_t>(b1 * 64);
-    B.pts[1] = ar.take<uint8_t>(b2 * 64);
+    B.pts[1] = ar.take<uint8_t>(b0 * 64);
     B.prefix = ar.take<Fp>(b1);
     B.totals = ar.take<Fp>(nt);
     B.tree = ar.take<Fp>(ba_tree_elems(nt));
@@ -1104,6 +1105,7 @@ static int ba_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void* 
     const uint32_t* off_in = S.offsets;
     const uint8_t* pts_in = (const uint8_t*)d_points;
     for (int r = 0; r < P.ba; r++) {
+        // level r + 1 goes to pts[0] (odd levels) or pts[1] (even; level 0 too)
         uint32_t* off_out = B.off[r & 1];
         uint8_t* pts_out = B.pts[r & 1];
         // the next level's offsets: exclusive scan of ceil(c_g / 2^(r + 1))
@@ -1115,15 +1117,15 @@ static int ba_accumulate_phase(DeviceContext* ctx, cudaStream_t st, const void* 
         const size_t nt = ba_threads(ba_bound(P, key_bound, r + 1));
         const unsigned blocks = (unsigned)((nt + kBaThreads - 1) / kBaThreads);
         if (r == 0)
-            ba_pass_a_kernel<true><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, B.pairs + r);
+            ba_pass_a_kernel<true><<<blocks, kBaThreads, 0, st>>>(S.keys, (const uint8_t*)d_points, B.pts[1], off_in, nullptr, off_out,
+                                                                  P.nb, B.prefix, B.totals, nt, B.pairs + r);
         else
-            ba_pass_a_kernel<false><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, B.pairs + r);
+            ba_pass_a_kernel<false><<<blocks, kBaThreads, 0, st>>>(nullptr, nullptr, nullptr, off_in, pts_in, off_out, P.nb, B.prefix,
+                                                                   B.totals, nt, B.pairs + r);
         lc++;
         ZK_TRY(batch_invert(st, B.totals, nt, B.tree, lc));
-        if (r == 0)
-            ba_pass_b_kernel<true><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, pts_out);
-        else
-            ba_pass_b_kernel<false><<<blocks, kBaThreads, 0, st>>>(S.keys, off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, pts_out);
+        if (r == 0) pts_in = B.pts[1];  // the dense level 0 written by pass A
+        ba_pass_b_kernel<<<blocks, kBaThreads, 0, st>>>(off_in, pts_in, off_out, P.nb, B.prefix, B.totals, nt, pts_out);
         lc++;
         off_in = off_out;
         pts_in = pts_out;
@@ -1520,46 +1522,70 @@ int msm_shared_scalars_run(DeviceContext* ctx, cudaStream_t st, const void* d_sc
     stats.window_bits = P.c;
     stats.num_windows = P.W;
 
-    size_t need = sort_scratch_bytes<G1>(P) + Arena::round(P2.max_segs * G2::kXyzzBytes) * 2 + Arena::round(P2.max_segs * 4) * 2 +
-                  Arena::round((size_t)P.nb * G2::kXyzzBytes) + reduce_scratch_bytes<G2>(P) +
-                  Arena::round((size_t)n_sets * P.W * G2::kXyzzBytes);
+    // The sets share the keys but nothing else: each gets its own partial
+    // slots, buckets and reduce scratch and runs on its own stream, so their
+    // chains of dependent additions (fixup rounds, running sums, window sums
+    // over a witness's few full buckets) overlap instead of queueing.
+    auto set_bytes = [&](bool g2) {
+        const MsmPlan& Q = g2 ? P2 : P;
+        const size_t xb = g2 ? G2::kXyzzBytes : G1::kXyzzBytes;
+        return 2 * Arena::round(Q.max_segs * xb) + 2 * Arena::round(Q.max_segs * 4) + Arena::round(4) +
+               Arena::round((size_t)P.nb * xb) + (g2 ? reduce_scratch_bytes<G2>(P2) : reduce_scratch_bytes<G1>(P));
+    };
+    size_t need = sort_scratch_bytes<G1>(P) + Arena::round((size_t)n_sets * P.W * G2::kXyzzBytes);
+    for (int k = 0; k < n_sets; k++) need += set_bytes(is_g2[k] != 0);
     ZK_TRY(ensure_scratch(ctx, need));
     ZK_TRY(ensure_pinned(ctx, (size_t)n_sets * P.W * G2::kXyzzBytes + 64));
+    ZK_TRY(ensure_set_streams(ctx));
     Arena ar;
     ar.base = (char*)ctx->scratch;
     const SortScratch S = take_sort_scratch<G1>(ar, P);
-    SortScratch S2 = S;  // same keys, G2-sized partial slots
-    S2.part_first = ar.take<uint8_t>(P2.max_segs * G2::kXyzzBytes);
-    S2.part_last = ar.take<uint8_t>(P2.max_segs * G2::kXyzzBytes);
-    S2.first_bucket = ar.take<uint32_t>(P2.max_segs);
-    S2.last_bucket = ar.take<uint32_t>(P2.max_segs);
-    uint8_t* buckets = ar.take<uint8_t>((size_t)P.nb * G2::kXyzzBytes);
-    const ReduceScratch R = take_reduce_scratch<G2>(ar, P);  // the larger record size serves both curves
     uint8_t* windows = ar.take<uint8_t>((size_t)n_sets * P.W * G2::kXyzzBytes);
+    SortScratch Sk[8];
+    uint8_t* buckets[8];
+    ReduceScratch Rk[8];
+    for (int k = 0; k < n_sets; k++) {
+        const bool g2 = is_g2[k] != 0;
+        const MsmPlan& Q = g2 ? P2 : P;
+        const size_t xb = g2 ? G2::kXyzzBytes : G1::kXyzzBytes;
+        Sk[k] = S;  // the keys and offsets are shared
+        Sk[k].part_first = ar.take<uint8_t>(Q.max_segs * xb);
+        Sk[k].part_last = ar.take<uint8_t>(Q.max_segs * xb);
+        Sk[k].first_bucket = ar.take<uint32_t>(Q.max_segs);
+        Sk[k].last_bucket = ar.take<uint32_t>(Q.max_segs);
+        Sk[k].max_span = ar.take<uint32_t>(1);
+        buckets[k] = ar.take<uint8_t>((size_t)P.nb * xb);
+        Rk[k] = g2 ? take_reduce_scratch<G2>(ar, P2) : take_reduce_scratch<G1>(ar, P);
+    }
     LaunchCounter lc;
-    ScopedEvent ev[9];
+    ScopedEvent ev[9], done[8];
     for (int k = 0; k <= n_sets; k++) ZK_TRY_CUDA(cudaEventCreate(&ev[k].e));
+    for (int k = 0; k < n_sets; k++) ZK_TRY_CUDA(cudaEventCreateWithFlags(&done[k].e, cudaEventDisableTiming));
     ZK_TRY(msm_sort_phase<G1>(ctx, st, d_scalars, n, P, S, lc));
     ZK_TRY_CUDA(cudaEventRecord(ev[0].e, st));
     for (int k = 0; k < n_sets; k++) {
+        cudaStream_t ss = ctx->set_stream[k];
+        ZK_TRY_CUDA(cudaStreamWaitEvent(ss, ev[0].e, 0));
         uint8_t* win = windows + (size_t)k * P.W * G2::kXyzzBytes;
         const uint32_t ilo = idx_range ? idx_range[2 * k] : 0u, ihi = idx_range ? idx_range[2 * k + 1] : 0xffffffffu;
         if (is_g2[k]) {
-            ZK_TRY(msm_accumulate_phase<G2>(ctx, st, d_points[k], P2, S2, buckets, nullptr, lc, ilo, ihi));
-            ZK_TRY(msm_reduce_phase<G2>(ctx, st, P2, S.offsets, buckets, R, win, lc));
+            ZK_TRY(msm_accumulate_phase<G2>(ctx, ss, d_points[k], P2, Sk[k], buckets[k], nullptr, lc, ilo, ihi));
+            ZK_TRY(msm_reduce_phase<G2>(ctx, ss, P2, S.offsets, buckets[k], Rk[k], win, lc));
         } else {
-            ZK_TRY(msm_accumulate_phase<G1>(ctx, st, d_points[k], P, S, buckets, nullptr, lc, ilo, ihi));
-            ZK_TRY(msm_reduce_phase<G1>(ctx, st, P, S.offsets, buckets, R, win, lc));
+            ZK_TRY(msm_accumulate_phase<G1>(ctx, ss, d_points[k], P, Sk[k], buckets[k], nullptr, lc, ilo, ihi));
+            ZK_TRY(msm_reduce_phase<G1>(ctx, ss, P, S.offsets, buckets[k], Rk[k], win, lc));
         }
-        ZK_TRY_CUDA(cudaEventRecord(ev[k + 1].e, st));
+        ZK_TRY_CUDA(cudaEventRecord(ev[k + 1].e, ss));
+        ZK_TRY_CUDA(cudaEventRecord(done[k].e, ss));
     }
+    for (int k = 0; k < n_sets; k++) ZK_TRY_CUDA(cudaStreamWaitEvent(st, done[k].e, 0));
     ZK_TRY_CUDA(cudaMemcpyAsync(ctx->pinned, windows, (size_t)n_sets * P.W * G2::kXyzzBytes, cudaMemcpyDeviceToHost, st));
     uint32_t* keys_host = (uint32_t*)((char*)ctx->pinned + (size_t)n_sets * P.W * G2::kXyzzBytes);
     ZK_TRY_CUDA(cudaMemcpyAsync(keys_host, S.offsets + P.nb, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     ZK_TRY(scratch_end(ctx, st));
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
-    if (set_ms)  // the shared sort is not in any set's time
-        for (int k = 0; k < n_sets; k++) cudaEventElapsedTime(&set_ms[k], ev[k].e, ev[k + 1].e);
+    if (set_ms)  // each set from the end of the shared sort (the sets overlap)
+        for (int k = 0; k < n_sets; k++) cudaEventElapsedTime(&set_ms[k], ev[0].e, ev[k + 1].e);
     stats.kernel_launches = lc.n;
     stats.bucket_adds = (long long)*keys_host * n_sets;
     for (int k = 0; k < n_sets; k++) {

@@ -97,9 +97,20 @@ int create_context(int device, DeviceContext** out) {
     return ZK_OK;
 }
 
+int ensure_set_streams(DeviceContext* ctx) {
+    for (auto& s : ctx->set_stream)
+        if (!s) ZK_TRY_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    return ZK_OK;
+}
+
 void destroy_context(DeviceContext* c) {
     if (!c) return;
     if (c->device >= 0) cudaSetDevice(c->device);
+    for (cudaStream_t s : c->set_stream)
+        if (s) {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
     cudaStream_t streams[3] = {c->stream, c->copy_stream, c->aux_stream};
     for (cudaStream_t s : streams)
         if (s) cudaStreamSynchronize(s);

@@ -109,6 +109,7 @@ struct DeviceContext {
     void* pinned = nullptr;          // small pinned host staging (results)
     size_t pinned_bytes = 0;
     NttTables* ntt = nullptr;
+    cudaStream_t set_stream[8] = {};  // MSMs sharing one sort: one stream per point set (created on first use)
     std::mutex mu;                   // one call at a time per device context
 };
 
@@ -128,6 +129,8 @@ int ensure_pinned(DeviceContext* ctx, size_t bytes);
 // Order a call's work on `st` after the previous user of the scratch arena
 // (which may have run on another stream), and mark the end of its use.
 int scratch_begin(DeviceContext* ctx, cudaStream_t st);
+// The per-set streams of a context (msm_shared_scalars_run).
+int ensure_set_streams(DeviceContext* ctx);
 int scratch_end(DeviceContext* ctx, cudaStream_t st);
 
 // per-thread statistics of the last MSM

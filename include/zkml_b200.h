@@ -261,7 +261,7 @@ int zk_groth16_prove(zk_groth16_pk* pk, const zk_r1cs* r1cs, void* stream, const
 typedef struct {
     float matvec_ms;     /* witness copy + sparse A*w, B*w, C*w */
     float compute_h_ms;  /* 7 NTTs with the fused coset steps */
-    float msm_ms[5];     /* A, B (G2), L, H, B1 */
+    float msm_ms[5];     /* A, B (G2), L, H, B1: H from its start, the other four (run side by side) from the end of their shared sort */
     float total_ms;      /* whole prove, device time incl. host assembly */
 } zk_prove_stats;
 int zk_groth16_last_stats(zk_prove_stats* out);
