@@ -23,7 +23,8 @@ cpu_baseline: the oracle's multi-threaded Pippenger (a CPU restatement of the
         own host arithmetic (compiled from its sources into oracle/_ref) on all
         host cores, over a 2^18-point sample per step; beside it, the
         reference's own GPU NTT (bn254::ntt_gpu built for sm_100a) at 2^16,
-        2^20 and 2^24 on the same B200.
+        2^20 and 2^24 on the same B200, and the reference's Groth16Prover::prove
+        linked against this library on configs 1 and 4.
 """
 import argparse
 import json
@@ -128,6 +129,51 @@ def reference_gpu_ntt(ref, sizes, reps=3):
     return out
 
 
+def reference_drop_in_prove(reps=3):
+    """The reference's own Groth16Prover::prove (src/prover/groth16.cu:655-920)
+    linked against this library's bn254::msm_g1 / msm_g2 / ntt_gpu
+    (oracle/_ref/libzkref_g16.so): what a zkml-prove user gets from swapping the
+    library in.  Configs 1 and 4 as the reference's build_statement_v2 builds
+    them, keys from this library's setup under the reference's deterministic
+    toxic waste, loaded by the reference from ZKMLPK3 files; the time is the
+    prove call alone (its host matvec, witness check and PCIe round trips
+    included), beside zk_groth16_prove on the same key and witness.  Every
+    proof is checked equal to this library's."""
+    import tempfile
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import groth16_oracle as G
+    import ref_statements as RS
+    import zkml_b200 as Z
+    for p in (RS.STMT_LIB, RS.G16_LIB):
+        if not os.path.exists(p):
+            return {"unavailable": f"{os.path.basename(p)} not built"}
+    lib = RS.g16(RS.G16_LIB)
+    out = {}
+    for name, build in (("config1_mlp_b4", RS.mlp_statement), ("config4_statement_v2_B", lambda: RS.tiny_cnn_statement("B"))):
+        c = build()
+        r1 = Z.R1cs(c)
+        pk = Z.ProvingKey.setup(r1, G.toxic_deterministic())
+        r, s = G.blinding_deterministic()
+        with tempfile.TemporaryDirectory() as d:
+            pk_path, vk_path = os.path.join(d, "pk.bin"), os.path.join(d, "vk.bin")
+            pk.save(pk_path)
+            pk.save_vk(vk_path)
+            ours, ref_ms, our_ms = None, [], []
+            for _ in range(reps + 1):
+                t0 = time.perf_counter()
+                ours = pk.prove(r1, c["witness"], r, s)[0]
+                our_ms.append(1e3 * (time.perf_counter() - t0))
+                proof, ok, ms = RS.prove_with_keys(lib, pk_path, vk_path, c)
+                if not ok or proof != ours:
+                    return {"error": f"{name}: the drop-in proof differs or fails to verify"}
+                ref_ms.append(ms)
+        out[name] = {"constraints": c["num_constraints"], "log_n": r1.log_n,
+                     "reference_prove_ms": statistics.median(ref_ms[1:]),
+                     "zk_groth16_prove_ms": statistics.median(our_ms[1:]), "reps": reps, "proofs_equal": True}
+        del pk, r1
+    return out
+
+
 def ctypes_ptr(t):
     import ctypes
     return ctypes.c_void_p(t.data_ptr())
@@ -157,7 +203,7 @@ def run_reference(args):
     sc = rng.fr_vector(n)
     out = np.zeros(8, np.uint64)
     inf = ctypes.c_int()
-    gpu_ntt = None
+    gpu_ntt = drop_in = None
     if O.ref_available():
         ref = O.ref()
         kind = "reference"
@@ -174,6 +220,13 @@ def run_reference(args):
                     gpu_ntt = reference_gpu_ntt(ref, (16, 20, 24))
             except Exception as e:  # reported, not fatal: the MSM arm stands alone
                 gpu_ntt = {"error": str(e)[:200]}
+        if not args.no_prove:
+            try:
+                import torch
+                if torch.cuda.is_available():
+                    drop_in = reference_drop_in_prove()
+            except Exception as e:
+                drop_in = {"error": str(e)[:200]}
     else:
         kind = "port"
 
@@ -195,7 +248,7 @@ def run_reference(args):
                      "sample_points": n},
           "cpu_baseline": {"value": value, "unit": "points/s", "cores": cores, "kind": kind, "sample": sample},
           "e2e": {"value": value, "unit": "points/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-          "reference_gpu_ntt": gpu_ntt})
+          "reference_gpu_ntt": gpu_ntt, "reference_drop_in_prove": drop_in})
 
 
 # ---------------------------------------------------------------- Groth16 prove

@@ -2,7 +2,8 @@
 (build_statement_v2, src/prover/statement_v2.cuh:82-257), through
 oracle/_ref/libzkref_stmt.so (test infrastructure, built by oracle/Makefile
 from the reference tree), and the reference's Groth16 prover/verifier entry
-points of oracle/ref_groth16_driver.cu.
+points of oracle/ref_groth16_driver.cu.  Test and measurement infrastructure:
+used by the tests and by bench.py's reference arm only.
 
 Circuits come back in the layout of zkml_b200.synth_*: SparseEntry arrays A, B,
 C, the witness (num_variables x 4 Montgomery limbs) and the counts."""
@@ -14,7 +15,7 @@ import numpy as np
 import zkml_b200 as Z
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_DIR = os.path.join(os.path.dirname(HERE), "oracle", "_ref")
+REF_DIR = os.path.join(HERE, "_ref")
 STMT_LIB = os.path.join(REF_DIR, "libzkref_stmt.so")
 G16_LIB = os.path.join(REF_DIR, "libzkref_g16.so")          # reference Groth16 + this library's msm/ntt
 G16_CPU_LIB = os.path.join(REF_DIR, "libzkref_g16_cpu.so")  # reference Groth16 + the CPU oracle's msm/ntt

@@ -301,18 +301,19 @@ def test_g1_batch_affine_rounds_on_edge_cases(mode, monkeypatch):
         assert np.array_equal(Z.msm_g1(p2, dev(s2)), O.msm_g1(Z.to_host(p2), s2, nthreads=os.cpu_count())), n
 
 
-def test_g1_batch_affine_matches_serial_at_2_22():
-    """2^22 uniform points: the default plan (batch-affine rounds, then the XYZZ
-    accumulation) equals the serial XYZZ accumulation and the identity."""
+def test_g1_batch_affine_matches_serial_at_2_22(monkeypatch):
+    """2^22 uniform points: the batch-affine rounds followed by the XYZZ
+    accumulation of what they leave (ZK_MSM_BATCH_AFFINE=1) equal the default
+    serial XYZZ accumulation and the identity sum k_i s_i G."""
     n = 1 << 22
     k = Z.random_fr(n, 0xBA22)
     sc = Z.random_fr(n, 0xBA23)
     pts = Z.g1_fixed_base(dev(k))
-    got = Z.msm_g1(pts, dev(sc))
     exp = O.g1_fixed_base(O.fr_dot(k, sc)[None, :])[0]
-    assert np.array_equal(got, exp)
-    os.environ["ZK_MSM_BATCH_AFFINE"] = "0"
-    try:
-        assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
-    finally:
-        del os.environ["ZK_MSM_BATCH_AFFINE"]
+    monkeypatch.setenv("ZK_MSM_BATCH_AFFINE", "1")
+    assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
+    st = Z.msm_last_stats()
+    assert st["batch_affine_pairs"] > n  # the rounds ran
+    monkeypatch.delenv("ZK_MSM_BATCH_AFFINE")
+    assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
+    assert Z.msm_last_stats()["batch_affine_pairs"] == 0

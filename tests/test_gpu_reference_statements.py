@@ -2,7 +2,7 @@
 byte-for-byte against the reference's Groth16Prover::prove.
 
 Circuits (built by the reference's build_statement_v2 through
-tests/ref_statements.py):
+oracle/ref_statements.py):
   * config 1: the quantised MLP 64 -> 32 (RELU_EXACT, 24 bits, shift 6) -> 10,
     int8 weights, inputs 0..16, batch 4, context-bound (7,762 constraints,
     domain 2^13);
