@@ -1031,6 +1031,7 @@ static int pk_load(int device, const char* path, zk_groth16_pk* pk) {
     const size_t raw_bytes = (size_t)(last - first);
     const size_t g1_count = (size_t)counts[0] + counts[1] + counts[3] + counts[4];
     DeviceBuffer raw_buf, g1_buf, g2_buf;
+    const auto a0 = std::chrono::steady_clock::now();
     ZK_TRY_CUDA(raw_buf.alloc(raw_bytes + 64));
     ZK_TRY_CUDA(g1_buf.alloc(std::max<size_t>(g1_count, 1) * 64));
     ZK_TRY_CUDA(g2_buf.alloc(std::max<size_t>(counts[2], 1) * 128));
@@ -1059,6 +1060,7 @@ static int pk_load(int device, const char* path, zk_groth16_pk* pk) {
         ZK_TRY_CUDA(cudaEventCreateWithFlags(&pin_free[i], cudaEventDisableTiming));
         ZK_TRY_CUDA(cudaEventRecord(pin_free[i], cs));
     }
+    st.alloc_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - a0).count();
     const int fd = fileno(f);
     double read_s = 0;
     for (size_t pos = 0, c = 0; pos < raw_bytes; pos += kChunk, c++) {

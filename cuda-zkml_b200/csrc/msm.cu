@@ -121,10 +121,20 @@ static size_t plan_key_bound(const MsmPlan& p, const uint32_t* hist) {
     return key_bound;
 }
 
-static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist, int num_sms) {
+// hist_exact: `hist` counts every scalar of the MSM (not an estimate from a
+// sample), so the windows above the longest scalar's top digit hold no digit
+// and are left out.
+static MsmPlan make_plan(size_t n, bool g2, const uint32_t* hist, int num_sms, bool hist_exact = true) {
     MsmPlan p;
     p.c = choose_window_bits(n, g2, hist);
     p.W = (255 + p.c - 1) / p.c;
+    if (hist && hist_exact) {
+        int maxbits = 0;
+        for (int b = 0; b < 256; b++)
+            if (hist[b]) maxbits = b;
+        // a b-bit scalar's signed digits fill ceil((b + 1) / c) windows at most
+        p.W = std::max(1, std::min(p.W, (maxbits + 1 + p.c - 1) / p.c));
+    }
     p.B = 1u << (p.c - 1);
     p.nb = (uint32_t)p.W * p.B;
     p.max_keys = n * (size_t)p.W;
@@ -199,7 +209,34 @@ __device__ __forceinline__ int next_digit(uint32_t v[8], int c, uint32_t& carry)
     return (int)raw;
 }
 
-// Bit lengths of the standard-form scalars (0..254), for the window choice.
+// A standard-form scalar s above (r - 1) / 2 is replaced by r - s, and the
+// caller negates its digits: s P = (r - s)(-P), the same point, so the result
+// does not change.  A signed value -v of a zkML witness (stored as r - v) then
+// costs the digits of v instead of a full-width scalar's; folded scalars have
+// at most 253 bits.  Returns whether s was replaced.
+__device__ __forceinline__ bool fold_scalar(uint32_t v[8]) {
+    bool gt = false, decided = false;
+#pragma unroll
+    for (int k = 7; k >= 0; k--) {
+        const uint32_t h = (ModR::m(k) >> 1) | (k < 7 ? ModR::m(k + 1) << 31 : 0u);  // (r - 1) / 2, r odd
+        if (!decided && v[k] != h) {
+            gt = v[k] > h;
+            decided = true;
+        }
+    }
+    if (gt) {
+        uint32_t borrow = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const uint64_t d = (uint64_t)ModR::m(k) - v[k] - borrow;
+            v[k] = (uint32_t)d;
+            borrow = (uint32_t)(d >> 63);
+        }
+    }
+    return gt;
+}
+
+// Bit lengths of the folded standard-form scalars (0..253), for the window choice.
 __global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restrict__ scalars, size_t n, uint32_t* __restrict__ hist) {
     __shared__ uint32_t h[256];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
@@ -208,6 +245,7 @@ __global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restri
         Fr s;
         fload_nc(s, scalars + i);
         ffrom_mont(s, s);
+        fold_scalar(s.v);
         int len = 0;
 #pragma unroll
         for (int k = 7; k >= 0; k--)
@@ -223,6 +261,7 @@ __global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restri
 // 0 for a zero digit) so that the scatter can run one window after another.
 // The lanes of a warp that hit the same bucket add their count with one atomic
 // (witness scalars put most digits in one bucket: 0/1 range-check bits).
+// Scalars are folded (fold_scalar): the digits of r - s with their signs flipped.
 template <bool kAgg>
 __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c, int W, uint32_t wstride,
                                  uint32_t* __restrict__ counts, uint32_t* __restrict__ digits) {
@@ -231,6 +270,7 @@ __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c
         Fr s;
         fload_nc(s, scalars + i);
         ffrom_mont(s, s);
+        const bool neg = fold_scalar(s.v);
         uint32_t carry = 0;
         for (int w = 0; w < W; w++) {
             const int d = next_digit(s.v, c, carry);
@@ -238,7 +278,7 @@ __global__ void msm_count_kernel(const Fr* __restrict__ scalars, size_t n, int c
             if (d) {
                 const uint32_t b = (uint32_t)(d < 0 ? -d : d) - 1;
                 key = (uint32_t)w * wstride + b;
-                code = (d < 0 ? 0x80000000u : 0u) | (b + 1);
+                code = ((d < 0) != neg ? 0x80000000u : 0u) | (b + 1);
             }
             if (kAgg) {
                 const uint32_t peers = __match_any_sync(__activemask(), key);
@@ -1283,7 +1323,7 @@ static int msm_run_host_pipelined(DeviceContext* ctx, cudaStream_t st, const voi
     ZK_TRY_CUDA(cudaStreamSynchronize(st));
     uint32_t hist[256];
     for (int b = 0; b < 256; b++) hist[b] = (uint32_t)std::min<double>(4e9, (double)hist_host[b] * (double)n / (double)nk[0]);
-    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms);
+    MsmPlan P = make_plan(n, std::is_same<Cv, G2>::value, hist, ctx->num_sms, false);
     // The batches are sized by the trivial key bound below: a narrow window
     // chosen from small first-batch scalars (many windows) could push that past
     // the 32-bit key space, so such a plan gives way to the full-width one.
@@ -1452,9 +1492,16 @@ static int msm_tables_run(int device, cudaStream_t st, const uint8_t* tables, si
 
 // Window width for precomputed tables of n bases: minimise the mixed additions
 // (n ceil(255 / c), 10 Fp mul each) plus one bucket reduction (2^(c-1) x 30).
+// ZK_H_TABLE_BITS (8..22) overrides the choice for tables built afterwards.
 void g1_window_tables_shape(size_t n, int* c_out, int* W_out) {
     int best = 12;
     double best_cost = 1e300;
+    const char* env = getenv("ZK_H_TABLE_BITS");
+    if (env && atoi(env) >= 8 && atoi(env) <= 22) {
+        *c_out = atoi(env);
+        *W_out = (255 + *c_out - 1) / *c_out;
+        return;
+    }
     for (int c = 8; c <= 22; c++) {
         const double W = (255 + c - 1) / c;
         const double cost = (double)n * W * 10.0 + (double)(1u << (c - 1)) * 30.0;

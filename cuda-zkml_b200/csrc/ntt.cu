@@ -16,8 +16,10 @@
 // f; one permutation kernel moves it to natural order and applies any final
 // scale (n^-1) and coset factor (g^-f), so the whole transform is P + 1
 // launches with 2 (P + 1) streaming passes over HBM.  Inter-pass twiddles
-// w_n^e come from two 2^(L/2)-entry tables (w^lo * w^(hi 2^h)), held in L2;
-// nothing of size n is ever read besides the data.
+// w_n^e and coset factors come from one table of all n factors up to
+// 2^kFullTableMaxLog (one 32-byte read per element in each pass that applies
+// them, in place of a Montgomery product), else from two 2^(L/2)-entry tables
+// (w^lo * w^(hi 2^h)) held in L2.
 //
 // A CTA owns C adjacent columns (C = 8: 256-byte contiguous runs per row) or,
 // in the last pass (M = 1), C adjacent contiguous sub-transforms, so every

@@ -3,7 +3,8 @@
 //
 // Every rank holds the whole proving key and R1CS on its own device and gets
 // the same proof bytes as the one-device prover:
-//   1. each rank uploads one slice of the witness; the slices are all-gathered;
+//   1. each rank uploads a quarter of its slice of the witness at a time, and
+//      each round's slices are all-gathered while the next round is uploaded;
 //   2. rank j computes constraint rows [j m, (j + 1) m) of A w, B w, C w
 //      (m = n / N) and checks them (R1CS::verify_witness, src/prover/
 //      circuit.cuh:93-124); the first failing row is an all-reduce MIN, read at
@@ -16,7 +17,8 @@
 //      cross-rank N-point step (ntt_cross_run).  The all-to-alls are grouped
 //      point-to-point copies whose send and receive blocks are contiguous by
 //      construction (a gather kernel writes the first one's send layout), so no
-//      layout copy surrounds them; the three polynomials travel together;
+//      layout copy surrounds them; they run one polynomial at a time on a
+//      second stream, so one polynomial travels while another is transformed;
 //   5. rank j's H MSM over its own coefficients of h (h_msm_blocks);
 //   6. the partial sums (384 B per rank) are all-gathered and every rank folds
 //      them and assembles the proof (zk_groth16_assemble_parts).
@@ -308,6 +310,7 @@ namespace split {
 
 static constexpr int kSumWords = 48;  // A (8) | B2 (16) | L (8) | H (8) | B1 (8)
 static constexpr int kRecWords = 49;  // the sums, then the rank's status (0: its part succeeded)
+static constexpr int kWitnessChunks = 4;  // upload rounds of the witness, each all-gathered behind the next
 
 // dst[k][j][t] = src[k][j + N t]: rows of this rank's block regrouped by
 // residue mod N, the send layout of the first all-to-all (to the "cyclic"
@@ -327,19 +330,23 @@ __global__ void cyclic_gather_kernel(const Fr* __restrict__ src, Fr* __restrict_
 struct State {
     int device = -1, nranks = 0, rank = 0;
     uint64_t n = 0, m = 0, q = 0;
-    size_t sw = 0;  // witness rows per rank (padded)
+    size_t cw = 0;  // witness rows per rank and upload round (padded: N kWitnessChunks cw >= witness rows)
     cudaStream_t st = nullptr;
-    Fr* w = nullptr;    // nranks * sw
+    cudaStream_t cst = nullptr;  // the all-to-alls of compute_h, beside the transforms on st
+    Fr* w = nullptr;    // kWitnessChunks * nranks * cw
     Fr* p[3] = {};      // three buffers of 3 m
     unsigned long long* bad = nullptr;
     uint64_t* rec = nullptr;          // nranks * kRecWords
     unsigned long long* h_bad = nullptr;  // pinned
     uint64_t* h_rec = nullptr;            // pinned, nranks * kRecWords
     cudaEvent_t ev[16] = {};
+    cudaEvent_t dep[16] = {};  // ordering between st and cst (no timing)
+    cudaEvent_t xev[20] = {};  // begin and end of each all-to-all on cst
     std::vector<Xfer> xf;
     ~State() {
         if (device >= 0) cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
+        if (cst) cudaStreamSynchronize(cst);
         cudaFree(w);
         for (auto b : p) cudaFree(b);
         cudaFree(bad);
@@ -348,7 +355,12 @@ struct State {
         cudaFreeHost(h_rec);
         for (auto e : ev)
             if (e) cudaEventDestroy(e);
+        for (auto e : dep)
+            if (e) cudaEventDestroy(e);
+        for (auto e : xev)
+            if (e) cudaEventDestroy(e);
         if (st) cudaStreamDestroy(st);
+        if (cst) cudaStreamDestroy(cst);
     }
 };
 
@@ -370,7 +382,7 @@ static int get_state(zk_groth16_pk* pk, const R1cs& R, int nranks, int rank, Sta
     s->n = R.n;
     s->m = R.n / (uint64_t)nranks;
     s->q = s->m / (uint64_t)nranks;
-    s->sw = ((size_t)R.m + nranks - 1) / nranks;
+    s->cw = ((size_t)R.m + (size_t)nranks * kWitnessChunks - 1) / ((size_t)nranks * kWitnessChunks);
 #define ZK_S(call)                                                                                           \
     do {                                                                                                     \
         cudaError_t e_ = (call);                                                                             \
@@ -381,13 +393,16 @@ static int get_state(zk_groth16_pk* pk, const R1cs& R, int nranks, int rank, Sta
     } while (0)
     ZK_S(cudaSetDevice(pk->device));
     ZK_S(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-    ZK_S(cudaMalloc(&s->w, s->sw * nranks * 32));
+    ZK_S(cudaStreamCreateWithFlags(&s->cst, cudaStreamNonBlocking));
+    ZK_S(cudaMalloc(&s->w, s->cw * nranks * kWitnessChunks * 32));
     for (auto& b : s->p) ZK_S(cudaMalloc(&b, 3 * s->m * 32));
     ZK_S(cudaMalloc(&s->bad, 8));
     ZK_S(cudaMalloc(&s->rec, (size_t)nranks * kRecWords * 8));
     ZK_S(cudaMallocHost(&s->h_bad, 8));
     ZK_S(cudaMallocHost(&s->h_rec, (size_t)nranks * kRecWords * 8));
     for (auto& e : s->ev) ZK_S(cudaEventCreate(&e));
+    for (auto& e : s->dep) ZK_S(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (auto& e : s->xev) ZK_S(cudaEventCreate(&e));
 #undef ZK_S
     pk->split[{nranks, rank}] = s;
     *out = s;
@@ -403,15 +418,47 @@ static float ev_ms(cudaEvent_t a, cudaEvent_t b) {
     return ms;
 }
 
-// An all-to-all of `nvec` vectors of m values: block j (q values) of vector k
-// goes to rank j, and the block from rank j lands at block j of vector k.
-static int all_to_all(Comm* comm, State* S, const Fr* send, Fr* recv, int nvec) {
+// An all-to-all of one vector of m values on the exchange stream: block j (q
+// values) goes to rank j, and the block from rank j lands at block j.
+static int all_to_all(Comm* comm, State* S, const Fr* send, Fr* recv) {
     S->xf.clear();
-    for (int k = 0; k < nvec; k++)
-        for (int j = 0; j < S->nranks; j++)
-            S->xf.push_back({j, send + (uint64_t)k * S->m + (uint64_t)j * S->q, recv + (uint64_t)k * S->m + (uint64_t)j * S->q, S->q * 32});
-    return comm->exchange(S->xf.data(), (int)S->xf.size(), S->st);
+    for (int j = 0; j < S->nranks; j++) S->xf.push_back({j, send + (uint64_t)j * S->q, recv + (uint64_t)j * S->q, S->q * 32});
+    return comm->exchange(S->xf.data(), (int)S->xf.size(), S->cst);
 }
+
+// The all-to-alls of compute_h run one polynomial at a time on the exchange
+// stream, each after the transform that produced its vector and before the
+// transform that consumes it, so that one polynomial crosses NVLink while
+// another is transformed.  Every rank issues them in the same order.
+struct Pipe {
+    State* S;
+    Comm* comm;
+    int nx = 0;  // all-to-alls issued (timing events xev[2 i], xev[2 i + 1])
+    int nd = 0;  // ordering events used
+    int xchg(cudaEvent_t after, const Fr* send, Fr* recv, cudaEvent_t* done) {
+        ZK_TRY_CUDA(cudaStreamWaitEvent(S->cst, after, 0));
+        ZK_TRY_CUDA(cudaEventRecord(S->xev[2 * nx], S->cst));
+        ZK_TRY(all_to_all(comm, S, send, recv));
+        ZK_TRY_CUDA(cudaEventRecord(S->xev[2 * nx + 1], S->cst));
+        nx++;
+        *done = S->xev[2 * nx - 1];
+        return ZK_OK;
+    }
+    int mark(cudaStream_t st, cudaEvent_t* e) {
+        *e = S->dep[nd++];
+        ZK_TRY_CUDA(cudaEventRecord(*e, st));
+        return ZK_OK;
+    }
+    float exchange_ms() const {
+        float t = 0;
+        for (int i = 0; i < nx; i++) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, S->xev[2 * i], S->xev[2 * i + 1]);
+            t += ms;
+        }
+        return t;
+    }
+};
 
 static int prove_split(zk_groth16_pk* pk, const R1cs& R, Comm* comm, const void* h_witness, const void* r, const void* s, void* proof256,
                        void* points) {
@@ -448,14 +495,29 @@ static int prove_split(zk_groth16_pk* pk, const R1cs& R, Comm* comm, const void*
     zkh::Fe g;
     ZK_TRY(zk_compute_h_coset_shift(R.log_n, g.v));
 
-    // 1. witness: this rank's slice, then the all-gather
+    // 1. witness: kWitnessChunks rounds; in round c rank r uploads global rows
+    //    [(c N + r) cw, (c N + r + 1) cw) and the round's N chunks are
+    //    all-gathered on the exchange stream while the next round's chunk crosses
+    //    PCIe on the work stream
+    Pipe pp{S, comm};
     ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
-    const size_t w_lo = std::min((size_t)R.m, S->sw * me), w_hi = std::min((size_t)R.m, S->sw * (me + 1));
-    Fr* my_w = S->w + S->sw * me;
-    if (w_hi > w_lo)
-        ZK_TRY_CUDA(cudaMemcpyAsync(my_w, (const uint8_t*)h_witness + w_lo * 32, (w_hi - w_lo) * 32, cudaMemcpyHostToDevice, st));
-    if (S->sw > w_hi - w_lo) ZK_TRY_CUDA(cudaMemsetAsync(my_w + (w_hi - w_lo), 0, (S->sw - (w_hi - w_lo)) * 32, st));
-    ZK_TRY(comm->all_gather(my_w, S->w, S->sw * 32, st));
+    const size_t cw = S->cw;
+    for (int c = 0; c < kWitnessChunks; c++) {
+        const size_t at = ((size_t)c * N + me) * cw;
+        const size_t lo_c = std::min((size_t)R.m, at), hi_c = std::min((size_t)R.m, at + cw);
+        if (hi_c > lo_c)
+            ZK_TRY_CUDA(cudaMemcpyAsync(S->w + at, (const uint8_t*)h_witness + lo_c * 32, (hi_c - lo_c) * 32, cudaMemcpyHostToDevice, st));
+        if (cw > hi_c - lo_c) ZK_TRY_CUDA(cudaMemsetAsync(S->w + at + (hi_c - lo_c), 0, (cw - (hi_c - lo_c)) * 32, st));
+        cudaEvent_t up;
+        ZK_TRY(pp.mark(st, &up));
+        ZK_TRY_CUDA(cudaStreamWaitEvent(S->cst, up, 0));
+        ZK_TRY(comm->all_gather(S->w + at, S->w + (size_t)c * N * cw, cw * 32, S->cst));
+    }
+    {
+        cudaEvent_t ag;
+        ZK_TRY(pp.mark(S->cst, &ag));
+        ZK_TRY_CUDA(cudaStreamWaitEvent(st, ag, 0));
+    }
     ZK_TRY_CUDA(cudaEventRecord(ev[1], st));
 
     // 3. the witness MSMs over an equal slice of the witness, from a host thread
@@ -493,32 +555,39 @@ static int prove_split(zk_groth16_pk* pk, const R1cs& R, Comm* comm, const void*
     ZK_TRY_CUDA(cudaMemcpyAsync(S->h_bad, S->bad, 8, cudaMemcpyDeviceToHost, st));
     ZK_TRY_CUDA(cudaEventRecord(ev[2], st));
 
-    // 4. compute_h, every transform split over the ranks
+    // 4. compute_h, every transform split over the ranks; the all-to-alls on
+    //    the exchange stream, one polynomial at a time (Pipe)
     {
         const unsigned grid = (unsigned)std::min<uint64_t>((3 * m + 255) / 256, (uint64_t)ctx->num_sms * 16);
         cyclic_gather_kernel<<<grid, 256, 0, st>>>(P0, P2, m, log_parts);
         ZK_TRY_CUDA(cudaGetLastError());
     }
-    ZK_TRY_CUDA(cudaEventRecord(ev[3], st));
-    ZK_TRY(all_to_all(comm, S, P2, P1, 3));  // evaluations, cyclic
-    ZK_TRY_CUDA(cudaEventRecord(ev[4], st));
-    for (int k = 0; k < 3; k++) ZK_TRY(zk_ntt_device(pk->device, st, P1 + k * m, P1 + k * m, (int)L - log_parts, 1, nullptr));
-    ZK_TRY_CUDA(cudaEventRecord(ev[5], st));
-    ZK_TRY(all_to_all(comm, S, P1, P2, 3));
-    ZK_TRY_CUDA(cudaEventRecord(ev[6], st));
+    cudaEvent_t e_rows, e_in[3], e_x[3], e_out[3], e_co[3], e_ev[3], e_h, e_hx;
+    ZK_TRY(pp.mark(st, &e_rows));
+    for (int k = 0; k < 3; k++)  // evaluations, cyclic
+        ZK_TRY(pp.xchg(e_rows, P2 + k * m, P1 + k * m, &e_in[k]));
+    for (int k = 0; k < 3; k++) {  // the size-m INTT of each polynomial as its values land
+        ZK_TRY_CUDA(cudaStreamWaitEvent(st, e_in[k], 0));
+        ZK_TRY(zk_ntt_device(pk->device, st, P1 + k * m, P1 + k * m, (int)L - log_parts, 1, nullptr));
+        ZK_TRY(pp.mark(st, &e_x[k]));
+        ZK_TRY(pp.xchg(e_x[k], P1 + k * m, P2 + k * m, &e_out[k]));
+    }
     for (int k = 0; k < 3; k++) {  // coefficients n^-1 g^i, blocks; then toward the coset evaluations
+        ZK_TRY_CUDA(cudaStreamWaitEvent(st, e_out[k], 0));
         ZK_TRY(zk_ntt_cross_device(pk->device, st, P1 + k * m, P2 + k * m, (int)L, log_parts, me, 1, 0, g.v, 0));
         ZK_TRY(zk_ntt_cross_device(pk->device, st, P0 + k * m, P1 + k * m, (int)L, log_parts, me, 0, 1, nullptr, 0));
+        ZK_TRY(pp.mark(st, &e_co[k]));
+        ZK_TRY(pp.xchg(e_co[k], P0 + k * m, P2 + k * m, &e_ev[k]));  // coset evaluations, cyclic
     }
-    ZK_TRY_CUDA(cudaEventRecord(ev[7], st));
-    ZK_TRY(all_to_all(comm, S, P0, P2, 3));  // coset evaluations, cyclic
-    ZK_TRY_CUDA(cudaEventRecord(ev[8], st));
-    for (int k = 0; k < 3; k++) ZK_TRY(zk_ntt_device(pk->device, st, P2 + k * m, P2 + k * m, (int)L - log_parts, 0, nullptr));
+    for (int k = 0; k < 3; k++) {
+        ZK_TRY_CUDA(cudaStreamWaitEvent(st, e_ev[k], 0));
+        ZK_TRY(zk_ntt_device(pk->device, st, P2 + k * m, P2 + k * m, (int)L - log_parts, 0, nullptr));
+    }
     ZK_TRY(zk_compute_h_pointwise_device(pk->device, st, P1, P2, P2 + m, P2 + 2 * m, (int)L, m));
     ZK_TRY(zk_ntt_device(pk->device, st, P1, P1, (int)L - log_parts, 1, nullptr));
-    ZK_TRY_CUDA(cudaEventRecord(ev[9], st));
-    ZK_TRY(all_to_all(comm, S, P1, P0, 1));
-    ZK_TRY_CUDA(cudaEventRecord(ev[10], st));
+    ZK_TRY(pp.mark(st, &e_h));
+    ZK_TRY(pp.xchg(e_h, P1, P0, &e_hx));
+    ZK_TRY_CUDA(cudaStreamWaitEvent(st, e_hx, 0));
     ZK_TRY(zk_ntt_cross_device(pk->device, st, P1, P0, (int)L, log_parts, me, 1, 0, g.v, 1));  // h, blocks, n^-1 g^-i
     ZK_TRY_CUDA(cudaEventRecord(ev[11], st));
 
@@ -560,7 +629,7 @@ static int prove_split(zk_groth16_pk* pk, const R1cs& R, Comm* comm, const void*
     stats.witness_ms = ev_ms(ev[0], ev[1]);
     stats.matvec_ms = ev_ms(ev[1], ev[2]);
     stats.compute_h_ms = ev_ms(ev[2], ev[11]);
-    stats.all_to_all_ms = ev_ms(ev[3], ev[4]) + ev_ms(ev[5], ev[6]) + ev_ms(ev[7], ev[8]) + ev_ms(ev[9], ev[10]);
+    stats.all_to_all_ms = pp.exchange_ms();  // on the exchange stream, overlapping the transforms
     stats.h_msm_ms = ev_ms(ev[11], ev[12]);
     stats.witness_msms_ms = wit_all;
     stats.gather_ms = ev_ms(ev[12], ev[13]);

@@ -488,7 +488,8 @@ class R1cs:
 
 
 class PkLoadStats(ctypes.Structure):
-    _fields_ = [("bytes", ctypes.c_double), ("read_ms", ctypes.c_double), ("total_ms", ctypes.c_double)]
+    _fields_ = [("bytes", ctypes.c_double), ("read_ms", ctypes.c_double), ("total_ms", ctypes.c_double),
+                ("alloc_ms", ctypes.c_double)]
 
 
 lib.zk_groth16_pk_last_load_stats.argtypes = [ctypes.POINTER(PkLoadStats)]
@@ -516,11 +517,12 @@ class ProvingKey:
 
     @staticmethod
     def last_load_stats():
-        """Bytes of query records, host read time and whole-call time of this
-        thread's last load (zk_groth16_pk_last_load_stats)."""
+        """Bytes of query records, host read time, whole-call time and
+        allocation time of this thread's last load
+        (zk_groth16_pk_last_load_stats)."""
         st = PkLoadStats()
         check(lib.zk_groth16_pk_last_load_stats(ctypes.byref(st)))
-        return {"bytes": st.bytes, "read_ms": st.read_ms, "total_ms": st.total_ms}
+        return {"bytes": st.bytes, "read_ms": st.read_ms, "total_ms": st.total_ms, "alloc_ms": st.alloc_ms}
 
     def save(self, path):
         check(lib.zk_groth16_pk_save(self.h, path.encode()))

@@ -233,11 +233,14 @@ int zk_groth16_setup(zk_r1cs* r1cs, const void* toxic, zk_groth16_pk** out);
 int zk_groth16_pk_load(int device, const char* path, zk_groth16_pk** out);
 /* The calling thread's last zk_groth16_pk_load: bytes of query records read,
  * host time spent reading them (parallel reads into pinned chunks, overlapped
- * with the copies to the device), and the whole call. */
+ * with the copies to the device), the whole call up to the release of its
+ * pinned staging, and the time spent allocating the device buffers and the
+ * pinned staging. */
 typedef struct {
     double bytes;
     double read_ms;
     double total_ms;
+    double alloc_ms;
 } zk_pk_load_stats;
 int zk_groth16_pk_last_load_stats(zk_pk_load_stats* out);
 int zk_groth16_pk_save(const zk_groth16_pk* pk, const char* path);
@@ -415,7 +418,7 @@ typedef struct {
     float witness_ms;       /* this rank's witness slice upload + the all-gather (device) */
     float matvec_ms;        /* its rows of A w, B w, C w, their check and its all-reduce */
     float compute_h_ms;     /* the split transforms, all-to-alls included */
-    float all_to_all_ms;    /* the four all-to-alls inside compute_h_ms */
+    float all_to_all_ms;    /* the all-to-alls of compute_h (one polynomial each), summed; they overlap its transforms */
     float h_msm_ms;         /* the H MSM over its coefficients */
     float witness_msms_ms;  /* A, B2, B1, L over its witness slice (side stream, overlapped) */
     float witness_wait_ms;  /* host time spent waiting for them after the H MSM */

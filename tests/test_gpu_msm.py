@@ -262,6 +262,58 @@ def test_g2_witness_size_identity(scalars):
     assert np.array_equal(got, exp)
 
 
+def _signed_scalars(n, seed):
+    """Scalars of a signed witness: the folding boundary (r - 1) / 2 and
+    (r + 1) / 2, r - 1, r - 2^k, then small positives and their negatives
+    r - v, zeros and ones."""
+    rng = np.random.default_rng(seed)
+    vals = [0, 1, (O.R - 1) // 2, (O.R + 1) // 2, (O.R - 1) // 2 - 1, (O.R + 1) // 2 + 1, O.R - 1, O.R - 2]
+    vals += [O.R - (1 << k) for k in (1, 31, 32, 63, 64, 128, 200, 252)]
+    while len(vals) < n:
+        v = int(rng.integers(1, 1 << 40))
+        vals.append(v if rng.random() < 0.5 else O.R - v)
+    return np.stack([O.fr_from_int(v) for v in vals[:n]])
+
+
+@pytest.mark.parametrize("g2", [False, True])
+def test_negative_scalars_fold(g2):
+    """Scalars above (r - 1) / 2 are processed as r - s against -P (the same
+    point): the boundary values and a signed witness match the oracle, and a
+    witness of small magnitudes needs only the windows of its magnitudes."""
+    n = 3000
+    _, pts, _ = _random_instance(n, 0xF01D + g2, g2=g2)
+    sc = _signed_scalars(n, 0xF01E)
+    msm, omsm = (Z.msm_g2, O.msm_g2) if g2 else (Z.msm_g1, O.msm_g1)
+    exp = omsm(Z.to_host(pts), sc, nthreads=os.cpu_count())
+    assert np.array_equal(msm(pts, dev(sc)), exp)
+    assert np.array_equal(msm(Z.to_host(pts), sc), exp)
+    # magnitudes below 2^40 only: every scalar folds to at most 40 bits
+    small = sc.copy()
+    small[:16] = Z.fr_from_int(5)
+    exp2 = omsm(Z.to_host(pts), small, nthreads=os.cpu_count())
+    assert np.array_equal(msm(pts, dev(small)), exp2)
+    st = Z.msm_last_stats()
+    assert st["num_windows"] * st["window_bits"] <= 41 + st["window_bits"], st
+
+
+def test_negative_scalars_fold_host_pipelined():
+    """2^20 + 9 scalars, 30 % of them negative (r - v, v < 2^24), through the
+    pipelined host path (its plan from the first batch's sample, all windows
+    kept) and the device path, against the identity.  The witness MSMs of a
+    proof (one shared sort) see such scalars in every prove test."""
+    n = (1 << 20) + 9
+    k = Z.random_fr(n, 0xF020)
+    sc = Z.random_fr(n, 0xF021)
+    rng = np.random.default_rng(0xF022)
+    neg = np.flatnonzero(rng.random(n) < 0.3)
+    mags = rng.integers(1, 1 << 24, neg.size)
+    sc[neg] = np.stack([O.fr_from_int(O.R - int(v)) for v in mags])
+    pts = Z.g1_fixed_base(dev(k))
+    exp = O.g1_fixed_base(O.fr_dot(k, sc)[None, :])[0]
+    assert np.array_equal(Z.msm_g1(pts, dev(sc)), exp)
+    assert np.array_equal(Z.msm_g1(Z.to_host(pts), sc), exp)
+
+
 def test_stats_and_probe():
     _, pts, sc = _random_instance(4096, 3)
     Z.msm_g1(pts, dev(sc))
