@@ -399,33 +399,6 @@ def bench_prove_sharded(Z, args, dev, world, rank):
 
 
 # ---------------------------------------------------------------- B200 arm
-def bind_near_gpu(index):
-    """Restrict this rank's host threads to the CPU cores NVML lists as local
-    to its GPU (read-only NVML queries; the GPU is not touched), so that the
-    pinned buffers it allocates next land in that socket's memory and its copies
-    cross no inter-socket link.  Returns a description, or why nothing changed."""
-    try:
-        import pynvml
-        import torch
-        pr = torch.cuda.get_device_properties(index)
-        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
-        pynvml.nvmlInit()
-        try:
-            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            words = (os.cpu_count() + 63) // 64
-            mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
-        finally:
-            pynvml.nvmlShutdown()
-        cpus = {64 * i + b for i, w in enumerate(mask) for b in range(64) if (w >> b) & 1}
-        cpus &= os.sched_getaffinity(0)
-        if not cpus:
-            return "unchanged (NVML gave no local cores)"
-        os.sched_setaffinity(0, cpus)
-        return f"{len(cpus)} GPU-local cores (NVML affinity of {bus})"
-    except Exception as e:  # reported in the config; the run goes on unbound
-        return f"unchanged ({type(e).__name__}: {str(e)[:80]})"
-
-
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -438,8 +411,6 @@ def run_b200(args):
         args.gpus = world
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    # several ranks pull their host inputs at once: keep each near its GPU
-    affinity = bind_near_gpu(local) if world > 1 else "all host cores (one rank)"
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
@@ -642,7 +613,7 @@ def run_b200(args):
                                      f"{world} x 2^{args.log_n} points", "log_n": args.log_n,
                          "window_bits": stats[-1]["window_bits"], "num_windows": stats[-1]["num_windows"],
                          "parallelism": f"points sharded over {world} GPU(s), partial sums all-gathered",
-                         "l2": "inputs 1.5 GiB per GPU > 126 MB L2 (no flush needed)", "host_affinity": affinity},
+                         "l2": "inputs 1.5 GiB per GPU > 126 MB L2 (no flush needed)"},
               "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "ntt": ntt, "prove": prove,
               "vs_cpu_baseline": ({"device": value / cpu["value"], "e2e": e2e["value"] / cpu["value"] if e2e else None}
                                   if cpu else None),
