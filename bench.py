@@ -276,6 +276,7 @@ def bench_prove(Z, args, dev, world=1, rank=0):
     w_pin = torch.empty((c["num_variables"], 4), dtype=torch.int64, pin_memory=True)
     w_pin.copy_(torch.from_numpy(c["witness"].view(np.int64)))
     w = w_pin.numpy().view(np.uint64)
+    pk.precompute()  # the H-query tables (else the first proofs run without them while they build)
     for _ in range(2):
         pk.prove(r1, w, 12345, 67890)
     torch.cuda.synchronize()
@@ -304,13 +305,18 @@ def bench_prove(Z, args, dev, world=1, rank=0):
             first = pk2.prove(r1, w, 12345, 67890)[0]
             first_s = time.perf_counter() - t0
             t0 = time.perf_counter()
+            pk2.precompute()  # waits for the table build the first proof started
+            tables_s = time.perf_counter() - t0
+            t0 = time.perf_counter()
             second = pk2.prove(r1, w, 12345, 67890)[0]
             warm_s = time.perf_counter() - t0
             cold = {"pk_bytes": size, "load_ms": load_s * 1e3, "load_read_ms": ls["read_ms"], "load_alloc_ms": ls["alloc_ms"],
                     "load_call_ms": ls["total_ms"], "first_prove_ms": first_s * 1e3,
-                    "cold_total_ms": (load_s + first_s) * 1e3, "warm_prove_ms": warm_s * 1e3,
+                    "cold_total_ms": (load_s + first_s) * 1e3, "tables_ready_after_ms": tables_s * 1e3,
+                    "warm_prove_ms": warm_s * 1e3,
                     "proofs_equal": first == second == pk.prove(r1, w, 12345, 67890)[0],
-                    "what": "ZKMLPK3 file (page cache) -> device key -> first proof; the first proof builds the H-query tables"}
+                    "what": ("ZKMLPK3 file (page cache) -> device key -> first proof (its H MSM without tables, "
+                             "whose build it starts beside itself) -> wait for the tables -> a warm proof")}
             del pk2
     # the timed proof checks out: this library's verifier (pairing on the host,
     # public-input MSM over the 32,779 IC points on the GPU)

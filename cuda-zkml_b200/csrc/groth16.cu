@@ -538,35 +538,74 @@ static void assemble(const zk_groth16_pk* pk, const zkh::Fe& r, const zkh::Fe& s
 // Below kHTablesMin points the plain MSM is as fast.
 static constexpr int kHTablesMin = 1 << 16;
 
-static int ensure_h_tables(zk_groth16_pk* pk, cudaStream_t st) {
-    std::lock_guard<std::mutex> lock(pk->h_mu);
-    if (pk->h_tab || pk->n_h < kHTablesMin) return ZK_OK;
+// Starts the table build on the key's table stream, once (caller holds h_mu).
+// In the background (beside proofs) the build takes 2 of the 8 blocks per SM a
+// full-GPU build uses, so that the proofs' kernels keep most of every SM.
+static constexpr int kBackgroundTableBlocks = 2;
+static int start_h_tables_locked(zk_groth16_pk* pk, bool background) {
+    if (pk->h_tab || pk->h_tab_pending || pk->n_h < kHTablesMin) return ZK_OK;
     int c, W;
     g1_window_tables_shape((size_t)pk->n_h, &c, &W);
     if ((size_t)W * pk->n_h > 0x7fffffffull) return ZK_OK;  // keys index 32 bits: the plain MSM runs in passes
-    uint8_t* tab = nullptr;
-    ZK_TRY_CUDA(cudaMalloc(&tab, (size_t)W * pk->n_h * 64));
-    const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
-    int rc = g1_window_tables_build(pk->device, st, hq, (size_t)pk->n_h, c, W, tab);
-    if (rc == ZK_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = ZK_ERR_CUDA;
-    if (rc != ZK_OK) {
-        cudaFree(tab);
-        return rc;
+    if (!pk->h_tab_stream) {
+        ZK_TRY_CUDA(cudaStreamCreateWithFlags(&pk->h_tab_stream, cudaStreamNonBlocking));
+        ZK_TRY_CUDA(cudaEventCreateWithFlags(&pk->h_tab_done, cudaEventDisableTiming));
     }
-    pk->h_tab = tab;
-    pk->h_c = c;
-    pk->h_W = W;
+    DeviceBuffer tab;
+    ZK_TRY_CUDA(tab.alloc((size_t)W * pk->n_h * 64));
+    const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
+    ZK_TRY(g1_window_tables_build(pk->device, pk->h_tab_stream, hq, (size_t)pk->n_h, c, W, tab.p, background ? kBackgroundTableBlocks : 8));
+    ZK_TRY_CUDA(cudaEventRecord(pk->h_tab_done, pk->h_tab_stream));
+    pk->h_tab_pending = (uint8_t*)tab.release();
+    pk->h_pc = c;
+    pk->h_pW = W;
     return ZK_OK;
+}
+
+// Publishes a finished build (caller holds h_mu); with `wait`, waits for it.
+static int publish_h_tables_locked(zk_groth16_pk* pk, bool wait) {
+    if (!pk->h_tab_pending) return ZK_OK;
+    const cudaError_t q = wait ? cudaEventSynchronize(pk->h_tab_done) : cudaEventQuery(pk->h_tab_done);
+    if (q == cudaErrorNotReady) return ZK_OK;
+    if (q != cudaSuccess) {
+        cudaFree(pk->h_tab_pending);
+        pk->h_tab_pending = nullptr;
+        set_error("H-query window tables: %s", cudaGetErrorString(q));
+        return ZK_ERR_CUDA;
+    }
+    pk->h_tab = pk->h_tab_pending;
+    pk->h_c = pk->h_pc;
+    pk->h_W = pk->h_pW;
+    pk->h_tab_pending = nullptr;
+    return ZK_OK;
+}
+
+// The tables, built now if need be (zk_groth16_precompute).
+static int ensure_h_tables(zk_groth16_pk* pk) {
+    std::lock_guard<std::mutex> lock(pk->h_mu);
+    ZK_TRY(start_h_tables_locked(pk, false));
+    return publish_h_tables_locked(pk, true);
 }
 
 // sum_{i in [lo, hi)} h_i H_i; d_h holds all n_h coefficients.  The tables are
 // shaped for the whole query: on a slice under 3/4 of it (a rank's share of a
 // split proof) their fixed bucket reduction and wider gathers cost more than a
 // plain MSM sized to the slice (measured at half the query: 10.3 vs 9.9 ms).
+// Until the tables are built (a build started by the first such call runs on
+// its own stream beside the proofs) the plain MSM serves.
 static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, size_t hi, uint64_t out[8]) {
     if ((hi - lo) * 4 >= (size_t)pk->n_h * 3) {
-        ZK_TRY(ensure_h_tables(pk, st));
-        if (pk->h_tab) return g1_window_tables_msm(pk->device, st, pk->h_tab, (size_t)pk->n_h, pk->h_c, pk->h_W, lo, hi, d_h + lo, out);
+        uint8_t* tab;
+        int c, W;
+        {
+            std::lock_guard<std::mutex> lock(pk->h_mu);
+            ZK_TRY(start_h_tables_locked(pk, true));
+            ZK_TRY(publish_h_tables_locked(pk, false));
+            tab = pk->h_tab;
+            c = pk->h_c;
+            W = pk->h_W;
+        }
+        if (tab) return g1_window_tables_msm(pk->device, st, tab, (size_t)pk->n_h, c, W, lo, hi, d_h + lo, out);
     }
     const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
     return zk_msm_g1_device(pk->device, st, hq + lo * 64, d_h + lo, hi - lo, out);
@@ -686,6 +725,22 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     ScopedEvent evs[5];
     for (auto& e : evs) ZK_TRY_CUDA(cudaEventCreate(&e.e));
     cudaEvent_t ev[5] = {evs[0].e, evs[1].e, evs[2].e, evs[3].e, evs[4].e};
+    // The matvec, compute_h and the H MSM run on a stream of the highest
+    // priority, ordered after the caller's stream and before its later work, so
+    // that the witness MSMs beside them take what they leave (measured: 29.10 ->
+    // 28.80 ms at config 5).  ZK_PROVE_PRIORITY=0 keeps them on the caller's stream.
+    const cudaStream_t user_st = st;
+    const char* pe = getenv("ZK_PROVE_PRIORITY");
+    if (!(pe && atoi(pe) == 0)) {
+        if (!pk->prio_stream) {
+            int least = 0, greatest = 0;
+            ZK_TRY_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+            ZK_TRY_CUDA(cudaStreamCreateWithPriority(&pk->prio_stream, cudaStreamNonBlocking, greatest));
+        }
+        ZK_TRY_CUDA(cudaEventRecord(ev[3], user_st));
+        ZK_TRY_CUDA(cudaStreamWaitEvent(pk->prio_stream, ev[3], 0));
+        st = pk->prio_stream;
+    }
     ZK_TRY_CUDA(cudaEventRecord(ev[0], st));
     ZK_TRY_CUDA(cudaMemcpyAsync(pk->w, h_witness, (size_t)m * 32, cudaMemcpyHostToDevice, st));
     ZK_TRY_CUDA(cudaEventRecord(ev[4], st));
@@ -763,6 +818,7 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
 
     assemble(pk, r, s, a_msm, b_msm, l_msm, h_msm_out, b1_msm, outA, outB, outC);
     ZK_TRY_CUDA(cudaEventRecord(ev[3], st));
+    if (st != user_st) ZK_TRY_CUDA(cudaStreamWaitEvent(user_st, ev[3], 0));
     ZK_TRY_CUDA(cudaEventSynchronize(ev[3]));
     cudaEventElapsedTime(&ms, ev[0], ev[3]);
     stats.total_ms = ms;
@@ -1232,7 +1288,15 @@ extern "C" void zk_groth16_pk_destroy(zk_groth16_pk* pk) {
     cudaFree(pk->h);
     cudaFree(pk->d_bad);
     cudaFreeHost(pk->h_bad);
+    if (pk->h_tab_stream) cudaStreamSynchronize(pk->h_tab_stream);
+    if (pk->prio_stream) {
+        cudaStreamSynchronize(pk->prio_stream);
+        cudaStreamDestroy(pk->prio_stream);
+    }
     cudaFree(pk->h_tab);
+    cudaFree(pk->h_tab_pending);
+    if (pk->h_tab_done) cudaEventDestroy(pk->h_tab_done);
+    if (pk->h_tab_stream) cudaStreamDestroy(pk->h_tab_stream);
     for (auto& kv : pk->hb) {
         cudaFree(kv.second.pts);
         cudaFree(kv.second.tab);
@@ -1384,7 +1448,8 @@ extern "C" int zk_groth16_precompute(zk_groth16_pk* pk, void* stream) {
     if (!pk) return ZK_ERR_INVALID;
     DeviceContext* ctx;
     ZK_TRY(get_context(pk->device, &ctx));
-    return ensure_h_tables(pk, (cudaStream_t)stream);
+    (void)stream;  // the tables are built on the key's own stream; this call returns when they are ready
+    return ensure_h_tables(pk);
 }
 
 extern "C" int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const void* d_h, uint64_t lo, uint64_t hi, void* out_affine) {

@@ -1511,11 +1511,12 @@ void g1_window_tables_shape(size_t n, int* c_out, int* W_out) {
     *W_out = (255 + best - 1) / best;
 }
 
-int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out) {
+int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out, int blocks_per_sm) {
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     if (!n) return ZK_OK;
-    window_tables_kernel<G1><<<grid_for(n, 128, ctx->num_sms * 8), 128, 0, st>>>((const uint8_t*)d_points, n, c, W, (uint8_t*)d_out);
+    window_tables_kernel<G1><<<grid_for(n, 128, ctx->num_sms * std::max(blocks_per_sm, 1)), 128, 0, st>>>((const uint8_t*)d_points, n, c, W,
+                                                                                                       (uint8_t*)d_out);
     ZK_TRY_CUDA(cudaGetLastError());
     return ZK_OK;
 }

@@ -76,13 +76,22 @@ struct zk_groth16_pk {
     mutable std::mutex tab_mu;
     mutable std::vector<zkh::Xyzz<zkh::Fe>> d1_pow;
     mutable std::vector<zkh::Xyzz<zkh::Fp2>> d2_pow;
-    // window tables of the H query (2^(c j) H_i, j < h_W), built on first use
+    // window tables of the H query (2^(c j) H_i, j < h_W).  The first proof
+    // that finds none starts their build on a stream of its own and runs its H
+    // MSM without them; a later call publishes them once the build's event has
+    // fired (zk_groth16_precompute builds them and waits).
     uint8_t* h_tab = nullptr;
     int h_c = 0, h_W = 0;
+    uint8_t* h_tab_pending = nullptr;
+    int h_pc = 0, h_pW = 0;
+    cudaStream_t h_tab_stream = nullptr;
+    cudaEvent_t h_tab_done = nullptr;
     std::mutex h_mu;
     // private device context of the witness MSMs inside prove (created on first
     // use), so that they run beside compute_h and the H MSM on the shared one
     zk::DeviceContext* wctx = nullptr;
+    // the one-device proof's critical path runs on this highest-priority stream
+    cudaStream_t prio_stream = nullptr;
     // per (log_parts, part): that part's H points in the "blocks" order of a
     // proof split over 2^log_parts parts, and window tables over them; built on
     // first use and kept until the key is destroyed (a process proving one part

@@ -555,7 +555,8 @@ class ProvingKey:
         return proof.tobytes(), pts[:8], pts[8:24], pts[24:32]
 
     def precompute(self, stream=None):
-        """Build the H-query window tables now (else the first proof does)."""
+        """Build the H-query window tables now and wait for them (else the
+        first proof starts their build and proofs run without them until done)."""
         check(lib.zk_groth16_precompute(self.h, stream))
 
     def witness_msms(self, d_w, lo, hi):

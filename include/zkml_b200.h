@@ -345,8 +345,11 @@ int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, c
  * (groth16.cu:817), with d_h the n_h device coefficients of h.  From 2^16
  * points, for a slice of at least 3/4 of the query, it runs over precomputed
  * window tables of the query (2^(c j) H_i: c = 20 and 13 tables, 3.5 GB, at
- * 2^22), built on first use or by zk_groth16_precompute; all windows then share
- * one bucket set and one reduce.  Smaller slices run the plain MSM. */
+ * 2^22); all windows then share one bucket set and one reduce.  The first call
+ * (or proof) without tables starts building them on a stream of the key's own
+ * (about 0.55 s of GPU time at 2^22) and runs the plain MSM, as do the calls
+ * made before the build has finished; zk_groth16_precompute builds them and
+ * waits.  Smaller slices run the plain MSM. */
 int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const void* d_h, uint64_t lo, uint64_t hi,
                             void* out_affine);
 /* One part's share of the H MSM of a proof split over 2^log_parts parts:
@@ -367,7 +370,9 @@ int zk_groth16_h_msm_blocks_device(zk_groth16_pk* pk, void* stream, const void* 
  * MSMs of the device's shared context; calls on one key run one at a time. */
 int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, const void* d_witness, uint64_t lo,
                                    uint64_t hi, void* sums);
-/* Build the key's precomputed tables now instead of at the first proof. */
+/* Build the key's precomputed H-query tables now (on the key's own stream;
+ * `stream` is not used) and return when they are ready; otherwise the first
+ * proof starts the build and proofs run without them until it is done. */
 int zk_groth16_precompute(zk_groth16_pk* pk, void* stream);
 
 /* The same from nparts partial records of 384 B (one per rank), summed first. */

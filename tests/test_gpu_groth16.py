@@ -152,6 +152,10 @@ def test_prove_2_16_config4_shape():
     pk_o = {"m": c["num_variables"], "num_public": c["num_public"], "_at": at, "_vanish": vanish, "_toxic": tox}
     h = G.compute_h(mats, G._ints(c["witness"]), n, log_n, c["num_variables"])
     assert G.trapdoor_verify(pk_o, c["witness"], r, s, h, A, B, C)
+    # that first proof started the H-query table build and ran its H MSM without
+    # the tables; once they are ready the same inputs give the same proof
+    pk.precompute()
+    assert pk.prove(r1, c["witness"], r, s)[0] == proof
     # the H MSM over the key's precomputed window tables (used from 2^16 points,
     # for slices of at least 3/4 of the query) equals the plain MSM over the same
     # query points, whole and in slices
