@@ -305,7 +305,7 @@ def bench_prove(Z, args, dev, world=1, rank=0):
             first = pk2.prove(r1, w, 12345, 67890)[0]
             first_s = time.perf_counter() - t0
             t0 = time.perf_counter()
-            pk2.precompute()  # waits for the table build the first proof started
+            pk2.precompute()  # waits for the table build the first proof started as it ended
             tables_s = time.perf_counter() - t0
             t0 = time.perf_counter()
             second = pk2.prove(r1, w, 12345, 67890)[0]
@@ -316,7 +316,7 @@ def bench_prove(Z, args, dev, world=1, rank=0):
                     "warm_prove_ms": warm_s * 1e3,
                     "proofs_equal": first == second == pk.prove(r1, w, 12345, 67890)[0],
                     "what": ("ZKMLPK3 file (page cache) -> device key -> first proof (its H MSM without tables, "
-                             "whose build it starts beside itself) -> wait for the tables -> a warm proof")}
+                             "whose build it starts as it ends) -> wait for the tables -> a warm proof")}
             del pk2
     # the timed proof checks out: this library's verifier (pairing on the host,
     # public-input MSM over the 32,779 IC points on the GPU)

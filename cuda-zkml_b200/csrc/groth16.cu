@@ -539,10 +539,10 @@ static void assemble(const zk_groth16_pk* pk, const zkh::Fe& r, const zkh::Fe& s
 static constexpr int kHTablesMin = 1 << 16;
 
 // Starts the table build on the key's table stream, once (caller holds h_mu).
-// In the background (beside proofs) the build takes 2 of the 8 blocks per SM a
-// full-GPU build uses, so that the proofs' kernels keep most of every SM.
-static constexpr int kBackgroundTableBlocks = 2;
-static int start_h_tables_locked(zk_groth16_pk* pk, bool background) {
+// The build's blocks are short (one launch per table entry), and a proof's
+// critical path runs at the highest stream priority, so a proof beside the
+// build gets SMs as the build's blocks retire.
+static int start_h_tables_locked(zk_groth16_pk* pk) {
     if (pk->h_tab || pk->h_tab_pending || pk->n_h < kHTablesMin) return ZK_OK;
     int c, W;
     g1_window_tables_shape((size_t)pk->n_h, &c, &W);
@@ -554,7 +554,7 @@ static int start_h_tables_locked(zk_groth16_pk* pk, bool background) {
     DeviceBuffer tab;
     ZK_TRY_CUDA(tab.alloc((size_t)W * pk->n_h * 64));
     const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
-    ZK_TRY(g1_window_tables_build(pk->device, pk->h_tab_stream, hq, (size_t)pk->n_h, c, W, tab.p, background ? kBackgroundTableBlocks : 8));
+    ZK_TRY(g1_window_tables_build(pk->device, pk->h_tab_stream, hq, (size_t)pk->n_h, c, W, tab.p));
     ZK_TRY_CUDA(cudaEventRecord(pk->h_tab_done, pk->h_tab_stream));
     pk->h_tab_pending = (uint8_t*)tab.release();
     pk->h_pc = c;
@@ -583,7 +583,7 @@ static int publish_h_tables_locked(zk_groth16_pk* pk, bool wait) {
 // The tables, built now if need be (zk_groth16_precompute).
 static int ensure_h_tables(zk_groth16_pk* pk) {
     std::lock_guard<std::mutex> lock(pk->h_mu);
-    ZK_TRY(start_h_tables_locked(pk, false));
+    ZK_TRY(start_h_tables_locked(pk));
     return publish_h_tables_locked(pk, true);
 }
 
@@ -593,13 +593,15 @@ static int ensure_h_tables(zk_groth16_pk* pk) {
 // plain MSM sized to the slice (measured at half the query: 10.3 vs 9.9 ms).
 // Until the tables are built (a build started by the first such call runs on
 // its own stream beside the proofs) the plain MSM serves.
-static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, size_t hi, uint64_t out[8]) {
+// start_build: a call without tables starts their build (a proof starts it
+// after its own work instead, so that its buffers grow before the build runs).
+static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, size_t hi, uint64_t out[8], bool start_build) {
     if ((hi - lo) * 4 >= (size_t)pk->n_h * 3) {
         uint8_t* tab;
         int c, W;
         {
             std::lock_guard<std::mutex> lock(pk->h_mu);
-            ZK_TRY(start_h_tables_locked(pk, true));
+            if (start_build) ZK_TRY(start_h_tables_locked(pk));
             ZK_TRY(publish_h_tables_locked(pk, false));
             tab = pk->h_tab;
             c = pk->h_c;
@@ -800,7 +802,7 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     zk_msm_stats ms_st;
     const int n_h = std::min<int>((int)n, pk->n_h);
     if (n_h > 0) {
-        ZK_TRY(h_msm(pk, st, pk->h, 0, (size_t)n_h, h_msm_out));
+        ZK_TRY(h_msm(pk, st, pk->h, 0, (size_t)n_h, h_msm_out, false));
         zk_msm_last_stats(&ms_st);
         stats.msm_ms[3] = ms_st.total_device_ms;
     }
@@ -820,6 +822,14 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     ZK_TRY_CUDA(cudaEventRecord(ev[3], st));
     if (st != user_st) ZK_TRY_CUDA(cudaStreamWaitEvent(user_st, ev[3], 0));
     ZK_TRY_CUDA(cudaEventSynchronize(ev[3]));
+    // The first proof ran its H MSM without window tables: their build starts
+    // now, on the key's own stream, and later proofs use them once it is done.
+    // Started inside the proof, the build delayed it (a first allocation of
+    // the witness context's scratch waits for the whole device).
+    if (n_h > 0 && (size_t)n_h * 4 >= (size_t)pk->n_h * 3) {
+        std::lock_guard<std::mutex> lock(pk->h_mu);
+        ZK_TRY(start_h_tables_locked(pk));
+    }
     cudaEventElapsedTime(&ms, ev[0], ev[3]);
     stats.total_ms = ms;
     return ZK_OK;
@@ -956,7 +966,7 @@ static void std_to_mont_host(uint64_t* v, size_t fe_count) {
 // 129 B (G2).  One thread per record: the record's bytes from aligned 32-bit
 // words (funnel shifts), then x R^2 R^-1 per coordinate (Montgomery form);
 // a set flag gives the all-zero record.  raw must extend 8 bytes past the
-// last record (the loader pads it).
+// last record (the loader's staging slots do).
 template <int kCoords>
 __global__ void unpack_records_kernel(const uint8_t* __restrict__ raw, size_t count, uint64_t* __restrict__ out) {
     constexpr int kRec = 1 + 32 * kCoords;
@@ -991,13 +1001,39 @@ __global__ void unpack_records_kernel(const uint8_t* __restrict__ raw, size_t co
 
 static thread_local zk_pk_load_stats g_load_stats;
 
+// Pinned host staging of the key loader: kBufs buffers, allocated by the first
+// load of the process (or grown by a later one) and kept until exit, so that a
+// load neither pins nor unpins host memory after the first.
+struct PinnedStaging {
+    static constexpr int kBufs = 3;
+    std::mutex mu;
+    uint8_t* p[kBufs] = {};
+    size_t bytes = 0;
+    int ensure(size_t need) {
+        if (bytes >= need) return ZK_OK;
+        for (auto& q : p) {
+            if (q) cudaFreeHost(q);
+            q = nullptr;
+        }
+        bytes = 0;
+        for (auto& q : p) ZK_TRY_CUDA(cudaMallocHost(&q, need));
+        bytes = need;
+        return ZK_OK;
+    }
+};
+static PinnedStaging& pinned_staging() {
+    static PinnedStaging* s = new PinnedStaging();  // never destroyed: freed with the process
+    return *s;
+}
+
 // ZKMLPK3 (ProvingKey::save / load_streaming, groth16.cu:1104-1314) straight
 // into device memory: the header and vector counts are read first (fixed-size
-// records give every offset), the five query vectors' bytes are read in 64 MiB
-// chunks by several threads into pinned buffers and copied to the device while
-// the next chunk is read, and one kernel per vector unpacks the records and
-// converts them to Montgomery form.  Fail-closed as the reference's loader:
-// bad magic or version, bad counts, truncation, incomplete query vectors.
+// records give every offset), then the five query vectors in pieces of whole
+// records (32 MiB at most): several threads read a piece into pinned staging,
+// it is copied to a device staging slot, and a kernel unpacks its records
+// into the key and converts them to Montgomery form, while the next piece is
+// read.  Fail-closed as the reference's loader: bad magic or version, bad
+// counts, truncation, incomplete query vectors.
 static int pk_load(int device, const char* path, zk_groth16_pk* pk) {
     zk_pk_load_stats& st = g_load_stats;
     std::memset(&st, 0, sizeof st);
@@ -1083,81 +1119,95 @@ static int pk_load(int device, const char* path, zk_groth16_pk* pk) {
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     pk->device = ctx->device;
-    const long long first = off[0], last = off[4] + (long long)counts[4] * 65;  // the vectors are contiguous
-    const size_t raw_bytes = (size_t)(last - first);
     const size_t g1_count = (size_t)counts[0] + counts[1] + counts[3] + counts[4];
-    DeviceBuffer raw_buf, g1_buf, g2_buf;
+    DeviceBuffer g1_buf, g2_buf;
     const auto a0 = std::chrono::steady_clock::now();
-    ZK_TRY_CUDA(raw_buf.alloc(raw_bytes + 64));
     ZK_TRY_CUDA(g1_buf.alloc(std::max<size_t>(g1_count, 1) * 64));
     ZK_TRY_CUDA(g2_buf.alloc(std::max<size_t>(counts[2], 1) * 128));
-    uint8_t* raw = (uint8_t*)raw_buf.p;
-    cudaStream_t cs = ctx->copy_stream;
-    ZK_TRY_CUDA(cudaMemsetAsync(raw + raw_bytes, 0, 64, cs));
-    // chunked read: kThreads readers fill one pinned chunk while the previous one
-    // is copied; ZKML_PK_LOAD_CHUNK_MB overrides the 64 MiB chunk
+    // ZKML_PK_LOAD_CHUNK_MB overrides the 32 MiB chunk
     const char* ce = getenv("ZKML_PK_LOAD_CHUNK_MB");
-    const size_t kChunk = (ce && atoi(ce) > 0 && atoi(ce) <= 4096 ? (size_t)atoi(ce) : (size_t)64) << 20;
-    constexpr int kBufs = 3, kThreads = 8;
-    uint8_t* pin[kBufs] = {};
-    cudaEvent_t pin_free[kBufs] = {};
-    struct PinnedSet {
-        uint8_t** p;
+    const size_t chunk = (ce && atoi(ce) > 0 && atoi(ce) <= 4096 ? (size_t)atoi(ce) : (size_t)32) << 20;
+    // a piece never exceeds the chunk nor the query vectors' total size
+    const size_t total = ((size_t)counts[0] + counts[1] + counts[3] + counts[4]) * 65 + (size_t)counts[2] * 129;
+    const size_t stage_bytes = std::max<size_t>(std::min(chunk, total), 1);
+    PinnedStaging& pool = pinned_staging();
+    std::lock_guard<std::mutex> pool_lock(pool.mu);
+    ZK_TRY(pool.ensure(stage_bytes));
+    const size_t slot = stage_bytes + 64;  // the unpack kernel reads up to 8 bytes past a piece's last record
+    // the device slots live in the context's scratch arena (grown once, kept):
+    // nothing is allocated or freed on the device for them after the first use
+    std::lock_guard<std::mutex> ctx_lock(ctx->mu);
+    ZK_TRY(ensure_scratch(ctx, PinnedStaging::kBufs * slot));
+    cudaStream_t cs = ctx->copy_stream;
+    ZK_TRY(scratch_begin(ctx, cs));
+    uint8_t* stage = (uint8_t*)ctx->scratch;
+    ZK_TRY_CUDA(cudaMemsetAsync(stage, 0, PinnedStaging::kBufs * slot, cs));
+    cudaEvent_t slot_free[PinnedStaging::kBufs] = {};
+    struct EventSet {
         cudaEvent_t* e;
-        ~PinnedSet() {
-            for (int i = 0; i < kBufs; i++) {
-                if (e[i]) { cudaEventSynchronize(e[i]); cudaEventDestroy(e[i]); }
-                if (p[i]) cudaFreeHost(p[i]);
-            }
+        cudaStream_t s;
+        ~EventSet() {
+            cudaStreamSynchronize(s);  // no copy or kernel still uses the staging on any exit path
+            for (int i = 0; i < PinnedStaging::kBufs; i++)
+                if (e[i]) cudaEventDestroy(e[i]);
         }
-    } pinned_set{pin, pin_free};
-    for (int i = 0; i < kBufs; i++) {
-        ZK_TRY_CUDA(cudaMallocHost(&pin[i], std::min(kChunk, std::max<size_t>(raw_bytes, 1))));
-        ZK_TRY_CUDA(cudaEventCreateWithFlags(&pin_free[i], cudaEventDisableTiming));
-        ZK_TRY_CUDA(cudaEventRecord(pin_free[i], cs));
+    } events{slot_free, cs};
+    for (int i = 0; i < PinnedStaging::kBufs; i++) {
+        ZK_TRY_CUDA(cudaEventCreateWithFlags(&slot_free[i], cudaEventDisableTiming));
+        ZK_TRY_CUDA(cudaEventRecord(slot_free[i], cs));
     }
     st.alloc_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - a0).count();
+    // Pieces of whole records of one vector, at most a chunk each: kThreads
+    // readers fill a pinned slot, the copy engine moves it to the device slot
+    // and one kernel unpacks it into the key, while the next piece is read.
+    // Output: A | B1 | L | H into g1 (file order A, B1, B2, L, H), B2 into g2.
+    constexpr int kThreads = 8;
     const int fd = fileno(f);
-    double read_s = 0;
-    for (size_t pos = 0, c = 0; pos < raw_bytes; pos += kChunk, c++) {
-        const size_t len = std::min(kChunk, raw_bytes - pos);
-        const int b = (int)(c % kBufs);
-        ZK_TRY_CUDA(cudaEventSynchronize(pin_free[b]));
-        const auto r0 = std::chrono::steady_clock::now();
-        std::atomic<bool> bad{false};
-        {
-            std::vector<std::thread> th;
-            for (int t = 0; t < kThreads; t++)
-                th.emplace_back([&, t]() {
-                    size_t a = len * t / kThreads, e = len * (t + 1) / kThreads;
-                    while (a < e) {
-                        const ssize_t got = pread(fd, pin[b] + a, e - a, (off_t)(first + (long long)(pos + a)));
-                        if (got <= 0) { bad = true; return; }
-                        a += (size_t)got;
-                    }
-                });
-            for (auto& x : th) x.join();
-        }
-        read_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - r0).count();
-        if (bad) { set_error("pk_load: read failed for %s", path); return ZK_ERR_INVALID; }
-        ZK_TRY_CUDA(cudaMemcpyAsync(raw + pos, pin[b], len, cudaMemcpyHostToDevice, cs));
-        ZK_TRY_CUDA(cudaEventRecord(pin_free[b], cs));
-    }
-    // unpack: A | B1 | L | H into g1, B2 into g2
-    uint8_t* g1 = (uint8_t*)g1_buf.p;
     const int grid = ctx->num_sms * 8;
-    size_t o1 = 0;
-    for (int v : {0, 1, 3, 4}) {
-        if (counts[v] > 0)
-            unpack_records_kernel<2><<<grid, 256, 0, cs>>>(raw + (off[v] - first), (size_t)counts[v], (uint64_t*)(g1 + o1 * 64));
-        o1 += (size_t)counts[v];
+    const size_t g1_at[5] = {0, (size_t)counts[0], 0, (size_t)counts[0] + counts[1], (size_t)counts[0] + counts[1] + counts[3]};
+    double read_s = 0, bytes = 0;
+    size_t piece = 0;
+    for (int v = 0; v < 5; v++) {
+        const size_t rec = v == 2 ? 129 : 65;
+        const size_t per = chunk / rec;
+        for (size_t r0 = 0; r0 < (size_t)counts[v]; r0 += per, piece++) {
+            const size_t nrec = std::min(per, (size_t)counts[v] - r0), len = nrec * rec;
+            const long long at = off[v] + (long long)(r0 * rec);
+            const int b = (int)(piece % PinnedStaging::kBufs);
+            ZK_TRY_CUDA(cudaEventSynchronize(slot_free[b]));
+            const auto r_start = std::chrono::steady_clock::now();
+            std::atomic<bool> bad{false};
+            {
+                std::vector<std::thread> th;
+                for (int t = 0; t < kThreads; t++)
+                    th.emplace_back([&, t]() {
+                        size_t x = len * t / kThreads, e = len * (t + 1) / kThreads;
+                        while (x < e) {
+                            const ssize_t got = pread(fd, pool.p[b] + x, e - x, (off_t)(at + (long long)x));
+                            if (got <= 0) { bad = true; return; }
+                            x += (size_t)got;
+                        }
+                    });
+                for (auto& x : th) x.join();
+            }
+            read_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - r_start).count();
+            if (bad) { set_error("pk_load: read failed for %s", path); return ZK_ERR_INVALID; }
+            bytes += (double)len;
+            uint8_t* dslot = stage + (size_t)b * slot;
+            ZK_TRY_CUDA(cudaMemcpyAsync(dslot, pool.p[b], len, cudaMemcpyHostToDevice, cs));
+            if (v == 2)
+                unpack_records_kernel<4><<<grid, 256, 0, cs>>>(dslot, nrec, (uint64_t*)((uint8_t*)g2_buf.p + r0 * 128));
+            else
+                unpack_records_kernel<2><<<grid, 256, 0, cs>>>(dslot, nrec, (uint64_t*)((uint8_t*)g1_buf.p + (g1_at[v] + r0) * 64));
+            ZK_TRY_CUDA(cudaGetLastError());
+            ZK_TRY_CUDA(cudaEventRecord(slot_free[b], cs));
+        }
     }
-    if (counts[2] > 0) unpack_records_kernel<4><<<grid, 256, 0, cs>>>(raw + (off[2] - first), (size_t)counts[2], (uint64_t*)g2_buf.p);
-    ZK_TRY_CUDA(cudaGetLastError());
+    ZK_TRY(scratch_end(ctx, cs));
     ZK_TRY_CUDA(cudaStreamSynchronize(cs));
     pk->g1 = (uint8_t*)g1_buf.release();
     pk->g2 = (uint8_t*)g2_buf.release();
-    st.bytes = (double)raw_bytes;
+    st.bytes = bytes;
     st.read_ms = read_s * 1e3;
     st.total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     return ZK_OK;
@@ -1461,7 +1511,7 @@ extern "C" int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const vo
     }
     DeviceContext* ctx;
     ZK_TRY(get_context(pk->device, &ctx));
-    return h_msm(pk, (cudaStream_t)stream, (const Fr*)d_h, lo, hi, (uint64_t*)out_affine);
+    return h_msm(pk, (cudaStream_t)stream, (const Fr*)d_h, lo, hi, (uint64_t*)out_affine, true);
 }
 
 extern "C" int zk_groth16_h_msm_blocks_device(zk_groth16_pk* pk, void* stream, const void* d_h_part, int log_parts, int part,

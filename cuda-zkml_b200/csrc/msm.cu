@@ -798,45 +798,54 @@ __global__ void fixed_base_kernel(const uint8_t* __restrict__ table, const Fr* _
     }
 }
 
-// out[j n + i] = 2^(c j) P_i (packed affine), j < W: the window tables of a
-// fixed set of bases (all-zero records stay the identity)
+// out[j n + i] = 2^(c j) P_i (packed affine) for the entries j in [j0, j1) of
+// the window tables of a fixed set of bases (all-zero records stay the
+// identity): one point per thread, starting from entry j0 - 1 (P_i itself,
+// written as entry 0, when j0 = 0), c doublings and one inversion per entry.
+// A build is one launch per entry, so that no block holds an SM for long and
+// proofs running beside a build get SMs as its blocks retire.
 template <class Cv>
-__global__ void window_tables_kernel(const uint8_t* __restrict__ pts, size_t n, int c, int W, uint8_t* __restrict__ out) {
+__global__ void window_tables_kernel(const uint8_t* __restrict__ pts, size_t n, int c, int j0, int j1, uint8_t* __restrict__ out) {
     using F = typename Cv::F;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        Affine<F> a;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    Affine<F> a;
+    if (j0 == 0) {
         load_affine(a, pts + i * Cv::kAffineBytes);
         fstore(out + i * Cv::kAffineBytes, a.x);
         fstore(out + i * Cv::kAffineBytes + sizeof(F), a.y);
-        const bool inf = fis_zero(a.x) && fis_zero(a.y);
-        Xyzz<F> cur, d;
-        cur.x = a.x;
-        cur.y = a.y;
-        fset_one(cur.zz);
-        fset_one(cur.zzz);
-        for (int j = 1; j < W; j++) {
-            Affine<F> r;
-            if (inf) {
-                fset_zero(r.x);
-                fset_zero(r.y);
-            } else {
-                for (int t = 0; t < c; t++) {
-                    dbl(d, cur);
-                    cur = d;
-                }
-                // 1 / zz = zzz / (zz zzz), 1 / zzz = zz / (zz zzz): one inversion
-                F q, qi, zi, zzi;
-                fmul(q, cur.zz, cur.zzz);
-                finv_dev(qi, q);
-                fmul(zi, cur.zzz, qi);
-                fmul(zzi, cur.zz, qi);
-                fmul(r.x, cur.x, zi);
-                fmul(r.y, cur.y, zzi);
+        j0 = 1;
+    } else {
+        load_affine(a, out + ((size_t)(j0 - 1) * n + i) * Cv::kAffineBytes);
+    }
+    const bool inf = fis_zero(a.x) && fis_zero(a.y);
+    Xyzz<F> cur, d;
+    cur.x = a.x;
+    cur.y = a.y;
+    fset_one(cur.zz);
+    fset_one(cur.zzz);
+    for (int j = j0; j < j1; j++) {
+        Affine<F> r;
+        if (inf) {
+            fset_zero(r.x);
+            fset_zero(r.y);
+        } else {
+            for (int t = 0; t < c; t++) {
+                dbl(d, cur);
+                cur = d;
             }
-            uint8_t* o = out + ((size_t)j * n + i) * Cv::kAffineBytes;
-            fstore(o, r.x);
-            fstore(o + sizeof(F), r.y);
+            // 1 / zz = zzz / (zz zzz), 1 / zzz = zz / (zz zzz): one inversion
+            F q, qi, zi, zzi;
+            fmul(q, cur.zz, cur.zzz);
+            finv_dev(qi, q);
+            fmul(zi, cur.zzz, qi);
+            fmul(zzi, cur.zz, qi);
+            fmul(r.x, cur.x, zi);
+            fmul(r.y, cur.y, zzi);
         }
+        uint8_t* o = out + ((size_t)j * n + i) * Cv::kAffineBytes;
+        fstore(o, r.x);
+        fstore(o + sizeof(F), r.y);
     }
 }
 
@@ -1511,13 +1520,17 @@ void g1_window_tables_shape(size_t n, int* c_out, int* W_out) {
     *W_out = (255 + best - 1) / best;
 }
 
-int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out, int blocks_per_sm) {
+int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out) {
     DeviceContext* ctx;
     ZK_TRY(get_context(device, &ctx));
     if (!n) return ZK_OK;
-    window_tables_kernel<G1><<<grid_for(n, 128, ctx->num_sms * std::max(blocks_per_sm, 1)), 128, 0, st>>>((const uint8_t*)d_points, n, c, W,
-                                                                                                       (uint8_t*)d_out);
-    ZK_TRY_CUDA(cudaGetLastError());
+    const unsigned blocks = (unsigned)((n + 127) / 128);
+    for (int j = 0; j < W; j++)  // entries 0 and 1 in the first launch
+        if (j != 1) {
+            window_tables_kernel<G1><<<blocks, 128, 0, st>>>((const uint8_t*)d_points, n, c, j, j == 0 ? std::min(W, 2) : j + 1,
+                                                             (uint8_t*)d_out);
+            ZK_TRY_CUDA(cudaGetLastError());
+        }
     return ZK_OK;
 }
 

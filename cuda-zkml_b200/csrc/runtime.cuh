@@ -150,9 +150,7 @@ MsmStats& msm_stats();
 // Precomputed window tables of fixed G1 bases (msm.cu): 2^(c j) P_i for j < W
 // at index j n + i; the MSM of scalars[0, hi - lo) against bases [lo, hi).
 void g1_window_tables_shape(size_t n, int* c, int* W);
-// blocks_per_sm: 8 fills the GPU; a build running beside proofs takes fewer
-// (its blocks stride over all points and hold their SMs until the end)
-int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out, int blocks_per_sm = 8);
+int g1_window_tables_build(int device, cudaStream_t st, const void* d_points, size_t n, int c, int W, void* d_out);
 // Several MSMs (G1 or G2 point sets) over the same device scalars with one
 // shared counting sort (msm.cu), in the scratch of `ctx`; outs[k]: 64 or 128
 // host bytes.

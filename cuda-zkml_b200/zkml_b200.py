@@ -556,7 +556,8 @@ class ProvingKey:
 
     def precompute(self, stream=None):
         """Build the H-query window tables now and wait for them (else the
-        first proof starts their build and proofs run without them until done)."""
+        first proof starts their build as it ends and proofs run without them
+        until it is done)."""
         check(lib.zk_groth16_precompute(self.h, stream))
 
     def witness_msms(self, d_w, lo, hi):

@@ -229,7 +229,11 @@ int zk_r1cs_domain(const zk_r1cs* r1cs, int* log_n);
  * (groth16.cu:446-642); the key is byte-identical for the same toxic waste. */
 int zk_groth16_setup(zk_r1cs* r1cs, const void* toxic, zk_groth16_pk** out);
 /* ZKMLPK3 proving-key files (ProvingKey::save / load_streaming,
- * groth16.cu:1104-1314), loaded straight into device memory. */
+ * groth16.cu:1104-1314), loaded straight into device memory: pieces of whole
+ * records read by several threads into pinned staging, copied and converted on
+ * the GPU while the next piece is read.  The first load of the process pins
+ * 3 x 32 MiB of host staging (less for a smaller key; ZKML_PK_LOAD_CHUNK_MB
+ * sets the piece size) and keeps it for later loads until the process exits. */
 int zk_groth16_pk_load(int device, const char* path, zk_groth16_pk** out);
 /* The calling thread's last zk_groth16_pk_load: bytes of query records read,
  * host time spent reading them (parallel reads into pinned chunks, overlapped
@@ -345,11 +349,11 @@ int zk_groth16_assemble(const zk_groth16_pk* pk, const void* r, const void* s, c
  * (groth16.cu:817), with d_h the n_h device coefficients of h.  From 2^16
  * points, for a slice of at least 3/4 of the query, it runs over precomputed
  * window tables of the query (2^(c j) H_i: c = 20 and 13 tables, 3.5 GB, at
- * 2^22); all windows then share one bucket set and one reduce.  The first call
- * (or proof) without tables starts building them on a stream of the key's own
- * (about 0.55 s of GPU time at 2^22) and runs the plain MSM, as do the calls
- * made before the build has finished; zk_groth16_precompute builds them and
- * waits.  Smaller slices run the plain MSM. */
+ * 2^22); all windows then share one bucket set and one reduce.  Without
+ * tables the plain MSM runs, and the first such call (or the end of the first
+ * proof) starts building them on a stream of the key's own (about 0.55 s of
+ * GPU time at 2^22); zk_groth16_precompute builds them and waits.  Smaller
+ * slices run the plain MSM. */
 int zk_groth16_h_msm_device(zk_groth16_pk* pk, void* stream, const void* d_h, uint64_t lo, uint64_t hi,
                             void* out_affine);
 /* One part's share of the H MSM of a proof split over 2^log_parts parts:
@@ -372,7 +376,8 @@ int zk_groth16_witness_msms_device(zk_groth16_pk* pk, void* stream, const void* 
                                    uint64_t hi, void* sums);
 /* Build the key's precomputed H-query tables now (on the key's own stream;
  * `stream` is not used) and return when they are ready; otherwise the first
- * proof starts the build and proofs run without them until it is done. */
+ * proof starts the build as it ends and proofs run without them until it is
+ * done. */
 int zk_groth16_precompute(zk_groth16_pk* pk, void* stream);
 
 /* The same from nparts partial records of 384 B (one per rank), summed first. */
