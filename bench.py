@@ -240,6 +240,16 @@ def run_reference(args):
         step()
     dt = (time.perf_counter() - t0) / args.steps
     value = n / dt
+    naive = None
+    if kind == "reference":
+        # for context: the sum of scalar_mul of the reference's CPU test helper
+        # (tests/test_msm.cu:20-28) and of msm_g1's small-n path (src/msm/
+        # msm.cu:330-339), with its host arithmetic, at 2^16 points on all cores
+        nn = 1 << 16
+        t0 = time.perf_counter()
+        ref.ref_msm_g1_naive_mt(O._p(out), ctypes.byref(inf), O._p(pts[:nn]), O._p(sc[:nn]), nn, cores)
+        nt = time.perf_counter() - t0
+        naive = {"points": nn, "ms": nt * 1e3, "points_per_s": nn / nt, "cores": cores}
     sample = f"{n} of the 2^{args.log_n} points per step, {what}, {cores} threads"
     emit({"impl": "reference", "metric": METRIC, "value": value, "unit": "points/s", "n_gpus": args.gpus,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
@@ -248,7 +258,7 @@ def run_reference(args):
                      "sample_points": n},
           "cpu_baseline": {"value": value, "unit": "points/s", "cores": cores, "kind": kind, "sample": sample},
           "e2e": {"value": value, "unit": "points/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-          "reference_gpu_ntt": gpu_ntt, "reference_drop_in_prove": drop_in})
+          "reference_gpu_ntt": gpu_ntt, "reference_drop_in_prove": drop_in, "reference_naive_msm": naive})
 
 
 # ---------------------------------------------------------------- Groth16 prove
