@@ -250,7 +250,10 @@ __global__ void __launch_bounds__(256) msm_bitlen_hist_kernel(const Fr* __restri
 #pragma unroll
         for (int k = 7; k >= 0; k--)
             if (len == 0 && s.v[k]) len = 32 * k + 32 - __clz(s.v[k]);
-        atomicAdd(&h[len], 1u);
+        // uniform scalars put nearly every lane on the same length or two: one
+        // shared-memory atomic per distinct length in the warp
+        const unsigned peers = __match_any_sync(__activemask(), len);
+        if ((threadIdx.x & 31) == (unsigned)(__ffs(peers) - 1)) atomicAdd(&h[len], (uint32_t)__popc(peers));
     }
     __syncthreads();
     for (int i = threadIdx.x; i < 256; i += blockDim.x)
