@@ -103,6 +103,20 @@ def emit(obj):
     print(json.dumps(obj), flush=True)
 
 
+def host_cpu():
+    """The host the CPU figures ran on: logical cores and the CPU model name."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "model": model}
+
+
 # ---------------------------------------------------------------- reference arm
 def reference_gpu_ntt(ref, sizes, reps=3):
     """The reference's own GPU NTT entry point bn254::ntt_gpu (src/ntt/ntt.cu:
@@ -256,7 +270,7 @@ def run_reference(args):
           "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
           "config": {"workload": f"G1 MSM, 2^{args.log_n} points per GPU (configs[1])", "log_n": args.log_n,
                      "sample_points": n},
-          "cpu_baseline": {"value": value, "unit": "points/s", "cores": cores, "kind": kind, "sample": sample},
+          "cpu_baseline": {"value": value, "unit": "points/s", "cores": cores, "kind": kind, "sample": sample, "host": host_cpu()},
           "e2e": {"value": value, "unit": "points/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
           "reference_gpu_ntt": gpu_ntt, "reference_drop_in_prove": drop_in, "reference_naive_msm": naive})
 
@@ -617,7 +631,7 @@ def run_b200(args):
         t0 = time.perf_counter()
         O.msm_g1(ph, sh, nthreads=cores)
         dt = time.perf_counter() - t0
-        cpu = {"value": m / dt, "unit": "points/s", "cores": cores, "kind": "port",
+        cpu = {"value": m / dt, "unit": "points/s", "cores": cores, "kind": "port", "host": host_cpu(),
                "sample": f"first 2^{args.cpu_log_n} of the rank-0 points/scalars, oracle Pippenger "
                          f"(reference windows c={'/'.join(map(str, (14 if m <= 1 << 18 else 15,)))}), {cores} threads"}
 

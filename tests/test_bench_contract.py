@@ -31,6 +31,7 @@ def test_reference_arm_prints_one_contract_line():
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert cb["host"]["nproc"] >= 1
     if cb["kind"] == "reference":
         nv = d["reference_naive_msm"]
         assert nv["points"] == 1 << 16 and nv["points_per_s"] > 0
