@@ -11,9 +11,10 @@
 // 2010, for BN curves): f_{6t+2, Q}(P) over the signed binary expansion of
 // 6t + 2 (t = 4965661367192848881, the BN parameter), then the lines through
 // [6t+2]Q and pi(Q), and through that sum and -pi^2(Q), pi the p-power
-// Frobenius.  Points of the loop are kept affine (one Fp2 inversion per step:
-// a verifier runs four loops per proof, so clarity wins over speed here).  The
-// line through T with slope l (on the twist), evaluated at P = (xP, yP), is
+// Frobenius.  Points of the loop are kept affine; the loops of the pairs of a
+// product advance together, so each step takes one Fp2 inversion for all of
+// them (Montgomery's trick).  The line through T with slope l (on the twist),
+// evaluated at P = (xP, yP), is
 //   yP - l xP w + (l xT - yT) w^3,
 // vertical lines omitted (they lie in a proper subfield and vanish under the
 // final exponentiation).
@@ -46,7 +47,17 @@ static Fp2 f2(const Fe& a, const Fe& b) { Fp2 r; r.c0 = a; r.c1 = b; return r; }
 static Fp2 add(const Fp2& a, const Fp2& b) { Fp2 r; zkh::fadd(r, a, b); return r; }
 static Fp2 sub(const Fp2& a, const Fp2& b) { Fp2 r; zkh::fsub(r, a, b); return r; }
 static Fp2 mul(const Fp2& a, const Fp2& b) { Fp2 r; zkh::fmul(r, a, b); return r; }
-static Fp2 sqr(const Fp2& a) { return mul(a, a); }
+// (a0 + a1 u)^2 = (a0 + a1)(a0 - a1) + 2 a0 a1 u: two products
+static Fp2 sqr(const Fp2& a) {
+    Fe s, d, t;
+    zkh::fadd(s, a.c0, a.c1);
+    zkh::fsub(d, a.c0, a.c1);
+    Fp2 r;
+    zkh::fmul(r.c0, s, d);
+    zkh::fmul(t, a.c0, a.c1);
+    zkh::fadd(r.c1, t, t);
+    return r;
+}
 static Fp2 neg(const Fp2& a) { Fp2 z; zkh::fset_zero(z); return sub(z, a); }
 static Fp2 inv(const Fp2& a) { Fp2 r; zkh::finv(r, a); return r; }
 static Fp2 conj(const Fp2& a) { Fp2 r; r.c0 = a.c0; zkh::fsub(r.c1, zkh::zero(), a.c1); return r; }
@@ -60,9 +71,22 @@ static Fe fp_small(uint64_t v) {
     zkh::from_std(zkh::kP, r, s);
     return r;
 }
-// xi = 9 + u
+// xi = 9 + u; (a0 + a1 u)(9 + u) = (9 a0 - a1) + (a0 + 9 a1) u, by additions
 static Fp2 xi() { return f2(fp_small(9), fp_small(1)); }
-static Fp2 mul_xi(const Fp2& a) { return mul(a, xi()); }
+static Fe times9(const Fe& a) {
+    Fe t;
+    zkh::fadd(t, a, a);  // 2a
+    zkh::fadd(t, t, t);  // 4a
+    zkh::fadd(t, t, t);  // 8a
+    zkh::fadd(t, t, a);  // 9a
+    return t;
+}
+static Fp2 mul_xi(const Fp2& a) {
+    Fp2 r;
+    zkh::fsub(r.c0, times9(a.c0), a.c1);
+    zkh::fadd(r.c1, a.c0, times9(a.c1));
+    return r;
+}
 static Fp2 pow2(const Fp2& a, const uint64_t e[4]) {
     Fp2 acc = one2();
     for (int bit = 255; bit >= 0; bit--) {
@@ -80,12 +104,12 @@ static Fp6 add(const Fp6& a, const Fp6& b) { return {add(a.c0, b.c0), add(a.c1, 
 static Fp6 sub(const Fp6& a, const Fp6& b) { return {sub(a.c0, b.c0), sub(a.c1, b.c1), sub(a.c2, b.c2)}; }
 static Fp6 neg(const Fp6& a) { return {neg(a.c0), neg(a.c1), neg(a.c2)}; }
 static Fp6 mul(const Fp6& a, const Fp6& b) {
-    // v^3 = xi
-    const Fp2 a0b0 = mul(a.c0, b.c0), a1b1 = mul(a.c1, b.c1), a2b2 = mul(a.c2, b.c2);
-    const Fp2 r0 = add(a0b0, mul_xi(add(mul(a.c1, b.c2), mul(a.c2, b.c1))));
-    const Fp2 r1 = add(add(mul(a.c0, b.c1), mul(a.c1, b.c0)), mul_xi(a2b2));
-    const Fp2 r2 = add(add(mul(a.c0, b.c2), a1b1), mul(a.c2, b.c0));
-    return {r0, r1, r2};
+    // v^3 = xi; Karatsuba: six Fp2 products
+    const Fp2 t0 = mul(a.c0, b.c0), t1 = mul(a.c1, b.c1), t2 = mul(a.c2, b.c2);
+    const Fp2 s12 = sub(sub(mul(add(a.c1, a.c2), add(b.c1, b.c2)), t1), t2);  // a1 b2 + a2 b1
+    const Fp2 s01 = sub(sub(mul(add(a.c0, a.c1), add(b.c0, b.c1)), t0), t1);  // a0 b1 + a1 b0
+    const Fp2 s02 = sub(sub(mul(add(a.c0, a.c2), add(b.c0, b.c2)), t0), t2);  // a0 b2 + a2 b0
+    return {add(t0, mul_xi(s12)), add(s01, mul_xi(t2)), add(s02, t1)};
 }
 static Fp6 mul_v(const Fp6& a) { return {mul_xi(a.c2), a.c0, a.c1}; }
 static Fp6 one6() { return {one2(), zero2(), zero2()}; }
@@ -101,10 +125,17 @@ static Fp6 inv(const Fp6& a) {
 struct Fp12 {
     Fp6 c0, c1;
 };
-static Fp12 mul(const Fp12& a, const Fp12& b) {  // w^2 = v
-    return {add(mul(a.c0, b.c0), mul_v(mul(a.c1, b.c1))), add(mul(a.c0, b.c1), mul(a.c1, b.c0))};
+static Fp12 mul(const Fp12& a, const Fp12& b) {  // w^2 = v; Karatsuba: three Fp6 products
+    const Fp6 t0 = mul(a.c0, b.c0), t1 = mul(a.c1, b.c1);
+    const Fp6 s = sub(sub(mul(add(a.c0, a.c1), add(b.c0, b.c1)), t0), t1);
+    return {add(t0, mul_v(t1)), s};
 }
-static Fp12 sqr(const Fp12& a) { return mul(a, a); }
+// (a0 + a1 w)^2 = (a0 + a1)(a0 + v a1) - t - v t + 2 t w, t = a0 a1: two Fp6 products
+static Fp12 sqr(const Fp12& a) {
+    const Fp6 t = mul(a.c0, a.c1);
+    const Fp6 c0 = sub(sub(mul(add(a.c0, a.c1), add(a.c0, mul_v(a.c1))), t), mul_v(t));
+    return {c0, add(t, t)};
+}
 static Fp12 conj(const Fp12& a) { return {a.c0, neg(a.c1)}; }
 static Fp12 one12() { return {one6(), {zero2(), zero2(), zero2()}}; }
 static Fp12 inv(const Fp12& a) {  // (c0 - c1 w) / (c0^2 - v c1^2)
@@ -276,25 +307,65 @@ static Fp12 frob(const Fp12& a) {
     r.c1.c2 = mul(conj(a.c1.c2), C.gamma[5]);
     return r;
 }
-static Fp12 pow12(const Fp12& a, const uint64_t e[4]) {
+// Squaring in the cyclotomic subgroup (order p^4 - p^2 + 1), after Granger and
+// Scott, "Faster squaring in the cyclotomic subgroup of sixth degree
+// extensions" (PKC 2010).  With X = w and Y = w^3 (Y^2 = xi, X^3 = Y) an element
+// is a0 + a1 X + a2 X^2 over Fp4 = Fp2[Y], with a0 = c0.c0 + c1.c1 Y,
+// a1 = c1.c0 + c0.c2 Y, a2 = c0.c1 + c1.c2 Y, and its square is
+//   (3 a0^2 - 2 conj(a0)) + (3 Y a2^2 + 2 conj(a1)) X + (3 a1^2 - 2 conj(a2)) X^2,
+// conj: Y -> -Y.  Three Fp4 squarings (x + y Y)^2 = (x^2 + xi y^2) + 2 x y Y.
+static void fp4_sqr(Fp2& r0, Fp2& r1, const Fp2& x, const Fp2& y) {
+    const Fp2 xy = mul(x, y);
+    r0 = add(sqr(x), mul_xi(sqr(y)));
+    r1 = add(xy, xy);
+}
+static Fp2 times3(const Fp2& a) { return add(add(a, a), a); }
+static Fp2 twice(const Fp2& a) { return add(a, a); }
+static Fp12 cyclotomic_sqr(const Fp12& a) {
+    Fp2 s0, s1, t0, t1, u0, u1;
+    fp4_sqr(s0, s1, a.c0.c0, a.c1.c1);  // a0^2
+    fp4_sqr(t0, t1, a.c1.c0, a.c0.c2);  // a1^2
+    fp4_sqr(u0, u1, a.c0.c1, a.c1.c2);  // a2^2
+    Fp12 r;
+    r.c0.c0 = sub(times3(s0), twice(a.c0.c0));        // 3 Re(a0^2) - 2 Re(a0)
+    r.c1.c1 = add(times3(s1), twice(a.c1.c1));        // 3 Im(a0^2) + 2 Im(a0)
+    r.c1.c0 = add(times3(mul_xi(u1)), twice(a.c1.c0));  // Y a2^2 = xi Im + Re Y
+    r.c0.c2 = sub(times3(u0), twice(a.c0.c2));
+    r.c0.c1 = sub(times3(t0), twice(a.c0.c1));
+    r.c1.c2 = add(times3(t1), twice(a.c1.c2));
+    return r;
+}
+// a^e for a in the cyclotomic subgroup
+static Fp12 pow_cyclotomic(const Fp12& a, const uint64_t e[4]) {
     Fp12 acc = one12();
     int top = 255;
     while (top >= 0 && !((e[top >> 6] >> (top & 63)) & 1)) top--;
     for (int bit = top; bit >= 0; bit--) {
-        acc = sqr(acc);
+        acc = cyclotomic_sqr(acc);
         if ((e[bit >> 6] >> (bit & 63)) & 1) acc = mul(acc, a);
     }
     return acc;
 }
+// The hard part m^d, d = l0 + l1 p + l2 p^2 + p^3, from A = m^t, B = m^(t^2),
+// Cc = m^(t^3) (three exponentiations by the 63-bit t) and short chains for the
+// small coefficients: m^l2 = B^6 m, m^l1 = conj(Cc^36 B^18 A^12) m,
+// m^l0 = conj(Cc^36 B^30 A^18 m^2) (conj inverts in the cyclotomic subgroup).
+// The same exponent as one exponentiation by each l_i, in about a third of the
+// operations.
 static Fp12 final_exp(const Fp12& f) {
-    const Consts& C = consts();
     Fp12 m = mul(conj(f), inv(f));  // f^(p^6 - 1)
-    m = mul(frob(frob(m)), m);       // ^(p^2 + 1)
-    const Fp12 a = conj(pow12(m, C.l0));
-    const Fp12 b = conj(pow12(frob(m), C.l1));
-    const Fp12 c = pow12(frob(frob(m)), C.l2);
-    const Fp12 d = frob(frob(frob(m)));
-    return mul(mul(a, b), mul(c, d));
+    m = mul(frob(frob(m)), m);       // ^(p^2 + 1): now in the cyclotomic subgroup
+    const uint64_t te[4] = {kT, 0, 0, 0};
+    const Fp12 A = pow_cyclotomic(m, te), B = pow_cyclotomic(A, te), Cc = pow_cyclotomic(B, te);
+    auto sq = [](const Fp12& x) { return cyclotomic_sqr(x); };
+    const Fp12 A2 = sq(A), A4 = sq(A2), A8 = sq(A4), A16 = sq(A8);
+    const Fp12 B2 = sq(B), B4 = sq(B2), B8 = sq(B4), B16 = sq(B8);
+    const Fp12 C4 = sq(sq(Cc)), C32 = sq(sq(sq(C4)));
+    const Fp12 C36 = mul(C32, C4);
+    const Fp12 m_l2 = mul(mul(B4, B2), m);                                         // B^6 m
+    const Fp12 m_l1 = mul(conj(mul(mul(C36, mul(B16, B2)), mul(A8, A4))), m);     // conj(Cc^36 B^18 A^12) m
+    const Fp12 m_l0 = conj(mul(mul(C36, mul(mul(B16, B8), mul(B4, B2))), mul(mul(A16, A2), sq(m))));
+    return mul(mul(m_l0, frob(m_l1)), mul(frob(frob(m_l2)), frob(frob(frob(m)))));
 }
 
 // ---------------------------------------------------------------- Miller loop
@@ -315,19 +386,19 @@ static Fp12 line(const Fp2& l, const Fp2& xT, const Fp2& yT, const G1a& P) {
     r.c1.c1 = sub(mul(l, xT), yT);
     return r;
 }
-// T <- 2T, returns the tangent line at T
-static Fp12 dbl_step(G2a& T, const G1a& P) {
+// T <- 2T given inv2y = 1 / (2 yT); returns the tangent line at T
+static Fp12 dbl_step(G2a& T, const Fp2& inv2y, const G1a& P) {
     const Fp2 x2 = sqr(T.x);
-    const Fp2 l = mul(add(add(x2, x2), x2), inv(add(T.y, T.y)));
+    const Fp2 l = mul(add(add(x2, x2), x2), inv2y);
     const Fp12 ln = line(l, T.x, T.y, P);
     const Fp2 x3 = sub(sub(sqr(l), T.x), T.x);
     T.y = sub(mul(l, sub(T.x, x3)), T.y);
     T.x = x3;
     return ln;
 }
-// T <- T + Q, returns the line through T and Q
-static Fp12 add_step(G2a& T, const G2a& Q, const G1a& P) {
-    const Fp2 l = mul(sub(Q.y, T.y), inv(sub(Q.x, T.x)));
+// T <- T + Q given invdx = 1 / (xQ - xT); returns the line through T and Q
+static Fp12 add_step(G2a& T, const G2a& Q, const Fp2& invdx, const G1a& P) {
+    const Fp2 l = mul(sub(Q.y, T.y), invdx);
     const Fp12 ln = line(l, T.x, T.y, P);
     const Fp2 x3 = sub(sub(sqr(l), T.x), Q.x);
     T.y = sub(mul(l, sub(T.x, x3)), T.y);
@@ -338,9 +409,24 @@ static G2a frob_g2(const G2a& Q) {
     const Consts& C = consts();
     return {mul(conj(Q.x), C.gamma[2]), mul(conj(Q.y), C.gamma[3]), Q.inf};
 }
+// v[i] <- 1 / v[i] with one inversion (Montgomery's trick): 3 (n - 1) products
+static void batch_inv(std::vector<Fp2>& v) {
+    if (v.empty()) return;
+    std::vector<Fp2> pre(v.size());
+    pre[0] = v[0];
+    for (size_t i = 1; i < v.size(); i++) pre[i] = mul(pre[i - 1], v[i]);
+    Fp2 acc = inv(pre.back());
+    for (size_t i = v.size() - 1; i > 0; i--) {
+        const Fp2 vi = mul(acc, pre[i - 1]);
+        acc = mul(acc, v[i]);
+        v[i] = vi;
+    }
+    v[0] = acc;
+}
 
 // prod_k f_{6t+2, Q_k}(P_k) (with the two Frobenius lines), pairs with an
-// infinite point skipped (their pairing is 1)
+// infinite point skipped (their pairing is 1).  The loops of all pairs advance
+// together, so each step's slope denominators share one inversion.
 static Fp12 multi_miller(const G1a* P, const G2a* Q, int n) {
     const Consts& C = consts();
     std::vector<G2a> T;
@@ -350,25 +436,37 @@ static Fp12 multi_miller(const G1a* P, const G2a* Q, int n) {
             T.push_back(Q[k]);
             idx.push_back(k);
         }
+    std::vector<Fp2> den(T.size());
     Fp12 f = one12();
     const int top = (int)C.naf.size() - 1;
     for (int i = top - 1; i >= 0; i--) {
         f = sqr(f);
-        for (size_t j = 0; j < T.size(); j++) f = mul(f, dbl_step(T[j], P[idx[j]]));
+        for (size_t j = 0; j < T.size(); j++) den[j] = add(T[j].y, T[j].y);
+        batch_inv(den);
+        for (size_t j = 0; j < T.size(); j++) f = mul(f, dbl_step(T[j], den[j], P[idx[j]]));
         if (C.naf[(size_t)i] != 0) {
+            std::vector<G2a> q(T.size());
             for (size_t j = 0; j < T.size(); j++) {
-                G2a q = Q[idx[j]];
-                if (C.naf[(size_t)i] < 0) q.y = neg(q.y);
-                f = mul(f, add_step(T[j], q, P[idx[j]]));
+                q[j] = Q[idx[j]];
+                if (C.naf[(size_t)i] < 0) q[j].y = neg(q[j].y);
+                den[j] = sub(q[j].x, T[j].x);
             }
+            batch_inv(den);
+            for (size_t j = 0; j < T.size(); j++) f = mul(f, add_step(T[j], q[j], den[j], P[idx[j]]));
         }
     }
-    for (size_t j = 0; j < T.size(); j++) {
-        const G2a q1 = frob_g2(Q[idx[j]]);
-        G2a q2 = frob_g2(q1);
-        q2.y = neg(q2.y);
-        f = mul(f, add_step(T[j], q1, P[idx[j]]));
-        f = mul(f, add_step(T[j], q2, P[idx[j]]));
+    for (int s2 = 0; s2 < 2; s2++) {  // the lines through pi(Q), then through -pi^2(Q)
+        std::vector<G2a> q(T.size());
+        for (size_t j = 0; j < T.size(); j++) {
+            q[j] = frob_g2(Q[idx[j]]);
+            if (s2 == 1) {
+                q[j] = frob_g2(q[j]);
+                q[j].y = neg(q[j].y);
+            }
+            den[j] = sub(q[j].x, T[j].x);
+        }
+        batch_inv(den);
+        for (size_t j = 0; j < T.size(); j++) f = mul(f, add_step(T[j], q[j], den[j], P[idx[j]]));
     }
     return f;
 }
