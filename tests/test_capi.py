@@ -168,3 +168,29 @@ def test_split_prove_entry_points_check_arguments():
     assert len(uid) == 128 and uid != Z.Comm.unique_id()
     if Z.device_count() == 0:
         assert Z.lib.zk_comm_init_local(0, 2, ctypes.cast(hs, ctypes.c_void_p)) == Z.ZK_ERR_NODEV
+
+
+def test_pk_load_refuses_bad_files_before_device_work(tmp_path):
+    """zk_groth16_pk_load walks the ZKMLPK3 header and the five vector counts
+    before it touches a device: a missing file, a wrong magic and a truncated
+    key are refused with ZK_ERR_INVALID on a machine without a GPU; an intact
+    key (the reference's own T4 pk.bin, read in place) passes the walk and then
+    reports ZK_ERR_NODEV (no CPU fallback)."""
+    import ctypes
+    h = ctypes.c_void_p()
+    assert Z.lib.zk_groth16_pk_load(0, str(tmp_path / "none.bin").encode(), ctypes.byref(h)) == Z.ZK_ERR_INVALID
+    assert "cannot open" in Z.last_error()
+    bad = tmp_path / "bad.bin"
+    bad.write_bytes(b"ZKMLPK2\0" + bytes(64))
+    assert Z.lib.zk_groth16_pk_load(0, str(bad).encode(), ctypes.byref(h)) == Z.ZK_ERR_INVALID
+    assert "not a ZKMLPK3" in Z.last_error()
+    ref_pk = os.path.join(O.reference_tree(), "results", "gpu_validation_2026", "artifacts", "p16", "pk.bin")
+    if not os.path.exists(ref_pk):
+        pytest.skip("reference artefacts not present")
+    raw = open(ref_pk, "rb").read()
+    cut = tmp_path / "cut.bin"
+    cut.write_bytes(raw[:-100])
+    assert Z.lib.zk_groth16_pk_load(0, str(cut).encode(), ctypes.byref(h)) == Z.ZK_ERR_INVALID
+    assert "truncated" in Z.last_error()
+    if Z.device_count() == 0:
+        assert Z.lib.zk_groth16_pk_load(0, ref_pk.encode(), ctypes.byref(h)) == Z.ZK_ERR_NODEV
