@@ -542,8 +542,11 @@ static constexpr int kHTablesMin = 1 << 16;
 // The build's blocks are short (one launch per table entry), and a proof's
 // critical path runs at the highest stream priority, so a proof beside the
 // build gets SMs as the build's blocks retire.
-static int start_h_tables_locked(zk_groth16_pk* pk) {
-    if (pk->h_tab || pk->h_tab_pending || pk->n_h < kHTablesMin) return ZK_OK;
+// optional: a start on behalf of a proof or an H MSM, for which the tables are
+// an optimisation: without device memory for them the plain MSM goes on serving
+// (and no later call tries again); zk_groth16_precompute asks for them outright.
+static int start_h_tables_locked(zk_groth16_pk* pk, bool optional) {
+    if (pk->h_tab || pk->h_tab_pending || pk->n_h < kHTablesMin || (optional && pk->h_tab_off)) return ZK_OK;
     int c, W;
     g1_window_tables_shape((size_t)pk->n_h, &c, &W);
     if ((size_t)W * pk->n_h > 0x7fffffffull) return ZK_OK;  // keys index 32 bits: the plain MSM runs in passes
@@ -552,7 +555,16 @@ static int start_h_tables_locked(zk_groth16_pk* pk) {
         ZK_TRY_CUDA(cudaEventCreateWithFlags(&pk->h_tab_done, cudaEventDisableTiming));
     }
     DeviceBuffer tab;
-    ZK_TRY_CUDA(tab.alloc((size_t)W * pk->n_h * 64));
+    const cudaError_t ae = tab.alloc((size_t)W * pk->n_h * 64);
+    if (ae != cudaSuccess) {
+        cudaGetLastError();  // an allocation failure is not sticky; clear it for the next call
+        if (optional) {
+            pk->h_tab_off = true;
+            return ZK_OK;
+        }
+        set_error("H-query window tables (%zu bytes): %s", (size_t)W * pk->n_h * 64, cudaGetErrorString(ae));
+        return ae == cudaErrorMemoryAllocation ? ZK_ERR_NOMEM : ZK_ERR_CUDA;
+    }
     const uint8_t* hq = pk->g1 + (2 * (size_t)pk->m + pk->l) * 64;
     ZK_TRY(g1_window_tables_build(pk->device, pk->h_tab_stream, hq, (size_t)pk->n_h, c, W, tab.p));
     ZK_TRY_CUDA(cudaEventRecord(pk->h_tab_done, pk->h_tab_stream));
@@ -583,7 +595,7 @@ static int publish_h_tables_locked(zk_groth16_pk* pk, bool wait) {
 // The tables, built now if need be (zk_groth16_precompute).
 static int ensure_h_tables(zk_groth16_pk* pk) {
     std::lock_guard<std::mutex> lock(pk->h_mu);
-    ZK_TRY(start_h_tables_locked(pk));
+    ZK_TRY(start_h_tables_locked(pk, false));
     return publish_h_tables_locked(pk, true);
 }
 
@@ -601,7 +613,7 @@ static int h_msm(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h, size_t lo, s
         int c, W;
         {
             std::lock_guard<std::mutex> lock(pk->h_mu);
-            if (start_build) ZK_TRY(start_h_tables_locked(pk));
+            if (start_build) ZK_TRY(start_h_tables_locked(pk, true));
             ZK_TRY(publish_h_tables_locked(pk, false));
             tab = pk->h_tab;
             c = pk->h_c;
@@ -648,8 +660,12 @@ int h_msm_blocks(zk_groth16_pk* pk, cudaStream_t st, const Fr* d_h_part, int log
             if (rc == ZK_OK && m >= (uint64_t)kHTablesMin && (uint64_t)pk->n_h >= n) {
                 g1_window_tables_shape(m, &hb.c, &hb.W);
                 if ((size_t)hb.W * m <= 0x7fffffffull) {  // keys index 32 bits: else the plain MSM, in passes
-                    if (cudaMalloc(&hb.tab, (size_t)hb.W * m * 64) != cudaSuccess) rc = ZK_ERR_CUDA;
-                    if (rc == ZK_OK) rc = g1_window_tables_build(pk->device, st, hb.pts, m, hb.c, hb.W, hb.tab);
+                    // the tables are an optimisation: without room for them the plain MSM serves
+                    if (cudaMalloc(&hb.tab, (size_t)hb.W * m * 64) != cudaSuccess) {
+                        cudaGetLastError();
+                        hb.tab = nullptr;
+                    }
+                    if (hb.tab) rc = g1_window_tables_build(pk->device, st, hb.pts, m, hb.c, hb.W, hb.tab);
                 }
             }
             if (rc == ZK_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = ZK_ERR_CUDA;
@@ -828,7 +844,7 @@ static int prove(zk_groth16_pk* pk, const R1cs& R, cudaStream_t st, const void* 
     // the witness context's scratch waits for the whole device).
     if (n_h > 0 && (size_t)n_h * 4 >= (size_t)pk->n_h * 3) {
         std::lock_guard<std::mutex> lock(pk->h_mu);
-        ZK_TRY(start_h_tables_locked(pk));
+        ZK_TRY(start_h_tables_locked(pk, true));
     }
     cudaEventElapsedTime(&ms, ev[0], ev[3]);
     stats.total_ms = ms;

@@ -84,6 +84,7 @@ struct zk_groth16_pk {
     int h_c = 0, h_W = 0;
     uint8_t* h_tab_pending = nullptr;
     int h_pc = 0, h_pW = 0;
+    bool h_tab_off = false;  // no device memory for them: proofs keep the plain MSM
     cudaStream_t h_tab_stream = nullptr;
     cudaEvent_t h_tab_done = nullptr;
     std::mutex h_mu;
