@@ -11,10 +11,9 @@
 // 2010, for BN curves): f_{6t+2, Q}(P) over the signed binary expansion of
 // 6t + 2 (t = 4965661367192848881, the BN parameter), then the lines through
 // [6t+2]Q and pi(Q), and through that sum and -pi^2(Q), pi the p-power
-// Frobenius.  Points of the loop are kept affine; the loops of the pairs of a
-// product advance together, so each step takes one Fp2 inversion for all of
-// them (Montgomery's trick).  The line through T with slope l (on the twist),
-// evaluated at P = (xP, yP), is
+// Frobenius.  Points of the loop are projective (no inversion in the loop);
+// the line through T with slope l (on the twist), evaluated at P = (xP, yP), is,
+// up to a factor in Fp2,
 //   yP - l xP w + (l xT - yT) w^3,
 // vertical lines omitted (they lie in a proper subfield and vanish under the
 // final exponentiation).
@@ -153,6 +152,7 @@ static bool eq(const Fp12& a, const Fp12& b) {
 // ---------------------------------------------------------------- derived constants
 struct Consts {
     Fp2 gamma[6];          // xi^(i (p - 1)/6): (w^i)^p = w^i gamma[i]
+    Fp2 b3;                // 3 b' = 9 / xi, b' = 3 / xi the twist's constant
     std::vector<int> naf;  // signed digits of 6t + 2, least significant first
     uint64_t l0[4], l1[4], l2[4];  // |l0|, |l1|, l2 (l0, l1 < 0)
     bool ok = false;
@@ -215,6 +215,7 @@ static Consts make_consts() {
     const Fp2 g1 = pow2(xi(), e);
     C.gamma[0] = one2();
     for (int i = 1; i < 6; i++) C.gamma[i] = mul(C.gamma[i - 1], g1);
+    C.b3 = mul(f2(fp_small(9), zkh::zero()), inv(xi()));
     // NAF of 6t + 2
     {
         uint64_t s[2];
@@ -378,95 +379,89 @@ struct G2a {
     bool inf;
 };
 
-// the line with slope l through (xT, yT) on the twist, at P
-static Fp12 line(const Fp2& l, const Fp2& xT, const Fp2& yT, const G1a& P) {
-    Fp12 r = {{zero2(), zero2(), zero2()}, {zero2(), zero2(), zero2()}};
-    r.c0.c0 = f2(P.y, zkh::zero());
-    r.c1.c0 = neg(mul_fp(l, P.x));
-    r.c1.c1 = sub(mul(l, xT), yT);
+// Points of the loop in homogeneous projective coordinates on the twist,
+// (X : Y : Z) for (X / Z, Y / Z), so that no step inverts.  A line is the
+// affine line yP - l xP w + (l xT - yT) w^3 times a factor in Fp2, which the
+// final exponentiation removes (Costello, Lange and Naehrig, "Faster pairing
+// computations on curves with high-degree twists", PKC 2010; the point formulas
+// after Aranha, Karabina, Longa, Gebotys and Lopez, Eurocrypt 2011).
+struct G2p {
+    Fp2 x, y, z;
+};
+static Fp12 line3(const Fp2& c_y, const Fp2& c_x, const Fp2& c_w3, const G1a& P) {
+    // c_y yP + c_x xP w + c_w3 w^3
+    Fp12 r = {{mul_fp(c_y, P.y), zero2(), zero2()}, {mul_fp(c_x, P.x), c_w3, zero2()}};
     return r;
 }
-// T <- 2T given inv2y = 1 / (2 yT); returns the tangent line at T
-static Fp12 dbl_step(G2a& T, const Fp2& inv2y, const G1a& P) {
-    const Fp2 x2 = sqr(T.x);
-    const Fp2 l = mul(add(add(x2, x2), x2), inv2y);
-    const Fp12 ln = line(l, T.x, T.y, P);
-    const Fp2 x3 = sub(sub(sqr(l), T.x), T.x);
-    T.y = sub(mul(l, sub(T.x, x3)), T.y);
-    T.x = x3;
+// T <- 2T; the tangent at T times 2 Y Z^2 / Z = 2 Y Z:
+//   2 Y Z yP - 3 X^2 xP w + (Y^2 - 3 b' Z^2) w^3
+// (from 3 X^3 - 2 Y^2 Z = Z (Y^2 - 3 b' Z^2) on Y^2 Z = X^3 + b' Z^3).  The new
+// point is the standard doubling scaled by 4 to avoid halving:
+//   (2 X Y (Y^2 - 9 b' Z^2), (Y^2 + 9 b' Z^2)^2 - 12 (3 b' Z^2)^2, 8 Y^3 Z)
+static Fp12 dbl_step(G2p& T, const G1a& P) {
+    const Consts& C = consts();
+    const Fp2 B = sqr(T.y), Cz = sqr(T.z), J = sqr(T.x);
+    const Fp2 E = mul(C.b3, Cz);          // 3 b' Z^2
+    const Fp2 F = add(add(E, E), E);      // 9 b' Z^2
+    const Fp2 H = sub(sub(sqr(add(T.y, T.z)), B), Cz);  // 2 Y Z
+    const Fp12 ln = line3(H, neg(add(add(J, J), J)), sub(B, E), P);
+    const Fp2 XY = mul(T.x, T.y);
+    const Fp2 E2 = sqr(E), E4 = add(add(E2, E2), add(E2, E2));
+    T.x = mul(add(XY, XY), sub(B, F));
+    T.y = sub(sqr(add(B, F)), add(add(E4, E4), E4));  // (B + F)^2 - 12 E^2
+    const Fp2 BH = mul(B, H);
+    T.z = add(add(BH, BH), add(BH, BH));  // 4 Y^2 (2 Y Z)
     return ln;
 }
-// T <- T + Q given invdx = 1 / (xQ - xT); returns the line through T and Q
-static Fp12 add_step(G2a& T, const G2a& Q, const Fp2& invdx, const G1a& P) {
-    const Fp2 l = mul(sub(Q.y, T.y), invdx);
-    const Fp12 ln = line(l, T.x, T.y, P);
-    const Fp2 x3 = sub(sub(sqr(l), T.x), Q.x);
-    T.y = sub(mul(l, sub(T.x, x3)), T.y);
-    T.x = x3;
+// T <- T + Q (Q affine); the line through T and Q times lambda = X - xQ Z:
+//   lambda yP - theta xP w + (theta xQ - lambda yQ) w^3, theta = Y - yQ Z
+static Fp12 add_step(G2p& T, const G2a& Q, const G1a& P) {
+    const Fp2 theta = sub(T.y, mul(Q.y, T.z)), lambda = sub(T.x, mul(Q.x, T.z));
+    const Fp12 ln = line3(lambda, neg(theta), sub(mul(theta, Q.x), mul(lambda, Q.y)), P);
+    const Fp2 Cc = sqr(theta), D = sqr(lambda);
+    const Fp2 E = mul(D, lambda), F = mul(T.z, Cc), G = mul(T.x, D);
+    const Fp2 H = sub(add(E, F), add(G, G));
+    const Fp2 y3 = sub(mul(theta, sub(G, H)), mul(T.y, E));
+    T.x = mul(lambda, H);
+    T.y = y3;
+    T.z = mul(T.z, E);
     return ln;
 }
 static G2a frob_g2(const G2a& Q) {
     const Consts& C = consts();
     return {mul(conj(Q.x), C.gamma[2]), mul(conj(Q.y), C.gamma[3]), Q.inf};
 }
-// v[i] <- 1 / v[i] with one inversion (Montgomery's trick): 3 (n - 1) products
-static void batch_inv(std::vector<Fp2>& v) {
-    if (v.empty()) return;
-    std::vector<Fp2> pre(v.size());
-    pre[0] = v[0];
-    for (size_t i = 1; i < v.size(); i++) pre[i] = mul(pre[i - 1], v[i]);
-    Fp2 acc = inv(pre.back());
-    for (size_t i = v.size() - 1; i > 0; i--) {
-        const Fp2 vi = mul(acc, pre[i - 1]);
-        acc = mul(acc, v[i]);
-        v[i] = vi;
-    }
-    v[0] = acc;
-}
 
 // prod_k f_{6t+2, Q_k}(P_k) (with the two Frobenius lines), pairs with an
-// infinite point skipped (their pairing is 1).  The loops of all pairs advance
-// together, so each step's slope denominators share one inversion.
+// infinite point skipped (their pairing is 1)
 static Fp12 multi_miller(const G1a* P, const G2a* Q, int n) {
     const Consts& C = consts();
-    std::vector<G2a> T;
+    std::vector<G2p> T;
     std::vector<int> idx;
     for (int k = 0; k < n; k++)
         if (!P[k].inf && !Q[k].inf) {
-            T.push_back(Q[k]);
+            T.push_back({Q[k].x, Q[k].y, one2()});
             idx.push_back(k);
         }
-    std::vector<Fp2> den(T.size());
     Fp12 f = one12();
     const int top = (int)C.naf.size() - 1;
     for (int i = top - 1; i >= 0; i--) {
         f = sqr(f);
-        for (size_t j = 0; j < T.size(); j++) den[j] = add(T[j].y, T[j].y);
-        batch_inv(den);
-        for (size_t j = 0; j < T.size(); j++) f = mul(f, dbl_step(T[j], den[j], P[idx[j]]));
+        for (size_t j = 0; j < T.size(); j++) f = mul(f, dbl_step(T[j], P[idx[j]]));
         if (C.naf[(size_t)i] != 0) {
-            std::vector<G2a> q(T.size());
             for (size_t j = 0; j < T.size(); j++) {
-                q[j] = Q[idx[j]];
-                if (C.naf[(size_t)i] < 0) q[j].y = neg(q[j].y);
-                den[j] = sub(q[j].x, T[j].x);
+                G2a q = Q[idx[j]];
+                if (C.naf[(size_t)i] < 0) q.y = neg(q.y);
+                f = mul(f, add_step(T[j], q, P[idx[j]]));
             }
-            batch_inv(den);
-            for (size_t j = 0; j < T.size(); j++) f = mul(f, add_step(T[j], q[j], den[j], P[idx[j]]));
         }
     }
-    for (int s2 = 0; s2 < 2; s2++) {  // the lines through pi(Q), then through -pi^2(Q)
-        std::vector<G2a> q(T.size());
-        for (size_t j = 0; j < T.size(); j++) {
-            q[j] = frob_g2(Q[idx[j]]);
-            if (s2 == 1) {
-                q[j] = frob_g2(q[j]);
-                q[j].y = neg(q[j].y);
-            }
-            den[j] = sub(q[j].x, T[j].x);
-        }
-        batch_inv(den);
-        for (size_t j = 0; j < T.size(); j++) f = mul(f, add_step(T[j], q[j], den[j], P[idx[j]]));
+    for (size_t j = 0; j < T.size(); j++) {
+        const G2a q1 = frob_g2(Q[idx[j]]);
+        G2a q2 = frob_g2(q1);
+        q2.y = neg(q2.y);
+        f = mul(f, add_step(T[j], q1, P[idx[j]]));
+        f = mul(f, add_step(T[j], q2, P[idx[j]]));
     }
     return f;
 }
